@@ -1,0 +1,416 @@
+"""Benchmark of the Polar Express step on B200 (one JSON line on rank 0).
+
+Workload: one ``polar_step`` on X bf16 [8, 512, 2048]
+per GPU, N(0,1) entries from seed (rank), each matrix scaled by
+1/(||X||_F*1.01 + 1e-6), step-1 coefficients.  With ``--gpus N`` (torchrun,
+one process per GPU) every rank runs its own batch of 8 matrices: the batch
+is sharded across GPUs with no collective on the data path (weak scaling).
+
+value     effective TFLOP/s of the whole job: nominal FLOPs
+          (4 M^2 N + 2 M^3 per matrix) x matrices x K / max-over-ranks time
+          of K steps, inputs resident in HBM, each step one replay of a CUDA
+          graph captured through the public API ``polar_step``.
+e2e       the same metric through the public API without graphs, with the
+          step's input copied host->device from pinned memory and its output
+          copied back inside the timed region.
+roofline  the dominant kernel's nominal FLOPs per launch / its CUDA-event
+          time (timed alone, same buffers), against the measured bf16 peak.
+
+``--impl reference`` times the reference's PyTorch formula
+(tests/test_polar_step.py:22-28 of the reference, restated in
+oracle/polar_oracle.py) on the host CPU with every thread, rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+if str(REPO) not in sys.path:
+    sys.path.insert(0, str(REPO))
+
+BATCH, M, N = 8, 512, 2048
+ROTATION = 8             # input sets cycled through: 8 x 42 MB > 126 MB L2
+L2_BYTES = 126 * 2 ** 20
+FALLBACK_TFLOPS = 1590.0
+
+
+def nominal_flops_per_matrix(m: int, n: int) -> int:
+    return 4 * m * m * n + 2 * m ** 3
+
+
+def parse_args():
+    p = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=2000)
+    p.add_argument("--warmup", type=int, default=20)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--e2e-steps", type=int, default=200,
+                   help="steps of the host-buffer end-to-end loop (<= --steps)")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    return p.parse_args()
+
+
+# --------------------------------------------------------------------- clocks
+class ClockSampler:
+    """Samples SM clock and clock-event reasons through NVML in a thread."""
+
+    REASONS = {
+        0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
+        0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
+        0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
+        0x100: "display_clock_setting",
+    }
+
+    def __init__(self, device_index: int, interval_s: float = 0.005):
+        self.samples = []
+        self.reasons = 0
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._thread = None
+        self._interval = interval_s
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self._nvml = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+        except Exception:  # noqa: BLE001 - clocks are reported as unavailable
+            self._nvml = None
+
+    def _sample(self):
+        nv = self._nvml
+        self.samples.append(nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM))
+        try:
+            r = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+        except Exception:  # noqa: BLE001
+            r = nv.nvmlDeviceGetCurrentClocksThrottleReasons(self._h)
+        self.reasons |= int(r) & ~0x1
+
+    def _run(self):
+        self._sample()
+        while not self._stop.wait(self._interval):
+            self._sample()
+
+    def __enter__(self):
+        if self._nvml is not None:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        if self._thread is not None:
+            self._stop.set()
+            self._thread.join()
+            self._sample()
+
+    def summary(self):
+        if self._nvml is None or not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvml unavailable"]}
+        return {
+            "sm_mhz": statistics.median(self.samples),
+            "sm_max_mhz": self.max_mhz,
+            "samples": len(self.samples),
+            "reasons": [name for bit, name in self.REASONS.items() if self.reasons & bit],
+        }
+
+
+# --------------------------------------------------------------------- helpers
+def measured_peaks():
+    path = REPO / "MEASURED_PEAKS.json"
+    if path.is_file():
+        peaks = json.loads(path.read_text())
+        return float(peaks["bf16_tflops"]), "measured"
+    return FALLBACK_TFLOPS, "fallback"
+
+
+def profiled_traffic():
+    """Per-launch DRAM bytes of the dominant kernel from the committed ncu
+    summary (profiles/ncu_traffic.json), or None."""
+    path = REPO / "profiles" / "ncu_traffic.json"
+    if path.is_file():
+        return json.loads(path.read_text())
+    return None
+
+
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", str(rank)))
+    return rank, world, local
+
+
+def cpu_reference_rate(steps: int, warmup: int, budget_s: float):
+    """Times the reference formula (bf16, CPU, all threads) on a sample of the
+    workload.  Returns (TFLOP/s, threads, sample description)."""
+    import torch
+
+    from oracle.polar_oracle import COEFFICIENTS, make_input, reference_formula
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    coeffs = COEFFICIENTS[:1]
+    probe = make_input((1, M, N), seed=0)
+    t0 = time.perf_counter()
+    reference_formula(probe, coeffs)
+    per_matrix = max(time.perf_counter() - t0, 1e-4)
+    total = max(steps + warmup, 1)
+    batch = max(1, min(BATCH, int(budget_s / (per_matrix * total))))
+    x = make_input((batch, M, N), seed=0)
+    for _ in range(warmup):
+        reference_formula(x, coeffs)
+    times = []
+    for _ in range(max(steps, 1)):
+        t0 = time.perf_counter()
+        reference_formula(x, coeffs)
+        times.append(time.perf_counter() - t0)
+    med = statistics.median(times)
+    rate = batch * nominal_flops_per_matrix(M, N) / med / 1e12
+    sample = (f"{len(times)} timed steps (median) of the reference formula on "
+              f"{batch} of the {BATCH} matrices [{M},{N}] bf16, after {warmup} warm-up")
+    return rate, threads, sample
+
+
+# --------------------------------------------------------------------- arms
+def run_reference(args):
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return
+    rate, threads, sample = cpu_reference_rate(args.steps, args.warmup, budget_s=120.0)
+    ms = BATCH * nominal_flops_per_matrix(M, N) / (rate * 1e12) * 1e3
+    line = {
+        "impl": "reference",
+        "metric": "polar_step effective TFLOP/s at [8,512,2048] bf16",
+        "value": rate, "unit": "TFLOP/s", "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "polar_step [8,512,2048] bf16 single step (BASELINE config 1)",
+                   "global_batch": BATCH, "m": M, "n": N,
+                   "parallelism": "host CPU, rank 0 only"},
+        "cpu_baseline": {"value": rate, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": rate, "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    import muon_fusion_ascend950_b200 as pkg
+    from muon_fusion_ascend950_b200.capi import capi
+
+    rank, world, local = dist_env()
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", device_id=device, timeout=timedelta(seconds=120))
+    api = capi()
+    a, b, c = (8.156554524902461, -22.48329292557795, 15.878769915207462)
+    flops_step = BATCH * nominal_flops_per_matrix(M, N)
+
+    # inputs generated on the device (seeded per rank and set), normalised as
+    # the reference test does
+    gen = torch.Generator(device=device)
+    xs = []
+    for i in range(ROTATION):
+        gen.manual_seed(1000 * rank + i)
+        x = torch.randn((BATCH, M, N), generator=gen, device=device, dtype=torch.float32)
+        x = x.to(torch.bfloat16)
+        xs.append(x / (x.norm(dim=(-2, -1), keepdim=True) * 1.01 + 1e-6))
+    stream = torch.cuda.Stream(device)
+
+    def sync_all():
+        torch.cuda.synchronize(device)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(device)
+
+    # ---- CUDA graphs, one step each, through the public API
+    graphs, outs = [], []
+    with torch.cuda.stream(stream):
+        for x in xs:  # eager warm-up of every set before capture
+            pkg.polar_step(x, a, b, c)
+    torch.cuda.synchronize(device)
+    launches_before = api.launch_count()
+    for x in xs:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            outs.append(pkg.polar_step(x, a, b, c))
+        graphs.append(g)
+    launches_per_step = (api.launch_count() - launches_before) // ROTATION
+
+    with torch.cuda.stream(stream):
+        for i in range(args.warmup):
+            graphs[i % ROTATION].replay()
+        # keep the GPU busy long enough for the clocks to settle
+        t_end = time.perf_counter() + 0.3
+        i = 0
+        while time.perf_counter() < t_end:
+            graphs[i % ROTATION].replay()
+            i += 1
+    sync_all()
+
+    sampler = ClockSampler(local)
+    start = torch.cuda.Event(enable_timing=True)
+    stop = torch.cuda.Event(enable_timing=True)
+    with sampler:
+        sync_all()
+        with torch.cuda.stream(stream):
+            start.record(stream)
+            for i in range(args.steps):
+                graphs[i % ROTATION].replay()
+            stop.record(stream)
+        stop.synchronize()
+        sync_all()
+    elapsed_ms = start.elapsed_time(stop)
+    if world > 1:
+        t = torch.tensor([elapsed_ms], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        elapsed_ms = float(t.item())
+    ms_per_step = elapsed_ms / args.steps
+    value = world * flops_step * args.steps / (elapsed_ms * 1e-3) / 1e12
+
+    # ---- per-kernel CUDA-event timing (same buffers, kernels timed alone)
+    mp = api.padded_rows(M)
+    gram = torch.empty((BATCH, mp, mp), dtype=torch.bfloat16, device=device)
+    poly = torch.empty_like(gram)
+    y = torch.empty_like(xs[0])
+    kernel_iters = max(50, min(args.steps, 1000))
+
+    def time_kernel(fn):
+        with torch.cuda.stream(stream):
+            for i in range(5):
+                fn(i)
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for i in range(kernel_iters):
+                fn(i)
+            e1.record(stream)
+        e1.synchronize()
+        return e0.elapsed_time(e1) / kernel_iters * 1e3  # us
+
+    with torch.cuda.stream(stream):
+        api.gram(xs[0], gram, stream=stream)
+        api.poly(gram, poly, b, c, stream=stream)
+    us = {
+        "gram": time_kernel(lambda i: api.gram(xs[i % ROTATION], gram, stream=stream)),
+        "poly": time_kernel(lambda i: api.poly(gram, poly, b, c, stream=stream)),
+        "apply": time_kernel(lambda i: api.apply(poly, xs[i % ROTATION], y, a, stream=stream)),
+    }
+    kernel_flops = {"gram": BATCH * 2 * M * M * N, "poly": BATCH * 2 * M ** 3,
+                    "apply": BATCH * 2 * M * M * N}
+    dominant = max(us, key=us.get)
+    peak, peak_kind = measured_peaks()
+    achieved = kernel_flops[dominant] / (us[dominant] * 1e-6) / 1e12
+    traffic_info = profiled_traffic()
+    traffic = None
+    if traffic_info and dominant in traffic_info.get("kernels", {}):
+        traffic = traffic_info["kernels"][dominant].get("dram_bytes_per_launch")
+    roofline = {
+        "bound": "tensor", "kernel": dominant, "achieved": achieved, "peak": peak,
+        "unit": "TFLOP/s", "frac": achieved / peak, "traffic": traffic,
+        "peak_source": f"{peak_kind} bf16 dense (burst)",
+        "kernel_us": us,
+        "kernel_tflops": {k: kernel_flops[k] / (us[k] * 1e-6) / 1e12 for k in us},
+    }
+
+    # ---- end to end through the public API with host buffers
+    e2e_steps = max(1, min(args.e2e_steps, args.steps))
+    host_in = [x.cpu().pin_memory() for x in xs]
+    host_out = torch.empty(xs[0].shape, dtype=torch.bfloat16).pin_memory()
+    with torch.cuda.stream(stream):
+        for i in range(3):
+            xd = host_in[i % ROTATION].to(device, non_blocking=True)
+            host_out.copy_(pkg.polar_step(xd, a, b, c), non_blocking=True)
+    sync_all()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for i in range(e2e_steps):
+            xd = host_in[i % ROTATION].to(device, non_blocking=True)
+            host_out.copy_(pkg.polar_step(xd, a, b, c), non_blocking=True)
+        e1.record(stream)
+    e1.synchronize()
+    e2e_ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e_value = world * flops_step * e2e_steps / (e2e_ms * 1e-3) / 1e12
+    step_bytes = xs[0].numel() * xs[0].element_size()
+
+    # ---- CPU baseline (rank 0, N=1 only)
+    cpu_baseline = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        rate, threads, sample = cpu_reference_rate(3, 1, budget_s=20.0)
+        cpu_baseline = {"value": rate, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+                        "sample": sample}
+
+    for g in graphs:
+        g.reset()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    line = {
+        "metric": "polar_step effective TFLOP/s at [8,512,2048] bf16",
+        "value": value,
+        "unit": "TFLOP/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms_per_step,
+        "us_per_step": ms_per_step * 1e3,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic",
+        "pct_of_bf16_peak": 100.0 * value / (world * peak),
+        "config": {
+            "workload": "polar_step [8,512,2048] bf16 single step (BASELINE config 1) per GPU",
+            "global_batch": BATCH * world, "m": M, "n": N,
+            "parallelism": f"batch-sharded x{world}, no data-path collective",
+            "timing": "CUDA-graph replay of the public polar_step, CUDA events, max over ranks",
+            "l2": f"inputs larger than L2: {ROTATION} rotating input sets "
+                  f"({ROTATION} x {(3 * step_bytes + 2 * BATCH * 512 * 512 * 2) >> 20} MB touched "
+                  f"per cycle > {L2_BYTES >> 20} MB L2)",
+        },
+        "roofline": roofline,
+        "cpu_baseline": cpu_baseline,
+        "e2e": {"value": e2e_value, "unit": "TFLOP/s", "steps": e2e_steps,
+                "h2d_bytes_per_step": step_bytes, "d2h_bytes_per_step": step_bytes,
+                "ms_per_step": e2e_ms / e2e_steps},
+        "clocks": sampler.summary(),
+        "gpu_launches": launches_per_step * args.steps,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,139 @@
+/*
+ * muon_polar_sm100.h -- C ABI of the B200 (sm_100a) Polar Express step.
+ *
+ * One Polar Express (Newton-Schulz) step of Muon:
+ *     A = X . X^T            (kernel 1, symmetric Gram, bf16 storage)
+ *     P = b . A + c . A . A  (kernel 2, polynomial, bf16 storage)
+ *     Y = a . X + P . X      (kernel 3, apply)
+ * for a batch of bf16 matrices X[batch][m][n] (row stride ldx elements,
+ * batch stride m*ldx elements).
+ *
+ * Every entry point
+ *   - takes plain device pointers, sizes and a cudaStream_t passed as void*,
+ *   - allocates nothing (the caller owns every buffer),
+ *   - launches asynchronously on `stream` and returns a status code:
+ *       0                      success
+ *       < 0                    MUON_POLAR_ERR_* (argument / setup error,
+ *                              nothing was launched)
+ *       > 0                    the cudaError_t reported by the launch.
+ *
+ * The reference (Ascend 950PR build) exposes three launchers with the
+ * signature `void launch_xxx(void* in..., void* out, void* tilingDevice,
+ * uint32_t blockDim, aclrtStream stream)`:
+ *   csrc/muon_polar_unified_ascend950.asc:512-517   launch_muon_gram_lowlevel_fused
+ *   csrc/muon_polar_unified_ascend950.asc:1030-1035 launch_muon_cube2_p_fused
+ *   csrc/muon_polar_unified_ascend950.asc:1535-1540 launch_muon_cube3_fused_lowlevel
+ * declared at csrc/muon_polar_step_binding.cpp:65-70.  Here the tiling
+ * struct and block count are computed inside the library (they depend only
+ * on sizes and the device), so each launcher takes sizes instead.
+ */
+#ifndef MUON_POLAR_SM100_H
+#define MUON_POLAR_SM100_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MUON_POLAR_ABI_VERSION 1
+
+#define MUON_POLAR_OK 0
+#define MUON_POLAR_ERR_INVALID_ARGUMENT (-1)
+#define MUON_POLAR_ERR_UNSUPPORTED_DEVICE (-2)
+#define MUON_POLAR_ERR_ALIGNMENT (-3)
+#define MUON_POLAR_ERR_TENSOR_MAP (-4)
+#define MUON_POLAR_ERR_WORKSPACE (-5)
+#define MUON_POLAR_ERR_DRIVER (-6)
+
+/* Bits of the device watchdog word (muon_polar_read_device_status). A bit is
+ * set when a bounded wait inside a kernel gave up; the kernel then left its
+ * loop, drained what it had in flight, released its tensor memory and
+ * returned instead of hanging. */
+#define MUON_POLAR_WATCHDOG_PRODUCER 0x1u
+#define MUON_POLAR_WATCHDOG_MMA 0x2u
+#define MUON_POLAR_WATCHDOG_EPILOGUE 0x4u
+#define MUON_POLAR_WATCHDOG_DRAIN 0x8u
+
+/* Library version of this ABI (MUON_POLAR_ABI_VERSION). */
+int muon_polar_abi_version(void);
+
+/* Human-readable text for a status code returned by any entry point. */
+const char* muon_polar_status_string(int status);
+
+/* Rows of the square Gram/polynomial buffers for `m` rows of X: m rounded up
+ * to 128, the tile height (reference rule rows = align(M,128),
+ * csrc/muon_polar_step_binding.cpp:630). */
+int64_t muon_polar_padded_rows(int64_t m);
+
+/* Bytes of the workspace muon_polar_step_sm100 needs: A and P, each
+ * [batch][Mp][Mp] bf16 with Mp = muon_polar_padded_rows(m).  Replaces the two
+ * at::empty calls of csrc/muon_polar_step_binding.cpp:646,657. */
+size_t muon_polar_workspace_bytes(int64_t batch, int64_t m);
+
+/* Kernel (1): gram[b] = X[b] . X[b]^T, bf16 [batch][Mp][Mp] (row stride Mp).
+ * fp32 accumulation, one round-to-nearest-even to bf16.  Only tiles with
+ * tile_row <= tile_col are computed; each is written at (tm,tn) and mirrored
+ * to (tn,tm).  Rows/cols >= m are written as zeros.
+ * Requirements: x 16-byte aligned, ldx % 8 == 0, ldx >= n, gram 16-byte
+ * aligned.
+ * Replaces launch_muon_gram_lowlevel_fused (asc:512-517). */
+int muon_polar_gram_sm100(const void* x, void* gram, int64_t batch, int64_t m,
+                          int64_t n, int64_t ldx, void* stream);
+
+/* Kernel (1), fp32 output variant: partial Gram in fp32 for the column-sharded
+ * multi-GPU path (the partials are summed across ranks before kernel 2).
+ * Same layout and requirements as muon_polar_gram_sm100, gram is float. */
+int muon_polar_gram_f32_sm100(const void* x, void* gram_f32, int64_t batch,
+                              int64_t m, int64_t n, int64_t ldx, void* stream);
+
+/* Kernel (2): poly[b] = bf16( b*f32(gram[b]) + c*(gram[b].gram[b])_f32 ),
+ * both [batch][Mp][Mp] bf16, Mp a multiple of 128.  Products and the sum are
+ * separately rounded fp32 operations (no FMA), as in
+ * csrc/muon_polar_unified_ascend950.asc:929-940.  Upper tiles are computed
+ * and mirrored.  Replaces launch_muon_cube2_p_fused (asc:1030-1035). */
+int muon_polar_poly_sm100(const void* gram, void* poly, int64_t batch,
+                          int64_t mp, float b, float c, void* stream);
+
+/* Kernel (3): y[b] = bf16(T) + bf16(alpha_bf16 * x) with T = (poly[b].x[b])
+ * accumulated in fp32 and the final add done on bf16 values, as in
+ * csrc/muon_polar_unified_ascend950.asc:1472-1476; alpha_bf16 is `a`
+ * rounded to bf16 (csrc/muon_polar_step_binding.cpp:156-162).  poly is
+ * [batch][Mp][Mp] bf16; x and y are [batch][m][ld] with ldx, ldy % 8 == 0.
+ * Replaces launch_muon_cube3_fused_lowlevel (asc:1535-1540). */
+int muon_polar_apply_sm100(const void* poly, const void* x, void* y,
+                           int64_t batch, int64_t m, int64_t n, int64_t ldx,
+                           int64_t ldy, float a, void* stream);
+
+/* The whole step: kernels 1, 2, 3 back to back on `stream` (programmatic
+ * dependent launch lets each kernel's prologue overlap the previous
+ * kernel's tail).  workspace must hold muon_polar_workspace_bytes(batch, m)
+ * bytes, 16-byte aligned.  y must not alias x.
+ * Replaces the launch sequence of csrc/muon_polar_step_binding.cpp:644-666. */
+int muon_polar_step_sm100(const void* x, void* y, void* workspace,
+                          size_t workspace_bytes, int64_t batch, int64_t m,
+                          int64_t n, int64_t ldx, int64_t ldy, float a,
+                          float b, float c, void* stream);
+
+/* dst[i] = bf16_rne(src[i]) for i < count (fp32 Gram after the cross-rank
+ * sum -> bf16 input of kernel 2). No counterpart in the reference, which has
+ * no multi-device path. */
+int muon_polar_cast_f32_bf16_sm100(const void* src, void* dst, int64_t count,
+                                   void* stream);
+
+/* Reads (and, if clear != 0, resets) the watchdog word of `device`.  This
+ * call synchronises the device.  No counterpart in the reference, whose
+ * kernels have no bounded waits (CheckAcl at binding.cpp:72-75 is the only
+ * error path). */
+int muon_polar_read_device_status(int device, uint32_t* flags, int clear);
+
+/* Number of kernels the library has launched in this process (all entry
+ * points, all devices).  Used by benchmarks to report launch counts. */
+uint64_t muon_polar_launch_count(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MUON_POLAR_SM100_H */

@@ -1,0 +1,164 @@
+"""ctypes binding of the C ABI in include/muon_polar_sm100.h.
+
+This is the binding a ctypes-based caller of the reference's launchers would
+add (csrc/muon_polar_step_binding.cpp:65-70 declares those).  The tests use
+it to drive the kernels through the exact boundary other languages see, and
+the multi-GPU drivers use the per-stage entry points.  Loading the library
+needs no GPU; every compute call needs an sm_100 device.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from pathlib import Path
+from typing import Optional
+
+LIB_FILENAME = "libmuon_polar_sm100.so"
+
+# Every entry point declared in include/muon_polar_sm100.h:
+# name -> (restype, argtypes)
+_I64 = ctypes.c_int64
+_VP = ctypes.c_void_p
+SIGNATURES = {
+    "muon_polar_abi_version": (ctypes.c_int, []),
+    "muon_polar_status_string": (ctypes.c_char_p, [ctypes.c_int]),
+    "muon_polar_padded_rows": (_I64, [_I64]),
+    "muon_polar_workspace_bytes": (ctypes.c_size_t, [_I64, _I64]),
+    "muon_polar_gram_sm100": (ctypes.c_int, [_VP, _VP, _I64, _I64, _I64, _I64, _VP]),
+    "muon_polar_gram_f32_sm100": (ctypes.c_int, [_VP, _VP, _I64, _I64, _I64, _I64, _VP]),
+    "muon_polar_poly_sm100": (ctypes.c_int, [_VP, _VP, _I64, _I64, ctypes.c_float,
+                                             ctypes.c_float, _VP]),
+    "muon_polar_apply_sm100": (ctypes.c_int, [_VP, _VP, _VP, _I64, _I64, _I64, _I64,
+                                              _I64, ctypes.c_float, _VP]),
+    "muon_polar_step_sm100": (ctypes.c_int, [_VP, _VP, _VP, ctypes.c_size_t, _I64, _I64,
+                                             _I64, _I64, _I64, ctypes.c_float,
+                                             ctypes.c_float, ctypes.c_float, _VP]),
+    "muon_polar_cast_f32_bf16_sm100": (ctypes.c_int, [_VP, _VP, _I64, _VP]),
+    "muon_polar_read_device_status": (ctypes.c_int, [ctypes.c_int,
+                                                     ctypes.POINTER(ctypes.c_uint32),
+                                                     ctypes.c_int]),
+    "muon_polar_launch_count": (ctypes.c_uint64, []),
+}
+
+WATCHDOG_PRODUCER = 0x1
+WATCHDOG_MMA = 0x2
+WATCHDOG_EPILOGUE = 0x4
+WATCHDOG_DRAIN = 0x8
+
+
+class MuonPolarError(RuntimeError):
+    """A C-ABI entry point returned a non-zero status."""
+
+    def __init__(self, func: str, status: int, text: str):
+        super().__init__(f"{func} failed, status={status}: {text}")
+        self.status = status
+
+
+def library_path() -> Path:
+    configured = os.environ.get("MUON_POLAR_SM100_LIBRARY")
+    if configured:
+        return Path(configured).expanduser().resolve()
+    return Path(__file__).resolve().parent / LIB_FILENAME
+
+
+class CAPI:
+    """Typed access to libmuon_polar_sm100.so."""
+
+    def __init__(self, path: Optional[Path] = None):
+        path = Path(path) if path is not None else library_path()
+        if not path.is_file():
+            raise RuntimeError(
+                f"{path} is missing; build it with `python -m muon_fusion_ascend950_b200.build`")
+        self.path = path
+        self.lib = ctypes.CDLL(str(path))
+        for name, (restype, argtypes) in SIGNATURES.items():
+            fn = getattr(self.lib, name)
+            fn.restype = restype
+            fn.argtypes = argtypes
+
+    # -------------------------------------------------------------- helpers
+    def status_string(self, status: int) -> str:
+        return self.lib.muon_polar_status_string(int(status)).decode()
+
+    def _check(self, func: str, status: int) -> None:
+        if status != 0:
+            raise MuonPolarError(func, status, self.status_string(status))
+
+    @staticmethod
+    def _stream(stream) -> int:
+        import torch
+
+        if stream is None:
+            stream = torch.cuda.current_stream()
+        return int(getattr(stream, "cuda_stream", stream))
+
+    def abi_version(self) -> int:
+        return int(self.lib.muon_polar_abi_version())
+
+    def padded_rows(self, m: int) -> int:
+        return int(self.lib.muon_polar_padded_rows(int(m)))
+
+    def workspace_bytes(self, batch: int, m: int) -> int:
+        return int(self.lib.muon_polar_workspace_bytes(int(batch), int(m)))
+
+    def launch_count(self) -> int:
+        return int(self.lib.muon_polar_launch_count())
+
+    def read_device_status(self, device: int, clear: bool = True) -> int:
+        flags = ctypes.c_uint32(0)
+        self._check("muon_polar_read_device_status",
+                    self.lib.muon_polar_read_device_status(int(device), ctypes.byref(flags),
+                                                           1 if clear else 0))
+        return int(flags.value)
+
+    # -------------------------------------------------------------- kernels
+    # Tensors are torch tensors on the current CUDA device; x is [B, M, ld]
+    # with the first n columns valid.
+    def gram(self, x, gram, n: Optional[int] = None, stream=None) -> None:
+        b, m, ld = x.shape
+        n = ld if n is None else n
+        self._check("muon_polar_gram_sm100", self.lib.muon_polar_gram_sm100(
+            x.data_ptr(), gram.data_ptr(), b, m, n, ld, self._stream(stream)))
+
+    def gram_f32(self, x, gram_f32, n: Optional[int] = None, stream=None) -> None:
+        b, m, ld = x.shape
+        n = ld if n is None else n
+        self._check("muon_polar_gram_f32_sm100", self.lib.muon_polar_gram_f32_sm100(
+            x.data_ptr(), gram_f32.data_ptr(), b, m, n, ld, self._stream(stream)))
+
+    def poly(self, gram, poly, b: float, c: float, stream=None) -> None:
+        bsz, mp, _ = gram.shape
+        self._check("muon_polar_poly_sm100", self.lib.muon_polar_poly_sm100(
+            gram.data_ptr(), poly.data_ptr(), bsz, mp, float(b), float(c),
+            self._stream(stream)))
+
+    def apply(self, poly, x, y, a: float, n: Optional[int] = None, stream=None) -> None:
+        bsz, m, ldx = x.shape
+        n = ldx if n is None else n
+        self._check("muon_polar_apply_sm100", self.lib.muon_polar_apply_sm100(
+            poly.data_ptr(), x.data_ptr(), y.data_ptr(), bsz, m, n, ldx, y.shape[-1],
+            float(a), self._stream(stream)))
+
+    def step(self, x, y, workspace, a: float, b: float, c: float,
+             n: Optional[int] = None, stream=None) -> None:
+        bsz, m, ldx = x.shape
+        n = ldx if n is None else n
+        self._check("muon_polar_step_sm100", self.lib.muon_polar_step_sm100(
+            x.data_ptr(), y.data_ptr(), workspace.data_ptr(),
+            workspace.numel() * workspace.element_size(), bsz, m, n, ldx, y.shape[-1],
+            float(a), float(b), float(c), self._stream(stream)))
+
+    def cast_f32_bf16(self, src, dst, stream=None) -> None:
+        self._check("muon_polar_cast_f32_bf16_sm100", self.lib.muon_polar_cast_f32_bf16_sm100(
+            src.data_ptr(), dst.data_ptr(), src.numel(), self._stream(stream)))
+
+
+_CAPI: Optional[CAPI] = None
+
+
+def capi() -> CAPI:
+    """Process-wide CAPI instance (the library is loaded once)."""
+    global _CAPI
+    if _CAPI is None:
+        _CAPI = CAPI()
+    return _CAPI

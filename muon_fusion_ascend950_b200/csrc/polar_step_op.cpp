@@ -1,0 +1,130 @@
+// polar_step_op.cpp -- PyTorch operator muon_ascend950::polar_step on CUDA.
+//
+// Host side of the drop-in boundary: the same schema, checks, error texts,
+// padding/crop contract and debug-sync switch as the reference binding
+// (csrc/muon_polar_step_binding.cpp:613-685), dispatching to the sm_100a
+// C ABI (include/muon_polar_sm100.h) instead of three AscendC launchers.
+//
+// Differences from the reference binding, none visible in results:
+//   * rows are never padded: the kernels read rows >= M as zeros through
+//     the TMA bounds check and mask their stores, so A/P keep align(M,128)
+//     rows without a padded copy of X;
+//   * columns are padded (to a multiple of 16, zero filled) only when N is
+//     not a multiple of 8 or the data pointer is not 16-byte aligned -- the
+//     TMA row-stride rule -- instead of always to max(align16(N), rows);
+//   * tiling is derived from sizes inside the library, so there is no
+//     tiling cache to key on stream/shape/coefficients (binding.cpp:103-611).
+#include <ATen/ATen.h>
+#include <c10/core/DeviceGuard.h>
+#include <c10/cuda/CUDAFunctions.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <c10/cuda/CUDAStream.h>
+#include <torch/library.h>
+
+#include <cstdint>
+#include <cstdlib>
+
+#include "muon_polar_sm100.h"
+
+namespace {
+
+int64_t AlignUp(int64_t value, int64_t alignment) {
+  return (value + alignment - 1) / alignment * alignment;
+}
+
+bool DebugSyncEnabled() {
+  // Read on every call, as the reference does (binding.cpp:93-101).
+  return std::getenv("MUON_POLAR_DEBUG_SYNC") != nullptr;
+}
+
+void CheckStatus(int rc, const char* stage) {
+  TORCH_CHECK(rc == MUON_POLAR_OK, "muon_polar_step: stage ", stage,
+              " failed, status=", rc, ", detail=", muon_polar_status_string(rc));
+}
+
+// Synchronises and surfaces asynchronous faults and watchdog trips per stage.
+void DebugSync(int device, const char* stage) {
+  uint32_t flags = 0;
+  const int rc = muon_polar_read_device_status(device, &flags, /*clear=*/1);
+  TORCH_CHECK(rc == MUON_POLAR_OK, "muon_polar_step: stage ", stage,
+              " failed, status=", rc, ", detail=", muon_polar_status_string(rc));
+  TORCH_CHECK(flags == 0, "muon_polar_step: stage ", stage,
+              " gave up on a bounded wait, watchdog=", flags);
+}
+
+at::Tensor MuonPolarStepCuda(const at::Tensor& x, double a, double b,
+                             double c) {
+  TORCH_CHECK(x.defined(), "muon_polar_step: x must be defined");
+  TORCH_CHECK(x.device().is_cuda(), "muon_polar_step: x must be a CUDA tensor");
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16,
+              "muon_polar_step: only bfloat16 is supported");
+  TORCH_CHECK(x.dim() == 3, "muon_polar_step: x must have shape [batch, M, N]");
+  TORCH_CHECK(x.size(0) > 0 && x.size(1) > 0 && x.size(2) > 0,
+              "muon_polar_step: all dimensions must be positive");
+  TORCH_CHECK(x.size(1) <= x.size(2),
+              "muon_polar_step: expects M <= N; transpose policy stays outside "
+              "this op");
+  const c10::cuda::CUDAGuard deviceGuard(x.device());
+  at::Tensor input = x.contiguous();
+  const int64_t batch = input.size(0);
+  const int64_t rows = input.size(1);
+  const int64_t cols = input.size(2);
+  const bool aligned =
+      (cols % 8) == 0 &&
+      (reinterpret_cast<uintptr_t>(input.data_ptr()) % 16) == 0;
+  int64_t ld = cols;
+  if (!aligned) {
+    ld = AlignUp(cols, 16);
+    at::Tensor padded = at::zeros({batch, rows, ld}, input.options());
+    padded.narrow(2, 0, cols).copy_(input);
+    input = padded;
+  }
+  const auto stream = c10::cuda::getCurrentCUDAStream(x.device().index());
+  void* raw_stream = static_cast<void*>(stream.stream());
+  const size_t wsBytes = muon_polar_workspace_bytes(batch, rows);
+  at::Tensor workspace =
+      at::empty({static_cast<int64_t>(wsBytes)}, input.options().dtype(at::kByte));
+  at::Tensor out = at::empty({batch, rows, ld}, input.options());
+  const float fa = static_cast<float>(a);
+  const float fb = static_cast<float>(b);
+  const float fc = static_cast<float>(c);
+
+  if (!DebugSyncEnabled()) {
+    CheckStatus(muon_polar_step_sm100(input.data_ptr(), out.data_ptr(),
+                                      workspace.data_ptr(), wsBytes, batch,
+                                      rows, cols, ld, ld, fa, fb, fc,
+                                      raw_stream),
+                "polar_step_sm100");
+  } else {
+    const int device = x.device().index();
+    const int64_t mp = muon_polar_padded_rows(rows);
+    uint8_t* ws = static_cast<uint8_t*>(workspace.data_ptr());
+    void* gram = ws;
+    void* poly = ws + static_cast<size_t>(batch * mp * mp * 2);
+    CheckStatus(muon_polar_gram_sm100(input.data_ptr(), gram, batch, rows,
+                                      cols, ld, raw_stream),
+                "gram_sm100");
+    DebugSync(device, "gram_sm100");
+    CheckStatus(muon_polar_poly_sm100(gram, poly, batch, mp, fb, fc,
+                                      raw_stream),
+                "poly_sm100");
+    DebugSync(device, "poly_sm100");
+    CheckStatus(muon_polar_apply_sm100(poly, input.data_ptr(), out.data_ptr(),
+                                       batch, rows, cols, ld, ld, fa,
+                                       raw_stream),
+                "apply_sm100");
+    DebugSync(device, "apply_sm100");
+  }
+  if (aligned) return out;
+  return out.narrow(2, 0, cols).contiguous();
+}
+
+}  // namespace
+
+TORCH_LIBRARY(muon_ascend950, m) {
+  m.def("polar_step(Tensor x, float a, float b, float c) -> Tensor");
+}
+
+TORCH_LIBRARY_IMPL(muon_ascend950, CUDA, m) {
+  m.impl("polar_step", &MuonPolarStepCuda);
+}

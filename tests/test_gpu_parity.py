@@ -1,0 +1,232 @@
+"""GPU parity of the sm_100a kernels against the CPU oracle.
+
+Stage tests drive each kernel through the C ABI (include/muon_polar_sm100.h)
+and compare it with the oracle fed the SAME inputs (the previous stage's GPU
+output), so each bound isolates one kernel:
+
+* Gram / Poly: the output is one round-to-nearest-even of an fp32
+  accumulation of K products, whose error is at most
+  gamma_K * sum|products| with gamma_K = K * 2^-24 (deterministic bound for
+  recursive fp32 summation; doubled here for the tensor core's blocked
+  order).  So |out - rne(exact)| <= 1 ulp_bf16(exact) + 2*gamma_K*sum|.|,
+  and only a small fraction of elements may differ at all.
+* Apply: Y = rne(rne(T) + rne(alpha*x)); the accumulation error of T plus a
+  one-ulp flip of rne(T) moves Y by at most
+  ulp(T) + ulp(Y) + 2*gamma_K*sum|P||X|.
+
+End-to-end tests use the reference test standard (fp32 compare,
+rtol = atol = 6e-2, tests/test_polar_step.py:42,53 of the reference), plus
+max abs error vs an fp32 evaluation of the formula no worse than 2x the
+oracle's own error (the emulated reference kernels) and relative Frobenius
+error <= 1e-2 per step.
+"""
+from __future__ import annotations
+
+import pytest
+import torch
+
+from oracle.polar_oracle import (
+    COEFFICIENTS,
+    error_stats,
+    kernel_dataflow_3d,
+    make_input,
+    polar_step_oracle,
+    reference_formula,
+    ulp_bf16,
+)
+
+pytestmark = pytest.mark.gpu
+
+A1, B1, C1 = COEFFICIENTS[0]
+
+
+@pytest.fixture(scope="module")
+def api(cuda_device):
+    from muon_fusion_ascend950_b200.capi import capi
+
+    return capi()
+
+
+@pytest.fixture(scope="module")
+def op(cuda_device):
+    import muon_fusion_ascend950_b200 as pkg
+
+    return pkg.polar_step
+
+
+def _rne(t64: torch.Tensor) -> torch.Tensor:
+    return t64.to(torch.float32).to(torch.bfloat16).to(torch.float64)
+
+
+def _gamma(k: int) -> float:
+    return 2.0 * k * 2.0 ** -24
+
+
+def _assert_within_ulps(actual, expected64, ulps, what, abs_slack=0.0, max_frac=0.02):
+    a = actual.to(torch.float64)
+    diff = (a - expected64).abs()
+    bound = ulps * ulp_bf16(expected64) + abs_slack + 1e-30
+    bad = diff > bound * (1 + 1e-9)
+    assert not bool(bad.any()), (
+        f"{what}: {int(bad.sum())} elements beyond {ulps} ulp, max diff {float(diff.max())}")
+    frac = float((diff > 0).double().mean())
+    assert frac <= max_frac, f"{what}: {frac:.4f} of elements differ (> {max_frac})"
+    return frac
+
+
+def _check_watchdog(api):
+    assert api.read_device_status(torch.cuda.current_device()) == 0
+
+
+# ------------------------------------------------------------------ stages
+@pytest.mark.parametrize("shape", [(1, 128, 128), (2, 150, 2064), (8, 512, 2048),
+                                   (1, 300, 1000), (3, 64, 72), (1, 640, 640)])
+def test_gram_stage(api, cuda_device, shape):
+    bsz, m, n = shape
+    x = make_input(shape, seed=1)
+    mp = api.padded_rows(m)
+    xd = x.to(cuda_device)
+    gram = torch.full((bsz, mp, mp), float("nan"), dtype=torch.bfloat16, device=cuda_device)
+    api.gram(xd, gram)
+    torch.cuda.synchronize()
+    _check_watchdog(api)
+    g = gram.cpu()
+    x64 = torch.zeros((bsz, mp, n), dtype=torch.float64)
+    x64[:, :m] = x.to(torch.float64)
+    exact = x64 @ x64.mT
+    slack = _gamma(n) * (x64.abs() @ x64.abs().mT)
+    _assert_within_ulps(g, _rne(exact), 1, f"gram {shape}", abs_slack=slack)
+    # padded rows/cols are exact zeros; the result is exactly symmetric
+    assert torch.equal(g[:, m:, :].float(), torch.zeros_like(g[:, m:, :].float()))
+    assert torch.equal(g.view(torch.int16), g.mT.contiguous().view(torch.int16))
+
+
+@pytest.mark.parametrize("shape", [(1, 128, 128), (2, 256, 2064), (8, 512, 2048)])
+def test_gram_f32_stage(api, cuda_device, shape):
+    bsz, m, n = shape
+    x = make_input(shape, seed=2)
+    mp = api.padded_rows(m)
+    gram = torch.full((bsz, mp, mp), float("nan"), dtype=torch.float32, device=cuda_device)
+    api.gram_f32(x.to(cuda_device), gram)
+    torch.cuda.synchronize()
+    g = gram.cpu().to(torch.float64)
+    x64 = x.to(torch.float64)
+    exact = x64 @ x64.mT
+    scale = (x64 * x64).sum(-1).max()
+    assert float((g[:, :m, :m] - exact).abs().max()) <= 1e-5 * float(scale)
+    assert torch.equal(g, g.mT)
+
+
+@pytest.mark.parametrize("shape", [(1, 128, 256), (2, 256, 512), (8, 512, 2048), (1, 1024, 1024)])
+def test_poly_stage(api, cuda_device, shape):
+    bsz, m, n = shape
+    x = make_input(shape, seed=3)
+    mp = api.padded_rows(m)
+    xd = x.to(cuda_device)
+    gram = torch.empty((bsz, mp, mp), dtype=torch.bfloat16, device=cuda_device)
+    poly = torch.full_like(gram, float("nan"))
+    api.gram(xd, gram)
+    api.poly(gram, poly, B1, C1)
+    torch.cuda.synchronize()
+    _check_watchdog(api)
+    a64 = gram.cpu().to(torch.float64)
+    a2 = (a64 @ a64.mT).to(torch.float32)
+    slack = abs(C1) * _gamma(mp) * (a64.abs() @ a64.abs().mT)
+    b32 = torch.tensor(B1, dtype=torch.float32)
+    c32 = torch.tensor(C1, dtype=torch.float32)
+    expected = ((b32 * a64.to(torch.float32)) + (c32 * a2)).to(torch.float64)
+    p = poly.cpu()
+    _assert_within_ulps(p, _rne(expected), 1, f"poly {shape}", abs_slack=slack)
+    assert torch.equal(p.view(torch.int16), p.mT.contiguous().view(torch.int16))
+
+
+@pytest.mark.parametrize("shape", [(1, 128, 256), (2, 150, 2064), (8, 512, 2048),
+                                   (1, 200, 1000), (2, 384, 520)])
+def test_apply_stage(api, cuda_device, shape):
+    bsz, m, n = shape
+    x = make_input(shape, seed=4)
+    mp = api.padded_rows(m)
+    xd = x.to(cuda_device)
+    gram = torch.empty((bsz, mp, mp), dtype=torch.bfloat16, device=cuda_device)
+    poly = torch.empty_like(gram)
+    api.gram(xd, gram)
+    api.poly(gram, poly, B1, C1)
+    y = torch.full_like(xd, float("nan"))
+    api.apply(poly, xd, y, A1)
+    torch.cuda.synchronize()
+    _check_watchdog(api)
+    p64 = poly.cpu().to(torch.float64)[:, :, :m]
+    x64 = x.to(torch.float64)
+    t = p64[:, :m] @ x64
+    alpha = torch.tensor(A1, dtype=torch.float32).to(torch.bfloat16).to(torch.float64)
+    expected = _rne(_rne(t) + _rne(alpha * x64))
+    got = y.cpu().to(torch.float64)
+    diff = (got - expected).abs()
+    bound = ulp_bf16(t) + ulp_bf16(expected) + _gamma(m) * (p64[:, :m].abs() @ x64.abs())
+    assert bool((diff <= bound).all()), f"apply {shape}: max diff {float(diff.max())}"
+    assert float((diff > 0).double().mean()) <= 0.05
+
+
+# ------------------------------------------------------------------ end to end
+def _end_to_end_check(y_gpu, x_cpu, steps, y_ref_bf16=None):
+    coeffs = COEFFICIENTS[:steps]
+    y32 = reference_formula(x_cpu.float(), coeffs)
+    df = x_cpu
+    for a, b, c in coeffs:
+        df = polar_step_oracle(df, a, b, c)
+    if y_ref_bf16 is None:
+        y_ref_bf16 = reference_formula(x_cpu, coeffs)
+    # reference test standard
+    torch.testing.assert_close(y_gpu.float(), y_ref_bf16.float(), rtol=6e-2, atol=6e-2)
+    e_gpu = error_stats(y_gpu, y32)
+    e_df = error_stats(df, y32)
+    assert e_gpu["max_abs"] <= 2.0 * e_df["max_abs"] + 1e-6, (e_gpu, e_df)
+    assert e_gpu["rel_fro"] <= 1e-2 * steps, e_gpu
+    return e_gpu, e_df
+
+
+@pytest.mark.parametrize("name", ["cfg2_129x130", "cfg2_2x150x2050", "cfg2_1x130x129",
+                                  "aligned_1x128x256"])
+def test_golden_one_step(op, cuda_device, golden, name):
+    _, cases = golden
+    case, x, y_ref = cases[name]
+    y = op(x.to(cuda_device), A1, B1, C1).cpu()
+    assert y.shape == x.shape and y.dtype == torch.bfloat16
+    _end_to_end_check(y, x, 1, y_ref)
+
+
+def test_golden_five_steps(op, cuda_device, golden):
+    _, cases = golden
+    case, x, y_ref = cases["five_step_1x129x130"]
+    y = x.to(cuda_device)
+    for a, b, c in COEFFICIENTS:
+        y = op(y, a, b, c)
+    y = y.cpu()
+    torch.testing.assert_close(y.float(), y_ref.float(), rtol=6e-2, atol=6e-2)
+    y32 = reference_formula(x.float(), COEFFICIENTS)
+    df = x
+    for a, b, c in COEFFICIENTS:
+        df = polar_step_oracle(df, a, b, c)
+    assert error_stats(y, y32)["max_abs"] <= 2.0 * error_stats(df, y32)["max_abs"] + 1e-6
+
+
+def test_config1_step(op, cuda_device):
+    x = make_input((8, 512, 2048), seed=0)
+    y = op(x.to(cuda_device), A1, B1, C1).cpu()
+    e_gpu, e_df = _end_to_end_check(y, x, 1)
+    # the kernels restate the reference dataflow: compare with it directly
+    df = kernel_dataflow_3d(x, A1, B1, C1)
+    d = (y.to(torch.float64) - df.to(torch.float64)).abs()
+    assert float(d.max()) <= 4 * float(ulp_bf16(df.abs().max().reshape(1)))
+
+
+def test_config3_five_step_loop(op, cuda_device):
+    x = make_input((8, 512, 2048), seed=0)
+    y = x.to(cuda_device)
+    for a, b, c in COEFFICIENTS:
+        y = op(y, a, b, c)
+    y = y.cpu()
+    y_ref = reference_formula(x, COEFFICIENTS)
+    torch.testing.assert_close(y.float(), y_ref.float(), rtol=6e-2, atol=6e-2)
+    y32 = reference_formula(x.float(), COEFFICIENTS)
+    assert error_stats(y, y32)["rel_fro"] <= 5e-2
