@@ -50,14 +50,6 @@ enum Kind : int { kGramBf16 = 0, kGramF32 = 1, kPoly = 2, kApply = 3 };
 __device__ uint32_t g_watchdog = 0;
 
 struct EpiParams {
-  void* out;
-  const void* aux;            // kPoly: A (bf16); kApply: X (bf16)
-  int64_t out_batch_stride;   // elements
-  int64_t aux_batch_stride;   // elements
-  int32_t out_ld;             // elements
-  int32_t aux_ld;             // elements
-  int32_t rows;               // valid rows of the output (kApply: m)
-  int32_t cols;               // valid cols of the output (kApply: n)
   int32_t tiles_m;
   int32_t tiles_n;
   int32_t tiles_per_batch;
@@ -65,19 +57,37 @@ struct EpiParams {
   int32_t k_blocks;
   float coef_b;
   float coef_c;
-  float alpha;                // kApply: a already rounded to bf16
+  float alpha;  // kApply: a already rounded to bf16
 };
 
-template <int BN>
+// Shared-memory plan of one CTA.  The output tile is staged in shared memory
+// as BN/box_cols boxes of [128 rows x 128 bytes] in the 128-byte swizzle TMA
+// uses, so the same bytes are (a) the landing zone of the epilogue input tile
+// (A for kPoly, X for kApply; updated in place) and (b) the source of the
+// TMA store.  Symmetric kinds add a second tile for the transposed mirror.
+template <int BN, int KIND>
 struct Config {
-  static constexpr int kStages = BN == 256 ? 4 : 6;
+  static constexpr bool kSym = KIND != kApply;
+  static constexpr bool kAux = KIND == kPoly || KIND == kApply;
+  static constexpr int kOutElem = KIND == kGramF32 ? 4 : 2;
+  static constexpr int kBoxCols = 128 / kOutElem;
+  static constexpr int kBoxes = BN / kBoxCols;
+  static constexpr uint32_t kBoxBytes = kBM * 128;
+  static constexpr uint32_t kOutBytes = kBoxes * kBoxBytes;
+  static constexpr uint32_t kMirBytes = kSym ? kOutBytes : 0;
   static constexpr uint32_t kBBytes = BN * kBK * 2;
   static constexpr uint32_t kStageBytes = kABytes + kBBytes;
-  static constexpr uint32_t kTmemCols = 2 * BN;  // two accumulators
   static constexpr uint32_t kBarrierBytes = 256;
-  static constexpr uint32_t kSmemBytes =
-      1024 + kStages * kStageBytes + kBarrierBytes;
+  static constexpr uint32_t kFixedBytes =
+      1024 + kOutBytes + kMirBytes + kBarrierBytes;
+  static constexpr int kStagesFit =
+      static_cast<int>((232448u - kFixedBytes) / kStageBytes);
+  static constexpr int kStages = kStagesFit > 8 ? 8 : kStagesFit;
+  static constexpr uint32_t kSmemBytes = kFixedBytes + kStages * kStageBytes;
+  static constexpr uint32_t kTmemCols = 2 * BN;  // two accumulators
+  static_assert(kStages >= 2, "pipeline depth");
   static_assert(kSmemBytes <= 232448, "shared memory budget");
+  static_assert(!kSym || BN == kBM, "symmetric kinds use square tiles");
 };
 
 struct TileCoord {
@@ -87,16 +97,18 @@ struct TileCoord {
 // Linear tile index -> (batch, tile row, tile col).  Symmetric kinds walk the
 // upper triangle row by row: row tm holds tiles (tm, tm..d-1) (the
 // reference enumerates the same set, asc:129-146, 609-630).
-template <int KIND>
-__device__ __forceinline__ TileCoord decode_tile(int tile, const EpiParams& p) {
+__host__ __device__ __forceinline__ TileCoord decode_tile(int tile, bool sym,
+                                                          int tiles_m,
+                                                          int tiles_n,
+                                                          int tiles_per_batch) {
   TileCoord t;
-  t.b = tile / p.tiles_per_batch;
-  int r = tile - t.b * p.tiles_per_batch;
-  if constexpr (KIND == kApply) {
-    t.tm = r / p.tiles_n;
-    t.tn = r - t.tm * p.tiles_n;
+  t.b = tile / tiles_per_batch;
+  int r = tile - t.b * tiles_per_batch;
+  if (!sym) {
+    t.tm = r / tiles_n;
+    t.tn = r - t.tm * tiles_n;
   } else {
-    const int d = p.tiles_m;
+    const int d = tiles_m;
     int tm = 0;
     while (r >= d - tm) {
       r -= d - tm;
@@ -119,153 +131,132 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   return float_to_bf16_bits(lo) | (float_to_bf16_bits(hi) << 16);
 }
 
-// Writes 32 values of tile row `row` (columns c0..c0+31 of the tile) of a
-// symmetric output at (tm,tn) and, off the diagonal, the mirrored column at
-// (tn,tm).  In the mirror, lanes of a warp hold consecutive rows, so each
-// column store of the warp is one contiguous 64-byte (bf16) or 128-byte
-// (fp32) segment.
-template <bool kF32>
-__device__ __forceinline__ void store_symmetric(const EpiParams& p,
-                                                const TileCoord& tc, int row,
-                                                int c0, const float (&v)[32]) {
-  const int64_t ld = p.out_ld;
-  const int64_t grow = static_cast<int64_t>(tc.tm) * kBM + row;
-  const int64_t gcol = static_cast<int64_t>(tc.tn) * kBM + c0;
-  if constexpr (kF32) {
-    float* base = static_cast<float*>(p.out) + tc.b * p.out_batch_stride;
-    float4* dst = reinterpret_cast<float4*>(base + grow * ld + gcol);
+// Byte offset of element (row, col) of a staged tile: boxes of 128 rows x 128
+// bytes, 16-byte units XOR-swizzled by (row & 7) -- the layout TMA writes
+// and reads with CU_TENSOR_MAP_SWIZZLE_128B.
+template <int ELEM>
+__device__ __forceinline__ uint32_t swz(int row, int col) {
+  constexpr int kPerRow = 128 / ELEM;
+  const int box = col / kPerRow;
+  const int byte = (col % kPerRow) * ELEM;
+  const int unit = byte >> 4;
+  return static_cast<uint32_t>(box * (kBM * 128) + row * 128 +
+                               (((unit ^ (row & 7)) << 4) | (byte & 15)));
+}
+
+// Epilogue of 32 accumulator columns [c0, c0+32) of tile row `row`: reads
+// the staged input (kPoly / kApply), writes the staged output and, for
+// symmetric kinds off the diagonal, the mirrored column into `mir`.
+template <int BN, int KIND>
+__device__ __forceinline__ void epilogue_chunk(const EpiParams& p,
+                                               uint32_t out, uint32_t mir,
+                                               bool mirror, int row, int c0,
+                                               const uint32_t (&r)[32]) {
+  float v[32];
 #pragma unroll
-    for (int i = 0; i < 8; ++i)
-      dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
-    if (tc.tm != tc.tn) {
+  for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+  if constexpr (KIND == kGramF32) {
 #pragma unroll
-      for (int j = 0; j < 32; ++j) base[(gcol + j) * ld + grow] = v[j];
+    for (int u = 0; u < 8; ++u)
+      st_shared_v4(out + swz<4>(row, c0 + 4 * u),
+                   make_uint4(__float_as_uint(v[4 * u]), __float_as_uint(v[4 * u + 1]),
+                              __float_as_uint(v[4 * u + 2]),
+                              __float_as_uint(v[4 * u + 3])));
+    if (mirror) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) st_shared_f32(mir + swz<4>(c0 + j, row), v[j]);
     }
+    return;
   } else {
-    uint16_t* base = static_cast<uint16_t*>(p.out) + tc.b * p.out_batch_stride;
-    uint32_t packed[16];
+    uint32_t w[16];
 #pragma unroll
-    for (int i = 0; i < 16; ++i) packed[i] = pack_bf16x2(v[2 * i], v[2 * i + 1]);
-    uint4* dst = reinterpret_cast<uint4*>(base + grow * ld + gcol);
+    for (int u = 0; u < 4; ++u) {
+      const uint32_t addr = out + swz<2>(row, c0 + 8 * u);
+      if constexpr (KIND == kGramBf16) {
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
-      dst[i] = make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2],
-                          packed[4 * i + 3]);
-    if (tc.tm != tc.tn) {
+        for (int e = 0; e < 4; ++e)
+          w[4 * u + e] = pack_bf16x2(v[8 * u + 2 * e], v[8 * u + 2 * e + 1]);
+      } else {
+        const uint4 q = ld_shared_v4(addr);
+        const uint32_t in[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        const uint16_t h = static_cast<uint16_t>(
-            (j & 1) ? (packed[j >> 1] >> 16) : (packed[j >> 1] & 0xFFFFu));
-        base[(gcol + j) * ld + grow] = h;
+        for (int e = 0; e < 4; ++e) {
+          const int j = 8 * u + 2 * e;
+          const float lo = bf16_bits_to_float(in[e] & 0xFFFFu);
+          const float hi = bf16_bits_to_float(in[e] >> 16);
+          if constexpr (KIND == kPoly) {
+            // P = bf16( fl(b*A) + fl(c*acc) ): the reference's separate
+            // Muls/Add (asc:929-940), no fused multiply-add.
+            w[4 * u + e] =
+                pack_bf16x2(__fadd_rn(__fmul_rn(p.coef_b, lo), __fmul_rn(p.coef_c, v[j])),
+                            __fadd_rn(__fmul_rn(p.coef_b, hi),
+                                      __fmul_rn(p.coef_c, v[j + 1])));
+          } else {
+            // Y = bf16( bf16(T) + bf16(alpha*x) ) (asc:1472-1476).
+            const float ax_lo = bf16_bits_to_float(float_to_bf16_bits(p.alpha * lo));
+            const float ax_hi = bf16_bits_to_float(float_to_bf16_bits(p.alpha * hi));
+            const float t_lo = bf16_bits_to_float(float_to_bf16_bits(v[j]));
+            const float t_hi = bf16_bits_to_float(float_to_bf16_bits(v[j + 1]));
+            w[4 * u + e] = pack_bf16x2(__fadd_rn(t_lo, ax_lo), __fadd_rn(t_hi, ax_hi));
+          }
+        }
+      }
+      st_shared_v4(addr, make_uint4(w[4 * u], w[4 * u + 1], w[4 * u + 2], w[4 * u + 3]));
+    }
+    if constexpr (KIND != kApply) {
+      if (mirror) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const uint16_t h = static_cast<uint16_t>((j & 1) ? (w[j >> 1] >> 16)
+                                                           : (w[j >> 1] & 0xFFFFu));
+          st_shared_u16(mir + swz<2>(c0 + j, row), h);
+        }
       }
     }
   }
 }
 
 template <int BN, int KIND>
-__device__ __forceinline__ void epilogue_chunk(const EpiParams& p,
-                                               const TileCoord& tc, int row,
-                                               int chunk,
-                                               const uint32_t (&r)[32]) {
-  float v[32];
+__device__ __forceinline__ void load_aux_tile(const CUtensorMap* map, uint8_t* dst,
+                                              uint64_t* bar, const TileCoord& tc) {
+  using Cfg = Config<BN, KIND>;
+  mbar_arrive_expect_tx(bar, Cfg::kOutBytes);
 #pragma unroll
-  for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-  const int c0 = chunk * 32;
-  if constexpr (KIND == kGramBf16) {
-    store_symmetric<false>(p, tc, row, c0, v);
-  } else if constexpr (KIND == kGramF32) {
-    store_symmetric<true>(p, tc, row, c0, v);
-  } else if constexpr (KIND == kPoly) {
-    // P = bf16( fl(b*A) + fl(c*acc) ), the reference's separate Muls/Add
-    // (asc:929-940): no fused multiply-add.
-    const int64_t grow = static_cast<int64_t>(tc.tm) * kBM + row;
-    const int64_t gcol = static_cast<int64_t>(tc.tn) * kBM + c0;
-    const uint16_t* ab = static_cast<const uint16_t*>(p.aux) +
-                         tc.b * p.aux_batch_stride + grow * p.aux_ld + gcol;
-    const uint4* src = reinterpret_cast<const uint4*>(ab);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const uint4 q = src[i];
-      const uint32_t w[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float a_lo = bf16_bits_to_float(w[e] & 0xFFFFu);
-        const float a_hi = bf16_bits_to_float(w[e] >> 16);
-        const int j = 8 * i + 2 * e;
-        v[j] = __fadd_rn(__fmul_rn(p.coef_b, a_lo), __fmul_rn(p.coef_c, v[j]));
-        v[j + 1] = __fadd_rn(__fmul_rn(p.coef_b, a_hi),
-                             __fmul_rn(p.coef_c, v[j + 1]));
-      }
-    }
-    store_symmetric<false>(p, tc, row, c0, v);
-  } else {  // kApply
-    const int64_t grow = static_cast<int64_t>(tc.tm) * kBM + row;
-    if (grow >= p.rows) return;
-    const int64_t gcol = static_cast<int64_t>(tc.tn) * BN + c0;
-    if (gcol >= p.cols) return;
-    const uint16_t* xr = static_cast<const uint16_t*>(p.aux) +
-                         tc.b * p.aux_batch_stride + grow * p.aux_ld + gcol;
-    uint16_t* yr = static_cast<uint16_t*>(p.out) + tc.b * p.out_batch_stride +
-                   grow * p.out_ld + gcol;
-    // Y = bf16( bf16(T) + bf16(alpha*x) ), alpha already a bf16 value.
-    if (gcol + 32 <= p.cols) {
-      const uint4* src = reinterpret_cast<const uint4*>(xr);
-      uint4* dst = reinterpret_cast<uint4*>(yr);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const uint4 q = src[i];
-        uint32_t w[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int j = 8 * i + 2 * e;
-          const float ax_lo = bf16_bits_to_float(float_to_bf16_bits(
-              p.alpha * bf16_bits_to_float(w[e] & 0xFFFFu)));
-          const float ax_hi = bf16_bits_to_float(
-              float_to_bf16_bits(p.alpha * bf16_bits_to_float(w[e] >> 16)));
-          const float t_lo = bf16_bits_to_float(float_to_bf16_bits(v[j]));
-          const float t_hi = bf16_bits_to_float(float_to_bf16_bits(v[j + 1]));
-          w[e] = pack_bf16x2(t_lo + ax_lo, t_hi + ax_hi);
-        }
-        dst[i] = make_uint4(w[0], w[1], w[2], w[3]);
-      }
-    } else {
-      const int nvalid = static_cast<int>(p.cols - gcol);
-#pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        if (j < nvalid) {
-          const float ax = bf16_bits_to_float(
-              float_to_bf16_bits(p.alpha * bf16_bits_to_float(xr[j])));
-          const float t = bf16_bits_to_float(float_to_bf16_bits(v[j]));
-          yr[j] = static_cast<uint16_t>(float_to_bf16_bits(t + ax));
-        }
-      }
-    }
-  }
+  for (int k = 0; k < Cfg::kBoxes; ++k)
+    tma_load_3d(dst + k * Cfg::kBoxBytes, map, bar, tc.tn * BN + k * Cfg::kBoxCols,
+                tc.tm * kBM, tc.b);
 }
 
 template <int BN, int KIND>
 __global__ void __launch_bounds__(kThreads, 1)
     polar_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
                       const __grid_constant__ CUtensorMap tmap_b,
+                      const __grid_constant__ CUtensorMap tmap_aux,
+                      const __grid_constant__ CUtensorMap tmap_out,
                       const EpiParams p) {
-  using Cfg = Config<BN>;
+  using Cfg = Config<BN, KIND>;
   constexpr int S = Cfg::kStages;
   constexpr bool kBmn = (KIND == kApply);
+  constexpr bool kSym = Cfg::kSym;
 
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_addr(smem_raw);
   uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
-  uint8_t* sA = smem;
-  uint8_t* sB = smem + S * kABytes;
+  uint8_t* sOut = smem;
+  uint8_t* sMir = sOut + Cfg::kOutBytes;
+  uint8_t* sA = sMir + Cfg::kMirBytes;
+  uint8_t* sB = sA + S * kABytes;
   uint64_t* full = reinterpret_cast<uint64_t*>(sB + S * Cfg::kBBytes);
   uint64_t* empty = full + S;
   uint64_t* tfull = empty + S;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* aux_full = drain + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(aux_full + 1);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  constexpr int kEpiLeader = 64;  // warp 2, lane 0
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -277,9 +268,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&tempty[a], 4);
     }
     mbar_init(drain, 1);
+    mbar_init(aux_full, 1);
     fence_mbar_init();
     prefetch_tensor_map(&tmap_a);
     prefetch_tensor_map(&tmap_b);
+    prefetch_tensor_map(&tmap_aux);
+    prefetch_tensor_map(&tmap_out);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, Cfg::kTmemCols);
@@ -299,9 +293,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       // ---------------- TMA producer
       uint32_t it = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; ok && tile < p.total_tiles;
-           tile += gridDim.x) {
-        const TileCoord tc = decode_tile<KIND>(tile, p);
+      for (int tile = blockIdx.x; ok && tile < p.total_tiles; tile += gridDim.x) {
+        const TileCoord tc =
+            decode_tile(tile, kSym, p.tiles_m, p.tiles_n, p.tiles_per_batch);
         for (int kb = 0; kb < p.k_blocks; ++kb, ++it) {
           const uint32_t s = it % S;
           const uint32_t ph = (it / S) & 1u;
@@ -310,8 +304,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           mbar_arrive_expect_tx(&full[s], Cfg::kStageBytes);
-          tma_load_3d(sA + s * kABytes, &tmap_a, &full[s], kb * kBK,
-                      tc.tm * kBM, tc.b);
+          tma_load_3d(sA + s * kABytes, &tmap_a, &full[s], kb * kBK, tc.tm * kBM,
+                      tc.b);
           if constexpr (!kBmn) {
             tma_load_3d(sB + s * Cfg::kBBytes, &tmap_b, &full[s], kb * kBK,
                         tc.tn * BN, tc.b);
@@ -388,23 +382,45 @@ __global__ void __launch_bounds__(kThreads, 1)
         atomicOr(&g_watchdog, MUON_POLAR_WATCHDOG_DRAIN);
     }
   } else {
-    // ---------------- epilogue warps 2..5
+    // ---------------- epilogue warps 2..5 (128 threads, one tile row each)
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     const int row = q * 32 + lane;
+    const uint32_t out_base = smem_addr(sOut);
+    const uint32_t mir_base = smem_addr(sMir);
+    const bool leader = threadIdx.x == kEpiLeader;
+    bool aux_inflight = false;  // leader only: an aux tile load not yet waited on
+    if constexpr (Cfg::kAux) {
+      if (leader && static_cast<int>(blockIdx.x) < p.total_tiles) {
+        load_aux_tile<BN, KIND>(&tmap_aux, sOut, aux_full,
+                                decode_tile(blockIdx.x, kSym, p.tiles_m, p.tiles_n,
+                                            p.tiles_per_batch));
+        aux_inflight = true;
+      }
+    }
     uint32_t t = 0;
-    for (int tile = blockIdx.x; tile < p.total_tiles;
-         tile += gridDim.x, ++t) {
-      const TileCoord tc = decode_tile<KIND>(tile, p);
+    for (int tile = blockIdx.x; tile < p.total_tiles; tile += gridDim.x, ++t) {
+      const TileCoord tc =
+          decode_tile(tile, kSym, p.tiles_m, p.tiles_n, p.tiles_per_batch);
       const uint32_t acc = t & 1u;
       const uint32_t uph = (t >> 1) & 1u;
       int ok = 1;
-      if (lane == 0) ok = mbar_wait_bounded(&tfull[acc], uph) ? 1 : 0;
+      if (lane == 0) {
+        ok = mbar_wait_bounded(&tfull[acc], uph) ? 1 : 0;
+        if (Cfg::kAux && ok) {
+          ok = mbar_wait_bounded(aux_full, t & 1u) ? 1 : 0;
+          if (ok) aux_inflight = false;
+        }
+      }
       ok = __shfl_sync(0xffffffffu, ok, 0);
       if (!ok) {
         if (lane == 0) atomicOr(&g_watchdog, MUON_POLAR_WATCHDOG_EPILOGUE);
         break;
       }
+      // Every lane reads the TMA-written input tile: each observes the
+      // completed phase itself (it has completed, so this returns at once).
+      if constexpr (Cfg::kAux) (void)mbar_try_wait(aux_full, t & 1u);
       tc_fence_after();
+      const bool mirror = kSym && tc.tm != tc.tn;
       const uint32_t t_row =
           tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
 #pragma unroll 1
@@ -412,11 +428,47 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t r[32];
         tmem_ld_32x32b_x32(t_row + c * 32, r);
         tmem_wait_ld();
-        epilogue_chunk<BN, KIND>(p, tc, row, c, r);
+        if (c == BN / 32 - 1) {
+          // accumulator fully read: hand it back to the MMA warp
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&tempty[acc]);
+        }
+        epilogue_chunk<BN, KIND>(p, out_base, mir_base, mirror, row, c * 32, r);
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty[acc]);
+      fence_proxy_async_smem();
+      named_barrier(1, 128);
+      if (leader) {
+#pragma unroll
+        for (int k = 0; k < Cfg::kBoxes; ++k)
+          tma_store_3d(&tmap_out, sOut + k * Cfg::kBoxBytes,
+                       tc.tn * BN + k * Cfg::kBoxCols, tc.tm * kBM, tc.b);
+        if (mirror) {
+#pragma unroll
+          for (int k = 0; k < Cfg::kBoxes; ++k)
+            tma_store_3d(&tmap_out, sMir + k * Cfg::kBoxBytes,
+                         tc.tm * kBM + k * Cfg::kBoxCols, tc.tn * BN, tc.b);
+        }
+        bulk_commit_group();
+        bulk_wait_group_read0();
+        if constexpr (Cfg::kAux) {
+          const int next = tile + static_cast<int>(gridDim.x);
+          if (next < p.total_tiles) {
+            load_aux_tile<BN, KIND>(&tmap_aux, sOut, aux_full,
+                                    decode_tile(next, kSym, p.tiles_m, p.tiles_n,
+                                                p.tiles_per_batch));
+            aux_inflight = true;
+          }
+        }
+      }
+      named_barrier(1, 128);
+    }
+    if (leader) {
+      bulk_wait_group0();
+      // After a watchdog exit an aux load may still be in flight; it must
+      // land before the CTA releases its shared memory.
+      if (aux_inflight && !mbar_wait_bounded(aux_full, t & 1u))
+        atomicOr(&g_watchdog, MUON_POLAR_WATCHDOG_DRAIN);
     }
   }
 
@@ -425,6 +477,414 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, Cfg::kTmemCols);
+  }
+}
+
+// ============================================================ CTA pairs
+// 256 x 256 tiles computed by a cluster of two CTAs with
+// tcgen05.mma.cta_group::2 (M = 256, N = 256, K = 16): CTA r of the pair
+// loads its own 128 rows of the A operand and its own half (128 rows, or 128
+// columns when MN-major) of the B operand with plain TMA loads; the leader
+// CTA (r = 0) issues the MMAs, which read both CTAs' shared memory and write
+// each CTA's 128 x 256 fp32 slice into its own tensor memory.  Per k-block
+// each SM ingests 32 KB for 128x256x64 MACs -- half the bytes per FLOP of a
+// 128 x 128 single-CTA tile.
+//
+// Epilogue: 64-column chunks staged in shared memory (128-byte swizzle) and
+// written with TMA stores; symmetric kinds also stage the transposed chunk
+// (64 rows x 128 columns) for the mirror tile.
+constexpr int kPairM = 256;
+constexpr int kPairN = 256;
+constexpr int kHalf = 128;
+constexpr int kChunkCols = 64;
+
+template <int KIND>
+struct PairCfg {
+  static constexpr bool kSym = KIND != kApply;
+  static constexpr bool kAux = KIND == kPoly || KIND == kApply;
+  static constexpr bool kF32 = KIND == kGramF32;
+  static constexpr int kElem = kF32 ? 4 : 2;
+  static constexpr int kBoxCols = 128 / kElem;  // columns of one 128-byte box row
+  static constexpr int kChunks = kPairN / kChunkCols;
+  static constexpr uint32_t kOutChunkBytes = kHalf * kChunkCols * kElem;
+  static constexpr uint32_t kMirChunkBytes = kSym ? kChunkCols * kHalf * kElem : 0;
+  // Output regions: kAux kinds keep the whole 128 x 256 input tile (updated
+  // in place, one region per chunk); the Gram double-buffers (bf16) or
+  // single-buffers (fp32) its chunk regions.
+  static constexpr int kOutRegions = kAux ? kChunks : (kF32 ? 1 : 2);
+  static constexpr int kMirRegions = kSym ? (kF32 ? 1 : 2) : 0;
+  // Store groups that may still read shared memory when a chunk starts.
+  static constexpr int kPending = kF32 ? 0 : 1;
+  static constexpr bool kWaitPerChunk = kSym;
+  static constexpr uint32_t kEpiBytes =
+      kOutRegions * kOutChunkBytes + kMirRegions * kMirChunkBytes;
+  static constexpr uint32_t kBHalfBytes = kHalf * kBK * 2;
+  static constexpr uint32_t kStageBytes = kABytes + kBHalfBytes;
+  static constexpr uint32_t kFixedBytes = 1024 + kEpiBytes + 256;
+  static constexpr int kStagesFit =
+      static_cast<int>((232448u - kFixedBytes) / kStageBytes);
+  static constexpr int kStages = kStagesFit > 8 ? 8 : kStagesFit;
+  static constexpr uint32_t kSmemBytes = kFixedBytes + kStages * kStageBytes;
+  static constexpr uint32_t kTmemCols = 2 * kPairN;
+  static_assert(kStages >= 3, "pipeline depth");
+  static_assert(kSmemBytes <= 232448, "shared memory budget");
+};
+
+// Offset inside a TMA box of 128-byte rows with the 128-byte swizzle.
+__device__ __forceinline__ uint32_t swz_box(int row, int byte) {
+  return static_cast<uint32_t>(row * 128 +
+                               ((((byte >> 4) ^ (row & 7))) << 4) + (byte & 15));
+}
+
+// Epilogue of one 64-column chunk for tile row `row` of this CTA's band.
+template <int KIND>
+__device__ __forceinline__ void pair_epilogue_chunk(const EpiParams& p, uint32_t out,
+                                                    uint32_t mir, bool mirror,
+                                                    int row, const float (&v)[64]) {
+  using Cfg = PairCfg<KIND>;
+  if constexpr (KIND == kGramF32) {
+    // out: 2 boxes [128 x 32 fp32]; mirror: 4 boxes [64 x 32 fp32]
+#pragma unroll
+    for (int u = 0; u < 16; ++u) {
+      const int col = 4 * u;
+      st_shared_v4(out + (col / 32) * (kHalf * 128) + swz_box(row, (col % 32) * 4),
+                   make_uint4(__float_as_uint(v[col]), __float_as_uint(v[col + 1]),
+                              __float_as_uint(v[col + 2]), __float_as_uint(v[col + 3])));
+    }
+    if (mirror) {
+      const uint32_t mbase = mir + (row / 32) * (kChunkCols * 128);
+#pragma unroll
+      for (int j = 0; j < 64; ++j)
+        st_shared_f32(mbase + swz_box(j, (row % 32) * 4), v[j]);
+    }
+  } else {
+    // out: 1 box [128 x 64 bf16]; mirror: 2 boxes [64 x 64 bf16]
+    uint32_t w[32];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const uint32_t addr = out + swz_box(row, u * 16);
+      if constexpr (KIND == kGramBf16) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          w[4 * u + e] = pack_bf16x2(v[8 * u + 2 * e], v[8 * u + 2 * e + 1]);
+      } else {
+        const uint4 q = ld_shared_v4(addr);
+        const uint32_t in[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int j = 8 * u + 2 * e;
+          const float lo = bf16_bits_to_float(in[e] & 0xFFFFu);
+          const float hi = bf16_bits_to_float(in[e] >> 16);
+          if constexpr (KIND == kPoly) {
+            // P = bf16( fl(b*A) + fl(c*acc) ), no fused multiply-add
+            // (asc:929-940).
+            w[4 * u + e] = pack_bf16x2(
+                __fadd_rn(__fmul_rn(p.coef_b, lo), __fmul_rn(p.coef_c, v[j])),
+                __fadd_rn(__fmul_rn(p.coef_b, hi), __fmul_rn(p.coef_c, v[j + 1])));
+          } else {
+            // Y = bf16( bf16(T) + bf16(alpha*x) ) (asc:1472-1476).
+            const float ax_lo = bf16_bits_to_float(float_to_bf16_bits(p.alpha * lo));
+            const float ax_hi = bf16_bits_to_float(float_to_bf16_bits(p.alpha * hi));
+            const float t_lo = bf16_bits_to_float(float_to_bf16_bits(v[j]));
+            const float t_hi = bf16_bits_to_float(float_to_bf16_bits(v[j + 1]));
+            w[4 * u + e] = pack_bf16x2(__fadd_rn(t_lo, ax_lo), __fadd_rn(t_hi, ax_hi));
+          }
+        }
+      }
+      st_shared_v4(addr, make_uint4(w[4 * u], w[4 * u + 1], w[4 * u + 2], w[4 * u + 3]));
+    }
+    if constexpr (Cfg::kSym) {
+      if (mirror) {
+        const uint32_t mbase = mir + (row / 64) * (kChunkCols * 128);
+#pragma unroll
+        for (int j = 0; j < 64; ++j) {
+          const uint16_t h = static_cast<uint16_t>((j & 1) ? (w[j >> 1] >> 16)
+                                                           : (w[j >> 1] & 0xFFFFu));
+          st_shared_u16(mbase + swz_box(j, (row % 64) * 2), h);
+        }
+      }
+    }
+  }
+}
+
+template <int KIND>
+__global__ void __launch_bounds__(kThreads, 1)
+    polar_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
+                      const __grid_constant__ CUtensorMap tmap_b,
+                      const __grid_constant__ CUtensorMap tmap_aux,
+                      const __grid_constant__ CUtensorMap tmap_out,
+                      const __grid_constant__ CUtensorMap tmap_mir,
+                      const EpiParams p) {
+  using Cfg = PairCfg<KIND>;
+  constexpr int S = Cfg::kStages;
+  constexpr bool kBmn = (KIND == kApply);
+  constexpr bool kSym = Cfg::kSym;
+
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_addr(smem_raw);
+  uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
+  uint8_t* sOut = smem;
+  uint8_t* sMir = sOut + Cfg::kOutRegions * Cfg::kOutChunkBytes;
+  uint8_t* sA = smem + Cfg::kEpiBytes;
+  uint8_t* sB = sA + S * kABytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + S * Cfg::kBHalfBytes);
+  uint64_t* empty = full + S;
+  uint64_t* tfull = empty + S;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint64_t* aux_full = drain + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(aux_full + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_cta_rank();
+  const int cluster = static_cast<int>(blockIdx.x >> 1);
+  const int nclusters = static_cast<int>(gridDim.x >> 1);
+  constexpr int kEpiLeader = 64;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 8);  // 4 epilogue warps in each CTA of the pair
+    }
+    mbar_init(drain, 1);
+    mbar_init(aux_full, 1);
+    fence_mbar_init();
+    prefetch_tensor_map(&tmap_a);
+    prefetch_tensor_map(&tmap_b);
+    prefetch_tensor_map(&tmap_aux);
+    prefetch_tensor_map(&tmap_out);
+    prefetch_tensor_map(&tmap_mir);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, Cfg::kTmemCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // the peer's barriers exist before anyone signals them
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  grid_dependency_wait();
+  grid_launch_dependents();
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer (both CTAs)
+      uint32_t it = 0;
+      bool ok = true;
+      for (int tile = cluster; ok && tile < p.total_tiles; tile += nclusters) {
+        const TileCoord tc =
+            decode_tile(tile, kSym, p.tiles_m, p.tiles_n, p.tiles_per_batch);
+        const int a_row = tc.tm * kPairM + static_cast<int>(rank) * kHalf;
+        for (int kb = 0; kb < p.k_blocks; ++kb, ++it) {
+          const uint32_t s = it % S;
+          const uint32_t ph = (it / S) & 1u;
+          if (!mbar_wait_bounded(&empty[s], ph ^ 1u)) {
+            ok = false;
+            break;
+          }
+          if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * Cfg::kStageBytes);
+          const uint32_t bar = map_to_cta(smem_addr(&full[s]), 0);
+          tma_load_3d_pair(sA + s * kABytes, &tmap_a, bar, kb * kBK, a_row, tc.b);
+          if constexpr (!kBmn) {
+            tma_load_3d_pair(sB + s * Cfg::kBHalfBytes, &tmap_b, bar, kb * kBK,
+                             tc.tn * kPairN + static_cast<int>(rank) * kHalf, tc.b);
+          } else {
+#pragma unroll
+            for (int j = 0; j < kHalf / 64; ++j)
+              tma_load_3d_pair(sB + s * Cfg::kBHalfBytes + j * (64 * kBK * 2), &tmap_b,
+                               bar,
+                               tc.tn * kPairN + static_cast<int>(rank) * kHalf + j * 64,
+                               kb * kBK, tc.b);
+          }
+        }
+      }
+      if (!ok) atomicOr(&g_watchdog, MUON_POLAR_WATCHDOG_PRODUCER);
+      if (rank == 0) {
+        // Drain: the pair's last loads land before the CTAs exit.
+        const uint32_t inflight = it < static_cast<uint32_t>(S) ? it : S;
+        for (uint32_t i = it - inflight; i < it; ++i) {
+          if (!mbar_wait_bounded(&full[i % S], (i / S) & 1u)) {
+            atomicOr(&g_watchdog, MUON_POLAR_WATCHDOG_DRAIN);
+            break;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && rank == 0) {
+      // ---------------- tcgen05 MMA issuer (leader CTA only)
+      constexpr uint32_t idesc = idesc_bf16_f32(kPairN, kBmn ? 1u : 0u, kPairM);
+      uint32_t it = 0;
+      uint32_t t = 0;
+      bool ok = true;
+      for (int tile = cluster; ok && tile < p.total_tiles; tile += nclusters, ++t) {
+        const uint32_t acc = t & 1u;
+        const uint32_t uph = (t >> 1) & 1u;
+        if (!mbar_wait_bounded(&tempty[acc], uph ^ 1u)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * kPairN;
+        for (int kb = 0; kb < p.k_blocks; ++kb, ++it) {
+          const uint32_t s = it % S;
+          const uint32_t ph = (it / S) & 1u;
+          if (!mbar_wait_bounded(&full[s], ph)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_base = smem_addr(sA + s * kABytes);
+          const uint32_t b_base = smem_addr(sB + s * Cfg::kBHalfBytes);
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k) {
+            const uint64_t ad = smem_desc_sw128(a_base + k * 32, 16, 1024);
+            uint64_t bd;
+            if constexpr (kBmn) {
+              bd = smem_desc_sw128(b_base + k * 2048, kBK * 128, 1024);
+            } else {
+              bd = smem_desc_sw128(b_base + k * 32, 16, 1024);
+            }
+            umma_bf16_pair(d_tmem, ad, bd, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+          }
+          const uint32_t e_own = map_to_cta(smem_addr(&empty[s]), 0);
+          umma_commit_pair(e_own);
+          umma_commit_pair(map_to_cta(smem_addr(&empty[s]), 1));
+        }
+        if (!ok) break;
+        umma_commit_pair(map_to_cta(smem_addr(&tfull[acc]), 0));
+        umma_commit_pair(map_to_cta(smem_addr(&tfull[acc]), 1));
+      }
+      if (!ok) atomicOr(&g_watchdog, MUON_POLAR_WATCHDOG_MMA);
+      umma_commit_pair(map_to_cta(smem_addr(drain), 0));
+      if (!mbar_wait_bounded(drain, 0)) atomicOr(&g_watchdog, MUON_POLAR_WATCHDOG_DRAIN);
+    }
+  } else {
+    // ---------------- epilogue warps 2..5 (both CTAs; one band row each)
+    const int q = warp & 3;
+    const int row = q * 32 + lane;
+    const uint32_t out_base = smem_addr(sOut);
+    const uint32_t mir_base = smem_addr(sMir);
+    const bool leader = threadIdx.x == kEpiLeader;
+    const uint32_t tempty_leader0 = map_to_cta(smem_addr(&tempty[0]), 0);
+    const uint32_t tempty_leader1 = map_to_cta(smem_addr(&tempty[1]), 0);
+    bool aux_inflight = false;
+    auto load_aux = [&](int tile) {
+      const TileCoord tc = decode_tile(tile, kSym, p.tiles_m, p.tiles_n, p.tiles_per_batch);
+      mbar_arrive_expect_tx(aux_full, Cfg::kChunks * Cfg::kOutChunkBytes);
+#pragma unroll
+      for (int c = 0; c < Cfg::kChunks; ++c)
+        tma_load_3d(sOut + c * Cfg::kOutChunkBytes, &tmap_aux, aux_full,
+                    tc.tn * kPairN + c * kChunkCols,
+                    tc.tm * kPairM + static_cast<int>(rank) * kHalf, tc.b);
+      aux_inflight = true;
+    };
+    if constexpr (Cfg::kAux) {
+      if (leader && cluster < p.total_tiles) load_aux(cluster);
+    }
+    uint32_t t = 0;
+    for (int tile = cluster; tile < p.total_tiles; tile += nclusters, ++t) {
+      const TileCoord tc =
+          decode_tile(tile, kSym, p.tiles_m, p.tiles_n, p.tiles_per_batch);
+      const uint32_t acc = t & 1u;
+      const uint32_t uph = (t >> 1) & 1u;
+      int ok = 1;
+      if (lane == 0) {
+        ok = mbar_wait_bounded(&tfull[acc], uph) ? 1 : 0;
+        if (Cfg::kAux && ok) {
+          ok = mbar_wait_bounded(aux_full, t & 1u) ? 1 : 0;
+          if (ok) aux_inflight = false;
+        }
+      }
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) {
+        if (lane == 0) atomicOr(&g_watchdog, MUON_POLAR_WATCHDOG_EPILOGUE);
+        break;
+      }
+      if constexpr (Cfg::kAux) (void)mbar_try_wait(aux_full, t & 1u);
+      tc_fence_after();
+      const bool mirror = kSym && tc.tm != tc.tn;
+      const int row0 = tc.tm * kPairM + static_cast<int>(rank) * kHalf;
+      const int col0 = tc.tn * kPairN;
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * kPairN;
+#pragma unroll 1
+      for (int c = 0; c < Cfg::kChunks; ++c) {
+        const int ro = c % Cfg::kOutRegions;
+        const uint32_t out = out_base + ro * Cfg::kOutChunkBytes;
+        constexpr int kMR = Cfg::kMirRegions > 0 ? Cfg::kMirRegions : 1;
+        const int rm = c % kMR;
+        const uint32_t mir = mir_base + rm * Cfg::kMirChunkBytes;
+        if constexpr (Cfg::kWaitPerChunk) {
+          if (leader) bulk_wait_group_read<Cfg::kPending>();
+          named_barrier(1, 128);
+        }
+        uint32_t r0[32], r1[32];
+        tmem_ld_32x32b_x32(t_row + c * kChunkCols, r0);
+        tmem_ld_32x32b_x32(t_row + c * kChunkCols + 32, r1);
+        tmem_wait_ld();
+        if (c == Cfg::kChunks - 1) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) {
+            if (rank == 0)
+              mbar_arrive(&tempty[acc]);
+            else
+              mbar_arrive_cluster(acc ? tempty_leader1 : tempty_leader0);
+          }
+        }
+        float v[64];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          v[j] = __uint_as_float(r0[j]);
+          v[32 + j] = __uint_as_float(r1[j]);
+        }
+        pair_epilogue_chunk<KIND>(p, out, mir, mirror, row, v);
+        fence_proxy_async_smem();
+        named_barrier(1, 128);
+        if (leader) {
+          const uint8_t* so = sOut + ro * Cfg::kOutChunkBytes;
+          const uint8_t* sm = sMir + rm * Cfg::kMirChunkBytes;
+#pragma unroll
+          for (int h = 0; h < kChunkCols / Cfg::kBoxCols; ++h)
+            tma_store_3d(&tmap_out, so + h * (kHalf * 128),
+                         col0 + c * kChunkCols + h * Cfg::kBoxCols, row0, tc.b);
+          if (mirror) {
+#pragma unroll
+            for (int h = 0; h < kHalf / Cfg::kBoxCols; ++h)
+              tma_store_3d(&tmap_mir, sm + h * (kChunkCols * 128), row0 + h * Cfg::kBoxCols,
+                           col0 + c * kChunkCols, tc.b);
+          }
+          bulk_commit_group();
+        }
+      }
+      if constexpr (Cfg::kAux) {
+        if (leader) {
+          bulk_wait_group_read<0>();
+          const int next = tile + nclusters;
+          if (next < p.total_tiles) load_aux(next);
+        }
+      }
+    }
+    if (leader) {
+      bulk_wait_group0();
+      if (aux_inflight && !mbar_wait_bounded(aux_full, t & 1u))
+        atomicOr(&g_watchdog, MUON_POLAR_WATCHDOG_DRAIN);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // the leader's MMAs are done with both CTAs' memory
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, Cfg::kTmemCols);
   }
 }
 
@@ -446,7 +906,7 @@ namespace {
 std::atomic<uint64_t> g_launch_count{0};
 
 constexpr int kMaxDevices = 64;
-constexpr int kNumInstances = 8;
+constexpr int kNumInstances = 12;
 
 struct DeviceState {
   std::once_flag once;
@@ -520,12 +980,15 @@ bool aligned16(const void* p) {
   return (reinterpret_cast<uintptr_t>(p) & 15u) == 0;
 }
 
+struct TensorMaps {
+  CUtensorMap a, b, aux, out;
+};
+
 template <int BN, int KIND>
-int launch_gemm(DeviceState* st, int instance, const CUtensorMap& ta,
-                const CUtensorMap& tb, const EpiParams& p,
-                cudaStream_t stream) {
+int launch_gemm(DeviceState* st, int instance, const TensorMaps& maps,
+                const EpiParams& p, cudaStream_t stream) {
   auto kern = polar_gemm_kernel<BN, KIND>;
-  const uint32_t smem = Config<BN>::kSmemBytes;
+  const uint32_t smem = Config<BN, KIND>::kSmemBytes;
   if (!st->smem_attr_set[instance]) {
     std::lock_guard<std::mutex> lock(g_attr_mutex);
     if (!st->smem_attr_set[instance]) {
@@ -546,13 +1009,64 @@ int launch_gemm(DeviceState* st, int instance, const CUtensorMap& ta,
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ta, tb, p);
+  cudaError_t e =
+      cudaLaunchKernelEx(&cfg, kern, maps.a, maps.b, maps.aux, maps.out, p);
   if (e != cudaSuccess) return static_cast<int>(e);
   g_launch_count.fetch_add(1, std::memory_order_relaxed);
   return MUON_POLAR_OK;
 }
 
-int64_t padded_rows(int64_t m) { return (m + kBM - 1) / kBM * kBM; }
+// Rows of the square A / P buffers: a multiple of the 256-row pair tile.
+int64_t padded_rows(int64_t m) { return (m + kPairM - 1) / kPairM * kPairM; }
+
+struct PairMaps {
+  CUtensorMap a, b, aux, out, mir;
+};
+
+bool use_pairs() {
+  static const bool value = [] {
+    const char* s = std::getenv("MUON_POLAR_PAIR");
+    return s == nullptr || std::atoi(s) != 0;
+  }();
+  return value;
+}
+
+template <int KIND>
+int launch_pair(DeviceState* st, int instance, const PairMaps& maps,
+                const EpiParams& p, cudaStream_t stream) {
+  auto kern = polar_pair_kernel<KIND>;
+  const uint32_t smem = PairCfg<KIND>::kSmemBytes;
+  if (!st->smem_attr_set[instance]) {
+    std::lock_guard<std::mutex> lock(g_attr_mutex);
+    if (!st->smem_attr_set[instance]) {
+      cudaError_t e = cudaFuncSetAttribute(
+          kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+      if (e != cudaSuccess) return static_cast<int>(e);
+      st->smem_attr_set[instance] = true;
+    }
+  }
+  const int max_pairs = st->sms / 2;
+  const int pairs = p.total_tiles < max_pairs ? p.total_tiles : max_pairs;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * pairs, 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, maps.a, maps.b, maps.aux,
+                                     maps.out, maps.mir, p);
+  if (e != cudaSuccess) return static_cast<int>(e);
+  g_launch_count.fetch_add(1, std::memory_order_relaxed);
+  return MUON_POLAR_OK;
+}
 
 int check_x_args(const void* x, int64_t batch, int64_t m, int64_t n,
                  int64_t ldx) {
@@ -562,6 +1076,16 @@ int check_x_args(const void* x, int64_t batch, int64_t m, int64_t n,
     return MUON_POLAR_ERR_INVALID_ARGUMENT;
   if (!aligned16(x) || (ldx % 8) != 0) return MUON_POLAR_ERR_ALIGNMENT;
   return MUON_POLAR_OK;
+}
+
+// Square [batch][mp][mp] buffer, bf16 or fp32, boxes of `box_rows` rows x
+// 128 bytes.
+int encode_square(CUtensorMap* map, const void* base, int64_t batch, int64_t mp,
+                  bool f32, uint32_t box_rows = kBM) {
+  return f32 ? encode_3d(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, base, mp, mp,
+                         batch, mp, mp * mp, 32, box_rows)
+             : encode_3d(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, mp, mp,
+                         batch, mp, mp * mp, kBK, box_rows);
 }
 
 template <int KIND>
@@ -578,23 +1102,43 @@ int gram_impl(const void* x, void* gram, int64_t batch, int64_t m, int64_t n,
   const int64_t d = mp / kBM;
   const int64_t tiles_per_batch = d * (d + 1) / 2;
   if (tiles_per_batch * batch > INT32_MAX) return MUON_POLAR_ERR_INVALID_ARGUMENT;
-  CUtensorMap tx;
-  rc = encode_3d(&tx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, x, n, m, batch, ldx,
-                 m * ldx, kBK, kBM);
+  if (use_pairs()) {
+    const int64_t dp = mp / kPairM;
+    const int64_t tp = dp * (dp + 1) / 2;
+    PairMaps pm;
+    rc = encode_3d(&pm.a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, x, n, m, batch,
+                   ldx, m * ldx, kBK, kHalf);
+    if (rc != MUON_POLAR_OK) return rc;
+    pm.b = pm.a;
+    pm.aux = pm.a;
+    rc = encode_square(&pm.out, gram, batch, mp, KIND == kGramF32, kHalf);
+    if (rc != MUON_POLAR_OK) return rc;
+    rc = encode_square(&pm.mir, gram, batch, mp, KIND == kGramF32, kChunkCols);
+    if (rc != MUON_POLAR_OK) return rc;
+    EpiParams p = {};
+    p.tiles_m = static_cast<int32_t>(dp);
+    p.tiles_n = static_cast<int32_t>(dp);
+    p.tiles_per_batch = static_cast<int32_t>(tp);
+    p.total_tiles = static_cast<int32_t>(tp * batch);
+    p.k_blocks = static_cast<int32_t>((n + kBK - 1) / kBK);
+    return launch_pair<KIND>(st, 5 + KIND, pm, p, stream);
+  }
+  TensorMaps maps;
+  // X: rows beyond m and columns beyond n read as zero.
+  rc = encode_3d(&maps.a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, x, n, m, batch,
+                 ldx, m * ldx, kBK, kBM);
+  if (rc != MUON_POLAR_OK) return rc;
+  maps.b = maps.a;
+  maps.aux = maps.a;
+  rc = encode_square(&maps.out, gram, batch, mp, KIND == kGramF32);
   if (rc != MUON_POLAR_OK) return rc;
   EpiParams p = {};
-  p.out = gram;
-  p.aux = nullptr;
-  p.out_batch_stride = mp * mp;
-  p.out_ld = static_cast<int32_t>(mp);
-  p.rows = static_cast<int32_t>(mp);
-  p.cols = static_cast<int32_t>(mp);
   p.tiles_m = static_cast<int32_t>(d);
   p.tiles_n = static_cast<int32_t>(d);
   p.tiles_per_batch = static_cast<int32_t>(tiles_per_batch);
   p.total_tiles = static_cast<int32_t>(tiles_per_batch * batch);
   p.k_blocks = static_cast<int32_t>((n + kBK - 1) / kBK);
-  return launch_gemm<128, KIND>(st, KIND, tx, tx, p, stream);
+  return launch_gemm<128, KIND>(st, KIND, maps, p, stream);
 }
 
 int poly_impl(const void* gram, void* poly, int64_t batch, int64_t mp, float b,
@@ -609,19 +1153,36 @@ int poly_impl(const void* gram, void* poly, int64_t batch, int64_t mp, float b,
   const int64_t d = mp / kBM;
   const int64_t tiles_per_batch = d * (d + 1) / 2;
   if (tiles_per_batch * batch > INT32_MAX) return MUON_POLAR_ERR_INVALID_ARGUMENT;
-  CUtensorMap ta;
-  rc = encode_3d(&ta, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, gram, mp, mp, batch,
-                 mp, mp * mp, kBK, kBM);
+  if (use_pairs() && (mp % kPairM) == 0) {
+    const int64_t dp = mp / kPairM;
+    const int64_t tp = dp * (dp + 1) / 2;
+    PairMaps pm;
+    rc = encode_square(&pm.a, gram, batch, mp, false, kHalf);
+    if (rc != MUON_POLAR_OK) return rc;
+    pm.b = pm.a;
+    pm.aux = pm.a;
+    rc = encode_square(&pm.out, poly, batch, mp, false, kHalf);
+    if (rc != MUON_POLAR_OK) return rc;
+    rc = encode_square(&pm.mir, poly, batch, mp, false, kChunkCols);
+    if (rc != MUON_POLAR_OK) return rc;
+    EpiParams p = {};
+    p.tiles_m = static_cast<int32_t>(dp);
+    p.tiles_n = static_cast<int32_t>(dp);
+    p.tiles_per_batch = static_cast<int32_t>(tp);
+    p.total_tiles = static_cast<int32_t>(tp * batch);
+    p.k_blocks = static_cast<int32_t>(mp / kBK);
+    p.coef_b = b;
+    p.coef_c = c;
+    return launch_pair<kPoly>(st, 5 + kPoly, pm, p, stream);
+  }
+  TensorMaps maps;
+  rc = encode_square(&maps.a, gram, batch, mp, false);
+  if (rc != MUON_POLAR_OK) return rc;
+  maps.b = maps.a;
+  maps.aux = maps.a;
+  rc = encode_square(&maps.out, poly, batch, mp, false);
   if (rc != MUON_POLAR_OK) return rc;
   EpiParams p = {};
-  p.out = poly;
-  p.aux = gram;
-  p.out_batch_stride = mp * mp;
-  p.aux_batch_stride = mp * mp;
-  p.out_ld = static_cast<int32_t>(mp);
-  p.aux_ld = static_cast<int32_t>(mp);
-  p.rows = static_cast<int32_t>(mp);
-  p.cols = static_cast<int32_t>(mp);
   p.tiles_m = static_cast<int32_t>(d);
   p.tiles_n = static_cast<int32_t>(d);
   p.tiles_per_batch = static_cast<int32_t>(tiles_per_batch);
@@ -629,7 +1190,7 @@ int poly_impl(const void* gram, void* poly, int64_t batch, int64_t mp, float b,
   p.k_blocks = static_cast<int32_t>(mp / kBK);
   p.coef_b = b;
   p.coef_c = c;
-  return launch_gemm<128, kPoly>(st, 2, ta, ta, p, stream);
+  return launch_gemm<128, kPoly>(st, 2, maps, p, stream);
 }
 
 // Host-side fp32 -> bf16 round-to-nearest-even, the same rule as the
@@ -666,6 +1227,32 @@ int apply_impl(const void* poly, const void* x, void* y, int64_t batch,
   rc = current_device_state(&st);
   if (rc != MUON_POLAR_OK) return rc;
   const int64_t mp = padded_rows(m);
+  if (use_pairs()) {
+    const int64_t tm = mp / kPairM;
+    const int64_t tn = (n + kPairN - 1) / kPairN;
+    if (tm * tn * batch > INT32_MAX) return MUON_POLAR_ERR_INVALID_ARGUMENT;
+    PairMaps pm;
+    rc = encode_square(&pm.a, poly, batch, mp, false, kHalf);
+    if (rc != MUON_POLAR_OK) return rc;
+    rc = encode_3d(&pm.b, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, x, n, m, batch,
+                   ldx, m * ldx, 64, kBK);
+    if (rc != MUON_POLAR_OK) return rc;
+    rc = encode_3d(&pm.aux, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, x, n, m, batch,
+                   ldx, m * ldx, 64, kHalf);
+    if (rc != MUON_POLAR_OK) return rc;
+    rc = encode_3d(&pm.out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, y, n, m, batch,
+                   ldy, m * ldy, 64, kHalf);
+    if (rc != MUON_POLAR_OK) return rc;
+    pm.mir = pm.out;
+    EpiParams p = {};
+    p.tiles_m = static_cast<int32_t>(tm);
+    p.tiles_n = static_cast<int32_t>(tn);
+    p.tiles_per_batch = static_cast<int32_t>(tm * tn);
+    p.total_tiles = static_cast<int32_t>(tm * tn * batch);
+    p.k_blocks = static_cast<int32_t>((m + kBK - 1) / kBK);
+    p.alpha = round_to_bf16(a);
+    return launch_pair<kApply>(st, 5 + kApply, pm, p, stream);
+  }
   const int64_t tiles_m = mp / kBM;
   // Tile width: fewest rounds of BN-column work over the SMs.
   const int64_t t128 = tiles_m * ((n + 127) / 128) * batch;
@@ -676,23 +1263,22 @@ int apply_impl(const void* poly, const void* x, void* y, int64_t batch,
   if (apply_bn_override() != 0) bn = apply_bn_override();
   const int64_t tiles_n = (n + bn - 1) / bn;
   if (tiles_m * tiles_n * batch > INT32_MAX) return MUON_POLAR_ERR_INVALID_ARGUMENT;
-  CUtensorMap tp, tx;
-  rc = encode_3d(&tp, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, poly, mp, mp, batch,
-                 mp, mp * mp, kBK, kBM);
+  TensorMaps maps;
+  rc = encode_square(&maps.a, poly, batch, mp, false);
   if (rc != MUON_POLAR_OK) return rc;
   // X as the B operand: rows are K, the 64-column box is the MN extent.
-  rc = encode_3d(&tx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, x, n, m, batch, ldx,
-                 m * ldx, 64, kBK);
+  rc = encode_3d(&maps.b, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, x, n, m, batch,
+                 ldx, m * ldx, 64, kBK);
+  if (rc != MUON_POLAR_OK) return rc;
+  // X as the epilogue input tile, Y as the output tile (rows >= m and
+  // columns >= n are neither read nor written).
+  rc = encode_3d(&maps.aux, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, x, n, m, batch,
+                 ldx, m * ldx, 64, kBM);
+  if (rc != MUON_POLAR_OK) return rc;
+  rc = encode_3d(&maps.out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, y, n, m, batch,
+                 ldy, m * ldy, 64, kBM);
   if (rc != MUON_POLAR_OK) return rc;
   EpiParams p = {};
-  p.out = y;
-  p.aux = x;
-  p.out_batch_stride = m * ldy;
-  p.aux_batch_stride = m * ldx;
-  p.out_ld = static_cast<int32_t>(ldy);
-  p.aux_ld = static_cast<int32_t>(ldx);
-  p.rows = static_cast<int32_t>(m);
-  p.cols = static_cast<int32_t>(n);
   p.tiles_m = static_cast<int32_t>(tiles_m);
   p.tiles_n = static_cast<int32_t>(tiles_n);
   p.tiles_per_batch = static_cast<int32_t>(tiles_m * tiles_n);
@@ -700,8 +1286,8 @@ int apply_impl(const void* poly, const void* x, void* y, int64_t batch,
   // P's columns >= m are zero and X's rows >= m read as zero: stop at m.
   p.k_blocks = static_cast<int32_t>((m + kBK - 1) / kBK);
   p.alpha = round_to_bf16(a);
-  if (bn == 256) return launch_gemm<256, kApply>(st, 3, tp, tx, p, stream);
-  return launch_gemm<128, kApply>(st, 4, tp, tx, p, stream);
+  if (bn == 256) return launch_gemm<256, kApply>(st, 3, maps, p, stream);
+  return launch_gemm<128, kApply>(st, 4, maps, p, stream);
 }
 
 }  // namespace
