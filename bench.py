@@ -289,6 +289,7 @@ def run_ours(args):
     gram = torch.empty((BATCH, mp, mp), dtype=torch.bfloat16, device=device)
     poly = torch.empty_like(gram)
     y = torch.empty_like(xs[0])
+    scratch = api.new_scratch(BATCH, M, N, device=device, stream=stream)
     kernel_iters = max(50, min(args.steps, 1000))
 
     def time_kernel(fn):
@@ -305,11 +306,13 @@ def run_ours(args):
         return e0.elapsed_time(e1) / kernel_iters * 1e3  # us
 
     with torch.cuda.stream(stream):
-        api.gram(xs[0], gram, stream=stream)
-        api.poly(gram, poly, b, c, stream=stream)
+        api.gram(xs[0], gram, scratch=scratch, stream=stream)
+        api.poly(gram, poly, b, c, scratch=scratch, stream=stream)
     us = {
-        "gram": time_kernel(lambda i: api.gram(xs[i % ROTATION], gram, stream=stream)),
-        "poly": time_kernel(lambda i: api.poly(gram, poly, b, c, stream=stream)),
+        "gram": time_kernel(lambda i: api.gram(xs[i % ROTATION], gram, scratch=scratch,
+                                               stream=stream)),
+        "poly": time_kernel(lambda i: api.poly(gram, poly, b, c, scratch=scratch,
+                                               stream=stream)),
         "apply": time_kernel(lambda i: api.apply(poly, xs[i % ROTATION], y, a, stream=stream)),
     }
     kernel_flops = {"gram": BATCH * 2 * M * M * N, "poly": BATCH * 2 * M ** 3,

@@ -63,8 +63,9 @@ int muon_polar_abi_version(void);
 const char* muon_polar_status_string(int status);
 
 /* Rows of the square Gram/polynomial buffers for `m` rows of X: m rounded up
- * to 128, the tile height (reference rule rows = align(M,128),
- * csrc/muon_polar_step_binding.cpp:630). */
+ * to 256, the height of a CTA-pair tile (the reference rounds to 128,
+ * csrc/muon_polar_step_binding.cpp:630; the extra rows are zeros and do not
+ * change any result). */
 int64_t muon_polar_padded_rows(int64_t m);
 
 /* Bytes of the workspace muon_polar_step_sm100 needs: A and P, each
@@ -72,29 +73,49 @@ int64_t muon_polar_padded_rows(int64_t m);
  * at::empty calls of csrc/muon_polar_step_binding.cpp:646,657. */
 size_t muon_polar_workspace_bytes(int64_t batch, int64_t m);
 
+/* Split-K scratch.  When a problem has fewer 256 x 256 output tiles than
+ * the device has SM pairs (small M), kernels 1 and 2 cut each tile's K range
+ * into up to 4 work items and reduce the fp32 partials -- always in the same
+ * split order, so results are deterministic.  The reduction needs scratch
+ * memory: muon_polar_scratch_bytes() bytes (0 when the problem does not
+ * split on the current device).  Its first 1024 bytes are arrival counters
+ * that must be zero before the first call (muon_polar_scratch_init); every
+ * call leaves them zero again.  Calls that share one scratch buffer must be
+ * ordered (same stream).  Passing scratch = NULL (or too few bytes) turns
+ * split-K off; results then come from the unsplit K order. */
+size_t muon_polar_scratch_bytes(int64_t batch, int64_t m, int64_t n);
+
+/* Zeroes the counter area of a scratch buffer (cudaMemsetAsync on `stream`).
+ * Needed once after allocation, and again after a watchdog report. */
+int muon_polar_scratch_init(void* scratch, size_t scratch_bytes, void* stream);
+
 /* Kernel (1): gram[b] = X[b] . X[b]^T, bf16 [batch][Mp][Mp] (row stride Mp).
  * fp32 accumulation, one round-to-nearest-even to bf16.  Only tiles with
  * tile_row <= tile_col are computed; each is written at (tm,tn) and mirrored
  * to (tn,tm).  Rows/cols >= m are written as zeros.
  * Requirements: x 16-byte aligned, ldx % 8 == 0, ldx >= n, gram 16-byte
- * aligned.
+ * aligned.  scratch: see muon_polar_scratch_bytes (may be NULL).
  * Replaces launch_muon_gram_lowlevel_fused (asc:512-517). */
 int muon_polar_gram_sm100(const void* x, void* gram, int64_t batch, int64_t m,
-                          int64_t n, int64_t ldx, void* stream);
+                          int64_t n, int64_t ldx, void* scratch,
+                          size_t scratch_bytes, void* stream);
 
 /* Kernel (1), fp32 output variant: partial Gram in fp32 for the column-sharded
  * multi-GPU path (the partials are summed across ranks before kernel 2).
  * Same layout and requirements as muon_polar_gram_sm100, gram is float. */
 int muon_polar_gram_f32_sm100(const void* x, void* gram_f32, int64_t batch,
-                              int64_t m, int64_t n, int64_t ldx, void* stream);
+                              int64_t m, int64_t n, int64_t ldx, void* scratch,
+                              size_t scratch_bytes, void* stream);
 
 /* Kernel (2): poly[b] = bf16( b*f32(gram[b]) + c*(gram[b].gram[b])_f32 ),
- * both [batch][Mp][Mp] bf16, Mp a multiple of 128.  Products and the sum are
- * separately rounded fp32 operations (no FMA), as in
+ * both [batch][Mp][Mp] bf16, Mp a multiple of 128 (256 for the CTA-pair
+ * kernels; muon_polar_padded_rows gives 256-multiples).  Products and the
+ * sum are separately rounded fp32 operations (no FMA), as in
  * csrc/muon_polar_unified_ascend950.asc:929-940.  Upper tiles are computed
  * and mirrored.  Replaces launch_muon_cube2_p_fused (asc:1030-1035). */
 int muon_polar_poly_sm100(const void* gram, void* poly, int64_t batch,
-                          int64_t mp, float b, float c, void* stream);
+                          int64_t mp, float b, float c, void* scratch,
+                          size_t scratch_bytes, void* stream);
 
 /* Kernel (3): y[b] = bf16(T) + bf16(alpha_bf16 * x) with T = (poly[b].x[b])
  * accumulated in fp32 and the final add done on bf16 values, as in
@@ -109,10 +130,12 @@ int muon_polar_apply_sm100(const void* poly, const void* x, void* y,
 /* The whole step: kernels 1, 2, 3 back to back on `stream` (programmatic
  * dependent launch lets each kernel's prologue overlap the previous
  * kernel's tail).  workspace must hold muon_polar_workspace_bytes(batch, m)
- * bytes, 16-byte aligned.  y must not alias x.
+ * bytes, 16-byte aligned; scratch as for kernels 1 and 2 (may be NULL).
+ * y must not alias x.
  * Replaces the launch sequence of csrc/muon_polar_step_binding.cpp:644-666. */
 int muon_polar_step_sm100(const void* x, void* y, void* workspace,
-                          size_t workspace_bytes, int64_t batch, int64_t m,
+                          size_t workspace_bytes, void* scratch,
+                          size_t scratch_bytes, int64_t batch, int64_t m,
                           int64_t n, int64_t ldx, int64_t ldy, float a,
                           float b, float c, void* stream);
 
@@ -127,6 +150,22 @@ int muon_polar_cast_f32_bf16_sm100(const void* src, void* dst, int64_t count,
  * kernels have no bounded waits (CheckAcl at binding.cpp:72-75 is the only
  * error path). */
 int muon_polar_read_device_status(int device, uint32_t* flags, int clear);
+
+/* Kernel selection, process-wide; returns the previous policy (or
+ * MUON_POLAR_ERR_INVALID_ARGUMENT).
+ *   0  by size (default): 256 x 256 tiles on tcgen05 CTA pairs when a launch
+ *      has at least half as many such tiles as the device runs pairs at once,
+ *      otherwise single-CTA 128-row tiles, which keep more SMs busy;
+ *   1  always CTA pairs (split-K, when scratch is given, happens only here);
+ *   2  always single-CTA tiles.
+ * The initial value comes from MUON_POLAR_PAIR (1 -> policy 1, 0 -> policy
+ * 2).  Every policy computes the same mathematical result; the fp32
+ * accumulation order (and so the last bit) may differ between them. */
+int muon_polar_set_kernel_policy(int policy);
+
+/* Number of 2-CTA clusters (tcgen05 CTA pairs) of the Gram kernel the
+ * current device runs at once; the persistent grids are this many pairs. */
+int muon_polar_device_pairs(int* pairs);
 
 /* Number of kernels the library has launched in this process (all entry
  * points, all devices).  Used by benchmarks to report launch counts. */

@@ -24,19 +24,26 @@ SIGNATURES = {
     "muon_polar_status_string": (ctypes.c_char_p, [ctypes.c_int]),
     "muon_polar_padded_rows": (_I64, [_I64]),
     "muon_polar_workspace_bytes": (ctypes.c_size_t, [_I64, _I64]),
-    "muon_polar_gram_sm100": (ctypes.c_int, [_VP, _VP, _I64, _I64, _I64, _I64, _VP]),
-    "muon_polar_gram_f32_sm100": (ctypes.c_int, [_VP, _VP, _I64, _I64, _I64, _I64, _VP]),
+    "muon_polar_scratch_bytes": (ctypes.c_size_t, [_I64, _I64, _I64]),
+    "muon_polar_scratch_init": (ctypes.c_int, [_VP, ctypes.c_size_t, _VP]),
+    "muon_polar_gram_sm100": (ctypes.c_int, [_VP, _VP, _I64, _I64, _I64, _I64, _VP,
+                                             ctypes.c_size_t, _VP]),
+    "muon_polar_gram_f32_sm100": (ctypes.c_int, [_VP, _VP, _I64, _I64, _I64, _I64, _VP,
+                                                 ctypes.c_size_t, _VP]),
     "muon_polar_poly_sm100": (ctypes.c_int, [_VP, _VP, _I64, _I64, ctypes.c_float,
-                                             ctypes.c_float, _VP]),
+                                             ctypes.c_float, _VP, ctypes.c_size_t, _VP]),
     "muon_polar_apply_sm100": (ctypes.c_int, [_VP, _VP, _VP, _I64, _I64, _I64, _I64,
                                               _I64, ctypes.c_float, _VP]),
-    "muon_polar_step_sm100": (ctypes.c_int, [_VP, _VP, _VP, ctypes.c_size_t, _I64, _I64,
-                                             _I64, _I64, _I64, ctypes.c_float,
-                                             ctypes.c_float, ctypes.c_float, _VP]),
+    "muon_polar_step_sm100": (ctypes.c_int, [_VP, _VP, _VP, ctypes.c_size_t, _VP,
+                                             ctypes.c_size_t, _I64, _I64, _I64, _I64, _I64,
+                                             ctypes.c_float, ctypes.c_float, ctypes.c_float,
+                                             _VP]),
     "muon_polar_cast_f32_bf16_sm100": (ctypes.c_int, [_VP, _VP, _I64, _VP]),
     "muon_polar_read_device_status": (ctypes.c_int, [ctypes.c_int,
                                                      ctypes.POINTER(ctypes.c_uint32),
                                                      ctypes.c_int]),
+    "muon_polar_set_kernel_policy": (ctypes.c_int, [ctypes.c_int]),
+    "muon_polar_device_pairs": (ctypes.c_int, [ctypes.POINTER(ctypes.c_int)]),
     "muon_polar_launch_count": (ctypes.c_uint64, []),
 }
 
@@ -59,6 +66,16 @@ def library_path() -> Path:
     if configured:
         return Path(configured).expanduser().resolve()
     return Path(__file__).resolve().parent / LIB_FILENAME
+
+
+def _nbytes(t) -> int:
+    return t.numel() * t.element_size()
+
+
+def _scratch(scratch):
+    if scratch is None or scratch.numel() == 0:
+        return None, 0
+    return scratch.data_ptr(), _nbytes(scratch)
 
 
 class CAPI:
@@ -101,6 +118,19 @@ class CAPI:
     def workspace_bytes(self, batch: int, m: int) -> int:
         return int(self.lib.muon_polar_workspace_bytes(int(batch), int(m)))
 
+    def set_kernel_policy(self, policy: int) -> int:
+        """0 = by size, 1 = always CTA pairs, 2 = always single-CTA; returns
+        the previous policy."""
+        prev = int(self.lib.muon_polar_set_kernel_policy(int(policy)))
+        if prev < 0:
+            raise MuonPolarError("muon_polar_set_kernel_policy", prev, self.status_string(prev))
+        return prev
+
+    def device_pairs(self) -> int:
+        pairs = ctypes.c_int(0)
+        self._check("muon_polar_device_pairs", self.lib.muon_polar_device_pairs(ctypes.byref(pairs)))
+        return int(pairs.value)
+
     def launch_count(self) -> int:
         return int(self.lib.muon_polar_launch_count())
 
@@ -111,25 +141,47 @@ class CAPI:
                                                            1 if clear else 0))
         return int(flags.value)
 
+    def scratch_bytes(self, batch: int, m: int, n: int) -> int:
+        return int(self.lib.muon_polar_scratch_bytes(int(batch), int(m), int(n)))
+
+    def scratch_init(self, scratch, stream=None) -> None:
+        self._check("muon_polar_scratch_init", self.lib.muon_polar_scratch_init(
+            scratch.data_ptr(), _nbytes(scratch), self._stream(stream)))
+
+    def new_scratch(self, batch: int, m: int, n: int, device=None, stream=None):
+        """A zero-initialised split-K scratch buffer (uint8 tensor, possibly
+        empty) for problems of this size on the current device."""
+        import torch
+
+        nbytes = self.scratch_bytes(batch, m, n)
+        scratch = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=device or "cuda")
+        if nbytes:
+            self.scratch_init(scratch, stream)
+        return scratch
+
     # -------------------------------------------------------------- kernels
     # Tensors are torch tensors on the current CUDA device; x is [B, M, ld]
-    # with the first n columns valid.
-    def gram(self, x, gram, n: Optional[int] = None, stream=None) -> None:
+    # with the first n columns valid.  `scratch` (optional) enables split-K.
+    def gram(self, x, gram, n: Optional[int] = None, scratch=None, stream=None) -> None:
         b, m, ld = x.shape
         n = ld if n is None else n
+        sp, sb = _scratch(scratch)
         self._check("muon_polar_gram_sm100", self.lib.muon_polar_gram_sm100(
-            x.data_ptr(), gram.data_ptr(), b, m, n, ld, self._stream(stream)))
+            x.data_ptr(), gram.data_ptr(), b, m, n, ld, sp, sb, self._stream(stream)))
 
-    def gram_f32(self, x, gram_f32, n: Optional[int] = None, stream=None) -> None:
+    def gram_f32(self, x, gram_f32, n: Optional[int] = None, scratch=None,
+                 stream=None) -> None:
         b, m, ld = x.shape
         n = ld if n is None else n
+        sp, sb = _scratch(scratch)
         self._check("muon_polar_gram_f32_sm100", self.lib.muon_polar_gram_f32_sm100(
-            x.data_ptr(), gram_f32.data_ptr(), b, m, n, ld, self._stream(stream)))
+            x.data_ptr(), gram_f32.data_ptr(), b, m, n, ld, sp, sb, self._stream(stream)))
 
-    def poly(self, gram, poly, b: float, c: float, stream=None) -> None:
+    def poly(self, gram, poly, b: float, c: float, scratch=None, stream=None) -> None:
         bsz, mp, _ = gram.shape
+        sp, sb = _scratch(scratch)
         self._check("muon_polar_poly_sm100", self.lib.muon_polar_poly_sm100(
-            gram.data_ptr(), poly.data_ptr(), bsz, mp, float(b), float(c),
+            gram.data_ptr(), poly.data_ptr(), bsz, mp, float(b), float(c), sp, sb,
             self._stream(stream)))
 
     def apply(self, poly, x, y, a: float, n: Optional[int] = None, stream=None) -> None:
@@ -140,13 +192,14 @@ class CAPI:
             float(a), self._stream(stream)))
 
     def step(self, x, y, workspace, a: float, b: float, c: float,
-             n: Optional[int] = None, stream=None) -> None:
+             n: Optional[int] = None, scratch=None, stream=None) -> None:
         bsz, m, ldx = x.shape
         n = ldx if n is None else n
+        sp, sb = _scratch(scratch)
         self._check("muon_polar_step_sm100", self.lib.muon_polar_step_sm100(
-            x.data_ptr(), y.data_ptr(), workspace.data_ptr(),
-            workspace.numel() * workspace.element_size(), bsz, m, n, ldx, y.shape[-1],
-            float(a), float(b), float(c), self._stream(stream)))
+            x.data_ptr(), y.data_ptr(), workspace.data_ptr(), _nbytes(workspace), sp, sb,
+            bsz, m, n, ldx, y.shape[-1], float(a), float(b), float(c),
+            self._stream(stream)))
 
     def cast_f32_bf16(self, src, dst, stream=None) -> None:
         self._check("muon_polar_cast_f32_bf16_sm100", self.lib.muon_polar_cast_f32_bf16_sm100(

@@ -58,6 +58,12 @@ struct EpiParams {
   float coef_b;
   float coef_c;
   float alpha;  // kApply: a already rounded to bf16
+  // Split-K (CTA-pair symmetric kinds): each tile's K range is cut into
+  // `splits` work items; item = tile * splits + split.
+  int32_t splits;
+  int32_t total_items;
+  float* partial;      // [total_items][2][128][256] fp32 partial sums
+  uint32_t* counters;  // [total_tiles][2] arrivals, zero between launches
 };
 
 // Shared-memory plan of one CTA.  The output tile is staged in shared memory
@@ -497,6 +503,7 @@ constexpr int kPairM = 256;
 constexpr int kPairN = 256;
 constexpr int kHalf = 128;
 constexpr int kChunkCols = 64;
+constexpr int kMaxSplits = 4;  // split-K items per tile, at most
 
 template <int KIND>
 struct PairCfg {
@@ -634,6 +641,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* drain = tempty + 2;
   uint64_t* aux_full = drain + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(aux_full + 1);
+  volatile uint32_t* last_flag = tmem_slot + 1;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -678,11 +686,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       // ---------------- TMA producer (both CTAs)
       uint32_t it = 0;
       bool ok = true;
-      for (int tile = cluster; ok && tile < p.total_tiles; tile += nclusters) {
+      for (int item = cluster; ok && item < p.total_items; item += nclusters) {
+        const int tile = item / p.splits;
+        const int split = item - tile * p.splits;
         const TileCoord tc =
             decode_tile(tile, kSym, p.tiles_m, p.tiles_n, p.tiles_per_batch);
         const int a_row = tc.tm * kPairM + static_cast<int>(rank) * kHalf;
-        for (int kb = 0; kb < p.k_blocks; ++kb, ++it) {
+        const int kb_end = (split + 1) * p.k_blocks / p.splits;
+        for (int kb = split * p.k_blocks / p.splits; kb < kb_end; ++kb, ++it) {
           const uint32_t s = it % S;
           const uint32_t ph = (it / S) & 1u;
           if (!mbar_wait_bounded(&empty[s], ph ^ 1u)) {
@@ -724,7 +735,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t it = 0;
       uint32_t t = 0;
       bool ok = true;
-      for (int tile = cluster; ok && tile < p.total_tiles; tile += nclusters, ++t) {
+      for (int item = cluster; ok && item < p.total_items; item += nclusters, ++t) {
+        const int split = item % p.splits;
+        const int kb_begin = split * p.k_blocks / p.splits;
+        const int kb_end = (split + 1) * p.k_blocks / p.splits;
         const uint32_t acc = t & 1u;
         const uint32_t uph = (t >> 1) & 1u;
         if (!mbar_wait_bounded(&tempty[acc], uph ^ 1u)) {
@@ -733,7 +747,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * kPairN;
-        for (int kb = 0; kb < p.k_blocks; ++kb, ++it) {
+        for (int kb = kb_begin; kb < kb_end; ++kb, ++it) {
           const uint32_t s = it % S;
           const uint32_t ph = (it / S) & 1u;
           if (!mbar_wait_bounded(&full[s], ph)) {
@@ -752,7 +766,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             } else {
               bd = smem_desc_sw128(b_base + k * 32, 16, 1024);
             }
-            umma_bf16_pair(d_tmem, ad, bd, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+            umma_bf16_pair(d_tmem, ad, bd, idesc, (kb > kb_begin || k > 0) ? 1u : 0u);
           }
           const uint32_t e_own = map_to_cta(smem_addr(&empty[s]), 0);
           umma_commit_pair(e_own);
@@ -776,8 +790,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t tempty_leader0 = map_to_cta(smem_addr(&tempty[0]), 0);
     const uint32_t tempty_leader1 = map_to_cta(smem_addr(&tempty[1]), 0);
     bool aux_inflight = false;
-    auto load_aux = [&](int tile) {
-      const TileCoord tc = decode_tile(tile, kSym, p.tiles_m, p.tiles_n, p.tiles_per_batch);
+    auto load_aux = [&](int item) {
+      const TileCoord tc =
+          decode_tile(item / p.splits, kSym, p.tiles_m, p.tiles_n, p.tiles_per_batch);
       mbar_arrive_expect_tx(aux_full, Cfg::kChunks * Cfg::kOutChunkBytes);
 #pragma unroll
       for (int c = 0; c < Cfg::kChunks; ++c)
@@ -786,11 +801,23 @@ __global__ void __launch_bounds__(kThreads, 1)
                     tc.tm * kPairM + static_cast<int>(rank) * kHalf, tc.b);
       aux_inflight = true;
     };
+    auto release_accumulator = [&](uint32_t acc) {
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        if (rank == 0)
+          mbar_arrive(&tempty[acc]);
+        else
+          mbar_arrive_cluster(acc ? tempty_leader1 : tempty_leader0);
+      }
+    };
     if constexpr (Cfg::kAux) {
-      if (leader && cluster < p.total_tiles) load_aux(cluster);
+      if (leader && cluster < p.total_items) load_aux(cluster);
     }
     uint32_t t = 0;
-    for (int tile = cluster; tile < p.total_tiles; tile += nclusters, ++t) {
+    for (int item = cluster; item < p.total_items; item += nclusters, ++t) {
+      const int tile = item / p.splits;
+      const int split = item - tile * p.splits;
       const TileCoord tc =
           decode_tile(tile, kSym, p.tiles_m, p.tiles_n, p.tiles_per_batch);
       const uint32_t acc = t & 1u;
@@ -814,6 +841,58 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int row0 = tc.tm * kPairM + static_cast<int>(rank) * kHalf;
       const int col0 = tc.tn * kPairN;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * kPairN;
+      bool reduce = false;
+      if (p.splits > 1) {
+        // Split-K: publish this split's partial band; the last split of the
+        // tile to arrive (per CTA band) sums all partials in split order --
+        // the same order whichever split arrives last -- and runs the
+        // epilogue.  Nobody waits for anybody.
+        // Partial band layout: float4 slots [chunk][vec 0..15][row 0..127],
+        // so the 32 lanes of a warp (consecutive rows) write 512
+        // contiguous bytes per store.
+        float4* mine = reinterpret_cast<float4*>(
+                           p.partial + (static_cast<size_t>(item) * 2 + rank) * (kHalf * kPairN)) +
+                       row;
+#pragma unroll 1
+        for (int c = 0; c < Cfg::kChunks; ++c) {
+          uint32_t r0[32], r1[32];
+          tmem_ld_32x32b_x32(t_row + c * kChunkCols, r0);
+          tmem_ld_32x32b_x32(t_row + c * kChunkCols + 32, r1);
+          tmem_wait_ld();
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            __stcg(mine + (c * 16 + u) * kHalf,
+                   make_float4(__uint_as_float(r0[4 * u]), __uint_as_float(r0[4 * u + 1]),
+                               __uint_as_float(r0[4 * u + 2]), __uint_as_float(r0[4 * u + 3])));
+            __stcg(mine + (c * 16 + 8 + u) * kHalf,
+                   make_float4(__uint_as_float(r1[4 * u]), __uint_as_float(r1[4 * u + 1]),
+                               __uint_as_float(r1[4 * u + 2]), __uint_as_float(r1[4 * u + 3])));
+          }
+        }
+        __threadfence();
+        named_barrier(1, 128);
+        if (leader) {
+          uint32_t* counter = p.counters + static_cast<size_t>(tile) * 2 + rank;
+          const uint32_t arrived = atomicAdd(counter, 1u) + 1u;
+          const bool last = arrived == static_cast<uint32_t>(p.splits);
+          if (last) atomicExch(counter, 0u);  // ready for the next launch
+          __threadfence();
+          *last_flag = last ? 1u : 0u;
+        }
+        named_barrier(1, 128);
+        reduce = *last_flag != 0u;
+        if (!reduce) {
+          release_accumulator(acc);
+          if constexpr (Cfg::kAux) {
+            if (leader) {
+              bulk_wait_group_read<0>();
+              const int next = item + nclusters;
+              if (next < p.total_items) load_aux(next);
+            }
+          }
+          continue;
+        }
+      }
 #pragma unroll 1
       for (int c = 0; c < Cfg::kChunks; ++c) {
         const int ro = c % Cfg::kOutRegions;
@@ -829,21 +908,59 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_ld_32x32b_x32(t_row + c * kChunkCols, r0);
         tmem_ld_32x32b_x32(t_row + c * kChunkCols + 32, r1);
         tmem_wait_ld();
-        if (c == Cfg::kChunks - 1) {
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) {
-            if (rank == 0)
-              mbar_arrive(&tempty[acc]);
-            else
-              mbar_arrive_cluster(acc ? tempty_leader1 : tempty_leader0);
-          }
-        }
+        if (c == Cfg::kChunks - 1) release_accumulator(acc);
         float v[64];
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
           v[j] = __uint_as_float(r0[j]);
           v[32 + j] = __uint_as_float(r1[j]);
+        }
+        if (reduce) {
+          // v <- sum over splits i = 0..splits-1, in that order, of the
+          // split's partial (this split's own from tensor memory).  All
+          // splits' loads of a half chunk are issued before the adds.
+          const float4* band0 = reinterpret_cast<const float4*>(
+                                    p.partial + static_cast<size_t>(tile) * p.splits * 2 *
+                                                    (kHalf * kPairN)) +
+                                static_cast<size_t>(rank) * (kHalf * kPairN / 4) + row;
+          const size_t split_stride = 2 * (kHalf * kPairN / 4);  // float4 per split item
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            float4 parts[kMaxSplits][8];
+#pragma unroll
+            for (int i = 0; i < kMaxSplits; ++i) {
+              if (i < p.splits && i != split) {
+#pragma unroll
+                for (int u = 0; u < 8; ++u)
+                  parts[i][u] = __ldcg(band0 + i * split_stride +
+                                       (c * 16 + h * 8 + u) * kHalf);
+              } else {
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                  const int j = (h * 8 + u) * 4;
+                  parts[i][u] = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+                }
+              }
+            }
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+              float4 acc4 = parts[0][u];
+#pragma unroll
+              for (int i = 1; i < kMaxSplits; ++i) {
+                if (i < p.splits) {
+                  acc4.x = __fadd_rn(acc4.x, parts[i][u].x);
+                  acc4.y = __fadd_rn(acc4.y, parts[i][u].y);
+                  acc4.z = __fadd_rn(acc4.z, parts[i][u].z);
+                  acc4.w = __fadd_rn(acc4.w, parts[i][u].w);
+                }
+              }
+              const int j = (h * 8 + u) * 4;
+              v[j] = acc4.x;
+              v[j + 1] = acc4.y;
+              v[j + 2] = acc4.z;
+              v[j + 3] = acc4.w;
+            }
+          }
         }
         pair_epilogue_chunk<KIND>(p, out, mir, mirror, row, v);
         fence_proxy_async_smem();
@@ -867,8 +984,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       if constexpr (Cfg::kAux) {
         if (leader) {
           bulk_wait_group_read<0>();
-          const int next = tile + nclusters;
-          if (next < p.total_tiles) load_aux(next);
+          const int next = item + nclusters;
+          if (next < p.total_items) load_aux(next);
         }
       }
     }
@@ -913,6 +1030,7 @@ struct DeviceState {
   int sms = 0;
   int cc_major = 0, cc_minor = 0;
   bool smem_attr_set[kNumInstances] = {};
+  int pair_capacity[kNumInstances] = {};  // co-resident 2-CTA clusters
 };
 DeviceState g_devices[kMaxDevices];
 std::mutex g_attr_mutex;
@@ -1023,12 +1141,106 @@ struct PairMaps {
   CUtensorMap a, b, aux, out, mir;
 };
 
-bool use_pairs() {
-  static const bool value = [] {
-    const char* s = std::getenv("MUON_POLAR_PAIR");
-    return s == nullptr || std::atoi(s) != 0;
-  }();
-  return value;
+// Kernel choice: 0 = by size (CTA-pair 256x256 tiles when a launch has at
+// least half as many pair tiles as the device runs pairs at once, else the
+// single-CTA 128-row kernels, which keep more SMs busy on small problems),
+// 1 = always CTA pairs, 2 = never.  Initial value from MUON_POLAR_PAIR.
+std::atomic<int> g_policy{[] {
+  const char* s = std::getenv("MUON_POLAR_PAIR");
+  if (s == nullptr) return 0;
+  const int v = std::atoi(s);
+  return v == 1 ? 1 : (v == 0 ? 2 : 0);
+}()};
+
+bool use_pairs(int64_t pair_tiles, int capacity) {
+  const int policy = g_policy.load(std::memory_order_relaxed);
+  if (policy == 1) return true;
+  if (policy == 2) return false;
+  return 2 * pair_tiles >= capacity;
+}
+
+// Split-K of the CTA-pair symmetric kernels: when a problem has fewer
+// 256 x 256 tiles than there are SM pairs, each tile's K range is cut into
+// up to kMaxSplits work items.  Scratch layout: kCounterBytes of arrival
+// counters (zero between launches) followed by the fp32 partials.
+constexpr size_t kCounterBytes = 1024;
+constexpr size_t kPartialItemBytes = 2ull * kHalf * kPairN * sizeof(float);
+
+int choose_splits(int64_t tiles, int64_t k_blocks, int pairs) {
+  if (tiles <= 0 || tiles * 2 > static_cast<int64_t>(kCounterBytes / 4)) return 1;
+  int64_t s = pairs / tiles;
+  if (s > kMaxSplits) s = kMaxSplits;
+  if (s > k_blocks / 2) s = k_blocks / 2;
+  return s < 2 ? 1 : static_cast<int>(s);
+}
+
+size_t split_scratch_bytes(int64_t tiles, int splits) {
+  return splits > 1 ? kCounterBytes + static_cast<size_t>(tiles) * splits * kPartialItemBytes
+                    : 0;
+}
+
+// Applies split-K to `p` if the scratch buffer allows it; `pairs` is the
+// number of CTA pairs the device runs at once.
+void plan_splits(EpiParams& p, void* scratch, size_t scratch_bytes, int pairs) {
+  p.splits = 1;
+  p.total_items = p.total_tiles;
+  p.partial = nullptr;
+  p.counters = nullptr;
+  if (scratch == nullptr || !aligned16(scratch)) return;
+  const int s = choose_splits(p.total_tiles, p.k_blocks, pairs);
+  if (s < 2 || split_scratch_bytes(p.total_tiles, s) > scratch_bytes) return;
+  p.splits = s;
+  p.total_items = p.total_tiles * s;
+  p.counters = static_cast<uint32_t*>(scratch);
+  p.partial = reinterpret_cast<float*>(static_cast<uint8_t*>(scratch) + kCounterBytes);
+}
+
+void plan_no_splits(EpiParams& p) {
+  p.splits = 1;
+  p.total_items = p.total_tiles;
+  p.partial = nullptr;
+  p.counters = nullptr;
+}
+
+// How many clusters of two CTAs of this kernel the device runs at once (a
+// tcgen05 CTA pair needs both SMs of a TPC; TPCs with one usable SM cannot
+// host one), after raising the kernel's shared-memory limit.  Cached.
+template <int KIND>
+int pair_capacity(DeviceState* st, int instance, int* capacity) {
+  if (st->pair_capacity[instance] > 0) {
+    *capacity = st->pair_capacity[instance];
+    return MUON_POLAR_OK;
+  }
+  std::lock_guard<std::mutex> lock(g_attr_mutex);
+  auto kern = polar_pair_kernel<KIND>;
+  const uint32_t smem = PairCfg<KIND>::kSmemBytes;
+  if (!st->smem_attr_set[instance]) {
+    cudaError_t e = cudaFuncSetAttribute(
+        kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return static_cast<int>(e);
+    st->smem_attr_set[instance] = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * (st->sms / 2), 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int clusters = 0;
+  cudaError_t e = cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg);
+  if (e != cudaSuccess || clusters <= 0) {
+    (void)cudaGetLastError();
+    clusters = st->sms / 2;
+  }
+  if (clusters > st->sms / 2) clusters = st->sms / 2;
+  st->pair_capacity[instance] = clusters;
+  *capacity = clusters;
+  return MUON_POLAR_OK;
 }
 
 template <int KIND>
@@ -1036,17 +1248,10 @@ int launch_pair(DeviceState* st, int instance, const PairMaps& maps,
                 const EpiParams& p, cudaStream_t stream) {
   auto kern = polar_pair_kernel<KIND>;
   const uint32_t smem = PairCfg<KIND>::kSmemBytes;
-  if (!st->smem_attr_set[instance]) {
-    std::lock_guard<std::mutex> lock(g_attr_mutex);
-    if (!st->smem_attr_set[instance]) {
-      cudaError_t e = cudaFuncSetAttribute(
-          kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-      if (e != cudaSuccess) return static_cast<int>(e);
-      st->smem_attr_set[instance] = true;
-    }
-  }
-  const int max_pairs = st->sms / 2;
-  const int pairs = p.total_tiles < max_pairs ? p.total_tiles : max_pairs;
+  int max_pairs = 0;
+  int rc = pair_capacity<KIND>(st, instance, &max_pairs);
+  if (rc != MUON_POLAR_OK) return rc;
+  const int pairs = p.total_items < max_pairs ? p.total_items : max_pairs;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * pairs, 1, 1);
   cfg.blockDim = dim3(kThreads, 1, 1);
@@ -1090,7 +1295,8 @@ int encode_square(CUtensorMap* map, const void* base, int64_t batch, int64_t mp,
 
 template <int KIND>
 int gram_impl(const void* x, void* gram, int64_t batch, int64_t m, int64_t n,
-              int64_t ldx, cudaStream_t stream) {
+              int64_t ldx, void* scratch, size_t scratch_bytes,
+              cudaStream_t stream) {
   int rc = check_x_args(x, batch, m, n, ldx);
   if (rc != MUON_POLAR_OK) return rc;
   if (gram == nullptr) return MUON_POLAR_ERR_INVALID_ARGUMENT;
@@ -1102,9 +1308,12 @@ int gram_impl(const void* x, void* gram, int64_t batch, int64_t m, int64_t n,
   const int64_t d = mp / kBM;
   const int64_t tiles_per_batch = d * (d + 1) / 2;
   if (tiles_per_batch * batch > INT32_MAX) return MUON_POLAR_ERR_INVALID_ARGUMENT;
-  if (use_pairs()) {
-    const int64_t dp = mp / kPairM;
-    const int64_t tp = dp * (dp + 1) / 2;
+  const int64_t dp = mp / kPairM;
+  const int64_t tp = dp * (dp + 1) / 2;
+  int pairs = 0;
+  rc = pair_capacity<KIND>(st, 5 + KIND, &pairs);
+  if (rc != MUON_POLAR_OK) return rc;
+  if (use_pairs(tp * batch, pairs)) {
     PairMaps pm;
     rc = encode_3d(&pm.a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, x, n, m, batch,
                    ldx, m * ldx, kBK, kHalf);
@@ -1121,6 +1330,7 @@ int gram_impl(const void* x, void* gram, int64_t batch, int64_t m, int64_t n,
     p.tiles_per_batch = static_cast<int32_t>(tp);
     p.total_tiles = static_cast<int32_t>(tp * batch);
     p.k_blocks = static_cast<int32_t>((n + kBK - 1) / kBK);
+    plan_splits(p, scratch, scratch_bytes, pairs);
     return launch_pair<KIND>(st, 5 + KIND, pm, p, stream);
   }
   TensorMaps maps;
@@ -1138,11 +1348,12 @@ int gram_impl(const void* x, void* gram, int64_t batch, int64_t m, int64_t n,
   p.tiles_per_batch = static_cast<int32_t>(tiles_per_batch);
   p.total_tiles = static_cast<int32_t>(tiles_per_batch * batch);
   p.k_blocks = static_cast<int32_t>((n + kBK - 1) / kBK);
+  plan_no_splits(p);
   return launch_gemm<128, KIND>(st, KIND, maps, p, stream);
 }
 
 int poly_impl(const void* gram, void* poly, int64_t batch, int64_t mp, float b,
-              float c, cudaStream_t stream) {
+              float c, void* scratch, size_t scratch_bytes, cudaStream_t stream) {
   if (gram == nullptr || poly == nullptr || batch <= 0 || mp <= 0 ||
       (mp % kBM) != 0 || batch > INT32_MAX || mp > (1 << 24))
     return MUON_POLAR_ERR_INVALID_ARGUMENT;
@@ -1153,9 +1364,12 @@ int poly_impl(const void* gram, void* poly, int64_t batch, int64_t mp, float b,
   const int64_t d = mp / kBM;
   const int64_t tiles_per_batch = d * (d + 1) / 2;
   if (tiles_per_batch * batch > INT32_MAX) return MUON_POLAR_ERR_INVALID_ARGUMENT;
-  if (use_pairs() && (mp % kPairM) == 0) {
-    const int64_t dp = mp / kPairM;
-    const int64_t tp = dp * (dp + 1) / 2;
+  const int64_t dp = mp / kPairM;
+  const int64_t tp = dp * (dp + 1) / 2;
+  int pairs = 0;
+  rc = pair_capacity<kPoly>(st, 5 + kPoly, &pairs);
+  if (rc != MUON_POLAR_OK) return rc;
+  if ((mp % kPairM) == 0 && use_pairs(tp * batch, pairs)) {
     PairMaps pm;
     rc = encode_square(&pm.a, gram, batch, mp, false, kHalf);
     if (rc != MUON_POLAR_OK) return rc;
@@ -1173,6 +1387,7 @@ int poly_impl(const void* gram, void* poly, int64_t batch, int64_t mp, float b,
     p.k_blocks = static_cast<int32_t>(mp / kBK);
     p.coef_b = b;
     p.coef_c = c;
+    plan_splits(p, scratch, scratch_bytes, pairs);
     return launch_pair<kPoly>(st, 5 + kPoly, pm, p, stream);
   }
   TensorMaps maps;
@@ -1190,6 +1405,7 @@ int poly_impl(const void* gram, void* poly, int64_t batch, int64_t mp, float b,
   p.k_blocks = static_cast<int32_t>(mp / kBK);
   p.coef_b = b;
   p.coef_c = c;
+  plan_no_splits(p);
   return launch_gemm<128, kPoly>(st, 2, maps, p, stream);
 }
 
@@ -1227,7 +1443,10 @@ int apply_impl(const void* poly, const void* x, void* y, int64_t batch,
   rc = current_device_state(&st);
   if (rc != MUON_POLAR_OK) return rc;
   const int64_t mp = padded_rows(m);
-  if (use_pairs()) {
+  int pairs = 0;
+  rc = pair_capacity<kApply>(st, 5 + kApply, &pairs);
+  if (rc != MUON_POLAR_OK) return rc;
+  if (use_pairs((mp / kPairM) * ((n + kPairN - 1) / kPairN) * batch, pairs)) {
     const int64_t tm = mp / kPairM;
     const int64_t tn = (n + kPairN - 1) / kPairN;
     if (tm * tn * batch > INT32_MAX) return MUON_POLAR_ERR_INVALID_ARGUMENT;
@@ -1251,6 +1470,7 @@ int apply_impl(const void* poly, const void* x, void* y, int64_t batch,
     p.total_tiles = static_cast<int32_t>(tm * tn * batch);
     p.k_blocks = static_cast<int32_t>((m + kBK - 1) / kBK);
     p.alpha = round_to_bf16(a);
+    plan_no_splits(p);
     return launch_pair<kApply>(st, 5 + kApply, pm, p, stream);
   }
   const int64_t tiles_m = mp / kBM;
@@ -1286,6 +1506,7 @@ int apply_impl(const void* poly, const void* x, void* y, int64_t batch,
   // P's columns >= m are zero and X's rows >= m read as zero: stop at m.
   p.k_blocks = static_cast<int32_t>((m + kBK - 1) / kBK);
   p.alpha = round_to_bf16(a);
+  plan_no_splits(p);
   if (bn == 256) return launch_gemm<256, kApply>(st, 3, maps, p, stream);
   return launch_gemm<128, kApply>(st, 4, maps, p, stream);
 }
@@ -1331,20 +1552,23 @@ size_t muon_polar_workspace_bytes(int64_t batch, int64_t m) {
 }
 
 int muon_polar_gram_sm100(const void* x, void* gram, int64_t batch, int64_t m,
-                          int64_t n, int64_t ldx, void* stream) {
-  return gram_impl<kGramBf16>(x, gram, batch, m, n, ldx,
+                          int64_t n, int64_t ldx, void* scratch,
+                          size_t scratch_bytes, void* stream) {
+  return gram_impl<kGramBf16>(x, gram, batch, m, n, ldx, scratch, scratch_bytes,
                               static_cast<cudaStream_t>(stream));
 }
 
 int muon_polar_gram_f32_sm100(const void* x, void* gram_f32, int64_t batch,
-                              int64_t m, int64_t n, int64_t ldx, void* stream) {
-  return gram_impl<kGramF32>(x, gram_f32, batch, m, n, ldx,
-                             static_cast<cudaStream_t>(stream));
+                              int64_t m, int64_t n, int64_t ldx, void* scratch,
+                              size_t scratch_bytes, void* stream) {
+  return gram_impl<kGramF32>(x, gram_f32, batch, m, n, ldx, scratch,
+                             scratch_bytes, static_cast<cudaStream_t>(stream));
 }
 
 int muon_polar_poly_sm100(const void* gram, void* poly, int64_t batch,
-                          int64_t mp, float b, float c, void* stream) {
-  return poly_impl(gram, poly, batch, mp, b, c,
+                          int64_t mp, float b, float c, void* scratch,
+                          size_t scratch_bytes, void* stream) {
+  return poly_impl(gram, poly, batch, mp, b, c, scratch, scratch_bytes,
                    static_cast<cudaStream_t>(stream));
 }
 
@@ -1356,7 +1580,8 @@ int muon_polar_apply_sm100(const void* poly, const void* x, void* y,
 }
 
 int muon_polar_step_sm100(const void* x, void* y, void* workspace,
-                          size_t workspace_bytes, int64_t batch, int64_t m,
+                          size_t workspace_bytes, void* scratch,
+                          size_t scratch_bytes, int64_t batch, int64_t m,
                           int64_t n, int64_t ldx, int64_t ldy, float a,
                           float b, float c, void* stream) {
   int rc = check_x_args(x, batch, m, n, ldx);
@@ -1370,11 +1595,38 @@ int muon_polar_step_sm100(const void* x, void* y, void* workspace,
   void* gram = ws;
   void* poly = ws + static_cast<size_t>(batch * mp * mp * 2);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  rc = gram_impl<kGramBf16>(x, gram, batch, m, n, ldx, s);
+  rc = gram_impl<kGramBf16>(x, gram, batch, m, n, ldx, scratch, scratch_bytes, s);
   if (rc != MUON_POLAR_OK) return rc;
-  rc = poly_impl(gram, poly, batch, mp, b, c, s);
+  rc = poly_impl(gram, poly, batch, mp, b, c, scratch, scratch_bytes, s);
   if (rc != MUON_POLAR_OK) return rc;
   return apply_impl(poly, x, y, batch, m, n, ldx, ldy, a, s);
+}
+
+size_t muon_polar_scratch_bytes(int64_t batch, int64_t m, int64_t n) {
+  if (batch <= 0 || m <= 0 || n <= 0) return 0;
+  int pairs = 0;
+  DeviceState* st = nullptr;
+  if (current_device_state(&st) != MUON_POLAR_OK ||
+      pair_capacity<kGramBf16>(st, 5 + kGramBf16, &pairs) != MUON_POLAR_OK || pairs <= 0) {
+    (void)cudaGetLastError();
+    pairs = 512;  // no usable device: the largest the split planner could use
+  }
+  const int64_t mp = padded_rows(m);
+  const int64_t d = mp / kPairM;
+  const int64_t tiles = d * (d + 1) / 2 * batch;
+  const int64_t kb_gram = (n + kBK - 1) / kBK;
+  const int64_t kb_poly = mp / kBK;
+  const size_t g = split_scratch_bytes(tiles, choose_splits(tiles, kb_gram, pairs));
+  const size_t q = split_scratch_bytes(tiles, choose_splits(tiles, kb_poly, pairs));
+  return g > q ? g : q;
+}
+
+int muon_polar_scratch_init(void* scratch, size_t scratch_bytes, void* stream) {
+  if (scratch == nullptr) return MUON_POLAR_ERR_INVALID_ARGUMENT;
+  if (scratch_bytes == 0) return MUON_POLAR_OK;
+  const size_t n = scratch_bytes < kCounterBytes ? scratch_bytes : kCounterBytes;
+  cudaError_t e = cudaMemsetAsync(scratch, 0, n, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? MUON_POLAR_OK : static_cast<int>(e);
 }
 
 int muon_polar_cast_f32_bf16_sm100(const void* src, void* dst, int64_t count,
@@ -1423,6 +1675,19 @@ int muon_polar_read_device_status(int device, uint32_t* flags, int clear) {
   if (e != cudaSuccess) return static_cast<int>(e);
   *flags = v;
   return MUON_POLAR_OK;
+}
+
+int muon_polar_set_kernel_policy(int policy) {
+  if (policy < 0 || policy > 2) return MUON_POLAR_ERR_INVALID_ARGUMENT;
+  return g_policy.exchange(policy);
+}
+
+int muon_polar_device_pairs(int* pairs) {
+  if (pairs == nullptr) return MUON_POLAR_ERR_INVALID_ARGUMENT;
+  DeviceState* st = nullptr;
+  int rc = current_device_state(&st);
+  if (rc != MUON_POLAR_OK) return rc;
+  return pair_capacity<kGramBf16>(st, 5 + kGramBf16, pairs);
 }
 
 uint64_t muon_polar_launch_count(void) {

@@ -7,13 +7,16 @@
 //
 // Differences from the reference binding, none visible in results:
 //   * rows are never padded: the kernels read rows >= M as zeros through
-//     the TMA bounds check and mask their stores, so A/P keep align(M,128)
-//     rows without a padded copy of X;
+//     the TMA bounds check and mask their stores, so A/P get align(M,256)
+//     rows (the CTA-pair tile height) without a padded copy of X;
 //   * columns are padded (to a multiple of 16, zero filled) only when N is
 //     not a multiple of 8 or the data pointer is not 16-byte aligned -- the
 //     TMA row-stride rule -- instead of always to max(align16(N), rows);
 //   * tiling is derived from sizes inside the library, so there is no
-//     tiling cache to key on stream/shape/coefficients (binding.cpp:103-611).
+//     tiling cache to key on stream/shape/coefficients (binding.cpp:103-611);
+//     what is cached per (device, stream) -- the role of the reference's
+//     LaunchState maps -- is the split-K scratch buffer, whose arrival
+//     counters must be zero before a launch and are left zero by it.
 #include <ATen/ATen.h>
 #include <c10/core/DeviceGuard.h>
 #include <c10/cuda/CUDAFunctions.h>
@@ -23,6 +26,9 @@
 
 #include <cstdint>
 #include <cstdlib>
+#include <mutex>
+#include <unordered_map>
+#include <vector>
 
 #include "muon_polar_sm100.h"
 
@@ -50,6 +56,51 @@ void DebugSync(int device, const char* stage) {
               " failed, status=", rc, ", detail=", muon_polar_status_string(rc));
   TORCH_CHECK(flags == 0, "muon_polar_step: stage ", stage,
               " gave up on a bounded wait, watchdog=", flags);
+}
+
+// Split-K scratch per (device, stream), zero-initialised once.  Buffers are
+// never freed while the process lives (a CUDA graph captured earlier may
+// still point at one); a larger problem allocates a larger buffer.
+struct ScratchKey {
+  int device;
+  uintptr_t stream;
+  bool operator==(const ScratchKey& o) const {
+    return device == o.device && stream == o.stream;
+  }
+};
+struct ScratchKeyHash {
+  size_t operator()(const ScratchKey& k) const {
+    return std::hash<uintptr_t>()(k.stream) * 31u + static_cast<size_t>(k.device);
+  }
+};
+std::mutex gScratchMutex;
+std::unordered_map<ScratchKey, at::Tensor, ScratchKeyHash> gScratch;
+std::vector<at::Tensor> gRetiredScratch;
+
+// Returns (pointer, bytes) of a zeroed scratch buffer of at least `bytes`,
+// or (nullptr, 0) -- split-K off -- when none is cached and the stream is
+// being captured into a CUDA graph (no allocation may happen then).
+std::pair<void*, size_t> GetScratch(const at::Tensor& like, int device,
+                                    cudaStream_t stream, size_t bytes) {
+  if (bytes == 0) return {nullptr, 0};
+  std::lock_guard<std::mutex> lock(gScratchMutex);
+  const ScratchKey key{device, reinterpret_cast<uintptr_t>(stream)};
+  auto it = gScratch.find(key);
+  if (it != gScratch.end() && static_cast<size_t>(it->second.numel()) >= bytes)
+    return {it->second.data_ptr(), static_cast<size_t>(it->second.numel())};
+  cudaStreamCaptureStatus capture = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(stream, &capture) != cudaSuccess ||
+      capture != cudaStreamCaptureStatusNone)
+    return {nullptr, 0};
+  at::Tensor fresh = at::empty({static_cast<int64_t>(bytes)}, like.options().dtype(at::kByte));
+  CheckStatus(muon_polar_scratch_init(fresh.data_ptr(), bytes, stream), "scratch_init");
+  if (it != gScratch.end()) {
+    gRetiredScratch.push_back(it->second);
+    it->second = fresh;
+  } else {
+    gScratch.emplace(key, fresh);
+  }
+  return {fresh.data_ptr(), bytes};
 }
 
 at::Tensor MuonPolarStepCuda(const at::Tensor& x, double a, double b,
@@ -88,12 +139,14 @@ at::Tensor MuonPolarStepCuda(const at::Tensor& x, double a, double b,
   const float fa = static_cast<float>(a);
   const float fb = static_cast<float>(b);
   const float fc = static_cast<float>(c);
+  const auto scratch = GetScratch(input, x.device().index(), stream.stream(),
+                                  muon_polar_scratch_bytes(batch, rows, cols));
 
   if (!DebugSyncEnabled()) {
     CheckStatus(muon_polar_step_sm100(input.data_ptr(), out.data_ptr(),
-                                      workspace.data_ptr(), wsBytes, batch,
-                                      rows, cols, ld, ld, fa, fb, fc,
-                                      raw_stream),
+                                      workspace.data_ptr(), wsBytes, scratch.first,
+                                      scratch.second, batch, rows, cols, ld, ld,
+                                      fa, fb, fc, raw_stream),
                 "polar_step_sm100");
   } else {
     const int device = x.device().index();
@@ -102,11 +155,12 @@ at::Tensor MuonPolarStepCuda(const at::Tensor& x, double a, double b,
     void* gram = ws;
     void* poly = ws + static_cast<size_t>(batch * mp * mp * 2);
     CheckStatus(muon_polar_gram_sm100(input.data_ptr(), gram, batch, rows,
-                                      cols, ld, raw_stream),
+                                      cols, ld, scratch.first, scratch.second,
+                                      raw_stream),
                 "gram_sm100");
     DebugSync(device, "gram_sm100");
     CheckStatus(muon_polar_poly_sm100(gram, poly, batch, mp, fb, fc,
-                                      raw_stream),
+                                      scratch.first, scratch.second, raw_stream),
                 "poly_sm100");
     DebugSync(device, "poly_sm100");
     CheckStatus(muon_polar_apply_sm100(poly, input.data_ptr(), out.data_ptr(),

@@ -74,22 +74,50 @@ def _assert_within_ulps(actual, expected64, ulps, what, abs_slack=0.0, max_frac=
     return frac
 
 
+MODES = ["single", "pair", "pair_split"]
+
+
+@pytest.fixture
+def mode_policy(api):
+    """Sets the kernel policy for one test and restores the default after."""
+    def set_mode(mode):
+        api.set_kernel_policy(2 if mode == "single" else 1)
+        return mode == "pair_split"
+    yield set_mode
+    api.set_kernel_policy(0)
+
+
 def _check_watchdog(api):
     assert api.read_device_status(torch.cuda.current_device()) == 0
 
 
+def _counters_zero(scratch):
+    """The split-K arrival counters (first 1024 bytes) are back to zero."""
+    if scratch.numel() > 1:
+        assert int(scratch[:1024].cpu().count_nonzero()) == 0
+
+
 # ------------------------------------------------------------------ stages
+@pytest.mark.parametrize("mode", MODES)
 @pytest.mark.parametrize("shape", [(1, 128, 128), (2, 150, 2064), (8, 512, 2048),
                                    (1, 300, 1000), (3, 64, 72), (1, 640, 640)])
-def test_gram_stage(api, cuda_device, shape):
+def test_gram_stage(api, cuda_device, shape, mode, mode_policy):
+    split = mode_policy(mode)
     bsz, m, n = shape
     x = make_input(shape, seed=1)
     mp = api.padded_rows(m)
     xd = x.to(cuda_device)
+    scratch = api.new_scratch(bsz, m, n) if split else None
     gram = torch.full((bsz, mp, mp), float("nan"), dtype=torch.bfloat16, device=cuda_device)
-    api.gram(xd, gram)
+    api.gram(xd, gram, scratch=scratch)
     torch.cuda.synchronize()
     _check_watchdog(api)
+    if split:
+        _counters_zero(scratch)
+        again = torch.empty_like(gram)
+        api.gram(xd, again, scratch=scratch)
+        torch.cuda.synchronize()
+        assert torch.equal(again.view(torch.int16), gram.view(torch.int16))
     g = gram.cpu()
     x64 = torch.zeros((bsz, mp, n), dtype=torch.float64)
     x64[:, :m] = x.to(torch.float64)
@@ -101,13 +129,16 @@ def test_gram_stage(api, cuda_device, shape):
     assert torch.equal(g.view(torch.int16), g.mT.contiguous().view(torch.int16))
 
 
+@pytest.mark.parametrize("mode", MODES)
 @pytest.mark.parametrize("shape", [(1, 128, 128), (2, 256, 2064), (8, 512, 2048)])
-def test_gram_f32_stage(api, cuda_device, shape):
+def test_gram_f32_stage(api, cuda_device, shape, mode, mode_policy):
+    split = mode_policy(mode)
     bsz, m, n = shape
     x = make_input(shape, seed=2)
     mp = api.padded_rows(m)
+    scratch = api.new_scratch(bsz, m, n) if split else None
     gram = torch.full((bsz, mp, mp), float("nan"), dtype=torch.float32, device=cuda_device)
-    api.gram_f32(x.to(cuda_device), gram)
+    api.gram_f32(x.to(cuda_device), gram, scratch=scratch)
     torch.cuda.synchronize()
     g = gram.cpu().to(torch.float64)
     x64 = x.to(torch.float64)
@@ -117,18 +148,23 @@ def test_gram_f32_stage(api, cuda_device, shape):
     assert torch.equal(g, g.mT)
 
 
+@pytest.mark.parametrize("mode", MODES)
 @pytest.mark.parametrize("shape", [(1, 128, 256), (2, 256, 512), (8, 512, 2048), (1, 1024, 1024)])
-def test_poly_stage(api, cuda_device, shape):
+def test_poly_stage(api, cuda_device, shape, mode, mode_policy):
+    split = mode_policy(mode)
     bsz, m, n = shape
     x = make_input(shape, seed=3)
     mp = api.padded_rows(m)
     xd = x.to(cuda_device)
+    scratch = api.new_scratch(bsz, m, n) if split else None
     gram = torch.empty((bsz, mp, mp), dtype=torch.bfloat16, device=cuda_device)
     poly = torch.full_like(gram, float("nan"))
-    api.gram(xd, gram)
-    api.poly(gram, poly, B1, C1)
+    api.gram(xd, gram, scratch=scratch)
+    api.poly(gram, poly, B1, C1, scratch=scratch)
     torch.cuda.synchronize()
     _check_watchdog(api)
+    if split:
+        _counters_zero(scratch)
     a64 = gram.cpu().to(torch.float64)
     a2 = (a64 @ a64.mT).to(torch.float32)
     slack = abs(C1) * _gamma(mp) * (a64.abs() @ a64.abs().mT)
@@ -140,17 +176,20 @@ def test_poly_stage(api, cuda_device, shape):
     assert torch.equal(p.view(torch.int16), p.mT.contiguous().view(torch.int16))
 
 
+@pytest.mark.parametrize("mode", ["single", "pair"])
 @pytest.mark.parametrize("shape", [(1, 128, 256), (2, 150, 2064), (8, 512, 2048),
                                    (1, 200, 1000), (2, 384, 520)])
-def test_apply_stage(api, cuda_device, shape):
+def test_apply_stage(api, cuda_device, shape, mode, mode_policy):
+    mode_policy(mode)
     bsz, m, n = shape
     x = make_input(shape, seed=4)
     mp = api.padded_rows(m)
     xd = x.to(cuda_device)
     gram = torch.empty((bsz, mp, mp), dtype=torch.bfloat16, device=cuda_device)
     poly = torch.empty_like(gram)
-    api.gram(xd, gram)
-    api.poly(gram, poly, B1, C1)
+    scratch = api.new_scratch(bsz, m, n)
+    api.gram(xd, gram, scratch=scratch)
+    api.poly(gram, poly, B1, C1, scratch=scratch)
     y = torch.full_like(xd, float("nan"))
     api.apply(poly, xd, y, A1)
     torch.cuda.synchronize()
