@@ -1,0 +1,78 @@
+"""CPU tests of the C ABI library: it loads without a GPU, exports every
+entry point declared in include/muon_polar_sm100.h, and rejects bad
+arguments before touching a device."""
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+from muon_fusion_ascend950_b200.capi import CAPI, SIGNATURES
+
+HEADER = Path(__file__).resolve().parent.parent / "include" / "muon_polar_sm100.h"
+
+
+def header_functions():
+    text = HEADER.read_text()
+    return sorted(set(re.findall(r"^\w[\w\s\*]*?\b(muon_polar_\w+)\s*\(", text, re.M)))
+
+
+@pytest.fixture(scope="module")
+def api():
+    return CAPI()
+
+
+def test_header_declares_entry_points():
+    names = header_functions()
+    assert "muon_polar_step_sm100" in names and "muon_polar_gram_sm100" in names
+    assert len(names) >= 12
+
+
+def test_library_exports_every_header_symbol(api):
+    for name in header_functions():
+        assert hasattr(api.lib, name), name
+
+
+def test_binding_covers_every_header_symbol():
+    assert set(header_functions()) == set(SIGNATURES)
+
+
+def test_abi_version_and_sizes(api):
+    assert api.abi_version() == 1
+    assert api.padded_rows(1) == 256 and api.padded_rows(256) == 256
+    assert api.padded_rows(257) == 512 and api.padded_rows(0) == 0
+    assert api.workspace_bytes(8, 512) == 2 * 8 * 512 * 512 * 2
+    assert api.workspace_bytes(0, 5) == 0
+
+
+def test_status_strings(api):
+    assert api.status_string(0) == "success"
+    for code in (-1, -2, -3, -4, -5, -6):
+        assert api.status_string(code) != "unknown status"
+
+
+def _vp(v):
+    return ctypes.c_void_p(v)
+
+
+def test_argument_validation_without_device(api):
+    lib = api.lib
+    # null input / bad sizes are rejected before any CUDA call
+    assert lib.muon_polar_gram_sm100(None, _vp(16), 1, 128, 128, 128, None, 0, None) == -1
+    assert lib.muon_polar_gram_sm100(_vp(16), _vp(16), 0, 128, 128, 128, None, 0, None) == -1
+    assert lib.muon_polar_gram_sm100(_vp(16), _vp(16), 1, 128, 128, 64, None, 0, None) == -1
+    # misaligned pointer / leading dimension
+    assert lib.muon_polar_gram_sm100(_vp(18), _vp(16), 1, 128, 128, 128, None, 0, None) == -3
+    assert lib.muon_polar_gram_sm100(_vp(16), _vp(16), 1, 128, 130, 130, None, 0, None) == -3
+    assert lib.muon_polar_poly_sm100(_vp(16), _vp(16), 1, 100, 1.0, 1.0, None, 0, None) == -1
+    assert lib.muon_polar_apply_sm100(_vp(16), _vp(16), None, 1, 8, 8, 8, 8, 1.0, None) == -1
+    # step: workspace too small, y aliasing x
+    assert lib.muon_polar_step_sm100(_vp(16), _vp(32), _vp(16), 8, None, 0, 1, 8, 8, 8, 8,
+                                     1.0, 1.0, 1.0, None) == -5
+    assert lib.muon_polar_step_sm100(_vp(16), _vp(16), _vp(16), 1 << 30, None, 0, 1, 8, 8, 8, 8,
+                                     1.0, 1.0, 1.0, None) == -1
+    assert lib.muon_polar_cast_f32_bf16_sm100(None, _vp(16), 4, None) == -1
+    assert lib.muon_polar_set_kernel_policy(7) == -1
+    assert lib.muon_polar_read_device_status(0, None, 0) == -1

@@ -1,0 +1,53 @@
+"""CPU tests of the Python entry point and the operator registration:
+argument checks with the reference's exception types (ops.py:13-22 of the
+reference), the torch op schema and the FakeTensor kernel (_loader.py:41-48)."""
+from __future__ import annotations
+
+import pytest
+import torch
+
+import muon_ascend950
+import muon_fusion_ascend950_b200 as pkg
+
+
+def test_drop_in_alias():
+    assert muon_ascend950.polar_step is pkg.polar_step
+    assert pkg.__version__ == "0.1.1"
+
+
+def test_rejects_non_tensor():
+    with pytest.raises(TypeError):
+        pkg.polar_step([[1.0]], 1.0, 1.0, 1.0)
+
+
+def test_rejects_cpu_tensor():
+    with pytest.raises(ValueError):
+        pkg.polar_step(torch.zeros(4, 8, dtype=torch.bfloat16), 1.0, 1.0, 1.0)
+
+
+def test_rejects_meta_device():
+    with pytest.raises(ValueError):
+        pkg.polar_step(torch.zeros(4, 8, dtype=torch.bfloat16, device="meta"), 1.0, 1.0, 1.0)
+
+
+def test_op_schema():
+    schema = str(torch.ops.muon_ascend950.polar_step.default._schema)
+    assert schema == "muon_ascend950::polar_step(Tensor x, float a, float b, float c) -> Tensor"
+
+
+@pytest.mark.parametrize("shape", [(2, 4, 8), (1, 129, 130)])
+def test_fake_tensor_kernel(shape):
+    from torch._subclasses.fake_tensor import FakeTensorMode
+
+    with FakeTensorMode():
+        x = torch.empty(shape, dtype=torch.bfloat16, device="cuda")
+        y = torch.ops.muon_ascend950.polar_step(x, 1.0, 2.0, 3.0)
+        assert y.shape == x.shape and y.dtype == x.dtype and y.is_contiguous()
+
+
+def test_loader_respects_library_override(tmp_path, monkeypatch):
+    from muon_fusion_ascend950_b200 import _loader
+
+    monkeypatch.setenv("MUON_ASCEND950_LIBRARY", str(tmp_path / "missing.so"))
+    with pytest.raises(RuntimeError, match="does not exist"):
+        _loader._library_path()
