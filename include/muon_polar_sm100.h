@@ -46,6 +46,12 @@ extern "C" {
 #define MUON_POLAR_ERR_TENSOR_MAP (-4)
 #define MUON_POLAR_ERR_WORKSPACE (-5)
 #define MUON_POLAR_ERR_DRIVER (-6)
+#define MUON_POLAR_ERR_STATIC_SCRATCH (-7)
+
+/* Size of the split-K scratch array built into the library for
+ * muon_polar_gram_static_scratch_sm100: 1 KiB of counters + 80 partial bands
+ * of 256 KiB (20 MiB + 1 KiB per GPU that loads the library). */
+#define MUON_POLAR_STATIC_SCRATCH_BYTES ((size_t)1024 + (size_t)80 * (size_t)262144)
 
 /* Bits of the device watchdog word (muon_polar_read_device_status). A bit is
  * set when a bounded wait inside a kernel gave up; the kernel then left its
@@ -99,6 +105,37 @@ int muon_polar_scratch_init(void* scratch, size_t scratch_bytes, void* stream);
 int muon_polar_gram_sm100(const void* x, void* gram, int64_t batch, int64_t m,
                           int64_t n, int64_t ldx, void* scratch,
                           size_t scratch_bytes, void* stream);
+
+/* Kernel (1) for callers that cannot allocate device memory.  No
+ * counterpart in the reference, whose binding allocates its buffers with
+ * at::empty on every call (binding.cpp:646-663).
+ *
+ * Some callers have no way to hand this library scratch memory: a plugin
+ * or real-time host that works inside a fixed device-memory budget, code
+ * running next to a framework whose allocator has already reserved nearly
+ * all of the GPU (so a cudaMalloc of its own fails or fragments that pool),
+ * or a hot path that must not call cudaMalloc/cudaFree because they can
+ * synchronise the device.  For them this entry computes exactly what
+ * muon_polar_gram_sm100 computes on its CTA-pair path with split-K -- same
+ * tiles, same split plan, same reduction order -- but takes its split-K
+ * scratch from an array compiled into the library
+ * (MUON_POLAR_STATIC_SCRATCH_BYTES per GPU, held until the process exits).
+ * The caller still passes x and gram; nothing is allocated.
+ *
+ *  - The first call on each device looks up the array's device address
+ *    (cudaGetSymbolAddress, with that device current); make that first call
+ *    before starting any stream capture.
+ *  - The array is shared by every call on a device and keeps the previous
+ *    call's contents; each call clears the counter part itself
+ *    (cudaMemsetAsync on `stream`).  Calls whose executions overlap on the
+ *    GPU (different streams, not ordered) race on the array and produce
+ *    wrong results: order them.
+ *  - A problem whose split plan needs more than the array returns
+ *    MUON_POLAR_ERR_STATIC_SCRATCH and launches nothing.
+ * Arguments and layout as for muon_polar_gram_sm100. */
+int muon_polar_gram_static_scratch_sm100(const void* x, void* gram, int64_t batch,
+                                         int64_t m, int64_t n, int64_t ldx,
+                                         void* stream);
 
 /* Kernel (1), fp32 output variant: partial Gram in fp32 for the column-sharded
  * multi-GPU path (the partials are summed across ranks before kernel 2).

@@ -28,6 +28,8 @@ SIGNATURES = {
     "muon_polar_scratch_init": (ctypes.c_int, [_VP, ctypes.c_size_t, _VP]),
     "muon_polar_gram_sm100": (ctypes.c_int, [_VP, _VP, _I64, _I64, _I64, _I64, _VP,
                                              ctypes.c_size_t, _VP]),
+    "muon_polar_gram_static_scratch_sm100": (ctypes.c_int, [_VP, _VP, _I64, _I64, _I64, _I64,
+                                                            _VP]),
     "muon_polar_gram_f32_sm100": (ctypes.c_int, [_VP, _VP, _I64, _I64, _I64, _I64, _VP,
                                                  ctypes.c_size_t, _VP]),
     "muon_polar_poly_sm100": (ctypes.c_int, [_VP, _VP, _I64, _I64, ctypes.c_float,
@@ -168,6 +170,15 @@ class CAPI:
         sp, sb = _scratch(scratch)
         self._check("muon_polar_gram_sm100", self.lib.muon_polar_gram_sm100(
             x.data_ptr(), gram.data_ptr(), b, m, n, ld, sp, sb, self._stream(stream)))
+
+    def gram_static_scratch(self, x, gram, n: Optional[int] = None, stream=None) -> None:
+        """Kernel 1 with split-K scratch taken from the array built into the
+        library (for callers that cannot allocate device memory)."""
+        b, m, ld = x.shape
+        n = ld if n is None else n
+        self._check("muon_polar_gram_static_scratch_sm100",
+                    self.lib.muon_polar_gram_static_scratch_sm100(
+                        x.data_ptr(), gram.data_ptr(), b, m, n, ld, self._stream(stream)))
 
     def gram_f32(self, x, gram_f32, n: Optional[int] = None, scratch=None,
                  stream=None) -> None:

@@ -1516,6 +1516,98 @@ int apply_impl(const void* poly, const void* x, void* y, int64_t batch,
 
 using namespace muon_sm100;
 
+// ============================================================ no allocation
+// Split-K scratch of muon_polar_gram_static_scratch_sm100, for callers that
+// cannot allocate device memory themselves: a file-scope device array (1 KiB
+// of arrival counters + fp32 partial bands for 80 split items, 20 MiB +
+// 1 KiB in all).  Every GPU that loads this library holds it until the
+// process exits.  Host code must not hand `g_static_scratch` to a kernel:
+// on the host that name is only a stand-in for the device symbol; the
+// device address comes from cudaGetSymbolAddress below.
+constexpr size_t kStaticScratchItems = 80;
+constexpr size_t kStaticScratchBytes =
+    muon_sm100::kCounterBytes + kStaticScratchItems * muon_sm100::kPartialItemBytes;
+static_assert(kStaticScratchBytes == MUON_POLAR_STATIC_SCRATCH_BYTES,
+              "header and library agree on the static scratch size");
+static __device__ __align__(256) uint8_t g_static_scratch[kStaticScratchBytes];
+
+namespace {
+struct StaticScratchAddress {
+  std::once_flag once;
+  void* ptr = nullptr;
+  cudaError_t err = cudaSuccess;
+};
+StaticScratchAddress g_static_scratch_address[muon_sm100::kMaxDevices];
+
+// Device address of g_static_scratch on the current device `dev`, looked up
+// once per device (with that device current).
+int static_scratch_address(int dev, void** out) {
+  StaticScratchAddress& sa = g_static_scratch_address[dev];
+  std::call_once(sa.once, [&sa] {
+    sa.err = cudaGetSymbolAddress(&sa.ptr, g_static_scratch);
+  });
+  if (sa.err != cudaSuccess) return static_cast<int>(sa.err);
+  *out = sa.ptr;
+  return MUON_POLAR_OK;
+}
+
+int gram_static_scratch_impl(const void* x, void* gram, int64_t batch, int64_t m,
+                             int64_t n, int64_t ldx, cudaStream_t stream) {
+  int rc = check_x_args(x, batch, m, n, ldx);
+  if (rc != MUON_POLAR_OK) return rc;
+  if (gram == nullptr) return MUON_POLAR_ERR_INVALID_ARGUMENT;
+  if (!aligned16(gram)) return MUON_POLAR_ERR_ALIGNMENT;
+  DeviceState* st = nullptr;
+  rc = current_device_state(&st);
+  if (rc != MUON_POLAR_OK) return rc;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return static_cast<int>(e);
+  void* scratch = nullptr;
+  rc = static_scratch_address(dev, &scratch);
+  if (rc != MUON_POLAR_OK) return rc;
+
+  const int64_t mp = padded_rows(m);
+  const int64_t dp = mp / kPairM;
+  const int64_t tp = dp * (dp + 1) / 2;
+  if (tp * batch > INT32_MAX) return MUON_POLAR_ERR_INVALID_ARGUMENT;
+  int pairs = 0;
+  rc = pair_capacity<kGramBf16>(st, 5 + kGramBf16, &pairs);
+  if (rc != MUON_POLAR_OK) return rc;
+  const int64_t k_blocks = (n + kBK - 1) / kBK;
+  // The same split plan as muon_polar_gram_sm100 on the CTA-pair path with
+  // enough scratch; a plan that needs more than the static array is refused.
+  const size_t need =
+      split_scratch_bytes(tp * batch, choose_splits(tp * batch, k_blocks, pairs));
+  if (need > kStaticScratchBytes) return MUON_POLAR_ERR_STATIC_SCRATCH;
+
+  PairMaps pm;
+  rc = encode_3d(&pm.a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, x, n, m, batch, ldx,
+                 m * ldx, kBK, kHalf);
+  if (rc != MUON_POLAR_OK) return rc;
+  pm.b = pm.a;
+  pm.aux = pm.a;
+  rc = encode_square(&pm.out, gram, batch, mp, false, kHalf);
+  if (rc != MUON_POLAR_OK) return rc;
+  rc = encode_square(&pm.mir, gram, batch, mp, false, kChunkCols);
+  if (rc != MUON_POLAR_OK) return rc;
+  EpiParams p = {};
+  p.tiles_m = static_cast<int32_t>(dp);
+  p.tiles_n = static_cast<int32_t>(dp);
+  p.tiles_per_batch = static_cast<int32_t>(tp);
+  p.total_tiles = static_cast<int32_t>(tp * batch);
+  p.k_blocks = static_cast<int32_t>(k_blocks);
+  plan_splits(p, scratch, kStaticScratchBytes, pairs);
+  if (p.splits > 1) {
+    // The array keeps the previous call's contents: the arrival counters
+    // must start at zero, so clear them before every launch.
+    e = cudaMemsetAsync(scratch, 0, kCounterBytes, stream);
+    if (e != cudaSuccess) return static_cast<int>(e);
+  }
+  return launch_pair<kGramBf16>(st, 5 + kGramBf16, pm, p, stream);
+}
+}  // namespace
+
 extern "C" {
 
 int muon_polar_abi_version(void) { return MUON_POLAR_ABI_VERSION; }
@@ -1536,6 +1628,10 @@ const char* muon_polar_status_string(int status) {
       return "workspace too small or misaligned";
     case MUON_POLAR_ERR_DRIVER:
       return "CUDA driver entry point cuTensorMapEncodeTiled unavailable";
+    case MUON_POLAR_ERR_STATIC_SCRATCH:
+      return "problem needs more split-K scratch than the library's static "
+             "buffer holds (MUON_POLAR_STATIC_SCRATCH_BYTES); use "
+             "muon_polar_gram_sm100 with caller-owned scratch";
     default:
       break;
   }
@@ -1627,6 +1723,13 @@ int muon_polar_scratch_init(void* scratch, size_t scratch_bytes, void* stream) {
   const size_t n = scratch_bytes < kCounterBytes ? scratch_bytes : kCounterBytes;
   cudaError_t e = cudaMemsetAsync(scratch, 0, n, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? MUON_POLAR_OK : static_cast<int>(e);
+}
+
+int muon_polar_gram_static_scratch_sm100(const void* x, void* gram, int64_t batch,
+                                         int64_t m, int64_t n, int64_t ldx,
+                                         void* stream) {
+  return gram_static_scratch_impl(x, gram, batch, m, n, ldx,
+                                  static_cast<cudaStream_t>(stream));
 }
 
 int muon_polar_cast_f32_bf16_sm100(const void* src, void* dst, int64_t count,

@@ -49,7 +49,7 @@ def test_abi_version_and_sizes(api):
 
 def test_status_strings(api):
     assert api.status_string(0) == "success"
-    for code in (-1, -2, -3, -4, -5, -6):
+    for code in (-1, -2, -3, -4, -5, -6, -7):
         assert api.status_string(code) != "unknown status"
 
 
@@ -74,5 +74,7 @@ def test_argument_validation_without_device(api):
     assert lib.muon_polar_step_sm100(_vp(16), _vp(16), _vp(16), 1 << 30, None, 0, 1, 8, 8, 8, 8,
                                      1.0, 1.0, 1.0, None) == -1
     assert lib.muon_polar_cast_f32_bf16_sm100(None, _vp(16), 4, None) == -1
+    assert lib.muon_polar_gram_static_scratch_sm100(None, _vp(16), 1, 8, 8, 8, None) == -1
+    assert lib.muon_polar_gram_static_scratch_sm100(_vp(16), _vp(24), 1, 8, 8, 8, None) == -3
     assert lib.muon_polar_set_kernel_policy(7) == -1
     assert lib.muon_polar_read_device_status(0, None, 0) == -1
