@@ -36,6 +36,13 @@ if str(REPO) not in sys.path:
     sys.path.insert(0, str(REPO))
 
 BATCH, M, N = 8, 512, 2048
+COEFFICIENTS = (
+    (8.156554524902461, -22.48329292557795, 15.878769915207462),
+    (4.042929935166739, -2.808917465908714, 0.5000178451051316),
+    (3.8916678022926607, -2.772484153217685, 0.5060648178503393),
+    (3.285753657755655, -2.3681294933425376, 0.46449024233003106),
+    (2.3465413258596377, -1.7097828382687081, 0.42323551169305323),
+)
 ROTATION = 8             # input sets cycled through: 8 x 42 MB > 126 MB L2
 L2_BYTES = 126 * 2 ** 20
 FALLBACK_TFLOPS = 1590.0
@@ -54,6 +61,16 @@ def parse_args():
     p.add_argument("--e2e-steps", type=int, default=200,
                    help="steps of the host-buffer end-to-end loop (<= --steps)")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--shape", default="8,512,2048",
+                   help="B,M,N of the `shape` workload (one polar_step per timed step)")
+    p.add_argument("--workload", choices=["cfg1", "cfg3", "cfg4", "cfg5", "shape"],
+                   default="cfg1",
+                   help="cfg1 (default, the headline): one step on [8,512,2048] per GPU; "
+                        "cfg3: the 5-step loop on [8,512,2048] per GPU; cfg4: 5-step Muon "
+                        "update of a 32-layer 7B model's matrices, batch-sharded over the "
+                        "GPUs; cfg5: 5 steps on one [8192,65536] matrix, column-sharded "
+                        "with an NCCL all-reduce of the fp32 Gram per step; shape: one "
+                        "step on --shape per GPU (config 2 shapes, profiling cases)")
     return p.parse_args()
 
 
@@ -147,16 +164,16 @@ def dist_env():
     return rank, world, local
 
 
-def cpu_reference_rate(steps: int, warmup: int, budget_s: float):
+def cpu_reference_rate(steps: int, warmup: int, budget_s: float, rows: int = 1):
     """Times the reference formula (bf16, CPU, all threads) on a sample of the
     workload.  Returns (TFLOP/s, threads, sample description)."""
     import torch
 
-    from oracle.polar_oracle import COEFFICIENTS, make_input, reference_formula
+    from oracle.polar_oracle import make_input, reference_formula
 
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    coeffs = COEFFICIENTS[:1]
+    coeffs = COEFFICIENTS[:rows]
     probe = make_input((1, M, N), seed=0)
     t0 = time.perf_counter()
     reference_formula(probe, coeffs)
@@ -172,9 +189,10 @@ def cpu_reference_rate(steps: int, warmup: int, budget_s: float):
         reference_formula(x, coeffs)
         times.append(time.perf_counter() - t0)
     med = statistics.median(times)
-    rate = batch * nominal_flops_per_matrix(M, N) / med / 1e12
-    sample = (f"{len(times)} timed steps (median) of the reference formula on "
-              f"{batch} of the {BATCH} matrices [{M},{N}] bf16, after {warmup} warm-up")
+    rate = rows * batch * nominal_flops_per_matrix(M, N) / med / 1e12
+    sample = (f"{len(times)} timed steps (median) of the reference formula "
+              f"({rows} coefficient row(s)) on {batch} of the {BATCH} matrices [{M},{N}] "
+              f"bf16, after {warmup} warm-up")
     return rate, threads, sample
 
 
@@ -219,11 +237,24 @@ def run_ours(args):
 
         dist.init_process_group("nccl", device_id=device, timeout=timedelta(seconds=120))
     api = capi()
-    a, b, c = (8.156554524902461, -22.48329292557795, 15.878769915207462)
-    flops_step = BATCH * nominal_flops_per_matrix(M, N)
+    global BATCH, M, N
+    if args.workload == "shape":
+        BATCH, M, N = (int(v) for v in args.shape.split(","))
+    a, b, c = COEFFICIENTS[0]
+    rows = COEFFICIENTS if args.workload == "cfg3" else COEFFICIENTS[:1]
+    flops_step = len(rows) * BATCH * nominal_flops_per_matrix(M, N)
+
+    def full_step(x):
+        for ra, rb, rc in rows:
+            x = pkg.polar_step(x, ra, rb, rc)
+        return x
 
     # inputs generated on the device (seeded per rank and set), normalised as
-    # the reference test does
+    # the reference test does; enough rotating sets that one cycle touches
+    # more than three times the L2 (8 sets at [8,512,2048])
+    global ROTATION
+    set_bytes = 3 * BATCH * M * N * 2 + 2 * BATCH * api.padded_rows(M) ** 2 * 2
+    ROTATION = int(min(8, max(2, -(-3 * L2_BYTES // set_bytes))))
     gen = torch.Generator(device=device)
     xs = []
     for i in range(ROTATION):
@@ -243,13 +274,13 @@ def run_ours(args):
     graphs, outs = [], []
     with torch.cuda.stream(stream):
         for x in xs:  # eager warm-up of every set before capture
-            pkg.polar_step(x, a, b, c)
+            full_step(x)
     torch.cuda.synchronize(device)
     launches_before = api.launch_count()
     for x in xs:
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g, stream=stream):
-            outs.append(pkg.polar_step(x, a, b, c))
+            outs.append(full_step(x))
         graphs.append(g)
     launches_per_step = (api.launch_count() - launches_before) // ROTATION
 
@@ -339,7 +370,7 @@ def run_ours(args):
     with torch.cuda.stream(stream):
         for i in range(3):
             xd = host_in[i % ROTATION].to(device, non_blocking=True)
-            host_out.copy_(pkg.polar_step(xd, a, b, c), non_blocking=True)
+            host_out.copy_(full_step(xd), non_blocking=True)
     sync_all()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
@@ -347,7 +378,7 @@ def run_ours(args):
         e0.record(stream)
         for i in range(e2e_steps):
             xd = host_in[i % ROTATION].to(device, non_blocking=True)
-            host_out.copy_(pkg.polar_step(xd, a, b, c), non_blocking=True)
+            host_out.copy_(full_step(xd), non_blocking=True)
         e1.record(stream)
     e1.synchronize()
     e2e_ms = e0.elapsed_time(e1)
@@ -361,7 +392,7 @@ def run_ours(args):
     # ---- CPU baseline (rank 0, N=1 only)
     cpu_baseline = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        rate, threads, sample = cpu_reference_rate(3, 1, budget_s=20.0)
+        rate, threads, sample = cpu_reference_rate(3, 1, budget_s=20.0, rows=len(rows))
         cpu_baseline = {"value": rate, "unit": "TFLOP/s", "cores": threads, "kind": "port",
                         "sample": sample}
 
@@ -372,8 +403,11 @@ def run_ours(args):
         dist.destroy_process_group()
     if rank != 0:
         return
+    cfg3 = args.workload == "cfg3"
+    shape_str = f"[{BATCH},{M},{N}]"
     line = {
-        "metric": "polar_step effective TFLOP/s at [8,512,2048] bf16",
+        "metric": (f"5-step Polar Express loop effective TFLOP/s at {shape_str} bf16" if cfg3
+                   else f"polar_step effective TFLOP/s at {shape_str} bf16"),
         "value": value,
         "unit": "TFLOP/s",
         "n_gpus": world,
@@ -388,12 +422,15 @@ def run_ours(args):
         "data": "synthetic",
         "pct_of_bf16_peak": 100.0 * value / (world * peak),
         "config": {
-            "workload": "polar_step [8,512,2048] bf16 single step (BASELINE config 1) per GPU",
+            "workload": ("5-step polar_step loop on [8,512,2048] bf16 (BASELINE config 3) per GPU"
+                         if cfg3 else
+                         f"polar_step {shape_str} bf16 single step per GPU" +
+                         (" (BASELINE config 1)" if args.workload == "cfg1" else "")),
             "global_batch": BATCH * world, "m": M, "n": N,
             "parallelism": f"batch-sharded x{world}, no data-path collective",
             "timing": "CUDA-graph replay of the public polar_step, CUDA events, max over ranks",
             "l2": f"inputs larger than L2: {ROTATION} rotating input sets "
-                  f"({ROTATION} x {(3 * step_bytes + 2 * BATCH * 512 * 512 * 2) >> 20} MB touched "
+                  f"({ROTATION} x {(3 * step_bytes + 2 * BATCH * mp * mp * 2) >> 20} MB touched "
                   f"per cycle > {L2_BYTES >> 20} MB L2)",
         },
         "roofline": roofline,
@@ -407,10 +444,137 @@ def run_ours(args):
     print(json.dumps(line), flush=True)
 
 
+def run_large(args):
+    """Configs 4 and 5: one Muon update (the 5-step loop) per timed step over
+    a fixed total problem (strong scaling), eager launches (the host issues a
+    few hundred microseconds of launches per ~0.1-1 s step)."""
+    import torch
+    import torch.distributed as dist
+
+    import muon_fusion_ascend950_b200 as pkg
+    from muon_fusion_ascend950_b200.capi import capi
+    from muon_fusion_ascend950_b200.distributed import (
+        ColumnShardedPolar, column_range, nominal_flops, partition_items)
+
+    rank, world, local = dist_env()
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", device_id=device, timeout=timedelta(seconds=300))
+    api = capi()
+    gen = torch.Generator(device=device)
+    gen.manual_seed(rank)
+
+    def normalised(shape):
+        x = torch.randn(shape, generator=gen, device=device, dtype=torch.float32)
+        x = x.to(torch.bfloat16)
+        return x / (x.norm(dim=(-2, -1), keepdim=True) * 1.01 + 1e-6)
+
+    if args.workload == "cfg4":
+        # 32 layers x (q, k, v, o) = 128 [4096,4096]; 32 x (gate, up, down^T)
+        # = 96 [4096,11008]; FLOP-balanced across ranks
+        kinds = [(4096, 4096)] * 128 + [(4096, 11008)] * 96
+        mine = partition_items([float(nominal_flops(*k)) for k in kinds], world)[rank]
+        n_att = sum(1 for i in mine if kinds[i] == (4096, 4096))
+        n_ffn = len(mine) - n_att
+        batches = [normalised((cnt, 4096, n)) for cnt, n in ((n_att, 4096), (n_ffn, 11008))
+                   if cnt > 0]
+        job_flops = 5 * sum(nominal_flops(*k) for k in kinds)
+
+        def step():
+            for x in batches:
+                y = x
+                for a, b, c in COEFFICIENTS:
+                    y = pkg.polar_step(y, a, b, c)
+
+        workload = ("Muon update of a 32-layer 7B model: 5-step loop on [128,4096,4096] + "
+                    "[96,4096,11008] bf16 (BASELINE config 4)")
+        parallelism = f"batch-sharded x{world} (FLOP-balanced, no data-path collective)"
+    else:
+        m, n = 8192, 65536
+        cols = column_range(n, rank, world)
+        x_local = torch.randn((m, len(cols)), generator=gen, device=device,
+                              dtype=torch.float32).to(torch.bfloat16)
+        sq = (x_local.float() ** 2).sum().reshape(1)
+        if world > 1:
+            dist.all_reduce(sq)
+        x_local = (x_local / (sq.sqrt() * 1.01 + 1e-6)).to(torch.bfloat16)
+        driver = ColumnShardedPolar(m, device)
+        job_flops = 5 * nominal_flops(m, n)
+
+        def step():
+            driver.run(x_local, COEFFICIENTS)
+
+        workload = "5-step loop on one [8192,65536] bf16 matrix (BASELINE config 5)"
+        parallelism = (f"column-sharded x{world}, one NCCL fp32 all-reduce of the 8192x8192 "
+                       "partial Gram per step" if world > 1 else "single GPU")
+
+    def sync_all():
+        torch.cuda.synchronize(device)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(device)
+
+    launches0 = api.launch_count()
+    step()
+    sync_all()
+    launches_per_step = api.launch_count() - launches0
+    for _ in range(max(0, args.warmup - 1)):
+        step()
+    sync_all()
+    sampler = ClockSampler(local)
+    start = torch.cuda.Event(enable_timing=True)
+    stop = torch.cuda.Event(enable_timing=True)
+    with sampler:
+        sync_all()
+        start.record()
+        for _ in range(args.steps):
+            step()
+        stop.record()
+        stop.synchronize()
+        sync_all()
+    elapsed_ms = start.elapsed_time(stop)
+    if world > 1:
+        t = torch.tensor([elapsed_ms], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        elapsed_ms = float(t.item())
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    value = job_flops * args.steps / (elapsed_ms * 1e-3) / 1e12
+    peak, peak_kind = measured_peaks()
+    line = {
+        "metric": f"{args.workload} effective TFLOP/s (nominal 4M^2N+2M^3 per matrix per step)",
+        "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": elapsed_ms / args.steps,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic",
+        "pct_of_bf16_peak": 100.0 * value / (world * peak),
+        "config": {"workload": workload, "parallelism": parallelism,
+                   "timing": "eager public API / column-sharded driver, CUDA events, max over ranks",
+                   "l2": "inputs larger than L2"},
+        "roofline": {"bound": "tensor", "kernel": "whole step", "achieved": value / world,
+                     "peak": peak, "unit": "TFLOP/s", "frac": value / world / peak,
+                     "traffic": None, "peak_source": f"{peak_kind} bf16 dense (burst)"},
+        "cpu_baseline": None,
+        "e2e": None,
+        "clocks": sampler.summary(),
+        "gpu_launches": launches_per_step * args.steps,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse_args()
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload in ("cfg4", "cfg5"):
+        run_large(args)
     else:
         run_ours(args)
 

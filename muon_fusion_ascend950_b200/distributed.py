@@ -1,0 +1,141 @@
+"""Multi-GPU drivers of the Polar Express step (one process per GPU).
+
+The reference has no distributed code (no HCCL or collective anywhere).  The
+workloads it is benchmarked on shard in two ways:
+
+* **Batch sharding** (independent matrices: configs 1, 3 and 4).  Each rank
+  owns a FLOP-balanced subset of the matrices and runs the local step on
+  them; there is no collective on the data path.  `partition_items` balances
+  by nominal FLOPs (4 M^2 N + 2 M^3 per matrix).
+* **Column sharding** (one large matrix: config 5).  Rank r owns the column
+  slab X[:, r*N/G : (r+1)*N/G] for the whole iteration.  Per step:
+    1. partial Gram G_r = X_r X_r^T in fp32 (kernel 1, fp32 output),
+    2. one all-reduce (sum, fp32, Mp x Mp) over NCCL,
+    3. A = bf16(sum) (cast kernel), P = b A + c A A (kernel 2, replicated),
+    4. Y_r = a X_r + P X_r on the local slab (kernel 3).
+  The result equals the single-GPU step up to the fp32 summation order of
+  the Gram (A is rounded to bf16 once, after the sum, as on one GPU).
+
+Kernels are reached through a backend object with the methods of
+`capi.CAPI` (gram_f32, cast_f32_bf16, poly, apply).  The default backend is
+the CUDA C ABI; there is no CPU fallback -- tests on CPU pass their own
+backend explicitly.
+"""
+from __future__ import annotations
+
+import heapq
+from typing import List, Optional, Sequence
+
+import torch
+import torch.distributed as dist
+
+
+def nominal_flops(m: int, n: int) -> int:
+    """Nominal FLOPs of one step on one [m, n] matrix (M <= N after the
+    transpose policy): 4 M^2 N + 2 M^3."""
+    m, n = min(m, n), max(m, n)
+    return 4 * m * m * n + 2 * m ** 3
+
+
+def partition_items(costs: Sequence[float], world: int) -> List[List[int]]:
+    """Assigns item indices to `world` ranks, balancing the summed cost
+    (longest-processing-time greedy: items by decreasing cost, each to the
+    currently lightest rank; ties to the lowest rank).  Every item lands on
+    exactly one rank; each rank's list is in increasing index order."""
+    if world <= 0:
+        raise ValueError("world must be positive")
+    order = sorted(range(len(costs)), key=lambda i: (-costs[i], i))
+    heap = [(0.0, r) for r in range(world)]
+    heapq.heapify(heap)
+    parts: List[List[int]] = [[] for _ in range(world)]
+    for i in order:
+        load, r = heapq.heappop(heap)
+        parts[r].append(i)
+        heapq.heappush(heap, (load + costs[i], r))
+    return [sorted(p) for p in parts]
+
+
+def column_range(n: int, rank: int, world: int, align: int = 8) -> range:
+    """Columns of rank `rank` when n columns are cut into `world` slabs whose
+    boundaries are multiples of `align` (TMA needs 16-byte row strides for a
+    slab stored on its own).  The last slab takes the remainder."""
+    if world <= 0 or not 0 <= rank < world:
+        raise ValueError("bad rank/world")
+    per = -(-n // world)
+    per = -(-per // align) * align
+    start = min(n, rank * per)
+    stop = n if rank == world - 1 else min(n, (rank + 1) * per)
+    return range(start, stop)
+
+
+class ColumnShardedPolar:
+    """Polar Express steps on a matrix whose columns are split across the
+    ranks of `group` (see the module docstring).  Buffers for the replicated
+    Mp x Mp Gram / polynomial are allocated once per instance."""
+
+    def __init__(self, m: int, device, group=None, backend=None):
+        if backend is None:
+            from .capi import capi
+
+            backend = capi()
+        self.backend = backend
+        self.group = group
+        self.m = m
+        self.mp = backend.padded_rows(m)
+        self.device = torch.device(device)
+        shape = (1, self.mp, self.mp)
+        self.gram_f32 = torch.empty(shape, dtype=torch.float32, device=self.device)
+        self.gram = torch.empty(shape, dtype=torch.bfloat16, device=self.device)
+        self.poly = torch.empty(shape, dtype=torch.bfloat16, device=self.device)
+
+    def step(self, x_local: torch.Tensor, a: float, b: float, c: float,
+             out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """One step on this rank's slab x_local [m, n_local] (bf16, row
+        stride a multiple of 8); returns the slab of Y."""
+        if x_local.dim() != 2 or x_local.shape[0] != self.m:
+            raise ValueError(f"x_local must be [{self.m}, n_local], got {tuple(x_local.shape)}")
+        x3 = x_local.contiguous().unsqueeze(0)
+        y3 = torch.empty_like(x3) if out is None else out.view(1, *out.shape[-2:])
+        self.backend.gram_f32(x3, self.gram_f32)
+        if dist.is_initialized() and dist.get_world_size(self.group) > 1:
+            dist.all_reduce(self.gram_f32, op=dist.ReduceOp.SUM, group=self.group)
+        self.backend.cast_f32_bf16(self.gram_f32, self.gram)
+        self.backend.poly(self.gram, self.poly, b, c)
+        self.backend.apply(self.poly, x3, y3, a)
+        return y3.squeeze(0)
+
+    def run(self, x_local: torch.Tensor, coefficients) -> torch.Tensor:
+        """The caller-side loop over (a, b, c) rows, slab kept local."""
+        y = x_local
+        for a, b, c in coefficients:
+            y = self.step(y, a, b, c)
+        return y
+
+
+def batch_sharded_steps(xs: Sequence[torch.Tensor], coefficients, rank: int, world: int,
+                        step=None) -> dict:
+    """Runs the caller-side loop on this rank's share of the matrices `xs`
+    (a list of [M, N] or [B, M, N] tensors, all ranks passing the same list
+    description).  Returns {index: result} for the items this rank owns.
+    No collective is issued."""
+    if step is None:
+        from .ops import polar_step as step
+    costs = [float(nominal_flops(x.shape[-2], x.shape[-1]) * (x.shape[0] if x.dim() == 3 else 1))
+             for x in xs]
+    mine = partition_items(costs, world)[rank]
+    results = {}
+    for i in mine:
+        y = xs[i]
+        for a, b, c in coefficients:
+            y = step(y, a, b, c)
+        results[i] = y
+    return results
+
+
+__all__ = [
+    "nominal_flops",
+    "partition_items",
+    "column_range",
+    "ColumnShardedPolar",
+    "batch_sharded_steps",
+]

@@ -139,6 +139,43 @@ def polar_step_oracle(x: torch.Tensor, a: float, b: float, c: float) -> torch.Te
     return out.squeeze(0) if squeeze else out
 
 
+class CpuKernels:
+    """CPU stand-in for the C-ABI kernel entry points (the methods of
+    muon_fusion_ascend950_b200.capi.CAPI used by the multi-GPU drivers), for
+    the gloo tests of those drivers.  Same buffer shapes and the same
+    arithmetic as kernels 1-3 of the reference (fp32 Gram, round-to-nearest
+    bf16, separate multiply/add in the polynomial, bf16 add in the apply)."""
+
+    @staticmethod
+    def padded_rows(m: int) -> int:
+        return align_up(m, 256)
+
+    @staticmethod
+    def gram_f32(x, out, n=None, scratch=None, stream=None):
+        m = x.shape[1]
+        xf = x.to(torch.float32)
+        out.zero_()
+        out[:, :m, :m] = xf @ xf.mT
+
+    @staticmethod
+    def cast_f32_bf16(src, dst, stream=None):
+        dst.copy_(src.to(torch.bfloat16))
+
+    @staticmethod
+    def poly(gram, poly, b, c, scratch=None, stream=None):
+        a32 = gram.to(torch.float32)
+        b32 = torch.tensor(b, dtype=torch.float32)
+        c32 = torch.tensor(c, dtype=torch.float32)
+        poly.copy_(((b32 * a32) + (c32 * (a32 @ a32.mT))).to(torch.bfloat16))
+
+    @staticmethod
+    def apply(poly, x, y, a, n=None, stream=None):
+        m = x.shape[1]
+        t = poly.to(torch.float32)[:, :m, :m] @ x.to(torch.float32)
+        alpha = torch.tensor(a, dtype=torch.float32).to(torch.bfloat16).to(torch.float32)
+        y.copy_((_rne_bf16(t) + _rne_bf16(alpha * x.to(torch.float32))).to(torch.bfloat16))
+
+
 def nominal_flops(m: int, n: int) -> int:
     """Nominal FLOPs of one step on one matrix (M <= N): 4 M^2 N + 2 M^3."""
     m, n = min(m, n), max(m, n)
@@ -182,6 +219,7 @@ __all__ = [
     "kernel_dataflow_3d",
     "polar_step_oracle",
     "nominal_flops",
+    "CpuKernels",
     "error_stats",
     "ulp_bf16",
     "bf16_bits",

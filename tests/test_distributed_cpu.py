@@ -1,0 +1,162 @@
+"""CPU tests of the multi-GPU drivers (muon_fusion_ascend950_b200.distributed):
+partitioning, the column-sharded step on 2 gloo ranks against the
+single-process oracle, and detection of a rank that dies before the
+all-reduce.  The CUDA kernels are replaced by oracle.CpuKernels, passed
+explicitly as the backend (the product default is the C ABI)."""
+from __future__ import annotations
+
+import multiprocessing as mp
+import os
+import socket
+import sys
+import time
+from pathlib import Path
+
+import pytest
+import torch
+
+REPO = Path(__file__).resolve().parent.parent
+sys.path.insert(0, str(REPO))
+
+from muon_fusion_ascend950_b200.distributed import (  # noqa: E402
+    batch_sharded_steps,
+    column_range,
+    nominal_flops,
+    partition_items,
+)
+from oracle.polar_oracle import COEFFICIENTS, kernel_dataflow_3d, make_input  # noqa: E402
+
+
+def test_partition_covers_and_balances_config4():
+    # config 4: 128 attention matrices [4096,4096] + 96 FFN [4096,11008]
+    costs = [nominal_flops(4096, 4096)] * 128 + [nominal_flops(4096, 11008)] * 96
+    total = sum(costs)
+    for world in (1, 2, 4, 8):
+        parts = partition_items(costs, world)
+        flat = sorted(i for p in parts for i in p)
+        assert flat == list(range(len(costs)))
+        loads = [sum(costs[i] for i in p) for p in parts]
+        assert max(loads) - min(loads) <= max(costs)
+        assert max(loads) <= total / world * 1.01
+
+
+def test_partition_edge_cases():
+    assert partition_items([], 3) == [[], [], []]
+    assert partition_items([5.0], 2) == [[0], []]
+    with pytest.raises(ValueError):
+        partition_items([1.0], 0)
+
+
+@pytest.mark.parametrize("n,world", [(65536, 2), (65536, 8), (130, 2), (2050, 4), (8, 4)])
+def test_column_ranges(n, world):
+    ranges = [column_range(n, r, world) for r in range(world)]
+    covered = [c for r in ranges for c in r]
+    assert covered == list(range(n))
+    for r in ranges[:-1]:
+        assert r.start % 8 == 0 and (r.stop - r.start) % 8 == 0 or len(r) == 0
+
+
+def test_batch_sharded_steps_no_collective():
+    xs = [make_input((64, 96), seed=i) for i in range(5)]
+
+    def step(x, a, b, c):
+        return x * 2
+
+    got = {}
+    for rank in range(2):
+        got.update(batch_sharded_steps(xs, [(1, 1, 1)], rank, 2, step=step))
+    assert sorted(got) == list(range(5))
+    for i, y in got.items():
+        assert torch.equal(y, xs[i] * 2)
+
+
+# ------------------------------------------------------------ multi-process
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _column_worker(rank, world, port, m, n, steps, out_dir):
+    import datetime
+
+    import torch.distributed as dist
+
+    from muon_fusion_ascend950_b200.distributed import ColumnShardedPolar, column_range
+    from oracle.polar_oracle import COEFFICIENTS, CpuKernels, make_input
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=30))
+    x = make_input((m, n), seed=7)
+    cols = column_range(n, rank, world)
+    x_local = x[:, cols.start:cols.stop].contiguous()
+    driver = ColumnShardedPolar(m, "cpu", backend=CpuKernels())
+    y = driver.run(x_local, COEFFICIENTS[:steps])
+    torch.save(y, os.path.join(out_dir, f"y{rank}.pt"))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("m,n,steps", [(96, 200, 1), (130, 256, 2)])
+def test_column_sharded_two_ranks_match_single(tmp_path, m, n, steps):
+    ctx = mp.get_context("spawn")
+    port = _free_port()
+    procs = [ctx.Process(target=_column_worker, args=(r, 2, port, m, n, steps, str(tmp_path)))
+             for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    y = torch.cat([torch.load(tmp_path / f"y{r}.pt") for r in range(2)], dim=1)
+    x = make_input((m, n), seed=7)
+    ref = x.unsqueeze(0)
+    for a, b, c in COEFFICIENTS[:steps]:
+        ref = kernel_dataflow_3d(ref, a, b, c)
+    ref = ref.squeeze(0)
+    d = (y.to(torch.float64) - ref.to(torch.float64)).abs()
+    # only the fp32 order of the Gram sum differs from the single-process run
+    assert float(d.max()) <= 2e-2 * steps
+    assert float(d.mean()) <= 1e-4 * steps
+
+
+def _dying_worker(rank, world, port, out_dir):
+    import datetime
+
+    import torch.distributed as dist
+
+    from muon_fusion_ascend950_b200.distributed import ColumnShardedPolar
+    from oracle.polar_oracle import COEFFICIENTS, CpuKernels, make_input
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=5))
+    if rank == 1:
+        os._exit(3)  # this rank dies between steps, before its all-reduce
+    driver = ColumnShardedPolar(64, "cpu", backend=CpuKernels())
+    t0 = time.time()
+    try:
+        driver.step(make_input((64, 64), seed=1), *COEFFICIENTS[0])
+        status = "no error"
+    except Exception as exc:  # noqa: BLE001 - the failure is the thing tested
+        status = f"error after {time.time() - t0:.1f}s: {type(exc).__name__}"
+    with open(os.path.join(out_dir, "rank0.txt"), "w") as f:
+        f.write(status)
+    os._exit(0)
+
+
+def test_dead_rank_is_detected_by_the_collective(tmp_path):
+    ctx = mp.get_context("spawn")
+    port = _free_port()
+    procs = [ctx.Process(target=_dying_worker, args=(r, 2, port, str(tmp_path)))
+             for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    assert procs[1].exitcode == 3
+    status = (tmp_path / "rank0.txt").read_text()
+    assert status.startswith("error after"), status
