@@ -49,6 +49,8 @@ FALLBACK_TFLOPS = 1590.0
 
 
 def nominal_flops_per_matrix(m: int, n: int) -> int:
+    """4 M^2 N + 2 M^3 with M <= N (the operator transposes when M > N)."""
+    m, n = min(m, n), max(m, n)
     return 4 * m * m * n + 2 * m ** 3
 
 
@@ -316,11 +318,24 @@ def run_ours(args):
     value = world * flops_step * args.steps / (elapsed_ms * 1e-3) / 1e12
 
     # ---- per-kernel CUDA-event timing (same buffers, kernels timed alone)
-    mp = api.padded_rows(M)
+    # The C ABI takes what the operator hands it: M <= N (transposed) and a
+    # row stride that is a multiple of 8 (zero-padded columns).
+    def kernel_input(x):
+        if x.shape[-2] > x.shape[-1]:
+            x = x.mT.contiguous()
+        if x.shape[-1] % 8:
+            xp = x.new_zeros((*x.shape[:-1], -(-x.shape[-1] // 16) * 16))
+            xp[..., : x.shape[-1]] = x
+            x = xp
+        return x
+
+    kn = min(M, N)
+    xs_k = [kernel_input(x) for x in xs]
+    mp = api.padded_rows(kn)
     gram = torch.empty((BATCH, mp, mp), dtype=torch.bfloat16, device=device)
     poly = torch.empty_like(gram)
-    y = torch.empty_like(xs[0])
-    scratch = api.new_scratch(BATCH, M, N, device=device, stream=stream)
+    y = torch.empty_like(xs_k[0])
+    scratch = api.new_scratch(BATCH, kn, max(M, N), device=device, stream=stream)
     kernel_iters = max(50, min(args.steps, 1000))
 
     def time_kernel(fn):
@@ -336,18 +351,20 @@ def run_ours(args):
         e1.synchronize()
         return e0.elapsed_time(e1) / kernel_iters * 1e3  # us
 
+    nv = max(M, N)
     with torch.cuda.stream(stream):
-        api.gram(xs[0], gram, scratch=scratch, stream=stream)
+        api.gram(xs_k[0], gram, n=nv, scratch=scratch, stream=stream)
         api.poly(gram, poly, b, c, scratch=scratch, stream=stream)
     us = {
-        "gram": time_kernel(lambda i: api.gram(xs[i % ROTATION], gram, scratch=scratch,
+        "gram": time_kernel(lambda i: api.gram(xs_k[i % ROTATION], gram, n=nv, scratch=scratch,
                                                stream=stream)),
         "poly": time_kernel(lambda i: api.poly(gram, poly, b, c, scratch=scratch,
                                                stream=stream)),
-        "apply": time_kernel(lambda i: api.apply(poly, xs[i % ROTATION], y, a, stream=stream)),
+        "apply": time_kernel(lambda i: api.apply(poly, xs_k[i % ROTATION], y, a, n=nv,
+                                                 stream=stream)),
     }
-    kernel_flops = {"gram": BATCH * 2 * M * M * N, "poly": BATCH * 2 * M ** 3,
-                    "apply": BATCH * 2 * M * M * N}
+    kernel_flops = {"gram": BATCH * 2 * kn * kn * nv, "poly": BATCH * 2 * kn ** 3,
+                    "apply": BATCH * 2 * kn * kn * nv}
     dominant = max(us, key=us.get)
     peak, peak_kind = measured_peaks()
     achieved = kernel_flops[dominant] / (us[dominant] * 1e-6) / 1e12
