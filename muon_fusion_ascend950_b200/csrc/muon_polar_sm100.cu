@@ -504,6 +504,18 @@ constexpr int kPairN = 256;
 constexpr int kHalf = 128;
 constexpr int kChunkCols = 64;
 constexpr int kMaxSplits = 4;  // split-K items per tile, at most
+constexpr int kAtom = 64;  // bf16 elements per 128-byte swizzle row
+constexpr uint32_t kAtomBytes = kHalf * kAtom * 2;  // one [128 x 64] box, 16 KiB
+
+// K depth of one pipeline stage of a pair kernel (see PairCfg::kBK).
+template <int KIND>
+constexpr int pair_bk() {
+  return KIND == kGramBf16 ? 128 : 64;
+}
+template <int KIND>
+constexpr int64_t pair_k_blocks(int64_t k) {
+  return (k + pair_bk<KIND>() - 1) / pair_bk<KIND>();
+}
 
 template <int KIND>
 struct PairCfg {
@@ -515,25 +527,37 @@ struct PairCfg {
   static constexpr int kChunks = kPairN / kChunkCols;
   static constexpr uint32_t kOutChunkBytes = kHalf * kChunkCols * kElem;
   static constexpr uint32_t kMirChunkBytes = kSym ? kChunkCols * kHalf * kElem : 0;
+  // K depth of a pipeline stage.  TMA ingest into one SM grows with the
+  // bytes completed per mbarrier phase (measured on B200: ~100 GB/s at 32
+  // KiB, ~130-145 GB/s at 64 KiB), but a stage is only refilled after the
+  // MMAs release it, so deep stages need room for at least three.  The bf16
+  // Gram (single-buffered epilogue, 32 KiB) gets three 64 KiB stages (K =
+  // 128); the others keep four or five 32 KiB stages (K = 64), which measured
+  // faster for them.
+  static constexpr int kBK = pair_bk<KIND>();
   // Output regions: kAux kinds keep the whole 128 x 256 input tile (updated
-  // in place, one region per chunk); the Gram double-buffers (bf16) or
-  // single-buffers (fp32) its chunk regions.
-  static constexpr int kOutRegions = kAux ? kChunks : (kF32 ? 1 : 2);
-  static constexpr int kMirRegions = kSym ? (kF32 ? 1 : 2) : 0;
-  // Store groups that may still read shared memory when a chunk starts.
-  static constexpr int kPending = kF32 ? 0 : 1;
+  // in place, one region per chunk, never reused within a tile); the Gram
+  // single-buffers its chunk region.
+  static constexpr int kOutRegions = kAux ? kChunks : 1;
+  // The polynomial double-buffers its mirror chunk (it still fits four
+  // stages); the Gram single-buffers it.
+  static constexpr int kMirRegions = kSym ? (kAux ? 2 : 1) : 0;
+  // Store groups that may still read shared memory when a chunk starts: the
+  // region a chunk writes was last used by the chunk kMirRegions before it.
+  static constexpr int kPending = (kSym && kAux) ? 1 : 0;
   static constexpr bool kWaitPerChunk = kSym;
   static constexpr uint32_t kEpiBytes =
       kOutRegions * kOutChunkBytes + kMirRegions * kMirChunkBytes;
+  static constexpr uint32_t kAHalfBytes = kHalf * kBK * 2;
   static constexpr uint32_t kBHalfBytes = kHalf * kBK * 2;
-  static constexpr uint32_t kStageBytes = kABytes + kBHalfBytes;
+  static constexpr uint32_t kStageBytes = kAHalfBytes + kBHalfBytes;
   static constexpr uint32_t kFixedBytes = 1024 + kEpiBytes + 256;
   static constexpr int kStagesFit =
       static_cast<int>((232448u - kFixedBytes) / kStageBytes);
   static constexpr int kStages = kStagesFit > 8 ? 8 : kStagesFit;
   static constexpr uint32_t kSmemBytes = kFixedBytes + kStages * kStageBytes;
   static constexpr uint32_t kTmemCols = 2 * kPairN;
-  static_assert(kStages >= 3, "pipeline depth");
+  static_assert(kStages >= 2, "pipeline depth");
   static_assert(kSmemBytes <= 232448, "shared memory budget");
 };
 
@@ -633,7 +657,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* sOut = smem;
   uint8_t* sMir = sOut + Cfg::kOutRegions * Cfg::kOutChunkBytes;
   uint8_t* sA = smem + Cfg::kEpiBytes;
-  uint8_t* sB = sA + S * kABytes;
+  uint8_t* sB = sA + S * Cfg::kAHalfBytes;
   uint64_t* full = reinterpret_cast<uint64_t*>(sB + S * Cfg::kBHalfBytes);
   uint64_t* empty = full + S;
   uint64_t* tfull = empty + S;
@@ -702,17 +726,22 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * Cfg::kStageBytes);
           const uint32_t bar = map_to_cta(smem_addr(&full[s]), 0);
-          tma_load_3d_pair(sA + s * kABytes, &tmap_a, bar, kb * kBK, a_row, tc.b);
-          if constexpr (!kBmn) {
-            tma_load_3d_pair(sB + s * Cfg::kBHalfBytes, &tmap_b, bar, kb * kBK,
-                             tc.tn * kPairN + static_cast<int>(rank) * kHalf, tc.b);
-          } else {
+          const int b_row = tc.tn * kPairN + static_cast<int>(rank) * kHalf;
 #pragma unroll
-            for (int j = 0; j < kHalf / 64; ++j)
-              tma_load_3d_pair(sB + s * Cfg::kBHalfBytes + j * (64 * kBK * 2), &tmap_b,
-                               bar,
-                               tc.tn * kPairN + static_cast<int>(rank) * kHalf + j * 64,
-                               kb * kBK, tc.b);
+          for (int j = 0; j < Cfg::kBK / kAtom; ++j)
+            tma_load_3d_pair(sA + s * Cfg::kAHalfBytes + j * kAtomBytes, &tmap_a, bar,
+                             kb * Cfg::kBK + j * kAtom, a_row, tc.b);
+          if constexpr (!kBmn) {
+#pragma unroll
+            for (int j = 0; j < Cfg::kBK / kAtom; ++j)
+              tma_load_3d_pair(sB + s * Cfg::kBHalfBytes + j * kAtomBytes, &tmap_b, bar,
+                               kb * Cfg::kBK + j * kAtom, b_row, tc.b);
+          } else {
+            // MN-major B: one [Cfg::kBK k-rows x 64 n] box per 64-column chunk
+#pragma unroll
+            for (int j = 0; j < kHalf / kAtom; ++j)
+              tma_load_3d_pair(sB + s * Cfg::kBHalfBytes + j * (Cfg::kBK * 128), &tmap_b, bar,
+                               b_row + j * kAtom, kb * Cfg::kBK, tc.b);
           }
         }
       }
@@ -755,16 +784,21 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t a_base = smem_addr(sA + s * kABytes);
+          const uint32_t a_base = smem_addr(sA + s * Cfg::kAHalfBytes);
           const uint32_t b_base = smem_addr(sB + s * Cfg::kBHalfBytes);
 #pragma unroll
-          for (int k = 0; k < kBK / 16; ++k) {
-            const uint64_t ad = smem_desc_sw128(a_base + k * 32, 16, 1024);
+          for (int k = 0; k < Cfg::kBK / 16; ++k) {
+            // K-major: K step k lies in swizzle atom k/4 (16 KiB apart), 32
+            // bytes per step inside the atom's 128-byte rows.
+            const uint32_t koff = (k / 4) * kAtomBytes + (k % 4) * 32;
+            const uint64_t ad = smem_desc_sw128(a_base + koff, 16, 1024);
             uint64_t bd;
             if constexpr (kBmn) {
-              bd = smem_desc_sw128(b_base + k * 2048, kBK * 128, 1024);
+              // MN-major: 16 k-rows of 128 bytes per step; 64-column chunks
+              // are Cfg::kBK*128 bytes apart (leading offset).
+              bd = smem_desc_sw128(b_base + k * 2048, Cfg::kBK * 128, 1024);
             } else {
-              bd = smem_desc_sw128(b_base + k * 32, 16, 1024);
+              bd = smem_desc_sw128(b_base + koff, 16, 1024);
             }
             umma_bf16_pair(d_tmem, ad, bd, idesc, (kb > kb_begin || k > 0) ? 1u : 0u);
           }
@@ -1329,7 +1363,7 @@ int gram_impl(const void* x, void* gram, int64_t batch, int64_t m, int64_t n,
     p.tiles_n = static_cast<int32_t>(dp);
     p.tiles_per_batch = static_cast<int32_t>(tp);
     p.total_tiles = static_cast<int32_t>(tp * batch);
-    p.k_blocks = static_cast<int32_t>((n + kBK - 1) / kBK);
+    p.k_blocks = static_cast<int32_t>(pair_k_blocks<KIND>(n));
     plan_splits(p, scratch, scratch_bytes, pairs);
     return launch_pair<KIND>(st, 5 + KIND, pm, p, stream);
   }
@@ -1384,7 +1418,7 @@ int poly_impl(const void* gram, void* poly, int64_t batch, int64_t mp, float b,
     p.tiles_n = static_cast<int32_t>(dp);
     p.tiles_per_batch = static_cast<int32_t>(tp);
     p.total_tiles = static_cast<int32_t>(tp * batch);
-    p.k_blocks = static_cast<int32_t>(mp / kBK);
+    p.k_blocks = static_cast<int32_t>(pair_k_blocks<kPoly>(mp));
     p.coef_b = b;
     p.coef_c = c;
     plan_splits(p, scratch, scratch_bytes, pairs);
@@ -1454,7 +1488,7 @@ int apply_impl(const void* poly, const void* x, void* y, int64_t batch,
     rc = encode_square(&pm.a, poly, batch, mp, false, kHalf);
     if (rc != MUON_POLAR_OK) return rc;
     rc = encode_3d(&pm.b, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, x, n, m, batch,
-                   ldx, m * ldx, 64, kBK);
+                   ldx, m * ldx, 64, PairCfg<kApply>::kBK);
     if (rc != MUON_POLAR_OK) return rc;
     rc = encode_3d(&pm.aux, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, x, n, m, batch,
                    ldx, m * ldx, 64, kHalf);
@@ -1468,7 +1502,7 @@ int apply_impl(const void* poly, const void* x, void* y, int64_t batch,
     p.tiles_n = static_cast<int32_t>(tn);
     p.tiles_per_batch = static_cast<int32_t>(tm * tn);
     p.total_tiles = static_cast<int32_t>(tm * tn * batch);
-    p.k_blocks = static_cast<int32_t>((m + kBK - 1) / kBK);
+    p.k_blocks = static_cast<int32_t>(pair_k_blocks<kApply>(m));
     p.alpha = round_to_bf16(a);
     plan_no_splits(p);
     return launch_pair<kApply>(st, 5 + kApply, pm, p, stream);
@@ -1574,7 +1608,7 @@ int gram_static_scratch_impl(const void* x, void* gram, int64_t batch, int64_t m
   int pairs = 0;
   rc = pair_capacity<kGramBf16>(st, 5 + kGramBf16, &pairs);
   if (rc != MUON_POLAR_OK) return rc;
-  const int64_t k_blocks = (n + kBK - 1) / kBK;
+  const int64_t k_blocks = pair_k_blocks<kGramBf16>(n);
   // The same split plan as muon_polar_gram_sm100 on the CTA-pair path with
   // enough scratch; a plan that needs more than the static array is refused.
   const size_t need =
@@ -1710,8 +1744,10 @@ size_t muon_polar_scratch_bytes(int64_t batch, int64_t m, int64_t n) {
   const int64_t mp = padded_rows(m);
   const int64_t d = mp / kPairM;
   const int64_t tiles = d * (d + 1) / 2 * batch;
-  const int64_t kb_gram = (n + kBK - 1) / kBK;
-  const int64_t kb_poly = mp / kBK;
+  const int64_t kb_gram = pair_k_blocks<kGramF32>(n) > pair_k_blocks<kGramBf16>(n)
+                              ? pair_k_blocks<kGramF32>(n)
+                              : pair_k_blocks<kGramBf16>(n);
+  const int64_t kb_poly = pair_k_blocks<kPoly>(mp);
   const size_t g = split_scratch_bytes(tiles, choose_splits(tiles, kb_gram, pairs));
   const size_t q = split_scratch_bytes(tiles, choose_splits(tiles, kb_poly, pairs));
   return g > q ? g : q;
