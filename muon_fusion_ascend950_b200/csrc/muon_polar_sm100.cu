@@ -567,58 +567,67 @@ __device__ __forceinline__ uint32_t swz_box(int row, int byte) {
                                ((((byte >> 4) ^ (row & 7))) << 4) + (byte & 15));
 }
 
-// Epilogue of one 64-column chunk for tile row `row` of this CTA's band.
+__device__ __forceinline__ uint32_t bf162_bits(__nv_bfloat162 v) {
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+__device__ __forceinline__ __nv_bfloat162 bits_bf162(uint32_t u) {
+  return *reinterpret_cast<__nv_bfloat162*>(&u);
+}
+
+// Epilogue of 32 accumulator columns (half `h` of a 64-column chunk) for
+// band row `row`, with packed bf16x2 arithmetic where the reference's
+// dataflow is bf16 (kApply) and fp32 where it is fp32 (kPoly).
 template <int KIND>
-__device__ __forceinline__ void pair_epilogue_chunk(const EpiParams& p, uint32_t out,
-                                                    uint32_t mir, bool mirror,
-                                                    int row, const float (&v)[64]) {
+__device__ __forceinline__ void pair_epilogue_half(const EpiParams& p, uint32_t out,
+                                                   uint32_t mir, bool mirror, int row,
+                                                   int h, const float (&v)[32]) {
   using Cfg = PairCfg<KIND>;
   if constexpr (KIND == kGramF32) {
-    // out: 2 boxes [128 x 32 fp32]; mirror: 4 boxes [64 x 32 fp32]
+    // out: box h of [128 x 32 fp32]; mirror rows h*32.. of 4 boxes [64 x 32]
+    const uint32_t ob = out + h * (kHalf * 128);
 #pragma unroll
-    for (int u = 0; u < 16; ++u) {
-      const int col = 4 * u;
-      st_shared_v4(out + (col / 32) * (kHalf * 128) + swz_box(row, (col % 32) * 4),
-                   make_uint4(__float_as_uint(v[col]), __float_as_uint(v[col + 1]),
-                              __float_as_uint(v[col + 2]), __float_as_uint(v[col + 3])));
-    }
+    for (int u = 0; u < 8; ++u)
+      st_shared_v4(ob + swz_box(row, u * 16),
+                   make_uint4(__float_as_uint(v[4 * u]), __float_as_uint(v[4 * u + 1]),
+                              __float_as_uint(v[4 * u + 2]), __float_as_uint(v[4 * u + 3])));
     if (mirror) {
       const uint32_t mbase = mir + (row / 32) * (kChunkCols * 128);
 #pragma unroll
-      for (int j = 0; j < 64; ++j)
-        st_shared_f32(mbase + swz_box(j, (row % 32) * 4), v[j]);
+      for (int j = 0; j < 32; ++j)
+        st_shared_f32(mbase + swz_box(h * 32 + j, (row % 32) * 4), v[j]);
     }
   } else {
-    // out: 1 box [128 x 64 bf16]; mirror: 2 boxes [64 x 64 bf16]
-    uint32_t w[32];
+    // out: columns h*32.. of one box [128 x 64 bf16] = 4 16-byte units
+    uint32_t w[16];
 #pragma unroll
-    for (int u = 0; u < 8; ++u) {
-      const uint32_t addr = out + swz_box(row, u * 16);
+    for (int u = 0; u < 4; ++u) {
+      const uint32_t addr = out + swz_box(row, h * 64 + u * 16);
       if constexpr (KIND == kGramBf16) {
 #pragma unroll
         for (int e = 0; e < 4; ++e)
-          w[4 * u + e] = pack_bf16x2(v[8 * u + 2 * e], v[8 * u + 2 * e + 1]);
+          w[4 * u + e] = bf162_bits(__floats2bfloat162_rn(v[8 * u + 2 * e], v[8 * u + 2 * e + 1]));
       } else {
-        const uint4 q = ld_shared_v4(addr);
-        const uint32_t in[4] = {q.x, q.y, q.z, q.w};
+        const uint4 qv = ld_shared_v4(addr);
+        const uint32_t in[4] = {qv.x, qv.y, qv.z, qv.w};
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const int j = 8 * u + 2 * e;
-          const float lo = bf16_bits_to_float(in[e] & 0xFFFFu);
-          const float hi = bf16_bits_to_float(in[e] >> 16);
           if constexpr (KIND == kPoly) {
             // P = bf16( fl(b*A) + fl(c*acc) ), no fused multiply-add
             // (asc:929-940).
-            w[4 * u + e] = pack_bf16x2(
-                __fadd_rn(__fmul_rn(p.coef_b, lo), __fmul_rn(p.coef_c, v[j])),
-                __fadd_rn(__fmul_rn(p.coef_b, hi), __fmul_rn(p.coef_c, v[j + 1])));
+            const float2 a2 = __bfloat1622float2(bits_bf162(in[e]));
+            w[4 * u + e] = bf162_bits(__floats2bfloat162_rn(
+                __fadd_rn(__fmul_rn(p.coef_b, a2.x), __fmul_rn(p.coef_c, v[j])),
+                __fadd_rn(__fmul_rn(p.coef_b, a2.y), __fmul_rn(p.coef_c, v[j + 1]))));
           } else {
-            // Y = bf16( bf16(T) + bf16(alpha*x) ) (asc:1472-1476).
-            const float ax_lo = bf16_bits_to_float(float_to_bf16_bits(p.alpha * lo));
-            const float ax_hi = bf16_bits_to_float(float_to_bf16_bits(p.alpha * hi));
-            const float t_lo = bf16_bits_to_float(float_to_bf16_bits(v[j]));
-            const float t_hi = bf16_bits_to_float(float_to_bf16_bits(v[j + 1]));
-            w[4 * u + e] = pack_bf16x2(__fadd_rn(t_lo, ax_lo), __fadd_rn(t_hi, ax_hi));
+            // Y = bf16( bf16(T) + bf16(alpha*x) ) (asc:1472-1476): bf16 x bf16
+            // is exact before its single rounding, and the bf16 add rounds
+            // the exact sum once.  The _rn forms keep the multiply and the
+            // add separately rounded (no contraction into one fma).
+            const __nv_bfloat162 alpha2 = __float2bfloat162_rn(p.alpha);
+            const __nv_bfloat162 ax = __hmul2_rn(bits_bf162(in[e]), alpha2);
+            const __nv_bfloat162 t = __floats2bfloat162_rn(v[j], v[j + 1]);
+            w[4 * u + e] = bf162_bits(__hadd2_rn(t, ax));
           }
         }
       }
@@ -628,18 +637,24 @@ __device__ __forceinline__ void pair_epilogue_chunk(const EpiParams& p, uint32_t
       if (mirror) {
         const uint32_t mbase = mir + (row / 64) * (kChunkCols * 128);
 #pragma unroll
-        for (int j = 0; j < 64; ++j) {
-          const uint16_t h = static_cast<uint16_t>((j & 1) ? (w[j >> 1] >> 16)
-                                                           : (w[j >> 1] & 0xFFFFu));
-          st_shared_u16(mbase + swz_box(j, (row % 64) * 2), h);
+        for (int j = 0; j < 32; ++j) {
+          const uint16_t hv = static_cast<uint16_t>((j & 1) ? (w[j >> 1] >> 16)
+                                                            : (w[j >> 1] & 0xFFFFu));
+          st_shared_u16(mbase + swz_box(h * 32 + j, (row % 64) * 2), hv);
         }
       }
     }
   }
 }
 
+// Threads of the pair kernel: warp 0 TMA producer, warp 1 MMA issuer and
+// tensor-memory owner, warps 2..9 epilogue (two per tensor-memory lane
+// quarter, each taking 32 of a chunk's 64 columns).
+constexpr int kPairThreads = 320;
+constexpr int kPairEpiThreads = 256;
+
 template <int KIND>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kPairThreads, 1)
     polar_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
                       const __grid_constant__ CUtensorMap tmap_b,
                       const __grid_constant__ CUtensorMap tmap_aux,
@@ -681,7 +696,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], 8);  // 4 epilogue warps in each CTA of the pair
+      mbar_init(&tempty[a], 16);  // 8 epilogue warps in each CTA of the pair
     }
     mbar_init(drain, 1);
     mbar_init(aux_full, 1);
@@ -815,8 +830,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!mbar_wait_bounded(drain, 0)) atomicOr(&g_watchdog, MUON_POLAR_WATCHDOG_DRAIN);
     }
   } else {
-    // ---------------- epilogue warps 2..5 (both CTAs; one band row each)
-    const int q = warp & 3;
+    // ---------------- epilogue warps 2..9 (both CTAs)
+    const int q = warp & 3;          // tensor-memory lane quarter of this warp
+    const int hc = (warp - 2) >> 2;  // which 32 columns of each 64-column chunk
     const int row = q * 32 + lane;
     const uint32_t out_base = smem_addr(sOut);
     const uint32_t mir_base = smem_addr(sMir);
@@ -889,22 +905,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                        row;
 #pragma unroll 1
         for (int c = 0; c < Cfg::kChunks; ++c) {
-          uint32_t r0[32], r1[32];
-          tmem_ld_32x32b_x32(t_row + c * kChunkCols, r0);
-          tmem_ld_32x32b_x32(t_row + c * kChunkCols + 32, r1);
+          uint32_t r0[32];
+          tmem_ld_32x32b_x32(t_row + c * kChunkCols + hc * 32, r0);
           tmem_wait_ld();
 #pragma unroll
-          for (int u = 0; u < 8; ++u) {
-            __stcg(mine + (c * 16 + u) * kHalf,
+          for (int u = 0; u < 8; ++u)
+            __stcg(mine + (c * 16 + hc * 8 + u) * kHalf,
                    make_float4(__uint_as_float(r0[4 * u]), __uint_as_float(r0[4 * u + 1]),
                                __uint_as_float(r0[4 * u + 2]), __uint_as_float(r0[4 * u + 3])));
-            __stcg(mine + (c * 16 + 8 + u) * kHalf,
-                   make_float4(__uint_as_float(r1[4 * u]), __uint_as_float(r1[4 * u + 1]),
-                               __uint_as_float(r1[4 * u + 2]), __uint_as_float(r1[4 * u + 3])));
-          }
         }
         __threadfence();
-        named_barrier(1, 128);
+        named_barrier(1, kPairEpiThreads);
         if (leader) {
           uint32_t* counter = p.counters + static_cast<size_t>(tile) * 2 + rank;
           const uint32_t arrived = atomicAdd(counter, 1u) + 1u;
@@ -913,7 +924,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           __threadfence();
           *last_flag = last ? 1u : 0u;
         }
-        named_barrier(1, 128);
+        named_barrier(1, kPairEpiThreads);
         reduce = *last_flag != 0u;
         if (!reduce) {
           release_accumulator(acc);
@@ -936,48 +947,41 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t mir = mir_base + rm * Cfg::kMirChunkBytes;
         if constexpr (Cfg::kWaitPerChunk) {
           if (leader) bulk_wait_group_read<Cfg::kPending>();
-          named_barrier(1, 128);
+          named_barrier(1, kPairEpiThreads);
         }
-        uint32_t r0[32], r1[32];
-        tmem_ld_32x32b_x32(t_row + c * kChunkCols, r0);
-        tmem_ld_32x32b_x32(t_row + c * kChunkCols + 32, r1);
+        uint32_t r0[32];
+        tmem_ld_32x32b_x32(t_row + c * kChunkCols + hc * 32, r0);
         tmem_wait_ld();
         if (c == Cfg::kChunks - 1) release_accumulator(acc);
-        float v[64];
+        float v[32];
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          v[j] = __uint_as_float(r0[j]);
-          v[32 + j] = __uint_as_float(r1[j]);
-        }
+        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r0[j]);
         if (reduce) {
           // v <- sum over splits i = 0..splits-1, in that order, of the
-          // split's partial (this split's own from tensor memory).  All
-          // splits' loads of a half chunk are issued before the adds.
+          // split's partial (this split's own from tensor memory); all
+          // splits' loads of a quarter chunk are issued before the adds.
           const float4* band0 = reinterpret_cast<const float4*>(
                                     p.partial + static_cast<size_t>(tile) * p.splits * 2 *
                                                     (kHalf * kPairN)) +
                                 static_cast<size_t>(rank) * (kHalf * kPairN / 4) + row;
           const size_t split_stride = 2 * (kHalf * kPairN / 4);  // float4 per split item
 #pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            float4 parts[kMaxSplits][8];
+          for (int g = 0; g < 2; ++g) {
+            float4 parts[kMaxSplits][4];
 #pragma unroll
             for (int i = 0; i < kMaxSplits; ++i) {
-              if (i < p.splits && i != split) {
 #pragma unroll
-                for (int u = 0; u < 8; ++u)
+              for (int u = 0; u < 4; ++u) {
+                const int j = (g * 4 + u) * 4;
+                if (i < p.splits && i != split)
                   parts[i][u] = __ldcg(band0 + i * split_stride +
-                                       (c * 16 + h * 8 + u) * kHalf);
-              } else {
-#pragma unroll
-                for (int u = 0; u < 8; ++u) {
-                  const int j = (h * 8 + u) * 4;
+                                       (c * 16 + hc * 8 + g * 4 + u) * kHalf);
+                else
                   parts[i][u] = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-                }
               }
             }
 #pragma unroll
-            for (int u = 0; u < 8; ++u) {
+            for (int u = 0; u < 4; ++u) {
               float4 acc4 = parts[0][u];
 #pragma unroll
               for (int i = 1; i < kMaxSplits; ++i) {
@@ -988,7 +992,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                   acc4.w = __fadd_rn(acc4.w, parts[i][u].w);
                 }
               }
-              const int j = (h * 8 + u) * 4;
+              const int j = (g * 4 + u) * 4;
               v[j] = acc4.x;
               v[j + 1] = acc4.y;
               v[j + 2] = acc4.z;
@@ -996,9 +1000,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
         }
-        pair_epilogue_chunk<KIND>(p, out, mir, mirror, row, v);
+        pair_epilogue_half<KIND>(p, out, mir, mirror, row, hc, v);
         fence_proxy_async_smem();
-        named_barrier(1, 128);
+        named_barrier(1, kPairEpiThreads);
         if (leader) {
           const uint8_t* so = sOut + ro * Cfg::kOutChunkBytes;
           const uint8_t* sm = sMir + rm * Cfg::kMirChunkBytes;
@@ -1256,7 +1260,7 @@ int pair_capacity(DeviceState* st, int instance, int* capacity) {
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * (st->sms / 2), 1, 1);
-  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.blockDim = dim3(kPairThreads, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -1288,7 +1292,7 @@ int launch_pair(DeviceState* st, int instance, const PairMaps& maps,
   const int pairs = p.total_items < max_pairs ? p.total_items : max_pairs;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * pairs, 1, 1);
-  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.blockDim = dim3(kPairThreads, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[2];

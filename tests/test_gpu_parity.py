@@ -269,3 +269,27 @@ def test_config3_five_step_loop(op, cuda_device):
     torch.testing.assert_close(y.float(), y_ref.float(), rtol=6e-2, atol=6e-2)
     y32 = reference_formula(x.float(), COEFFICIENTS)
     assert error_stats(y, y32)["rel_fro"] <= 5e-2
+
+
+@pytest.mark.parametrize("shape", [(1, 128, 256), (2, 150, 2064), (8, 512, 2048)])
+def test_kernel_paths_agree_bitwise(api, cuda_device, shape, mode_policy):
+    """The single-CTA and CTA-pair kernels accumulate each output in the same
+    K order and apply the same epilogue arithmetic, so they give identical
+    bits.  (Regression guard: a multiply and an add that the reference rounds
+    separately must not be contracted into one fused multiply-add.)"""
+    bsz, m, n = shape
+    x = make_input(shape, seed=6).to(cuda_device)
+    mp = api.padded_rows(m)
+    outs = {}
+    for mode in ("single", "pair"):
+        mode_policy(mode)
+        gram = torch.empty((bsz, mp, mp), dtype=torch.bfloat16, device=cuda_device)
+        poly = torch.empty_like(gram)
+        y = torch.empty_like(x)
+        api.gram(x, gram)
+        api.poly(gram, poly, B1, C1)
+        api.apply(poly, x, y, A1)
+        torch.cuda.synchronize()
+        outs[mode] = (gram.cpu(), poly.cpu(), y.cpu())
+    for a, b, what in zip(outs["single"], outs["pair"], ("gram", "poly", "apply")):
+        assert torch.equal(a.view(torch.int16), b.view(torch.int16)), what
