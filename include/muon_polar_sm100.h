@@ -61,6 +61,7 @@ extern "C" {
 #define MUON_POLAR_WATCHDOG_MMA 0x2u
 #define MUON_POLAR_WATCHDOG_EPILOGUE 0x4u
 #define MUON_POLAR_WATCHDOG_DRAIN 0x8u
+#define MUON_POLAR_WATCHDOG_DEPENDENCY 0x10u
 
 /* Library version of this ABI (MUON_POLAR_ABI_VERSION). */
 int muon_polar_abi_version(void);
@@ -79,14 +80,17 @@ int64_t muon_polar_padded_rows(int64_t m);
  * at::empty calls of csrc/muon_polar_step_binding.cpp:646,657. */
 size_t muon_polar_workspace_bytes(int64_t batch, int64_t m);
 
-/* Split-K scratch.  When a problem has fewer 256 x 256 output tiles than
+/* Scratch.  Its first 1024 bytes are counters that must be zero before the
+ * first call (muon_polar_scratch_init) and that every call leaves at zero:
+ * the fused step keeps its per-matrix dependency counts there, split-K its
+ * arrival counts.  muon_polar_scratch_bytes() is at least 1024.
+ *
+ * Split-K.  When a problem has fewer 256 x 256 output tiles than
  * the device has SM pairs (small M), kernels 1 and 2 cut each tile's K range
  * into up to 4 work items and reduce the fp32 partials -- always in the same
  * split order, so results are deterministic.  The reduction needs scratch
- * memory: muon_polar_scratch_bytes() bytes (0 when the problem does not
- * split on the current device).  Its first 1024 bytes are arrival counters
- * that must be zero before the first call (muon_polar_scratch_init); every
- * call leaves them zero again.  Calls that share one scratch buffer must be
+ * memory after the counters: muon_polar_scratch_bytes() covers it on the
+ * current device.  Calls that share one scratch buffer must be
  * ordered (same stream).  Passing scratch = NULL (or too few bytes) turns
  * split-K off; results then come from the unsplit K order. */
 size_t muon_polar_scratch_bytes(int64_t batch, int64_t m, int64_t n);
@@ -199,6 +203,17 @@ int muon_polar_read_device_status(int device, uint32_t* flags, int clear);
  * 2).  Every policy computes the same mathematical result; the fp32
  * accumulation order (and so the last bit) may differ between them. */
 int muon_polar_set_kernel_policy(int policy);
+
+/* How muon_polar_step_sm100 runs a step, process-wide; returns the previous
+ * mode (or MUON_POLAR_ERR_INVALID_ARGUMENT).
+ *   0  default: the three kernels (the fused launch has not yet measured
+ *      faster on any shape);
+ *   1  one fused persistent launch for all three stages, with per-matrix
+ *      dependencies tracked in the scratch counter area (needs scratch);
+ *   2  always three kernels.
+ * Initial value from MUON_POLAR_FUSED (1 -> 1, 0 -> 2).  Results are the
+ * same in every mode (identical bits). */
+int muon_polar_set_step_mode(int mode);
 
 /* Number of 2-CTA clusters (tcgen05 CTA pairs) of the Gram kernel the
  * current device runs at once; the persistent grids are this many pairs. */

@@ -45,6 +45,7 @@ SIGNATURES = {
                                                      ctypes.POINTER(ctypes.c_uint32),
                                                      ctypes.c_int]),
     "muon_polar_set_kernel_policy": (ctypes.c_int, [ctypes.c_int]),
+    "muon_polar_set_step_mode": (ctypes.c_int, [ctypes.c_int]),
     "muon_polar_device_pairs": (ctypes.c_int, [ctypes.POINTER(ctypes.c_int)]),
     "muon_polar_launch_count": (ctypes.c_uint64, []),
 }
@@ -126,6 +127,14 @@ class CAPI:
         prev = int(self.lib.muon_polar_set_kernel_policy(int(policy)))
         if prev < 0:
             raise MuonPolarError("muon_polar_set_kernel_policy", prev, self.status_string(prev))
+        return prev
+
+    def set_step_mode(self, mode: int) -> int:
+        """0 = by size, 1 = always one fused launch, 2 = always three kernels;
+        returns the previous mode."""
+        prev = int(self.lib.muon_polar_set_step_mode(int(mode)))
+        if prev < 0:
+            raise MuonPolarError("muon_polar_set_step_mode", prev, self.status_string(prev))
         return prev
 
     def device_pairs(self) -> int:

@@ -1043,6 +1043,406 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   }
 }
 
+// ============================================================ fused step
+// One launch for a whole Polar Express step on CTA pairs.  The work items of
+// the step -- Gram tiles of every matrix, then polynomial tiles, then apply
+// tiles -- are dealt round-robin to the co-resident pairs; an item waits
+// (bounded) until the items it reads are complete:
+//   polynomial tile of matrix b  <- every Gram tile of b
+//   apply tile of matrix b       <- every polynomial tile of b
+// Completion is counted per matrix in scratch (one increment per CTA band
+// and tile, released after the band's TMA stores have completed; acquired
+// with a proxy fence before the TMA loads of the dependent item).  Every
+// dependency has a lower item index than its dependent and items of a pair
+// run in index order, so the wait always ends.  The last CTA to exit resets
+// the counters, so each launch starts from zero.  Phases of different
+// matrices overlap and the three launch/fill/drain overheads become one.
+enum FusedKind : int { kFGram = 0, kFPoly = 1, kFApply = 2 };
+
+struct FusedParams {
+  int32_t batch;
+  int32_t d;          // Mp / 256
+  int32_t sym_tiles;  // d (d + 1) / 2 per matrix
+  int32_t apply_tn;   // ceil(n / 256)
+  int32_t n_gram;     // batch * sym_tiles
+  int32_t n_poly;     // batch * sym_tiles
+  int32_t total;      // n_gram + n_poly + batch * d * apply_tn
+  int32_t kb_gram;    // 64-deep k-blocks of each kind
+  int32_t kb_poly;
+  int32_t kb_apply;
+  float coef_b;
+  float coef_c;
+  float alpha;        // a rounded to bf16
+  uint32_t* counters; // [0, batch): Gram done; [batch, 2 batch): poly done; [2 batch]: exits
+};
+
+struct FusedMaps {
+  CUtensorMap x_k;   // X, box {64, 128}: Gram operands, apply epilogue tile
+  CUtensorMap x_mn;  // X, box {64, 64}: apply B operand (MN-major)
+  CUtensorMap a128;  // A, box {64, 128}: Gram output, poly operands and tile
+  CUtensorMap a64;   // A, box {64, 64}: Gram mirror
+  CUtensorMap p128;  // P, box {64, 128}: poly output, apply A operand
+  CUtensorMap p64;   // P, box {64, 64}: poly mirror
+  CUtensorMap y128;  // Y, box {64, 128}: apply output
+};
+
+struct FusedItem {
+  int kind, b, tm, tn, k_blocks;
+};
+
+__device__ __forceinline__ FusedItem fused_item(int w, const FusedParams& p) {
+  FusedItem it;
+  TileCoord tc;
+  if (w < p.n_gram) {
+    it.kind = kFGram;
+    it.k_blocks = p.kb_gram;
+    tc = decode_tile(w, true, p.d, p.d, p.sym_tiles);
+  } else if (w < p.n_gram + p.n_poly) {
+    it.kind = kFPoly;
+    it.k_blocks = p.kb_poly;
+    tc = decode_tile(w - p.n_gram, true, p.d, p.d, p.sym_tiles);
+  } else {
+    it.kind = kFApply;
+    it.k_blocks = p.kb_apply;
+    tc = decode_tile(w - p.n_gram - p.n_poly, false, p.d, p.apply_tn, p.d * p.apply_tn);
+  }
+  it.b = tc.b;
+  it.tm = tc.tm;
+  it.tn = tc.tn;
+  return it;
+}
+
+// The item's inputs are complete (bounded wait; false on timeout).
+__device__ __forceinline__ bool fused_wait_inputs(const FusedItem& it, const FusedParams& p) {
+  bool ok = true;
+  if (it.kind == kFPoly)
+    ok = wait_counter_bounded(p.counters + it.b, 2u * p.sym_tiles);
+  else if (it.kind == kFApply)
+    ok = wait_counter_bounded(p.counters + p.batch + it.b, 2u * p.sym_tiles);
+  fence_proxy_async_global();
+  return ok;
+}
+
+// Smem plan of the fused kernel: 4 output / epilogue-input regions of
+// [128 x 64] bf16, 2 mirror regions of [64 x 128] bf16, 4 stages of 32 KiB.
+struct FusedCfg {
+  static constexpr int kChunks = kPairN / kChunkCols;
+  static constexpr uint32_t kRegionBytes = kHalf * kChunkCols * 2;      // 16 KiB
+  static constexpr uint32_t kEpiBytes = 4 * kRegionBytes + 2 * kRegionBytes;
+  static constexpr uint32_t kAHalfBytes = kHalf * kAtom * 2;
+  static constexpr uint32_t kBHalfBytes = kHalf * kAtom * 2;
+  static constexpr uint32_t kStageBytes = kAHalfBytes + kBHalfBytes;    // 32 KiB
+  static constexpr uint32_t kFixedBytes = 1024 + kEpiBytes + 256;
+  static constexpr int kStages = static_cast<int>((232448u - kFixedBytes) / kStageBytes);
+  static constexpr uint32_t kSmemBytes = kFixedBytes + kStages * kStageBytes;
+  static constexpr uint32_t kTmemCols = 2 * kPairN;
+  static_assert(kStages >= 3, "pipeline depth");
+};
+
+__global__ void __launch_bounds__(kPairThreads, 1)
+    polar_fused_kernel(const __grid_constant__ FusedMaps maps, const FusedParams p) {
+  using Cfg = FusedCfg;
+  constexpr int S = Cfg::kStages;
+
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_addr(smem_raw);
+  uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
+  uint8_t* sOut = smem;
+  uint8_t* sMir = sOut + 4 * Cfg::kRegionBytes;
+  uint8_t* sA = smem + Cfg::kEpiBytes;
+  uint8_t* sB = sA + S * Cfg::kAHalfBytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + S * Cfg::kBHalfBytes);
+  uint64_t* empty = full + S;
+  uint64_t* tfull = empty + S;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint64_t* aux_full = drain + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(aux_full + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_cta_rank();
+  const int cluster = static_cast<int>(blockIdx.x >> 1);
+  const int nclusters = static_cast<int>(gridDim.x >> 1);
+  constexpr int kEpiLeader = 64;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 16);
+    }
+    mbar_init(drain, 1);
+    mbar_init(aux_full, 1);
+    fence_mbar_init();
+    prefetch_tensor_map(&maps.x_k);
+    prefetch_tensor_map(&maps.x_mn);
+    prefetch_tensor_map(&maps.a128);
+    prefetch_tensor_map(&maps.a64);
+    prefetch_tensor_map(&maps.p128);
+    prefetch_tensor_map(&maps.p64);
+    prefetch_tensor_map(&maps.y128);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, Cfg::kTmemCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  grid_dependency_wait();
+  grid_launch_dependents();
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer (both CTAs)
+      uint32_t it = 0;
+      bool ok = true;
+      for (int w = cluster; ok && w < p.total; w += nclusters) {
+        const FusedItem item = fused_item(w, p);
+        if (!fused_wait_inputs(item, p)) {
+          atomicOr(&g_watchdog, MUON_POLAR_WATCHDOG_DEPENDENCY);
+          ok = false;
+          break;
+        }
+        const int a_row = item.tm * kPairM + static_cast<int>(rank) * kHalf;
+        const int b_row = item.tn * kPairN + static_cast<int>(rank) * kHalf;
+        const CUtensorMap* ma = item.kind == kFGram ? &maps.x_k
+                                : item.kind == kFPoly ? &maps.a128 : &maps.p128;
+        for (int kb = 0; kb < item.k_blocks; ++kb, ++it) {
+          const uint32_t s = it % S;
+          const uint32_t ph = (it / S) & 1u;
+          if (!mbar_wait_bounded(&empty[s], ph ^ 1u)) {
+            ok = false;
+            break;
+          }
+          if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * Cfg::kStageBytes);
+          const uint32_t bar = map_to_cta(smem_addr(&full[s]), 0);
+          tma_load_3d_pair(sA + s * Cfg::kAHalfBytes, ma, bar, kb * kAtom, a_row, item.b);
+          if (item.kind != kFApply) {
+            tma_load_3d_pair(sB + s * Cfg::kBHalfBytes, ma, bar, kb * kAtom, b_row, item.b);
+          } else {
+#pragma unroll
+            for (int j = 0; j < kHalf / kAtom; ++j)
+              tma_load_3d_pair(sB + s * Cfg::kBHalfBytes + j * (kAtom * 128), &maps.x_mn, bar,
+                               b_row + j * kAtom, kb * kAtom, item.b);
+          }
+        }
+      }
+      if (!ok) atomicOr(&g_watchdog, MUON_POLAR_WATCHDOG_PRODUCER);
+      if (rank == 0) {
+        const uint32_t inflight = it < static_cast<uint32_t>(S) ? it : S;
+        for (uint32_t i = it - inflight; i < it; ++i) {
+          if (!mbar_wait_bounded(&full[i % S], (i / S) & 1u)) {
+            atomicOr(&g_watchdog, MUON_POLAR_WATCHDOG_DRAIN);
+            break;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && rank == 0) {
+      // ---------------- tcgen05 MMA issuer (leader CTA only)
+      constexpr uint32_t idesc_k = idesc_bf16_f32(kPairN, 0u, kPairM);
+      constexpr uint32_t idesc_mn = idesc_bf16_f32(kPairN, 1u, kPairM);
+      uint32_t it = 0;
+      uint32_t t = 0;
+      bool ok = true;
+      for (int w = cluster; ok && w < p.total; w += nclusters, ++t) {
+        const FusedItem item = fused_item(w, p);
+        const bool bmn = item.kind == kFApply;
+        const uint32_t acc = t & 1u;
+        const uint32_t uph = (t >> 1) & 1u;
+        if (!mbar_wait_bounded(&tempty[acc], uph ^ 1u)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * kPairN;
+        for (int kb = 0; kb < item.k_blocks; ++kb, ++it) {
+          const uint32_t s = it % S;
+          const uint32_t ph = (it / S) & 1u;
+          if (!mbar_wait_bounded(&full[s], ph)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_base = smem_addr(sA + s * Cfg::kAHalfBytes);
+          const uint32_t b_base = smem_addr(sB + s * Cfg::kBHalfBytes);
+#pragma unroll
+          for (int k = 0; k < kAtom / 16; ++k) {
+            const uint64_t ad = smem_desc_sw128(a_base + k * 32, 16, 1024);
+            const uint64_t bd = bmn ? smem_desc_sw128(b_base + k * 2048, kAtom * 128, 1024)
+                                    : smem_desc_sw128(b_base + k * 32, 16, 1024);
+            umma_bf16_pair(d_tmem, ad, bd, bmn ? idesc_mn : idesc_k,
+                           (kb > 0 || k > 0) ? 1u : 0u);
+          }
+          umma_commit_pair(map_to_cta(smem_addr(&empty[s]), 0));
+          umma_commit_pair(map_to_cta(smem_addr(&empty[s]), 1));
+        }
+        if (!ok) break;
+        umma_commit_pair(map_to_cta(smem_addr(&tfull[acc]), 0));
+        umma_commit_pair(map_to_cta(smem_addr(&tfull[acc]), 1));
+      }
+      if (!ok) atomicOr(&g_watchdog, MUON_POLAR_WATCHDOG_MMA);
+      umma_commit_pair(map_to_cta(smem_addr(drain), 0));
+      if (!mbar_wait_bounded(drain, 0)) atomicOr(&g_watchdog, MUON_POLAR_WATCHDOG_DRAIN);
+    }
+  } else {
+    // ---------------- epilogue warps 2..9 (both CTAs)
+    const int q = warp & 3;
+    const int hc = (warp - 2) >> 2;
+    const int row = q * 32 + lane;
+    const uint32_t out_base = smem_addr(sOut);
+    const uint32_t mir_base = smem_addr(sMir);
+    const bool leader = threadIdx.x == kEpiLeader;
+    const uint32_t tempty_leader0 = map_to_cta(smem_addr(&tempty[0]), 0);
+    const uint32_t tempty_leader1 = map_to_cta(smem_addr(&tempty[1]), 0);
+    EpiParams ep = {};
+    ep.coef_b = p.coef_b;
+    ep.coef_c = p.coef_c;
+    ep.alpha = p.alpha;
+    bool aux_inflight = false;
+    bool dep_failed = false;
+    // Leader: load the epilogue input tile of item w (poly: A; apply: X).
+    auto load_aux = [&](int w) {
+      const FusedItem item = fused_item(w, p);
+      if (item.kind == kFGram) return;
+      if (!fused_wait_inputs(item, p)) {
+        atomicOr(&g_watchdog, MUON_POLAR_WATCHDOG_DEPENDENCY);
+        dep_failed = true;
+      }
+      const CUtensorMap* m = item.kind == kFPoly ? &maps.a128 : &maps.x_k;
+      mbar_arrive_expect_tx(aux_full, 4 * Cfg::kRegionBytes);
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+        tma_load_3d(sOut + c * Cfg::kRegionBytes, m, aux_full, item.tn * kPairN + c * kChunkCols,
+                    item.tm * kPairM + static_cast<int>(rank) * kHalf, item.b);
+      aux_inflight = true;
+    };
+    auto release_accumulator = [&](uint32_t acc) {
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        if (rank == 0)
+          mbar_arrive(&tempty[acc]);
+        else
+          mbar_arrive_cluster(acc ? tempty_leader1 : tempty_leader0);
+      }
+    };
+    if (leader && cluster < p.total) load_aux(cluster);
+    uint32_t t = 0;
+    uint32_t aux_uses = 0;  // completed aux_full phases
+    for (int w = cluster; w < p.total; w += nclusters, ++t) {
+      const FusedItem item = fused_item(w, p);
+      const bool has_aux = item.kind != kFGram;
+      const uint32_t acc = t & 1u;
+      const uint32_t uph = (t >> 1) & 1u;
+      int ok = 1;
+      if (lane == 0) {
+        ok = mbar_wait_bounded(&tfull[acc], uph) ? 1 : 0;
+        if (has_aux && ok) {
+          ok = mbar_wait_bounded(aux_full, aux_uses & 1u) ? 1 : 0;
+          if (ok) aux_inflight = false;
+        }
+      }
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) {
+        if (lane == 0) atomicOr(&g_watchdog, MUON_POLAR_WATCHDOG_EPILOGUE);
+        break;
+      }
+      if (has_aux) {
+        (void)mbar_try_wait(aux_full, aux_uses & 1u);
+        ++aux_uses;
+      }
+      tc_fence_after();
+      const bool mirror = item.kind != kFApply && item.tm != item.tn;
+      const int row0 = item.tm * kPairM + static_cast<int>(rank) * kHalf;
+      const int col0 = item.tn * kPairN;
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * kPairN;
+      const CUtensorMap* m_out = item.kind == kFGram ? &maps.a128
+                                 : item.kind == kFPoly ? &maps.p128 : &maps.y128;
+      const CUtensorMap* m_mir = item.kind == kFGram ? &maps.a64 : &maps.p64;
+#pragma unroll 1
+      for (int c = 0; c < Cfg::kChunks; ++c) {
+        const uint32_t out = out_base + c * Cfg::kRegionBytes;
+        const uint32_t mir = mir_base + (c & 1) * Cfg::kRegionBytes;
+        if (item.kind != kFApply) {
+          if (leader) bulk_wait_group_read<1>();
+          named_barrier(1, kPairEpiThreads);
+        }
+        uint32_t r0[32];
+        tmem_ld_32x32b_x32(t_row + c * kChunkCols + hc * 32, r0);
+        tmem_wait_ld();
+        if (c == Cfg::kChunks - 1) release_accumulator(acc);
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r0[j]);
+        if (item.kind == kFGram)
+          pair_epilogue_half<kGramBf16>(ep, out, mir, mirror, row, hc, v);
+        else if (item.kind == kFPoly)
+          pair_epilogue_half<kPoly>(ep, out, mir, mirror, row, hc, v);
+        else
+          pair_epilogue_half<kApply>(ep, out, mir, false, row, hc, v);
+        fence_proxy_async_smem();
+        named_barrier(1, kPairEpiThreads);
+        if (leader) {
+          tma_store_3d(m_out, sOut + c * Cfg::kRegionBytes, col0 + c * kChunkCols, row0, item.b);
+          if (mirror) {
+#pragma unroll
+            for (int h = 0; h < kHalf / kChunkCols; ++h)
+              tma_store_3d(m_mir, sMir + (c & 1) * Cfg::kRegionBytes + h * (kChunkCols * 128),
+                           row0 + h * kChunkCols, col0 + c * kChunkCols, item.b);
+          }
+          bulk_commit_group();
+        }
+      }
+      if (leader) {
+        if (item.kind != kFApply) {
+          // Publish this band of the tile: its stores must have landed.
+          bulk_wait_group0();
+          fence_proxy_async_global();
+          __threadfence();
+          red_release_gpu_add(p.counters + (item.kind == kFGram ? 0 : p.batch) + item.b, 1u);
+        } else {
+          bulk_wait_group_read<0>();
+        }
+        const int next = w + nclusters;
+        if (next < p.total && !dep_failed) load_aux(next);
+      }
+      if (dep_failed) break;
+    }
+    if (leader) {
+      bulk_wait_group0();
+      if (aux_inflight && !mbar_wait_bounded(aux_full, aux_uses & 1u))
+        atomicOr(&g_watchdog, MUON_POLAR_WATCHDOG_DRAIN);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, Cfg::kTmemCols);
+  }
+  // The last CTA out resets the dependency counters for the next launch.
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const uint32_t exits = atomicAdd(p.counters + 2 * p.batch, 1u);
+    if (exits == gridDim.x - 1) {
+      for (int i = 0; i <= 2 * p.batch; ++i) p.counters[i] = 0u;
+      __threadfence();
+    }
+  }
+}
+
 __global__ void cast_f32_bf16_kernel(const float* __restrict__ src,
                                      uint16_t* __restrict__ dst,
                                      int64_t count) {
@@ -1549,6 +1949,142 @@ int apply_impl(const void* poly, const void* x, void* y, int64_t batch,
   return launch_gemm<128, kApply>(st, 4, maps, p, stream);
 }
 
+// ---------------------------------------------------------------- fused step
+// Step mode: 0 = by size (the fused kernel when the Gram has fewer pair tiles
+// than the device runs pairs at once, else three kernels), 1 = always fused,
+// 2 = never.  Initial value from MUON_POLAR_FUSED (1 -> 1, 0 -> 2).
+std::atomic<int> g_step_mode{[] {
+  const char* s = std::getenv("MUON_POLAR_FUSED");
+  if (s == nullptr) return 0;
+  const int v = std::atoi(s);
+  return v == 1 ? 1 : (v == 0 ? 2 : 0);
+}()};
+
+struct FusedDeviceState {
+  std::once_flag once;
+  cudaError_t err = cudaSuccess;
+  int capacity = 0;
+};
+FusedDeviceState g_fused_state[kMaxDevices];
+
+int fused_capacity(DeviceState* st, int dev, int* capacity) {
+  FusedDeviceState& fs = g_fused_state[dev];
+  std::call_once(fs.once, [&fs, st] {
+    fs.err = cudaFuncSetAttribute(polar_fused_kernel,
+                                  cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  FusedCfg::kSmemBytes);
+    if (fs.err != cudaSuccess) return;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * (st->sms / 2), 1, 1);
+    cfg.blockDim = dim3(kPairThreads, 1, 1);
+    cfg.dynamicSmemBytes = FusedCfg::kSmemBytes;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int clusters = 0;
+    if (cudaOccupancyMaxActiveClusters(&clusters, polar_fused_kernel, &cfg) != cudaSuccess ||
+        clusters <= 0) {
+      (void)cudaGetLastError();
+      clusters = st->sms / 2;
+    }
+    fs.capacity = clusters < st->sms / 2 ? clusters : st->sms / 2;
+  });
+  if (fs.err != cudaSuccess) return static_cast<int>(fs.err);
+  *capacity = fs.capacity;
+  return MUON_POLAR_OK;
+}
+
+// Runs the whole step as one fused launch if the mode and sizes allow it;
+// *done = false means the caller should run the three kernels instead.
+int step_fused_impl(const void* x, void* y, void* gram, void* poly, void* scratch,
+                    size_t scratch_bytes, int64_t batch, int64_t m, int64_t n,
+                    int64_t ldx, int64_t ldy, float a, float b, float c,
+                    cudaStream_t stream, bool* done) {
+  *done = false;
+  const int mode = g_step_mode.load(std::memory_order_relaxed);
+  if (mode == 2 || scratch == nullptr || !aligned16(scratch) ||
+      static_cast<size_t>(2 * batch + 1) * 4 > kCounterBytes || scratch_bytes < kCounterBytes)
+    return MUON_POLAR_OK;
+  DeviceState* st = nullptr;
+  int rc = current_device_state(&st);
+  if (rc != MUON_POLAR_OK) return rc;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return static_cast<int>(e);
+  int capacity = 0;
+  rc = fused_capacity(st, dev, &capacity);
+  if (rc != MUON_POLAR_OK) return rc;
+  const int64_t mp = padded_rows(m);
+  const int64_t d = mp / kPairM;
+  const int64_t sym = d * (d + 1) / 2;
+  const int64_t tn = (n + kPairN - 1) / kPairN;
+  const int64_t total = 2 * batch * sym + batch * d * tn;
+  if (total > INT32_MAX) return MUON_POLAR_OK;
+  // By size: not yet faster than the three kernels on any measured shape
+  // (the stages of all matrices still run in lockstep), so only on request.
+  if (mode == 0) return MUON_POLAR_OK;
+
+  FusedMaps maps;
+  rc = encode_3d(&maps.x_k, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, x, n, m, batch, ldx,
+                 m * ldx, kAtom, kHalf);
+  if (rc != MUON_POLAR_OK) return rc;
+  rc = encode_3d(&maps.x_mn, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, x, n, m, batch, ldx,
+                 m * ldx, kAtom, kAtom);
+  if (rc != MUON_POLAR_OK) return rc;
+  rc = encode_square(&maps.a128, gram, batch, mp, false, kHalf);
+  if (rc != MUON_POLAR_OK) return rc;
+  rc = encode_square(&maps.a64, gram, batch, mp, false, kChunkCols);
+  if (rc != MUON_POLAR_OK) return rc;
+  rc = encode_square(&maps.p128, poly, batch, mp, false, kHalf);
+  if (rc != MUON_POLAR_OK) return rc;
+  rc = encode_square(&maps.p64, poly, batch, mp, false, kChunkCols);
+  if (rc != MUON_POLAR_OK) return rc;
+  rc = encode_3d(&maps.y128, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, y, n, m, batch, ldy,
+                 m * ldy, kAtom, kHalf);
+  if (rc != MUON_POLAR_OK) return rc;
+
+  FusedParams p = {};
+  p.batch = static_cast<int32_t>(batch);
+  p.d = static_cast<int32_t>(d);
+  p.sym_tiles = static_cast<int32_t>(sym);
+  p.apply_tn = static_cast<int32_t>(tn);
+  p.n_gram = static_cast<int32_t>(batch * sym);
+  p.n_poly = static_cast<int32_t>(batch * sym);
+  p.total = static_cast<int32_t>(total);
+  p.kb_gram = static_cast<int32_t>((n + kAtom - 1) / kAtom);
+  p.kb_poly = static_cast<int32_t>(mp / kAtom);
+  p.kb_apply = static_cast<int32_t>((m + kAtom - 1) / kAtom);
+  p.coef_b = b;
+  p.coef_c = c;
+  p.alpha = round_to_bf16(a);
+  p.counters = static_cast<uint32_t*>(scratch);
+
+  const int pairs = total < capacity ? static_cast<int>(total) : capacity;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * pairs, 1, 1);
+  cfg.blockDim = dim3(kPairThreads, 1, 1);
+  cfg.dynamicSmemBytes = FusedCfg::kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  e = cudaLaunchKernelEx(&cfg, polar_fused_kernel, maps, p);
+  if (e != cudaSuccess) return static_cast<int>(e);
+  g_launch_count.fetch_add(1, std::memory_order_relaxed);
+  *done = true;
+  return MUON_POLAR_OK;
+}
+
 }  // namespace
 }  // namespace muon_sm100
 
@@ -1729,6 +2265,10 @@ int muon_polar_step_sm100(const void* x, void* y, void* workspace,
   void* gram = ws;
   void* poly = ws + static_cast<size_t>(batch * mp * mp * 2);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  bool fused = false;
+  rc = step_fused_impl(x, y, gram, poly, scratch, scratch_bytes, batch, m, n, ldx, ldy, a, b,
+                       c, s, &fused);
+  if (rc != MUON_POLAR_OK || fused) return rc;
   rc = gram_impl<kGramBf16>(x, gram, batch, m, n, ldx, scratch, scratch_bytes, s);
   if (rc != MUON_POLAR_OK) return rc;
   rc = poly_impl(gram, poly, batch, mp, b, c, scratch, scratch_bytes, s);
@@ -1754,7 +2294,9 @@ size_t muon_polar_scratch_bytes(int64_t batch, int64_t m, int64_t n) {
   const int64_t kb_poly = pair_k_blocks<kPoly>(mp);
   const size_t g = split_scratch_bytes(tiles, choose_splits(tiles, kb_gram, pairs));
   const size_t q = split_scratch_bytes(tiles, choose_splits(tiles, kb_poly, pairs));
-  return g > q ? g : q;
+  const size_t need = g > q ? g : q;
+  // The fused step's dependency counters live in the counter area.
+  return need > kCounterBytes ? need : kCounterBytes;
 }
 
 int muon_polar_scratch_init(void* scratch, size_t scratch_bytes, void* stream) {
@@ -1823,6 +2365,11 @@ int muon_polar_read_device_status(int device, uint32_t* flags, int clear) {
 int muon_polar_set_kernel_policy(int policy) {
   if (policy < 0 || policy > 2) return MUON_POLAR_ERR_INVALID_ARGUMENT;
   return g_policy.exchange(policy);
+}
+
+int muon_polar_set_step_mode(int mode) {
+  if (mode < 0 || mode > 2) return MUON_POLAR_ERR_INVALID_ARGUMENT;
+  return g_step_mode.exchange(mode);
 }
 
 int muon_polar_device_pairs(int* pairs) {

@@ -121,6 +121,31 @@ __device__ __forceinline__ void bulk_wait_group0() {
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
+// Orders async-proxy (TMA) global accesses against generic-proxy ones, both
+// ways: after waiting for a TMA store before publishing it, and after
+// observing a published flag before a TMA load of the data it guards.
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void red_release_gpu_add(uint32_t* p, uint32_t v) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+// Waits until *p >= target (written by other CTAs with release semantics).
+// Returns false once kWaitLimitNs of wall-clock time have passed.
+__device__ __forceinline__ bool wait_counter_bounded(const uint32_t* p, uint32_t target) {
+  if (ld_acquire_gpu(p) >= target) return true;
+  const uint64_t t0 = global_timer_ns();
+  while (true) {
+    __nanosleep(64);
+    if (ld_acquire_gpu(p) >= target) return true;
+    if (global_timer_ns() - t0 > kWaitLimitNs) return false;
+  }
+}
 // Named barrier over `count` threads (id 0 is __syncthreads).
 __device__ __forceinline__ void named_barrier(uint32_t id, uint32_t count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");

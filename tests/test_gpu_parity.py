@@ -293,3 +293,41 @@ def test_kernel_paths_agree_bitwise(api, cuda_device, shape, mode_policy):
         outs[mode] = (gram.cpu(), poly.cpu(), y.cpu())
     for a, b, what in zip(outs["single"], outs["pair"], ("gram", "poly", "apply")):
         assert torch.equal(a.view(torch.int16), b.view(torch.int16)), what
+
+
+@pytest.fixture
+def step_mode(api):
+    """Sets the step mode for one test and restores the default after."""
+    def set_mode(mode):
+        api.set_step_mode(mode)
+    yield set_mode
+    api.set_step_mode(0)
+
+
+@pytest.mark.parametrize("shape", [(8, 512, 2048), (2, 150, 2064), (1, 128, 256),
+                                   (3, 640, 1000), (1, 1024, 1024)])
+def test_fused_step_matches_three_kernels(api, cuda_device, shape, step_mode):
+    """One fused persistent launch gives the bits of the three kernels, and
+    repeated launches reuse the scratch counters correctly (they are reset by
+    the last CTA of each launch)."""
+    bsz, m, n = shape
+    x = make_input(shape, seed=8).to(cuda_device)
+    ws = torch.empty(api.workspace_bytes(bsz, m), dtype=torch.uint8, device=cuda_device)
+    scratch = api.new_scratch(bsz, m, n)
+    outs = {}
+    for mode in (2, 1):
+        step_mode(mode)
+        ys = []
+        for _ in range(3):
+            y = torch.full_like(x, float("nan"))
+            api.step(x, y, ws, A1, B1, C1, scratch=scratch)
+            ys.append(y)
+        torch.cuda.synchronize()
+        _check_watchdog(api)
+        _counters_zero(scratch)
+        for y in ys[1:]:
+            assert torch.equal(y.view(torch.int16), ys[0].view(torch.int16))
+        outs[mode] = ys[0].cpu()
+    assert torch.equal(outs[1].view(torch.int16), outs[2].view(torch.int16))
+    e = error_stats(outs[1], reference_formula(make_input(shape, seed=8).float(), COEFFICIENTS[:1]))
+    assert e["rel_fro"] <= 1e-2, e
