@@ -11,13 +11,15 @@
 //   kPoly       A rows tm             A rows tn  (K-major)    bf16(b*A + c*acc), tile + mirror
 //   kApply      P rows tm             X[k, n-block] (MN-major) bf16(bf16(acc) + bf16(alpha*X))
 //
-// CTA layout (192 threads): warp 0 lane 0 issues TMA loads into a ring of
-// shared-memory stages; warp 1 owns the tensor memory and its lane 0 issues
-// tcgen05.mma (128 x BN x 16 per instruction) into one of two TMEM
-// accumulators; warps 2-5 drain the other accumulator (tcgen05.ld), apply
-// the epilogue and store to global memory, so the epilogue of tile i
-// overlaps the main loop of tile i+1.  Every wait is bounded in wall-clock
-// time; a kernel that gives up records a watchdog bit and returns.
+// Two engines of the same kernel (polar_tile_kernel<KIND, PAIR>): 256 x 256
+// tiles on a tcgen05 CTA pair (PAIR = 2) and 128 x 128 tiles on one CTA
+// (PAIR = 1), chosen by problem size.  CTA layout (320 threads): warp 0 lane
+// 0 issues TMA loads into a ring of shared-memory stages; warp 1 owns the
+// tensor memory and its lane 0 (leader CTA) issues tcgen05.mma into one of
+// two TMEM accumulators; warps 2-9 drain the other accumulator
+// (tcgen05.ld), apply the epilogue and store with TMA, so the epilogue of
+// tile i overlaps the main loop of tile i+1.  Every wait is bounded in
+// wall-clock time; a kernel that gives up records a watchdog bit and returns.
 //
 // Reference behaviour restated here (Ascend 950PR AscendC kernels):
 //   symmetric upper-tile Gram + mirror ........ asc:129-146, 376-474
@@ -40,11 +42,6 @@
 
 namespace muon_sm100 {
 
-constexpr int kBM = 128;        // tile rows = TMEM lanes
-constexpr int kBK = 64;         // bf16 elements per 128-byte swizzle row
-constexpr int kThreads = 192;   // 6 warps
-constexpr uint32_t kABytes = kBM * kBK * 2;  // 16 KiB per stage
-
 enum Kind : int { kGramBf16 = 0, kGramF32 = 1, kPoly = 2, kApply = 3 };
 
 __device__ uint32_t g_watchdog = 0;
@@ -64,36 +61,6 @@ struct EpiParams {
   int32_t total_items;
   float* partial;      // [total_items][2][128][256] fp32 partial sums
   uint32_t* counters;  // [total_tiles][2] arrivals, zero between launches
-};
-
-// Shared-memory plan of one CTA.  The output tile is staged in shared memory
-// as BN/box_cols boxes of [128 rows x 128 bytes] in the 128-byte swizzle TMA
-// uses, so the same bytes are (a) the landing zone of the epilogue input tile
-// (A for kPoly, X for kApply; updated in place) and (b) the source of the
-// TMA store.  Symmetric kinds add a second tile for the transposed mirror.
-template <int BN, int KIND>
-struct Config {
-  static constexpr bool kSym = KIND != kApply;
-  static constexpr bool kAux = KIND == kPoly || KIND == kApply;
-  static constexpr int kOutElem = KIND == kGramF32 ? 4 : 2;
-  static constexpr int kBoxCols = 128 / kOutElem;
-  static constexpr int kBoxes = BN / kBoxCols;
-  static constexpr uint32_t kBoxBytes = kBM * 128;
-  static constexpr uint32_t kOutBytes = kBoxes * kBoxBytes;
-  static constexpr uint32_t kMirBytes = kSym ? kOutBytes : 0;
-  static constexpr uint32_t kBBytes = BN * kBK * 2;
-  static constexpr uint32_t kStageBytes = kABytes + kBBytes;
-  static constexpr uint32_t kBarrierBytes = 256;
-  static constexpr uint32_t kFixedBytes =
-      1024 + kOutBytes + kMirBytes + kBarrierBytes;
-  static constexpr int kStagesFit =
-      static_cast<int>((232448u - kFixedBytes) / kStageBytes);
-  static constexpr int kStages = kStagesFit > 8 ? 8 : kStagesFit;
-  static constexpr uint32_t kSmemBytes = kFixedBytes + kStages * kStageBytes;
-  static constexpr uint32_t kTmemCols = 2 * BN;  // two accumulators
-  static_assert(kStages >= 2, "pipeline depth");
-  static_assert(kSmemBytes <= 232448, "shared memory budget");
-  static_assert(!kSym || BN == kBM, "symmetric kinds use square tiles");
 };
 
 struct TileCoord {
@@ -126,368 +93,13 @@ __host__ __device__ __forceinline__ TileCoord decode_tile(int tile, bool sym,
   return t;
 }
 
-__device__ __forceinline__ float bf16_bits_to_float(uint32_t bits16) {
-  return __uint_as_float(bits16 << 16);
-}
 __device__ __forceinline__ uint32_t float_to_bf16_bits(float v) {
   __nv_bfloat16 h = __float2bfloat16_rn(v);
   return static_cast<uint32_t>(*reinterpret_cast<uint16_t*>(&h));
 }
-__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
-  return float_to_bf16_bits(lo) | (float_to_bf16_bits(hi) << 16);
-}
 
-// Byte offset of element (row, col) of a staged tile: boxes of 128 rows x 128
-// bytes, 16-byte units XOR-swizzled by (row & 7) -- the layout TMA writes
-// and reads with CU_TENSOR_MAP_SWIZZLE_128B.
-template <int ELEM>
-__device__ __forceinline__ uint32_t swz(int row, int col) {
-  constexpr int kPerRow = 128 / ELEM;
-  const int box = col / kPerRow;
-  const int byte = (col % kPerRow) * ELEM;
-  const int unit = byte >> 4;
-  return static_cast<uint32_t>(box * (kBM * 128) + row * 128 +
-                               (((unit ^ (row & 7)) << 4) | (byte & 15)));
-}
-
-// Epilogue of 32 accumulator columns [c0, c0+32) of tile row `row`: reads
-// the staged input (kPoly / kApply), writes the staged output and, for
-// symmetric kinds off the diagonal, the mirrored column into `mir`.
-template <int BN, int KIND>
-__device__ __forceinline__ void epilogue_chunk(const EpiParams& p,
-                                               uint32_t out, uint32_t mir,
-                                               bool mirror, int row, int c0,
-                                               const uint32_t (&r)[32]) {
-  float v[32];
-#pragma unroll
-  for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-  if constexpr (KIND == kGramF32) {
-#pragma unroll
-    for (int u = 0; u < 8; ++u)
-      st_shared_v4(out + swz<4>(row, c0 + 4 * u),
-                   make_uint4(__float_as_uint(v[4 * u]), __float_as_uint(v[4 * u + 1]),
-                              __float_as_uint(v[4 * u + 2]),
-                              __float_as_uint(v[4 * u + 3])));
-    if (mirror) {
-#pragma unroll
-      for (int j = 0; j < 32; ++j) st_shared_f32(mir + swz<4>(c0 + j, row), v[j]);
-    }
-    return;
-  } else {
-    uint32_t w[16];
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const uint32_t addr = out + swz<2>(row, c0 + 8 * u);
-      if constexpr (KIND == kGramBf16) {
-#pragma unroll
-        for (int e = 0; e < 4; ++e)
-          w[4 * u + e] = pack_bf16x2(v[8 * u + 2 * e], v[8 * u + 2 * e + 1]);
-      } else {
-        const uint4 q = ld_shared_v4(addr);
-        const uint32_t in[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int j = 8 * u + 2 * e;
-          const float lo = bf16_bits_to_float(in[e] & 0xFFFFu);
-          const float hi = bf16_bits_to_float(in[e] >> 16);
-          if constexpr (KIND == kPoly) {
-            // P = bf16( fl(b*A) + fl(c*acc) ): the reference's separate
-            // Muls/Add (asc:929-940), no fused multiply-add.
-            w[4 * u + e] =
-                pack_bf16x2(__fadd_rn(__fmul_rn(p.coef_b, lo), __fmul_rn(p.coef_c, v[j])),
-                            __fadd_rn(__fmul_rn(p.coef_b, hi),
-                                      __fmul_rn(p.coef_c, v[j + 1])));
-          } else {
-            // Y = bf16( bf16(T) + bf16(alpha*x) ) (asc:1472-1476).
-            const float ax_lo = bf16_bits_to_float(float_to_bf16_bits(p.alpha * lo));
-            const float ax_hi = bf16_bits_to_float(float_to_bf16_bits(p.alpha * hi));
-            const float t_lo = bf16_bits_to_float(float_to_bf16_bits(v[j]));
-            const float t_hi = bf16_bits_to_float(float_to_bf16_bits(v[j + 1]));
-            w[4 * u + e] = pack_bf16x2(__fadd_rn(t_lo, ax_lo), __fadd_rn(t_hi, ax_hi));
-          }
-        }
-      }
-      st_shared_v4(addr, make_uint4(w[4 * u], w[4 * u + 1], w[4 * u + 2], w[4 * u + 3]));
-    }
-    if constexpr (KIND != kApply) {
-      if (mirror) {
-#pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const uint16_t h = static_cast<uint16_t>((j & 1) ? (w[j >> 1] >> 16)
-                                                           : (w[j >> 1] & 0xFFFFu));
-          st_shared_u16(mir + swz<2>(c0 + j, row), h);
-        }
-      }
-    }
-  }
-}
-
-template <int BN, int KIND>
-__device__ __forceinline__ void load_aux_tile(const CUtensorMap* map, uint8_t* dst,
-                                              uint64_t* bar, const TileCoord& tc) {
-  using Cfg = Config<BN, KIND>;
-  mbar_arrive_expect_tx(bar, Cfg::kOutBytes);
-#pragma unroll
-  for (int k = 0; k < Cfg::kBoxes; ++k)
-    tma_load_3d(dst + k * Cfg::kBoxBytes, map, bar, tc.tn * BN + k * Cfg::kBoxCols,
-                tc.tm * kBM, tc.b);
-}
-
-template <int BN, int KIND>
-__global__ void __launch_bounds__(kThreads, 1)
-    polar_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
-                      const __grid_constant__ CUtensorMap tmap_b,
-                      const __grid_constant__ CUtensorMap tmap_aux,
-                      const __grid_constant__ CUtensorMap tmap_out,
-                      const EpiParams p) {
-  using Cfg = Config<BN, KIND>;
-  constexpr int S = Cfg::kStages;
-  constexpr bool kBmn = (KIND == kApply);
-  constexpr bool kSym = Cfg::kSym;
-
-  extern __shared__ uint8_t smem_raw[];
-  const uint32_t raw_addr = smem_addr(smem_raw);
-  uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
-  uint8_t* sOut = smem;
-  uint8_t* sMir = sOut + Cfg::kOutBytes;
-  uint8_t* sA = sMir + Cfg::kMirBytes;
-  uint8_t* sB = sA + S * kABytes;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sB + S * Cfg::kBBytes);
-  uint64_t* empty = full + S;
-  uint64_t* tfull = empty + S;
-  uint64_t* tempty = tfull + 2;
-  uint64_t* drain = tempty + 2;
-  uint64_t* aux_full = drain + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(aux_full + 1);
-
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
-  constexpr int kEpiLeader = 64;  // warp 2, lane 0
-
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < S; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
-    }
-    for (int a = 0; a < 2; ++a) {
-      mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], 4);
-    }
-    mbar_init(drain, 1);
-    mbar_init(aux_full, 1);
-    fence_mbar_init();
-    prefetch_tensor_map(&tmap_a);
-    prefetch_tensor_map(&tmap_b);
-    prefetch_tensor_map(&tmap_aux);
-    prefetch_tensor_map(&tmap_out);
-  }
-  if (warp == 1) {
-    tmem_alloc(tmem_slot, Cfg::kTmemCols);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem_base = *tmem_slot;
-
-  // Inputs may come from the kernel launched just before this one.
-  grid_dependency_wait();
-  grid_launch_dependents();
-
-  if (warp == 0) {
-    if (lane == 0) {
-      // ---------------- TMA producer
-      uint32_t it = 0;
-      bool ok = true;
-      for (int tile = blockIdx.x; ok && tile < p.total_tiles; tile += gridDim.x) {
-        const TileCoord tc =
-            decode_tile(tile, kSym, p.tiles_m, p.tiles_n, p.tiles_per_batch);
-        for (int kb = 0; kb < p.k_blocks; ++kb, ++it) {
-          const uint32_t s = it % S;
-          const uint32_t ph = (it / S) & 1u;
-          if (!mbar_wait_bounded(&empty[s], ph ^ 1u)) {
-            ok = false;
-            break;
-          }
-          mbar_arrive_expect_tx(&full[s], Cfg::kStageBytes);
-          tma_load_3d(sA + s * kABytes, &tmap_a, &full[s], kb * kBK, tc.tm * kBM,
-                      tc.b);
-          if constexpr (!kBmn) {
-            tma_load_3d(sB + s * Cfg::kBBytes, &tmap_b, &full[s], kb * kBK,
-                        tc.tn * BN, tc.b);
-          } else {
-#pragma unroll
-            for (int j = 0; j < BN / 64; ++j)
-              tma_load_3d(sB + s * Cfg::kBBytes + j * (64 * kBK * 2), &tmap_b,
-                          &full[s], tc.tn * BN + j * 64, kb * kBK, tc.b);
-          }
-        }
-      }
-      if (!ok) atomicOr(&g_watchdog, MUON_POLAR_WATCHDOG_PRODUCER);
-      // Drain: the loads of the last stages must land before the CTA exits.
-      const uint32_t inflight = it < static_cast<uint32_t>(S) ? it : S;
-      for (uint32_t i = it - inflight; i < it; ++i) {
-        if (!mbar_wait_bounded(&full[i % S], (i / S) & 1u)) {
-          atomicOr(&g_watchdog, MUON_POLAR_WATCHDOG_DRAIN);
-          break;
-        }
-      }
-    }
-  } else if (warp == 1) {
-    if (lane == 0) {
-      // ---------------- tcgen05 MMA issuer
-      constexpr uint32_t idesc = idesc_bf16_f32(BN, kBmn ? 1u : 0u);
-      uint32_t it = 0;
-      uint32_t t = 0;
-      bool ok = true;
-      for (int tile = blockIdx.x; ok && tile < p.total_tiles;
-           tile += gridDim.x, ++t) {
-        const uint32_t acc = t & 1u;
-        const uint32_t uph = (t >> 1) & 1u;
-        if (!mbar_wait_bounded(&tempty[acc], uph ^ 1u)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t d_tmem = tmem_base + acc * BN;
-        for (int kb = 0; kb < p.k_blocks; ++kb, ++it) {
-          const uint32_t s = it % S;
-          const uint32_t ph = (it / S) & 1u;
-          if (!mbar_wait_bounded(&full[s], ph)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t a_base = smem_addr(sA + s * kABytes);
-          const uint32_t b_base = smem_addr(sB + s * Cfg::kBBytes);
-#pragma unroll
-          for (int k = 0; k < kBK / 16; ++k) {
-            // K-major, 128B swizzle: a K step of 16 bf16 is 32 bytes inside
-            // the swizzle row; 8-row groups are 1024 bytes apart.
-            const uint64_t ad = smem_desc_sw128(a_base + k * 32, 16, 1024);
-            uint64_t bd;
-            if constexpr (kBmn) {
-              // MN-major, 128B swizzle: 64-column chunks are kBK*128 bytes
-              // apart (leading offset), 8-row K groups 1024 bytes (stride
-              // offset); a K step of 16 rows is 2048 bytes.
-              bd = smem_desc_sw128(b_base + k * 2048, kBK * 128, 1024);
-            } else {
-              bd = smem_desc_sw128(b_base + k * 32, 16, 1024);
-            }
-            umma_bf16(d_tmem, ad, bd, idesc, (kb > 0 || k > 0) ? 1u : 0u);
-          }
-          umma_commit(&empty[s]);
-        }
-        if (!ok) break;
-        umma_commit(&tfull[acc]);
-      }
-      if (!ok) atomicOr(&g_watchdog, MUON_POLAR_WATCHDOG_MMA);
-      // Drain: every MMA issued above completes before TMEM is released.
-      umma_commit(drain);
-      if (!mbar_wait_bounded(drain, 0))
-        atomicOr(&g_watchdog, MUON_POLAR_WATCHDOG_DRAIN);
-    }
-  } else {
-    // ---------------- epilogue warps 2..5 (128 threads, one tile row each)
-    const int q = warp & 3;  // TMEM lane quarter this warp may access
-    const int row = q * 32 + lane;
-    const uint32_t out_base = smem_addr(sOut);
-    const uint32_t mir_base = smem_addr(sMir);
-    const bool leader = threadIdx.x == kEpiLeader;
-    bool aux_inflight = false;  // leader only: an aux tile load not yet waited on
-    if constexpr (Cfg::kAux) {
-      if (leader && static_cast<int>(blockIdx.x) < p.total_tiles) {
-        load_aux_tile<BN, KIND>(&tmap_aux, sOut, aux_full,
-                                decode_tile(blockIdx.x, kSym, p.tiles_m, p.tiles_n,
-                                            p.tiles_per_batch));
-        aux_inflight = true;
-      }
-    }
-    uint32_t t = 0;
-    for (int tile = blockIdx.x; tile < p.total_tiles; tile += gridDim.x, ++t) {
-      const TileCoord tc =
-          decode_tile(tile, kSym, p.tiles_m, p.tiles_n, p.tiles_per_batch);
-      const uint32_t acc = t & 1u;
-      const uint32_t uph = (t >> 1) & 1u;
-      int ok = 1;
-      if (lane == 0) {
-        ok = mbar_wait_bounded(&tfull[acc], uph) ? 1 : 0;
-        if (Cfg::kAux && ok) {
-          ok = mbar_wait_bounded(aux_full, t & 1u) ? 1 : 0;
-          if (ok) aux_inflight = false;
-        }
-      }
-      ok = __shfl_sync(0xffffffffu, ok, 0);
-      if (!ok) {
-        if (lane == 0) atomicOr(&g_watchdog, MUON_POLAR_WATCHDOG_EPILOGUE);
-        break;
-      }
-      // Every lane reads the TMA-written input tile: each observes the
-      // completed phase itself (it has completed, so this returns at once).
-      if constexpr (Cfg::kAux) (void)mbar_try_wait(aux_full, t & 1u);
-      tc_fence_after();
-      const bool mirror = kSym && tc.tm != tc.tn;
-      const uint32_t t_row =
-          tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
-#pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(t_row + c * 32, r);
-        tmem_wait_ld();
-        if (c == BN / 32 - 1) {
-          // accumulator fully read: hand it back to the MMA warp
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&tempty[acc]);
-        }
-        epilogue_chunk<BN, KIND>(p, out_base, mir_base, mirror, row, c * 32, r);
-      }
-      fence_proxy_async_smem();
-      named_barrier(1, 128);
-      if (leader) {
-#pragma unroll
-        for (int k = 0; k < Cfg::kBoxes; ++k)
-          tma_store_3d(&tmap_out, sOut + k * Cfg::kBoxBytes,
-                       tc.tn * BN + k * Cfg::kBoxCols, tc.tm * kBM, tc.b);
-        if (mirror) {
-#pragma unroll
-          for (int k = 0; k < Cfg::kBoxes; ++k)
-            tma_store_3d(&tmap_out, sMir + k * Cfg::kBoxBytes,
-                         tc.tm * kBM + k * Cfg::kBoxCols, tc.tn * BN, tc.b);
-        }
-        bulk_commit_group();
-        bulk_wait_group_read0();
-        if constexpr (Cfg::kAux) {
-          const int next = tile + static_cast<int>(gridDim.x);
-          if (next < p.total_tiles) {
-            load_aux_tile<BN, KIND>(&tmap_aux, sOut, aux_full,
-                                    decode_tile(next, kSym, p.tiles_m, p.tiles_n,
-                                                p.tiles_per_batch));
-            aux_inflight = true;
-          }
-        }
-      }
-      named_barrier(1, 128);
-    }
-    if (leader) {
-      bulk_wait_group0();
-      // After a watchdog exit an aux load may still be in flight; it must
-      // land before the CTA releases its shared memory.
-      if (aux_inflight && !mbar_wait_bounded(aux_full, t & 1u))
-        atomicOr(&g_watchdog, MUON_POLAR_WATCHDOG_DRAIN);
-    }
-  }
-
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 1) {
-    tc_fence_after();
-    tmem_dealloc(tmem_base, Cfg::kTmemCols);
-  }
-}
-
-// ============================================================ CTA pairs
-// 256 x 256 tiles computed by a cluster of two CTAs with
+// ============================================================ tile engine
+// PAIR = 2: 256 x 256 tiles computed by a cluster of two CTAs with
 // tcgen05.mma.cta_group::2 (M = 256, N = 256, K = 16): CTA r of the pair
 // loads its own 128 rows of the A operand and its own half (128 rows, or 128
 // columns when MN-major) of the B operand with plain TMA loads; the leader
@@ -495,6 +107,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 // each CTA's 128 x 256 fp32 slice into its own tensor memory.  Per k-block
 // each SM ingests 32 KB for 128x256x64 MACs -- half the bytes per FLOP of a
 // 128 x 128 single-CTA tile.
+// PAIR = 1: 128 x 128 tiles on one CTA (M = 128, N = 128), the same
+// pipeline and epilogue; twice the tiles for a given problem, so small
+// problems keep more SMs busy.
 //
 // Epilogue: 64-column chunks staged in shared memory (128-byte swizzle) and
 // written with TMA stores; symmetric kinds also stage the transposed chunk
@@ -517,14 +132,19 @@ constexpr int64_t pair_k_blocks(int64_t k) {
   return (k + pair_bk<KIND>() - 1) / pair_bk<KIND>();
 }
 
-template <int KIND>
+// Shared-memory and tensor-memory plan of one CTA of polar_tile_kernel.
+// PAIR = 2: a 256 x 256 tile on a tcgen05 CTA pair (each CTA owns a 128 x 256
+// band); PAIR = 1: a 128 x 128 tile on one CTA.
+template <int KIND, int PAIR = 2>
 struct PairCfg {
   static constexpr bool kSym = KIND != kApply;
   static constexpr bool kAux = KIND == kPoly || KIND == kApply;
   static constexpr bool kF32 = KIND == kGramF32;
+  static constexpr int kTileM = kHalf * PAIR;
+  static constexpr int kTileN = PAIR == 2 ? kPairN : kHalf;
   static constexpr int kElem = kF32 ? 4 : 2;
   static constexpr int kBoxCols = 128 / kElem;  // columns of one 128-byte box row
-  static constexpr int kChunks = kPairN / kChunkCols;
+  static constexpr int kChunks = kTileN / kChunkCols;
   static constexpr uint32_t kOutChunkBytes = kHalf * kChunkCols * kElem;
   static constexpr uint32_t kMirChunkBytes = kSym ? kChunkCols * kHalf * kElem : 0;
   // K depth of a pipeline stage.  TMA ingest into one SM grows with the
@@ -535,7 +155,7 @@ struct PairCfg {
   // 128); the others keep four or five 32 KiB stages (K = 64), which measured
   // faster for them.
   static constexpr int kBK = pair_bk<KIND>();
-  // Output regions: kAux kinds keep the whole 128 x 256 input tile (updated
+  // Output regions: kAux kinds keep the whole 128 x kTileN input band (updated
   // in place, one region per chunk, never reused within a tile); the Gram
   // single-buffers its chunk region.
   static constexpr int kOutRegions = kAux ? kChunks : 1;
@@ -556,7 +176,8 @@ struct PairCfg {
       static_cast<int>((232448u - kFixedBytes) / kStageBytes);
   static constexpr int kStages = kStagesFit > 8 ? 8 : kStagesFit;
   static constexpr uint32_t kSmemBytes = kFixedBytes + kStages * kStageBytes;
-  static constexpr uint32_t kTmemCols = 2 * kPairN;
+  static constexpr uint32_t kTmemCols = 2 * kTileN;
+  static constexpr uint32_t kBandFloats = kHalf * kTileN;  // one CTA's fp32 band
   static_assert(kStages >= 2, "pipeline depth");
   static_assert(kSmemBytes <= 232448, "shared memory budget");
 };
@@ -653,15 +274,17 @@ __device__ __forceinline__ void pair_epilogue_half(const EpiParams& p, uint32_t 
 constexpr int kPairThreads = 320;
 constexpr int kPairEpiThreads = 256;
 
-template <int KIND>
+template <int KIND, int PAIR>
 __global__ void __launch_bounds__(kPairThreads, 1)
-    polar_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
+    polar_tile_kernel(const __grid_constant__ CUtensorMap tmap_a,
                       const __grid_constant__ CUtensorMap tmap_b,
                       const __grid_constant__ CUtensorMap tmap_aux,
                       const __grid_constant__ CUtensorMap tmap_out,
                       const __grid_constant__ CUtensorMap tmap_mir,
                       const EpiParams p) {
-  using Cfg = PairCfg<KIND>;
+  using Cfg = PairCfg<KIND, PAIR>;
+  constexpr int kTileM = Cfg::kTileM;
+  constexpr int kTileN = Cfg::kTileN;
   constexpr int S = Cfg::kStages;
   constexpr bool kBmn = (KIND == kApply);
   constexpr bool kSym = Cfg::kSym;
@@ -684,9 +307,9 @@ __global__ void __launch_bounds__(kPairThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const uint32_t rank = cluster_cta_rank();
-  const int cluster = static_cast<int>(blockIdx.x >> 1);
-  const int nclusters = static_cast<int>(gridDim.x >> 1);
+  const uint32_t rank = PAIR == 2 ? cluster_cta_rank() : 0u;
+  const int cluster = static_cast<int>(blockIdx.x) / PAIR;
+  const int nclusters = static_cast<int>(gridDim.x) / PAIR;
   constexpr int kEpiLeader = 64;
 
   if (threadIdx.x == 0) {
@@ -696,7 +319,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], 16);  // 8 epilogue warps in each CTA of the pair
+      mbar_init(&tempty[a], 8 * PAIR);  // 8 epilogue warps in each CTA
     }
     mbar_init(drain, 1);
     mbar_init(aux_full, 1);
@@ -708,12 +331,17 @@ __global__ void __launch_bounds__(kPairThreads, 1)
     prefetch_tensor_map(&tmap_mir);
   }
   if (warp == 1) {
-    tmem_alloc_pair(tmem_slot, Cfg::kTmemCols);
-    tmem_relinquish_pair();
+    if constexpr (PAIR == 2) {
+      tmem_alloc_pair(tmem_slot, Cfg::kTmemCols);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_slot, Cfg::kTmemCols);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
   __syncthreads();
-  cluster_sync();  // the peer's barriers exist before anyone signals them
+  if constexpr (PAIR == 2) cluster_sync();  // the peer's barriers exist first
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
@@ -730,7 +358,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
         const int split = item - tile * p.splits;
         const TileCoord tc =
             decode_tile(tile, kSym, p.tiles_m, p.tiles_n, p.tiles_per_batch);
-        const int a_row = tc.tm * kPairM + static_cast<int>(rank) * kHalf;
+        const int a_row = tc.tm * kTileM + static_cast<int>(rank) * kHalf;
         const int kb_end = (split + 1) * p.k_blocks / p.splits;
         for (int kb = split * p.k_blocks / p.splits; kb < kb_end; ++kb, ++it) {
           const uint32_t s = it % S;
@@ -739,24 +367,32 @@ __global__ void __launch_bounds__(kPairThreads, 1)
             ok = false;
             break;
           }
-          if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * Cfg::kStageBytes);
-          const uint32_t bar = map_to_cta(smem_addr(&full[s]), 0);
-          const int b_row = tc.tn * kPairN + static_cast<int>(rank) * kHalf;
+          if (rank == 0) mbar_arrive_expect_tx(&full[s], PAIR * Cfg::kStageBytes);
+          const uint32_t bar = PAIR == 2 ? map_to_cta(smem_addr(&full[s]), 0) : 0u;
+          const int b_row = tc.tn * kTileN + static_cast<int>(rank) * kHalf;
+          // loads into this CTA's stage; PAIR = 2 counts the bytes on the
+          // leader's barrier, PAIR = 1 on its own
+          auto load = [&](void* dst, const CUtensorMap* map, int c0, int c1) {
+            if constexpr (PAIR == 2)
+              tma_load_3d_pair(dst, map, bar, c0, c1, tc.b);
+            else
+              tma_load_3d(dst, map, &full[s], c0, c1, tc.b);
+          };
 #pragma unroll
           for (int j = 0; j < Cfg::kBK / kAtom; ++j)
-            tma_load_3d_pair(sA + s * Cfg::kAHalfBytes + j * kAtomBytes, &tmap_a, bar,
-                             kb * Cfg::kBK + j * kAtom, a_row, tc.b);
+            load(sA + s * Cfg::kAHalfBytes + j * kAtomBytes, &tmap_a, kb * Cfg::kBK + j * kAtom,
+                 a_row);
           if constexpr (!kBmn) {
 #pragma unroll
             for (int j = 0; j < Cfg::kBK / kAtom; ++j)
-              tma_load_3d_pair(sB + s * Cfg::kBHalfBytes + j * kAtomBytes, &tmap_b, bar,
-                               kb * Cfg::kBK + j * kAtom, b_row, tc.b);
+              load(sB + s * Cfg::kBHalfBytes + j * kAtomBytes, &tmap_b,
+                   kb * Cfg::kBK + j * kAtom, b_row);
           } else {
-            // MN-major B: one [Cfg::kBK k-rows x 64 n] box per 64-column chunk
+            // MN-major B: one [kBK k-rows x 64 n] box per 64-column chunk
 #pragma unroll
             for (int j = 0; j < kHalf / kAtom; ++j)
-              tma_load_3d_pair(sB + s * Cfg::kBHalfBytes + j * (Cfg::kBK * 128), &tmap_b, bar,
-                               b_row + j * kAtom, kb * Cfg::kBK, tc.b);
+              load(sB + s * Cfg::kBHalfBytes + j * (Cfg::kBK * 128), &tmap_b, b_row + j * kAtom,
+                   kb * Cfg::kBK);
           }
         }
       }
@@ -775,7 +411,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   } else if (warp == 1) {
     if (lane == 0 && rank == 0) {
       // ---------------- tcgen05 MMA issuer (leader CTA only)
-      constexpr uint32_t idesc = idesc_bf16_f32(kPairN, kBmn ? 1u : 0u, kPairM);
+      constexpr uint32_t idesc = idesc_bf16_f32(kTileN, kBmn ? 1u : 0u, kTileM);
       uint32_t it = 0;
       uint32_t t = 0;
       bool ok = true;
@@ -790,7 +426,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
           break;
         }
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + acc * kPairN;
+        const uint32_t d_tmem = tmem_base + acc * kTileN;
         for (int kb = kb_begin; kb < kb_end; ++kb, ++it) {
           const uint32_t s = it % S;
           const uint32_t ph = (it / S) & 1u;
@@ -815,18 +451,31 @@ __global__ void __launch_bounds__(kPairThreads, 1)
             } else {
               bd = smem_desc_sw128(b_base + koff, 16, 1024);
             }
-            umma_bf16_pair(d_tmem, ad, bd, idesc, (kb > kb_begin || k > 0) ? 1u : 0u);
+            if constexpr (PAIR == 2)
+              umma_bf16_pair(d_tmem, ad, bd, idesc, (kb > kb_begin || k > 0) ? 1u : 0u);
+            else
+              umma_bf16(d_tmem, ad, bd, idesc, (kb > kb_begin || k > 0) ? 1u : 0u);
           }
-          const uint32_t e_own = map_to_cta(smem_addr(&empty[s]), 0);
-          umma_commit_pair(e_own);
-          umma_commit_pair(map_to_cta(smem_addr(&empty[s]), 1));
+          if constexpr (PAIR == 2) {
+            umma_commit_pair(map_to_cta(smem_addr(&empty[s]), 0));
+            umma_commit_pair(map_to_cta(smem_addr(&empty[s]), 1));
+          } else {
+            umma_commit(&empty[s]);
+          }
         }
         if (!ok) break;
-        umma_commit_pair(map_to_cta(smem_addr(&tfull[acc]), 0));
-        umma_commit_pair(map_to_cta(smem_addr(&tfull[acc]), 1));
+        if constexpr (PAIR == 2) {
+          umma_commit_pair(map_to_cta(smem_addr(&tfull[acc]), 0));
+          umma_commit_pair(map_to_cta(smem_addr(&tfull[acc]), 1));
+        } else {
+          umma_commit(&tfull[acc]);
+        }
       }
       if (!ok) atomicOr(&g_watchdog, MUON_POLAR_WATCHDOG_MMA);
-      umma_commit_pair(map_to_cta(smem_addr(drain), 0));
+      if constexpr (PAIR == 2)
+        umma_commit_pair(map_to_cta(smem_addr(drain), 0));
+      else
+        umma_commit(drain);
       if (!mbar_wait_bounded(drain, 0)) atomicOr(&g_watchdog, MUON_POLAR_WATCHDOG_DRAIN);
     }
   } else {
@@ -837,8 +486,8 @@ __global__ void __launch_bounds__(kPairThreads, 1)
     const uint32_t out_base = smem_addr(sOut);
     const uint32_t mir_base = smem_addr(sMir);
     const bool leader = threadIdx.x == kEpiLeader;
-    const uint32_t tempty_leader0 = map_to_cta(smem_addr(&tempty[0]), 0);
-    const uint32_t tempty_leader1 = map_to_cta(smem_addr(&tempty[1]), 0);
+    const uint32_t tempty_leader0 = PAIR == 2 ? map_to_cta(smem_addr(&tempty[0]), 0) : 0u;
+    const uint32_t tempty_leader1 = PAIR == 2 ? map_to_cta(smem_addr(&tempty[1]), 0) : 0u;
     bool aux_inflight = false;
     auto load_aux = [&](int item) {
       const TileCoord tc =
@@ -847,15 +496,15 @@ __global__ void __launch_bounds__(kPairThreads, 1)
 #pragma unroll
       for (int c = 0; c < Cfg::kChunks; ++c)
         tma_load_3d(sOut + c * Cfg::kOutChunkBytes, &tmap_aux, aux_full,
-                    tc.tn * kPairN + c * kChunkCols,
-                    tc.tm * kPairM + static_cast<int>(rank) * kHalf, tc.b);
+                    tc.tn * kTileN + c * kChunkCols,
+                    tc.tm * kTileM + static_cast<int>(rank) * kHalf, tc.b);
       aux_inflight = true;
     };
     auto release_accumulator = [&](uint32_t acc) {
       tc_fence_before();
       __syncwarp();
       if (lane == 0) {
-        if (rank == 0)
+        if (PAIR == 1 || rank == 0)
           mbar_arrive(&tempty[acc]);
         else
           mbar_arrive_cluster(acc ? tempty_leader1 : tempty_leader0);
@@ -888,9 +537,9 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       if constexpr (Cfg::kAux) (void)mbar_try_wait(aux_full, t & 1u);
       tc_fence_after();
       const bool mirror = kSym && tc.tm != tc.tn;
-      const int row0 = tc.tm * kPairM + static_cast<int>(rank) * kHalf;
-      const int col0 = tc.tn * kPairN;
-      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * kPairN;
+      const int row0 = tc.tm * kTileM + static_cast<int>(rank) * kHalf;
+      const int col0 = tc.tn * kTileN;
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * kTileN;
       bool reduce = false;
       if (p.splits > 1) {
         // Split-K: publish this split's partial band; the last split of the
@@ -901,7 +550,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
         // so the 32 lanes of a warp (consecutive rows) write 512
         // contiguous bytes per store.
         float4* mine = reinterpret_cast<float4*>(
-                           p.partial + (static_cast<size_t>(item) * 2 + rank) * (kHalf * kPairN)) +
+                           p.partial + (static_cast<size_t>(item) * PAIR + rank) * Cfg::kBandFloats) +
                        row;
 #pragma unroll 1
         for (int c = 0; c < Cfg::kChunks; ++c) {
@@ -917,7 +566,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
         __threadfence();
         named_barrier(1, kPairEpiThreads);
         if (leader) {
-          uint32_t* counter = p.counters + static_cast<size_t>(tile) * 2 + rank;
+          uint32_t* counter = p.counters + static_cast<size_t>(tile) * PAIR + rank;
           const uint32_t arrived = atomicAdd(counter, 1u) + 1u;
           const bool last = arrived == static_cast<uint32_t>(p.splits);
           if (last) atomicExch(counter, 0u);  // ready for the next launch
@@ -961,10 +610,10 @@ __global__ void __launch_bounds__(kPairThreads, 1)
           // split's partial (this split's own from tensor memory); all
           // splits' loads of a quarter chunk are issued before the adds.
           const float4* band0 = reinterpret_cast<const float4*>(
-                                    p.partial + static_cast<size_t>(tile) * p.splits * 2 *
-                                                    (kHalf * kPairN)) +
-                                static_cast<size_t>(rank) * (kHalf * kPairN / 4) + row;
-          const size_t split_stride = 2 * (kHalf * kPairN / 4);  // float4 per split item
+                                    p.partial + static_cast<size_t>(tile) * p.splits * PAIR *
+                                                    Cfg::kBandFloats) +
+                                static_cast<size_t>(rank) * (Cfg::kBandFloats / 4) + row;
+          const size_t split_stride = PAIR * (Cfg::kBandFloats / 4);  // float4 per split item
 #pragma unroll
           for (int g = 0; g < 2; ++g) {
             float4 parts[kMaxSplits][4];
@@ -1036,10 +685,13 @@ __global__ void __launch_bounds__(kPairThreads, 1)
 
   tc_fence_before();
   __syncthreads();
-  cluster_sync();  // the leader's MMAs are done with both CTAs' memory
+  if constexpr (PAIR == 2) cluster_sync();  // the leader's MMAs are done with both CTAs
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc_pair(tmem_base, Cfg::kTmemCols);
+    if constexpr (PAIR == 2)
+      tmem_dealloc_pair(tmem_base, Cfg::kTmemCols);
+    else
+      tmem_dealloc(tmem_base, Cfg::kTmemCols);
   }
 }
 
@@ -1461,14 +1113,14 @@ namespace {
 std::atomic<uint64_t> g_launch_count{0};
 
 constexpr int kMaxDevices = 64;
-constexpr int kNumInstances = 12;
+constexpr int kNumInstances = 8;
 
 struct DeviceState {
   std::once_flag once;
   int sms = 0;
   int cc_major = 0, cc_minor = 0;
   bool smem_attr_set[kNumInstances] = {};
-  int pair_capacity[kNumInstances] = {};  // co-resident 2-CTA clusters
+  int capacity[kNumInstances] = {};  // tiles worked on at once (tile_capacity)
 };
 DeviceState g_devices[kMaxDevices];
 std::mutex g_attr_mutex;
@@ -1536,52 +1188,23 @@ bool aligned16(const void* p) {
   return (reinterpret_cast<uintptr_t>(p) & 15u) == 0;
 }
 
-struct TensorMaps {
-  CUtensorMap a, b, aux, out;
-};
-
-template <int BN, int KIND>
-int launch_gemm(DeviceState* st, int instance, const TensorMaps& maps,
-                const EpiParams& p, cudaStream_t stream) {
-  auto kern = polar_gemm_kernel<BN, KIND>;
-  const uint32_t smem = Config<BN, KIND>::kSmemBytes;
-  if (!st->smem_attr_set[instance]) {
-    std::lock_guard<std::mutex> lock(g_attr_mutex);
-    if (!st->smem_attr_set[instance]) {
-      cudaError_t e = cudaFuncSetAttribute(
-          kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-      if (e != cudaSuccess) return static_cast<int>(e);
-      st->smem_attr_set[instance] = true;
-    }
-  }
-  const int grid = p.total_tiles < st->sms ? p.total_tiles : st->sms;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(grid, 1, 1);
-  cfg.blockDim = dim3(kThreads, 1, 1);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  cudaError_t e =
-      cudaLaunchKernelEx(&cfg, kern, maps.a, maps.b, maps.aux, maps.out, p);
-  if (e != cudaSuccess) return static_cast<int>(e);
-  g_launch_count.fetch_add(1, std::memory_order_relaxed);
-  return MUON_POLAR_OK;
-}
-
 // Rows of the square A / P buffers: a multiple of the 256-row pair tile.
 int64_t padded_rows(int64_t m) { return (m + kPairM - 1) / kPairM * kPairM; }
 
-struct PairMaps {
+struct TileMaps {
   CUtensorMap a, b, aux, out, mir;
 };
 
+// Slot of (KIND, PAIR) in the per-device caches.
+template <int KIND, int PAIR>
+constexpr int instance_of() {
+  return (PAIR - 1) * 4 + KIND;
+}
+static_assert(instance_of<kApply, 2>() < kNumInstances, "instance slots");
+
 // Kernel choice: 0 = by size (CTA-pair 256x256 tiles when a launch has at
-// least half as many pair tiles as the device runs pairs at once, else the
-// single-CTA 128-row kernels, which keep more SMs busy on small problems),
+// least half as many pair tiles as the device runs pairs at once, else
+// single-CTA 128x128 tiles, which keep more SMs busy on small problems),
 // 1 = always CTA pairs, 2 = never.  Initial value from MUON_POLAR_PAIR.
 std::atomic<int> g_policy{[] {
   const char* s = std::getenv("MUON_POLAR_PAIR");
@@ -1597,40 +1220,34 @@ bool use_pairs(int64_t pair_tiles, int capacity) {
   return 2 * pair_tiles >= capacity;
 }
 
-// Split-K of the CTA-pair symmetric kernels: when a problem has fewer
-// 256 x 256 tiles than there are SM pairs, each tile's K range is cut into
-// up to kMaxSplits work items.  Scratch layout: kCounterBytes of arrival
-// counters (zero between launches) followed by the fp32 partials.
+// Split-K of the symmetric kinds: when a problem has fewer tiles than the
+// device works on at once, each tile's K range is cut into up to kMaxSplits
+// work items.  Scratch layout: kCounterBytes of arrival counters (one per
+// tile and CTA band, zero between launches) followed by the fp32 partial
+// bands, PAIR bands of 128 x tile-width floats per item.
 constexpr size_t kCounterBytes = 1024;
-constexpr size_t kPartialItemBytes = 2ull * kHalf * kPairN * sizeof(float);
 
-int choose_splits(int64_t tiles, int64_t k_blocks, int pairs) {
-  if (tiles <= 0 || tiles * 2 > static_cast<int64_t>(kCounterBytes / 4)) return 1;
-  int64_t s = pairs / tiles;
+template <int PAIR>
+constexpr size_t partial_item_bytes() {
+  return static_cast<size_t>(PAIR) * kHalf * PairCfg<kGramBf16, PAIR>::kTileN * sizeof(float);
+}
+constexpr size_t kPartialItemBytes = partial_item_bytes<2>();
+
+// `units`: tiles the device works on at once (CTA pairs, or single CTAs).
+template <int PAIR>
+int choose_splits(int64_t tiles, int64_t k_blocks, int units) {
+  if (tiles <= 0 || tiles * PAIR > static_cast<int64_t>(kCounterBytes / 4)) return 1;
+  int64_t s = units / tiles;
   if (s > kMaxSplits) s = kMaxSplits;
   if (s > k_blocks / 2) s = k_blocks / 2;
   return s < 2 ? 1 : static_cast<int>(s);
 }
 
+template <int PAIR>
 size_t split_scratch_bytes(int64_t tiles, int splits) {
-  return splits > 1 ? kCounterBytes + static_cast<size_t>(tiles) * splits * kPartialItemBytes
+  return splits > 1 ? kCounterBytes + static_cast<size_t>(tiles) * splits *
+                                          partial_item_bytes<PAIR>()
                     : 0;
-}
-
-// Applies split-K to `p` if the scratch buffer allows it; `pairs` is the
-// number of CTA pairs the device runs at once.
-void plan_splits(EpiParams& p, void* scratch, size_t scratch_bytes, int pairs) {
-  p.splits = 1;
-  p.total_items = p.total_tiles;
-  p.partial = nullptr;
-  p.counters = nullptr;
-  if (scratch == nullptr || !aligned16(scratch)) return;
-  const int s = choose_splits(p.total_tiles, p.k_blocks, pairs);
-  if (s < 2 || split_scratch_bytes(p.total_tiles, s) > scratch_bytes) return;
-  p.splits = s;
-  p.total_items = p.total_tiles * s;
-  p.counters = static_cast<uint32_t*>(scratch);
-  p.partial = reinterpret_cast<float*>(static_cast<uint8_t*>(scratch) + kCounterBytes);
 }
 
 void plan_no_splits(EpiParams& p) {
@@ -1640,72 +1257,95 @@ void plan_no_splits(EpiParams& p) {
   p.counters = nullptr;
 }
 
-// How many clusters of two CTAs of this kernel the device runs at once (a
-// tcgen05 CTA pair needs both SMs of a TPC; TPCs with one usable SM cannot
-// host one), after raising the kernel's shared-memory limit.  Cached.
-template <int KIND>
-int pair_capacity(DeviceState* st, int instance, int* capacity) {
-  if (st->pair_capacity[instance] > 0) {
-    *capacity = st->pair_capacity[instance];
+// Applies split-K to `p` if the scratch buffer allows it.
+template <int PAIR>
+void plan_splits(EpiParams& p, void* scratch, size_t scratch_bytes, int units) {
+  plan_no_splits(p);
+  if (scratch == nullptr || !aligned16(scratch)) return;
+  const int s = choose_splits<PAIR>(p.total_tiles, p.k_blocks, units);
+  if (s < 2 || split_scratch_bytes<PAIR>(p.total_tiles, s) > scratch_bytes) return;
+  p.splits = s;
+  p.total_items = p.total_tiles * s;
+  p.counters = static_cast<uint32_t*>(scratch);
+  p.partial = reinterpret_cast<float*>(static_cast<uint8_t*>(scratch) + kCounterBytes);
+}
+
+// How many tiles of polar_tile_kernel<KIND, PAIR> the device works on at
+// once, after raising the kernel's shared-memory limit: co-resident clusters
+// of two CTAs for PAIR = 2 (a tcgen05 CTA pair needs both SMs of a TPC; a TPC
+// with one usable SM cannot host one), co-resident CTAs for PAIR = 1.
+// Cached per device.
+template <int KIND, int PAIR>
+int tile_capacity(DeviceState* st, int* capacity) {
+  constexpr int inst = instance_of<KIND, PAIR>();
+  std::lock_guard<std::mutex> lock(g_attr_mutex);
+  if (st->capacity[inst] > 0) {
+    *capacity = st->capacity[inst];
     return MUON_POLAR_OK;
   }
-  std::lock_guard<std::mutex> lock(g_attr_mutex);
-  auto kern = polar_pair_kernel<KIND>;
-  const uint32_t smem = PairCfg<KIND>::kSmemBytes;
-  if (!st->smem_attr_set[instance]) {
-    cudaError_t e = cudaFuncSetAttribute(
-        kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  auto kern = polar_tile_kernel<KIND, PAIR>;
+  const uint32_t smem = PairCfg<KIND, PAIR>::kSmemBytes;
+  if (!st->smem_attr_set[inst]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return static_cast<int>(e);
-    st->smem_attr_set[instance] = true;
+    st->smem_attr_set[inst] = true;
   }
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(2 * (st->sms / 2), 1, 1);
-  cfg.blockDim = dim3(kPairThreads, 1, 1);
-  cfg.dynamicSmemBytes = smem;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 2;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  int clusters = 0;
-  cudaError_t e = cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg);
-  if (e != cudaSuccess || clusters <= 0) {
-    (void)cudaGetLastError();
-    clusters = st->sms / 2;
+  int units = 0;
+  if constexpr (PAIR == 2) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * (st->sms / 2), 1, 1);
+    cfg.blockDim = dim3(kPairThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaOccupancyMaxActiveClusters(&units, kern, &cfg) != cudaSuccess || units <= 0) {
+      (void)cudaGetLastError();
+      units = st->sms / 2;
+    }
+    if (units > st->sms / 2) units = st->sms / 2;
+  } else {
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kPairThreads, smem) !=
+            cudaSuccess ||
+        per_sm <= 0) {
+      (void)cudaGetLastError();
+      per_sm = 1;
+    }
+    units = per_sm * st->sms;
   }
-  if (clusters > st->sms / 2) clusters = st->sms / 2;
-  st->pair_capacity[instance] = clusters;
-  *capacity = clusters;
+  st->capacity[inst] = units;
+  *capacity = units;
   return MUON_POLAR_OK;
 }
 
-template <int KIND>
-int launch_pair(DeviceState* st, int instance, const PairMaps& maps,
-                const EpiParams& p, cudaStream_t stream) {
-  auto kern = polar_pair_kernel<KIND>;
-  const uint32_t smem = PairCfg<KIND>::kSmemBytes;
-  int max_pairs = 0;
-  int rc = pair_capacity<KIND>(st, instance, &max_pairs);
+template <int KIND, int PAIR>
+int launch_tile(DeviceState* st, const TileMaps& maps, const EpiParams& p,
+                cudaStream_t stream) {
+  int units = 0;
+  int rc = tile_capacity<KIND, PAIR>(st, &units);
   if (rc != MUON_POLAR_OK) return rc;
-  const int pairs = p.total_items < max_pairs ? p.total_items : max_pairs;
+  const int ctas = PAIR * (p.total_items < units ? p.total_items : units);
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(2 * pairs, 1, 1);
+  cfg.gridDim = dim3(ctas, 1, 1);
   cfg.blockDim = dim3(kPairThreads, 1, 1);
-  cfg.dynamicSmemBytes = smem;
+  cfg.dynamicSmemBytes = PairCfg<KIND, PAIR>::kSmemBytes;
   cfg.stream = stream;
   cudaLaunchAttribute attr[2];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 2;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = 2;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 2;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, maps.a, maps.b, maps.aux,
-                                     maps.out, maps.mir, p);
+  cfg.numAttrs = PAIR == 2 ? 2 : 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, polar_tile_kernel<KIND, PAIR>, maps.a, maps.b,
+                                     maps.aux, maps.out, maps.mir, p);
   if (e != cudaSuccess) return static_cast<int>(e);
   g_launch_count.fetch_add(1, std::memory_order_relaxed);
   return MUON_POLAR_OK;
@@ -1724,17 +1364,68 @@ int check_x_args(const void* x, int64_t batch, int64_t m, int64_t n,
 // Square [batch][mp][mp] buffer, bf16 or fp32, boxes of `box_rows` rows x
 // 128 bytes.
 int encode_square(CUtensorMap* map, const void* base, int64_t batch, int64_t mp,
-                  bool f32, uint32_t box_rows = kBM) {
+                  bool f32, uint32_t box_rows) {
   return f32 ? encode_3d(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, base, mp, mp,
                          batch, mp, mp * mp, 32, box_rows)
              : encode_3d(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, mp, mp,
-                         batch, mp, mp * mp, kBK, box_rows);
+                         batch, mp, mp * mp, kAtom, box_rows);
 }
 
+// Upper-triangle tile grid of a symmetric kind: d x d tiles of kHalf * PAIR
+// rows per matrix, d (d + 1) / 2 of them computed.
+template <int PAIR>
+void sym_grid(EpiParams& p, int64_t batch, int64_t mp) {
+  const int64_t d = mp / (kHalf * PAIR);
+  p.tiles_m = static_cast<int32_t>(d);
+  p.tiles_n = static_cast<int32_t>(d);
+  p.tiles_per_batch = static_cast<int32_t>(d * (d + 1) / 2);
+  p.total_tiles = static_cast<int32_t>(d * (d + 1) / 2 * batch);
+}
+
+// Kernel (1) on one engine.  `fixed_scratch`: the scratch is a fixed buffer
+// that keeps the previous call's contents -- a plan that needs more than it
+// holds is refused, and the arrival counters are cleared before the launch.
+template <int KIND, int PAIR>
+int gram_launch(DeviceState* st, const void* x, void* gram, int64_t batch, int64_t m,
+                int64_t n, int64_t ldx, void* scratch, size_t scratch_bytes,
+                bool fixed_scratch, cudaStream_t stream) {
+  const int64_t mp = padded_rows(m);
+  int units = 0;
+  int rc = tile_capacity<KIND, PAIR>(st, &units);
+  if (rc != MUON_POLAR_OK) return rc;
+  TileMaps tm;
+  // X: rows beyond m and columns beyond n read as zero.
+  rc = encode_3d(&tm.a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, x, n, m, batch, ldx, m * ldx,
+                 kAtom, kHalf);
+  if (rc != MUON_POLAR_OK) return rc;
+  tm.b = tm.a;
+  tm.aux = tm.a;
+  rc = encode_square(&tm.out, gram, batch, mp, KIND == kGramF32, kHalf);
+  if (rc != MUON_POLAR_OK) return rc;
+  rc = encode_square(&tm.mir, gram, batch, mp, KIND == kGramF32, kChunkCols);
+  if (rc != MUON_POLAR_OK) return rc;
+  EpiParams p = {};
+  sym_grid<PAIR>(p, batch, mp);
+  p.k_blocks = static_cast<int32_t>(pair_k_blocks<KIND>(n));
+  if (fixed_scratch &&
+      split_scratch_bytes<PAIR>(p.total_tiles,
+                                choose_splits<PAIR>(p.total_tiles, p.k_blocks, units)) >
+          scratch_bytes)
+    return MUON_POLAR_ERR_STATIC_SCRATCH;
+  plan_splits<PAIR>(p, scratch, scratch_bytes, units);
+  if (fixed_scratch && p.splits > 1) {
+    cudaError_t e = cudaMemsetAsync(scratch, 0, kCounterBytes, stream);
+    if (e != cudaSuccess) return static_cast<int>(e);
+  }
+  return launch_tile<KIND, PAIR>(st, tm, p, stream);
+}
+
+// `fixed_scratch` callers always run the CTA-pair engine (the size of their
+// buffer is stated in pair split items).
 template <int KIND>
 int gram_impl(const void* x, void* gram, int64_t batch, int64_t m, int64_t n,
               int64_t ldx, void* scratch, size_t scratch_bytes,
-              cudaStream_t stream) {
+              cudaStream_t stream, bool fixed_scratch = false) {
   int rc = check_x_args(x, batch, m, n, ldx);
   if (rc != MUON_POLAR_OK) return rc;
   if (gram == nullptr) return MUON_POLAR_ERR_INVALID_ARGUMENT;
@@ -1742,109 +1433,61 @@ int gram_impl(const void* x, void* gram, int64_t batch, int64_t m, int64_t n,
   DeviceState* st = nullptr;
   rc = current_device_state(&st);
   if (rc != MUON_POLAR_OK) return rc;
-  const int64_t mp = padded_rows(m);
-  const int64_t d = mp / kBM;
-  const int64_t tiles_per_batch = d * (d + 1) / 2;
-  if (tiles_per_batch * batch > INT32_MAX) return MUON_POLAR_ERR_INVALID_ARGUMENT;
-  const int64_t dp = mp / kPairM;
-  const int64_t tp = dp * (dp + 1) / 2;
+  const int64_t d = padded_rows(m) / kHalf;
+  if (d * (d + 1) / 2 * batch > INT32_MAX) return MUON_POLAR_ERR_INVALID_ARGUMENT;
+  const int64_t dp = padded_rows(m) / kPairM;
   int pairs = 0;
-  rc = pair_capacity<KIND>(st, 5 + KIND, &pairs);
+  rc = tile_capacity<KIND, 2>(st, &pairs);
   if (rc != MUON_POLAR_OK) return rc;
-  if (use_pairs(tp * batch, pairs)) {
-    PairMaps pm;
-    rc = encode_3d(&pm.a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, x, n, m, batch,
-                   ldx, m * ldx, kBK, kHalf);
-    if (rc != MUON_POLAR_OK) return rc;
-    pm.b = pm.a;
-    pm.aux = pm.a;
-    rc = encode_square(&pm.out, gram, batch, mp, KIND == kGramF32, kHalf);
-    if (rc != MUON_POLAR_OK) return rc;
-    rc = encode_square(&pm.mir, gram, batch, mp, KIND == kGramF32, kChunkCols);
-    if (rc != MUON_POLAR_OK) return rc;
-    EpiParams p = {};
-    p.tiles_m = static_cast<int32_t>(dp);
-    p.tiles_n = static_cast<int32_t>(dp);
-    p.tiles_per_batch = static_cast<int32_t>(tp);
-    p.total_tiles = static_cast<int32_t>(tp * batch);
-    p.k_blocks = static_cast<int32_t>(pair_k_blocks<KIND>(n));
-    plan_splits(p, scratch, scratch_bytes, pairs);
-    return launch_pair<KIND>(st, 5 + KIND, pm, p, stream);
-  }
-  TensorMaps maps;
-  // X: rows beyond m and columns beyond n read as zero.
-  rc = encode_3d(&maps.a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, x, n, m, batch,
-                 ldx, m * ldx, kBK, kBM);
+  if (fixed_scratch || use_pairs(dp * (dp + 1) / 2 * batch, pairs))
+    return gram_launch<KIND, 2>(st, x, gram, batch, m, n, ldx, scratch, scratch_bytes,
+                                fixed_scratch, stream);
+  return gram_launch<KIND, 1>(st, x, gram, batch, m, n, ldx, scratch, scratch_bytes,
+                              fixed_scratch, stream);
+}
+
+template <int PAIR>
+int poly_launch(DeviceState* st, const void* gram, void* poly, int64_t batch, int64_t mp,
+                float b, float c, void* scratch, size_t scratch_bytes, cudaStream_t stream) {
+  int units = 0;
+  int rc = tile_capacity<kPoly, PAIR>(st, &units);
   if (rc != MUON_POLAR_OK) return rc;
-  maps.b = maps.a;
-  maps.aux = maps.a;
-  rc = encode_square(&maps.out, gram, batch, mp, KIND == kGramF32);
+  TileMaps tm;
+  rc = encode_square(&tm.a, gram, batch, mp, false, kHalf);
+  if (rc != MUON_POLAR_OK) return rc;
+  tm.b = tm.a;
+  tm.aux = tm.a;
+  rc = encode_square(&tm.out, poly, batch, mp, false, kHalf);
+  if (rc != MUON_POLAR_OK) return rc;
+  rc = encode_square(&tm.mir, poly, batch, mp, false, kChunkCols);
   if (rc != MUON_POLAR_OK) return rc;
   EpiParams p = {};
-  p.tiles_m = static_cast<int32_t>(d);
-  p.tiles_n = static_cast<int32_t>(d);
-  p.tiles_per_batch = static_cast<int32_t>(tiles_per_batch);
-  p.total_tiles = static_cast<int32_t>(tiles_per_batch * batch);
-  p.k_blocks = static_cast<int32_t>((n + kBK - 1) / kBK);
-  plan_no_splits(p);
-  return launch_gemm<128, KIND>(st, KIND, maps, p, stream);
+  sym_grid<PAIR>(p, batch, mp);
+  p.k_blocks = static_cast<int32_t>(pair_k_blocks<kPoly>(mp));
+  p.coef_b = b;
+  p.coef_c = c;
+  plan_splits<PAIR>(p, scratch, scratch_bytes, units);
+  return launch_tile<kPoly, PAIR>(st, tm, p, stream);
 }
 
 int poly_impl(const void* gram, void* poly, int64_t batch, int64_t mp, float b,
               float c, void* scratch, size_t scratch_bytes, cudaStream_t stream) {
   if (gram == nullptr || poly == nullptr || batch <= 0 || mp <= 0 ||
-      (mp % kBM) != 0 || batch > INT32_MAX || mp > (1 << 24))
+      (mp % kHalf) != 0 || batch > INT32_MAX || mp > (1 << 24))
     return MUON_POLAR_ERR_INVALID_ARGUMENT;
   if (!aligned16(gram) || !aligned16(poly)) return MUON_POLAR_ERR_ALIGNMENT;
   DeviceState* st = nullptr;
   int rc = current_device_state(&st);
   if (rc != MUON_POLAR_OK) return rc;
-  const int64_t d = mp / kBM;
-  const int64_t tiles_per_batch = d * (d + 1) / 2;
-  if (tiles_per_batch * batch > INT32_MAX) return MUON_POLAR_ERR_INVALID_ARGUMENT;
+  const int64_t d = mp / kHalf;
+  if (d * (d + 1) / 2 * batch > INT32_MAX) return MUON_POLAR_ERR_INVALID_ARGUMENT;
   const int64_t dp = mp / kPairM;
-  const int64_t tp = dp * (dp + 1) / 2;
   int pairs = 0;
-  rc = pair_capacity<kPoly>(st, 5 + kPoly, &pairs);
+  rc = tile_capacity<kPoly, 2>(st, &pairs);
   if (rc != MUON_POLAR_OK) return rc;
-  if ((mp % kPairM) == 0 && use_pairs(tp * batch, pairs)) {
-    PairMaps pm;
-    rc = encode_square(&pm.a, gram, batch, mp, false, kHalf);
-    if (rc != MUON_POLAR_OK) return rc;
-    pm.b = pm.a;
-    pm.aux = pm.a;
-    rc = encode_square(&pm.out, poly, batch, mp, false, kHalf);
-    if (rc != MUON_POLAR_OK) return rc;
-    rc = encode_square(&pm.mir, poly, batch, mp, false, kChunkCols);
-    if (rc != MUON_POLAR_OK) return rc;
-    EpiParams p = {};
-    p.tiles_m = static_cast<int32_t>(dp);
-    p.tiles_n = static_cast<int32_t>(dp);
-    p.tiles_per_batch = static_cast<int32_t>(tp);
-    p.total_tiles = static_cast<int32_t>(tp * batch);
-    p.k_blocks = static_cast<int32_t>(pair_k_blocks<kPoly>(mp));
-    p.coef_b = b;
-    p.coef_c = c;
-    plan_splits(p, scratch, scratch_bytes, pairs);
-    return launch_pair<kPoly>(st, 5 + kPoly, pm, p, stream);
-  }
-  TensorMaps maps;
-  rc = encode_square(&maps.a, gram, batch, mp, false);
-  if (rc != MUON_POLAR_OK) return rc;
-  maps.b = maps.a;
-  maps.aux = maps.a;
-  rc = encode_square(&maps.out, poly, batch, mp, false);
-  if (rc != MUON_POLAR_OK) return rc;
-  EpiParams p = {};
-  p.tiles_m = static_cast<int32_t>(d);
-  p.tiles_n = static_cast<int32_t>(d);
-  p.tiles_per_batch = static_cast<int32_t>(tiles_per_batch);
-  p.total_tiles = static_cast<int32_t>(tiles_per_batch * batch);
-  p.k_blocks = static_cast<int32_t>(mp / kBK);
-  p.coef_b = b;
-  p.coef_c = c;
-  plan_no_splits(p);
-  return launch_gemm<128, kPoly>(st, 2, maps, p, stream);
+  if ((mp % kPairM) == 0 && use_pairs(dp * (dp + 1) / 2 * batch, pairs))
+    return poly_launch<2>(st, gram, poly, batch, mp, b, c, scratch, scratch_bytes, stream);
+  return poly_launch<1>(st, gram, poly, batch, mp, b, c, scratch, scratch_bytes, stream);
 }
 
 // Host-side fp32 -> bf16 round-to-nearest-even, the same rule as the
@@ -1858,14 +1501,41 @@ float round_to_bf16(float v) {
   return out;
 }
 
-int apply_bn_override() {
-  static int value = [] {
-    const char* s = std::getenv("MUON_POLAR_APPLY_BN");
-    if (s == nullptr) return 0;
-    const int v = std::atoi(s);
-    return (v == 128 || v == 256) ? v : 0;
-  }();
-  return value;
+template <int PAIR>
+int apply_launch(DeviceState* st, const void* poly, const void* x, void* y, int64_t batch,
+                 int64_t m, int64_t n, int64_t ldx, int64_t ldy, float a,
+                 cudaStream_t stream) {
+  using Cfg = PairCfg<kApply, PAIR>;
+  const int64_t mp = padded_rows(m);
+  const int64_t tiles_m = (m + Cfg::kTileM - 1) / Cfg::kTileM;
+  const int64_t tiles_n = (n + Cfg::kTileN - 1) / Cfg::kTileN;
+  if (tiles_m * tiles_n * batch > INT32_MAX) return MUON_POLAR_ERR_INVALID_ARGUMENT;
+  TileMaps tm;
+  int rc = encode_square(&tm.a, poly, batch, mp, false, kHalf);
+  if (rc != MUON_POLAR_OK) return rc;
+  // X as the B operand: rows are K, a 64-column box is the MN extent.
+  rc = encode_3d(&tm.b, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, x, n, m, batch, ldx, m * ldx,
+                 kAtom, Cfg::kBK);
+  if (rc != MUON_POLAR_OK) return rc;
+  // X as the epilogue input tile, Y as the output tile (rows >= m and
+  // columns >= n are neither read nor written).
+  rc = encode_3d(&tm.aux, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, x, n, m, batch, ldx, m * ldx,
+                 kAtom, kHalf);
+  if (rc != MUON_POLAR_OK) return rc;
+  rc = encode_3d(&tm.out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, y, n, m, batch, ldy, m * ldy,
+                 kAtom, kHalf);
+  if (rc != MUON_POLAR_OK) return rc;
+  tm.mir = tm.out;
+  EpiParams p = {};
+  p.tiles_m = static_cast<int32_t>(tiles_m);
+  p.tiles_n = static_cast<int32_t>(tiles_n);
+  p.tiles_per_batch = static_cast<int32_t>(tiles_m * tiles_n);
+  p.total_tiles = static_cast<int32_t>(tiles_m * tiles_n * batch);
+  // P's columns >= m are zero and X's rows >= m read as zero: stop at m.
+  p.k_blocks = static_cast<int32_t>(pair_k_blocks<kApply>(m));
+  p.alpha = round_to_bf16(a);
+  plan_no_splits(p);
+  return launch_tile<kApply, PAIR>(st, tm, p, stream);
 }
 
 int apply_impl(const void* poly, const void* x, void* y, int64_t batch,
@@ -1880,73 +1550,12 @@ int apply_impl(const void* poly, const void* x, void* y, int64_t batch,
   DeviceState* st = nullptr;
   rc = current_device_state(&st);
   if (rc != MUON_POLAR_OK) return rc;
-  const int64_t mp = padded_rows(m);
   int pairs = 0;
-  rc = pair_capacity<kApply>(st, 5 + kApply, &pairs);
+  rc = tile_capacity<kApply, 2>(st, &pairs);
   if (rc != MUON_POLAR_OK) return rc;
-  if (use_pairs((mp / kPairM) * ((n + kPairN - 1) / kPairN) * batch, pairs)) {
-    const int64_t tm = mp / kPairM;
-    const int64_t tn = (n + kPairN - 1) / kPairN;
-    if (tm * tn * batch > INT32_MAX) return MUON_POLAR_ERR_INVALID_ARGUMENT;
-    PairMaps pm;
-    rc = encode_square(&pm.a, poly, batch, mp, false, kHalf);
-    if (rc != MUON_POLAR_OK) return rc;
-    rc = encode_3d(&pm.b, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, x, n, m, batch,
-                   ldx, m * ldx, 64, PairCfg<kApply>::kBK);
-    if (rc != MUON_POLAR_OK) return rc;
-    rc = encode_3d(&pm.aux, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, x, n, m, batch,
-                   ldx, m * ldx, 64, kHalf);
-    if (rc != MUON_POLAR_OK) return rc;
-    rc = encode_3d(&pm.out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, y, n, m, batch,
-                   ldy, m * ldy, 64, kHalf);
-    if (rc != MUON_POLAR_OK) return rc;
-    pm.mir = pm.out;
-    EpiParams p = {};
-    p.tiles_m = static_cast<int32_t>(tm);
-    p.tiles_n = static_cast<int32_t>(tn);
-    p.tiles_per_batch = static_cast<int32_t>(tm * tn);
-    p.total_tiles = static_cast<int32_t>(tm * tn * batch);
-    p.k_blocks = static_cast<int32_t>(pair_k_blocks<kApply>(m));
-    p.alpha = round_to_bf16(a);
-    plan_no_splits(p);
-    return launch_pair<kApply>(st, 5 + kApply, pm, p, stream);
-  }
-  const int64_t tiles_m = mp / kBM;
-  // Tile width: fewest rounds of BN-column work over the SMs.
-  const int64_t t128 = tiles_m * ((n + 127) / 128) * batch;
-  const int64_t t256 = tiles_m * ((n + 255) / 256) * batch;
-  const int64_t cost128 = (t128 + st->sms - 1) / st->sms * 128;
-  const int64_t cost256 = (t256 + st->sms - 1) / st->sms * 256;
-  int bn = (n > 128 && cost256 <= cost128) ? 256 : 128;
-  if (apply_bn_override() != 0) bn = apply_bn_override();
-  const int64_t tiles_n = (n + bn - 1) / bn;
-  if (tiles_m * tiles_n * batch > INT32_MAX) return MUON_POLAR_ERR_INVALID_ARGUMENT;
-  TensorMaps maps;
-  rc = encode_square(&maps.a, poly, batch, mp, false);
-  if (rc != MUON_POLAR_OK) return rc;
-  // X as the B operand: rows are K, the 64-column box is the MN extent.
-  rc = encode_3d(&maps.b, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, x, n, m, batch,
-                 ldx, m * ldx, 64, kBK);
-  if (rc != MUON_POLAR_OK) return rc;
-  // X as the epilogue input tile, Y as the output tile (rows >= m and
-  // columns >= n are neither read nor written).
-  rc = encode_3d(&maps.aux, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, x, n, m, batch,
-                 ldx, m * ldx, 64, kBM);
-  if (rc != MUON_POLAR_OK) return rc;
-  rc = encode_3d(&maps.out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, y, n, m, batch,
-                 ldy, m * ldy, 64, kBM);
-  if (rc != MUON_POLAR_OK) return rc;
-  EpiParams p = {};
-  p.tiles_m = static_cast<int32_t>(tiles_m);
-  p.tiles_n = static_cast<int32_t>(tiles_n);
-  p.tiles_per_batch = static_cast<int32_t>(tiles_m * tiles_n);
-  p.total_tiles = static_cast<int32_t>(tiles_m * tiles_n * batch);
-  // P's columns >= m are zero and X's rows >= m read as zero: stop at m.
-  p.k_blocks = static_cast<int32_t>((m + kBK - 1) / kBK);
-  p.alpha = round_to_bf16(a);
-  plan_no_splits(p);
-  if (bn == 256) return launch_gemm<256, kApply>(st, 3, maps, p, stream);
-  return launch_gemm<128, kApply>(st, 4, maps, p, stream);
+  if (use_pairs(padded_rows(m) / kPairM * ((n + kPairN - 1) / kPairN) * batch, pairs))
+    return apply_launch<2>(st, poly, x, y, batch, m, n, ldx, ldy, a, stream);
+  return apply_launch<1>(st, poly, x, y, batch, m, n, ldx, ldy, a, stream);
 }
 
 // ---------------------------------------------------------------- fused step
@@ -2131,54 +1740,19 @@ int gram_static_scratch_impl(const void* x, void* gram, int64_t batch, int64_t m
   if (rc != MUON_POLAR_OK) return rc;
   if (gram == nullptr) return MUON_POLAR_ERR_INVALID_ARGUMENT;
   if (!aligned16(gram)) return MUON_POLAR_ERR_ALIGNMENT;
-  DeviceState* st = nullptr;
-  rc = current_device_state(&st);
-  if (rc != MUON_POLAR_OK) return rc;
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return static_cast<int>(e);
+  if (dev < 0 || dev >= kMaxDevices) return MUON_POLAR_ERR_UNSUPPORTED_DEVICE;
   void* scratch = nullptr;
   rc = static_scratch_address(dev, &scratch);
   if (rc != MUON_POLAR_OK) return rc;
-
-  const int64_t mp = padded_rows(m);
-  const int64_t dp = mp / kPairM;
-  const int64_t tp = dp * (dp + 1) / 2;
-  if (tp * batch > INT32_MAX) return MUON_POLAR_ERR_INVALID_ARGUMENT;
-  int pairs = 0;
-  rc = pair_capacity<kGramBf16>(st, 5 + kGramBf16, &pairs);
-  if (rc != MUON_POLAR_OK) return rc;
-  const int64_t k_blocks = pair_k_blocks<kGramBf16>(n);
-  // The same split plan as muon_polar_gram_sm100 on the CTA-pair path with
-  // enough scratch; a plan that needs more than the static array is refused.
-  const size_t need =
-      split_scratch_bytes(tp * batch, choose_splits(tp * batch, k_blocks, pairs));
-  if (need > kStaticScratchBytes) return MUON_POLAR_ERR_STATIC_SCRATCH;
-
-  PairMaps pm;
-  rc = encode_3d(&pm.a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, x, n, m, batch, ldx,
-                 m * ldx, kBK, kHalf);
-  if (rc != MUON_POLAR_OK) return rc;
-  pm.b = pm.a;
-  pm.aux = pm.a;
-  rc = encode_square(&pm.out, gram, batch, mp, false, kHalf);
-  if (rc != MUON_POLAR_OK) return rc;
-  rc = encode_square(&pm.mir, gram, batch, mp, false, kChunkCols);
-  if (rc != MUON_POLAR_OK) return rc;
-  EpiParams p = {};
-  p.tiles_m = static_cast<int32_t>(dp);
-  p.tiles_n = static_cast<int32_t>(dp);
-  p.tiles_per_batch = static_cast<int32_t>(tp);
-  p.total_tiles = static_cast<int32_t>(tp * batch);
-  p.k_blocks = static_cast<int32_t>(k_blocks);
-  plan_splits(p, scratch, kStaticScratchBytes, pairs);
-  if (p.splits > 1) {
-    // The array keeps the previous call's contents: the arrival counters
-    // must start at zero, so clear them before every launch.
-    e = cudaMemsetAsync(scratch, 0, kCounterBytes, stream);
-    if (e != cudaSuccess) return static_cast<int>(e);
-  }
-  return launch_pair<kGramBf16>(st, 5 + kGramBf16, pm, p, stream);
+  // The split plan of muon_polar_gram_sm100 on the CTA-pair path with enough
+  // scratch; a plan that needs more than the static array is refused, and the
+  // array's arrival counters (left as the previous call left them) are
+  // cleared before the launch.
+  return gram_impl<kGramBf16>(x, gram, batch, m, n, ldx, scratch, kStaticScratchBytes, stream,
+                              /*fixed_scratch=*/true);
 }
 }  // namespace
 
@@ -2278,25 +1852,32 @@ int muon_polar_step_sm100(const void* x, void* y, void* workspace,
 
 size_t muon_polar_scratch_bytes(int64_t batch, int64_t m, int64_t n) {
   if (batch <= 0 || m <= 0 || n <= 0) return 0;
-  int pairs = 0;
+  int pairs = 0, ctas = 0;
   DeviceState* st = nullptr;
   if (current_device_state(&st) != MUON_POLAR_OK ||
-      pair_capacity<kGramBf16>(st, 5 + kGramBf16, &pairs) != MUON_POLAR_OK || pairs <= 0) {
+      tile_capacity<kGramBf16, 2>(st, &pairs) != MUON_POLAR_OK || pairs <= 0 ||
+      tile_capacity<kGramBf16, 1>(st, &ctas) != MUON_POLAR_OK || ctas <= 0) {
     (void)cudaGetLastError();
     pairs = 512;  // no usable device: the largest the split planner could use
+    ctas = 1024;
   }
   const int64_t mp = padded_rows(m);
-  const int64_t d = mp / kPairM;
-  const int64_t tiles = d * (d + 1) / 2 * batch;
   const int64_t kb_gram = pair_k_blocks<kGramF32>(n) > pair_k_blocks<kGramBf16>(n)
                               ? pair_k_blocks<kGramF32>(n)
                               : pair_k_blocks<kGramBf16>(n);
   const int64_t kb_poly = pair_k_blocks<kPoly>(mp);
-  const size_t g = split_scratch_bytes(tiles, choose_splits(tiles, kb_gram, pairs));
-  const size_t q = split_scratch_bytes(tiles, choose_splits(tiles, kb_poly, pairs));
-  const size_t need = g > q ? g : q;
-  // The fused step's dependency counters live in the counter area.
-  return need > kCounterBytes ? need : kCounterBytes;
+  const int64_t d2 = mp / kPairM, d1 = mp / kHalf;
+  const int64_t t2 = d2 * (d2 + 1) / 2 * batch, t1 = d1 * (d1 + 1) / 2 * batch;
+  // The largest plan either engine makes for kernels (1) and (2); the fused
+  // step's dependency counters live in the counter area.
+  size_t need = kCounterBytes;
+  const size_t plans[4] = {
+      split_scratch_bytes<2>(t2, choose_splits<2>(t2, kb_gram, pairs)),
+      split_scratch_bytes<2>(t2, choose_splits<2>(t2, kb_poly, pairs)),
+      split_scratch_bytes<1>(t1, choose_splits<1>(t1, kb_gram, ctas)),
+      split_scratch_bytes<1>(t1, choose_splits<1>(t1, kb_poly, ctas))};
+  for (size_t v : plans) need = v > need ? v : need;
+  return need;
 }
 
 int muon_polar_scratch_init(void* scratch, size_t scratch_bytes, void* stream) {
@@ -2377,7 +1958,7 @@ int muon_polar_device_pairs(int* pairs) {
   DeviceState* st = nullptr;
   int rc = current_device_state(&st);
   if (rc != MUON_POLAR_OK) return rc;
-  return pair_capacity<kGramBf16>(st, 5 + kGramBf16, pairs);
+  return tile_capacity<kGramBf16, 2>(st, pairs);
 }
 
 uint64_t muon_polar_launch_count(void) {
