@@ -194,10 +194,11 @@ int muon_polar_read_device_status(int device, uint32_t* flags, int clear);
 
 /* Kernel selection, process-wide; returns the previous policy (or
  * MUON_POLAR_ERR_INVALID_ARGUMENT).
- *   0  by size (default): 256 x 256 tiles on tcgen05 CTA pairs when a launch
- *      has at least half as many such tiles as the device runs pairs at once,
- *      otherwise single-CTA 128-row tiles, which keep more SMs busy;
- *   1  always CTA pairs (split-K, when scratch is given, happens only here);
+ *   0  by size (default): of 256 x 256 tiles on tcgen05 CTA pairs and
+ *      128 x 128 tiles on single CTAs, the engine with the smaller estimated
+ *      time (rounds of tiles over the device times the measured cost of the
+ *      K loop of a tile);
+ *   1  always CTA pairs;
  *   2  always single-CTA tiles.
  * The initial value comes from MUON_POLAR_PAIR (1 -> policy 1, 0 -> policy
  * 2).  Every policy computes the same mathematical result; the fp32
@@ -214,6 +215,16 @@ int muon_polar_set_kernel_policy(int policy);
  * Initial value from MUON_POLAR_FUSED (1 -> 1, 0 -> 2).  Results are the
  * same in every mode (identical bits). */
 int muon_polar_set_step_mode(int mode);
+
+/* Split-K of kernels (1) and (2) when scratch is given, process-wide;
+ * returns the previous mode (or MUON_POLAR_ERR_INVALID_ARGUMENT).
+ *   0  by size (default): only when the shorter K loops save more time than
+ *      the partial sums' round trip through L2 costs;
+ *   1  whenever the device has room for more work items than tiles;
+ *   2  never.
+ * Results are the same mathematical quantity in every mode; the fp32
+ * summation order, and so the last bit, depends on the split. */
+int muon_polar_set_split_mode(int mode);
 
 /* Number of 2-CTA clusters (tcgen05 CTA pairs) of the Gram kernel the
  * current device runs at once; the persistent grids are this many pairs. */

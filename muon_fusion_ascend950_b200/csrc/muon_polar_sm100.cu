@@ -55,12 +55,12 @@ struct EpiParams {
   float coef_b;
   float coef_c;
   float alpha;  // kApply: a already rounded to bf16
-  // Split-K (CTA-pair symmetric kinds): each tile's K range is cut into
-  // `splits` work items; item = tile * splits + split.
+  // Split-K (symmetric kinds): each tile's K range is cut into `splits`
+  // work items of (nearly) equal length; item = tile * splits + split.
   int32_t splits;
   int32_t total_items;
-  float* partial;      // [total_items][2][128][256] fp32 partial sums
-  uint32_t* counters;  // [total_tiles][2] arrivals, zero between launches
+  float* partial;      // [total_items][PAIR][128][tile width] fp32 partial sums
+  uint32_t* counters;  // [total_tiles][PAIR] arrivals, zero between launches
 };
 
 struct TileCoord {
@@ -93,6 +93,30 @@ __host__ __device__ __forceinline__ TileCoord decode_tile(int tile, bool sym,
   return t;
 }
 
+// One work item: its tile, its K range (k-blocks [kb_begin, kb_end)) and
+// its place among the tile's splits.
+struct WorkItem {
+  int tile, b, tm, tn;
+  int split, nsplit;
+  int kb_begin, kb_end;
+};
+
+__host__ __device__ __forceinline__ WorkItem decode_item(const EpiParams& p, int item,
+                                                         bool sym) {
+  WorkItem w;
+  const int tile = item / p.splits;
+  const TileCoord tc = decode_tile(tile, sym, p.tiles_m, p.tiles_n, p.tiles_per_batch);
+  w.tile = tile;
+  w.b = tc.b;
+  w.tm = tc.tm;
+  w.tn = tc.tn;
+  w.split = item - tile * p.splits;
+  w.nsplit = p.splits;
+  w.kb_begin = w.split * p.k_blocks / w.nsplit;
+  w.kb_end = (w.split + 1) * p.k_blocks / w.nsplit;
+  return w;
+}
+
 __device__ __forceinline__ uint32_t float_to_bf16_bits(float v) {
   __nv_bfloat16 h = __float2bfloat16_rn(v);
   return static_cast<uint32_t>(*reinterpret_cast<uint16_t*>(&h));
@@ -119,17 +143,24 @@ constexpr int kPairN = 256;
 constexpr int kHalf = 128;
 constexpr int kChunkCols = 64;
 constexpr int kMaxSplits = 4;  // split-K items per tile, at most
+// One 64-column chunk of a CTA band's fp32 partial sums (split-K).
+constexpr uint32_t kPartChunkBytes = 128 * 64 * 4;
 constexpr int kAtom = 64;  // bf16 elements per 128-byte swizzle row
+
 constexpr uint32_t kAtomBytes = kHalf * kAtom * 2;  // one [128 x 64] box, 16 KiB
 
-// K depth of one pipeline stage of a pair kernel (see PairCfg::kBK).
-template <int KIND>
-constexpr int pair_bk() {
-  return KIND == kGramBf16 ? 128 : 64;
+// K depth of one pipeline stage: two 128-byte swizzle atoms for single-CTA
+// tiles, one for CTA pairs.  A 128 x 128 tile's MMAs are short (64 cycles for
+// K = 16), so their per-stage handshake (wait, commit, refill) is only hidden
+// behind eight of them; a pair's 256 x 256 MMAs take twice as long, and four
+// per stage measured as fast as eight.
+template <int PAIR>
+constexpr int stage_k() {
+  return PAIR == 1 ? 128 : 64;
 }
-template <int KIND>
-constexpr int64_t pair_k_blocks(int64_t k) {
-  return (k + pair_bk<KIND>() - 1) / pair_bk<KIND>();
+template <int PAIR>
+constexpr int64_t k_blocks_of(int64_t k) {
+  return (k + stage_k<PAIR>() - 1) / stage_k<PAIR>();
 }
 
 // Shared-memory and tensor-memory plan of one CTA of polar_tile_kernel.
@@ -147,14 +178,7 @@ struct PairCfg {
   static constexpr int kChunks = kTileN / kChunkCols;
   static constexpr uint32_t kOutChunkBytes = kHalf * kChunkCols * kElem;
   static constexpr uint32_t kMirChunkBytes = kSym ? kChunkCols * kHalf * kElem : 0;
-  // K depth of a pipeline stage.  TMA ingest into one SM grows with the
-  // bytes completed per mbarrier phase (measured on B200: ~100 GB/s at 32
-  // KiB, ~130-145 GB/s at 64 KiB), but a stage is only refilled after the
-  // MMAs release it, so deep stages need room for at least three.  The bf16
-  // Gram (single-buffered epilogue, 32 KiB) gets three 64 KiB stages (K =
-  // 128); the others keep four or five 32 KiB stages (K = 64), which measured
-  // faster for them.
-  static constexpr int kBK = pair_bk<KIND>();
+  static constexpr int kBK = stage_k<PAIR>();
   // Output regions: kAux kinds keep the whole 128 x kTileN input band (updated
   // in place, one region per chunk, never reused within a tile); the Gram
   // single-buffers its chunk region.
@@ -175,7 +199,19 @@ struct PairCfg {
   static constexpr int kStagesFit =
       static_cast<int>((232448u - kFixedBytes) / kStageBytes);
   static constexpr int kStages = kStagesFit > 8 ? 8 : kStagesFit;
+  // TMA producers: two warps fill alternate stages when the stage count is
+  // even (each stage then always has the same producer, which fills it in
+  // order).  Measured on B200, one thread's loads into successive mbarrier
+  // phases reach about 90 GB/s per SM with 32 KiB phases, two threads about
+  // 150 GB/s, the per-SM limit.
+  static constexpr int kProducers = kStages % 2 == 0 ? 2 : 1;
   static constexpr uint32_t kSmemBytes = kFixedBytes + kStages * kStageBytes;
+  // Split-K stages partial sums in the pipeline stages: a whole band to
+  // publish, or two buffers of (splits - 1) chunks to reduce.
+  static constexpr uint32_t kRingBytes = kStages * kStageBytes;
+  static constexpr int kSplitsFit = 1 + static_cast<int>(kRingBytes / (2 * kPartChunkBytes));
+  static constexpr int kMaxSplitsHere = kSplitsFit < kMaxSplits ? kSplitsFit : kMaxSplits;
+  static_assert(kChunks * kPartChunkBytes <= kRingBytes, "split-K staging");
   static constexpr uint32_t kTmemCols = 2 * kTileN;
   static constexpr uint32_t kBandFloats = kHalf * kTileN;  // one CTA's fp32 band
   static_assert(kStages >= 2, "pipeline depth");
@@ -268,14 +304,18 @@ __device__ __forceinline__ void pair_epilogue_half(const EpiParams& p, uint32_t 
   }
 }
 
-// Threads of the pair kernel: warp 0 TMA producer, warp 1 MMA issuer and
-// tensor-memory owner, warps 2..9 epilogue (two per tensor-memory lane
+// Threads of the fused step kernel: warp 0 TMA producer, warp 1 MMA issuer
+// and tensor-memory owner, warps 2..9 epilogue (two per tensor-memory lane
 // quarter, each taking 32 of a chunk's 64 columns).
 constexpr int kPairThreads = 320;
 constexpr int kPairEpiThreads = 256;
+// Threads of polar_tile_kernel: the same roles plus a second TMA producer,
+// warp 10.
+constexpr int kTileThreads = 352;
+constexpr int kProducerWarp2 = 10;
 
 template <int KIND, int PAIR>
-__global__ void __launch_bounds__(kPairThreads, 1)
+__global__ void __launch_bounds__(kTileThreads, 1)
     polar_tile_kernel(const __grid_constant__ CUtensorMap tmap_a,
                       const __grid_constant__ CUtensorMap tmap_b,
                       const __grid_constant__ CUtensorMap tmap_aux,
@@ -302,7 +342,8 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
   uint64_t* aux_full = drain + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(aux_full + 1);
+  uint64_t* part_full = aux_full + 1;  // split-K partial chunks, two buffers
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(part_full + 2);
   volatile uint32_t* last_flag = tmem_slot + 1;
 
   const int warp = threadIdx.x >> 5;
@@ -323,6 +364,8 @@ __global__ void __launch_bounds__(kPairThreads, 1)
     }
     mbar_init(drain, 1);
     mbar_init(aux_full, 1);
+    mbar_init(&part_full[0], 1);
+    mbar_init(&part_full[1], 1);
     fence_mbar_init();
     prefetch_tensor_map(&tmap_a);
     prefetch_tensor_map(&tmap_b);
@@ -348,45 +391,51 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   grid_dependency_wait();
   grid_launch_dependents();
 
-  if (warp == 0) {
-    if (lane == 0) {
-      // ---------------- TMA producer (both CTAs)
+  if (warp == 0 || warp == kProducerWarp2) {
+    // (warp kProducerWarp2 idles when the stage count is odd)
+    if (lane == 0 && (warp == 0 || Cfg::kProducers == 2)) {
+      // ---------------- TMA producers (both CTAs): producer `pid` fills the
+      // stages of the pipeline iterations with it % kProducers == pid.
+      const uint32_t pid = warp == 0 ? 0u : 1u;
       uint32_t it = 0;
       bool ok = true;
       for (int item = cluster; ok && item < p.total_items; item += nclusters) {
-        const int tile = item / p.splits;
-        const int split = item - tile * p.splits;
-        const TileCoord tc =
-            decode_tile(tile, kSym, p.tiles_m, p.tiles_n, p.tiles_per_batch);
-        const int a_row = tc.tm * kTileM + static_cast<int>(rank) * kHalf;
-        const int kb_end = (split + 1) * p.k_blocks / p.splits;
-        for (int kb = split * p.k_blocks / p.splits; kb < kb_end; ++kb, ++it) {
+        const WorkItem w = decode_item(p, item, kSym);
+        // A diagonal tile of a symmetric kind multiplies a row block by
+        // itself: only the A operand is loaded, and the MMA reads it twice.
+        const bool diag = kSym && w.tm == w.tn;
+        const int a_row = w.tm * kTileM + static_cast<int>(rank) * kHalf;
+        const int b_row = w.tn * kTileN + static_cast<int>(rank) * kHalf;
+        for (int kb = w.kb_begin; kb < w.kb_end; ++kb, ++it) {
+          if (it % Cfg::kProducers != pid) continue;
           const uint32_t s = it % S;
           const uint32_t ph = (it / S) & 1u;
           if (!mbar_wait_bounded(&empty[s], ph ^ 1u)) {
             ok = false;
             break;
           }
-          if (rank == 0) mbar_arrive_expect_tx(&full[s], PAIR * Cfg::kStageBytes);
+          if (rank == 0)
+            mbar_arrive_expect_tx(&full[s], PAIR * (diag ? Cfg::kAHalfBytes : Cfg::kStageBytes));
           const uint32_t bar = PAIR == 2 ? map_to_cta(smem_addr(&full[s]), 0) : 0u;
-          const int b_row = tc.tn * kTileN + static_cast<int>(rank) * kHalf;
           // loads into this CTA's stage; PAIR = 2 counts the bytes on the
           // leader's barrier, PAIR = 1 on its own
           auto load = [&](void* dst, const CUtensorMap* map, int c0, int c1) {
             if constexpr (PAIR == 2)
-              tma_load_3d_pair(dst, map, bar, c0, c1, tc.b);
+              tma_load_3d_pair(dst, map, bar, c0, c1, w.b);
             else
-              tma_load_3d(dst, map, &full[s], c0, c1, tc.b);
+              tma_load_3d(dst, map, &full[s], c0, c1, w.b);
           };
 #pragma unroll
           for (int j = 0; j < Cfg::kBK / kAtom; ++j)
             load(sA + s * Cfg::kAHalfBytes + j * kAtomBytes, &tmap_a, kb * Cfg::kBK + j * kAtom,
                  a_row);
           if constexpr (!kBmn) {
+            if (!diag) {
 #pragma unroll
-            for (int j = 0; j < Cfg::kBK / kAtom; ++j)
-              load(sB + s * Cfg::kBHalfBytes + j * kAtomBytes, &tmap_b,
-                   kb * Cfg::kBK + j * kAtom, b_row);
+              for (int j = 0; j < Cfg::kBK / kAtom; ++j)
+                load(sB + s * Cfg::kBHalfBytes + j * kAtomBytes, &tmap_b,
+                     kb * Cfg::kBK + j * kAtom, b_row);
+            }
           } else {
             // MN-major B: one [kBK k-rows x 64 n] box per 64-column chunk
 #pragma unroll
@@ -398,9 +447,11 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       }
       if (!ok) atomicOr(&g_watchdog, MUON_POLAR_WATCHDOG_PRODUCER);
       if (rank == 0) {
-        // Drain: the pair's last loads land before the CTAs exit.
+        // Drain: the pair's last loads (this producer's stages) land before
+        // the CTAs exit.
         const uint32_t inflight = it < static_cast<uint32_t>(S) ? it : S;
         for (uint32_t i = it - inflight; i < it; ++i) {
+          if (i % Cfg::kProducers != pid) continue;
           if (!mbar_wait_bounded(&full[i % S], (i / S) & 1u)) {
             atomicOr(&g_watchdog, MUON_POLAR_WATCHDOG_DRAIN);
             break;
@@ -416,9 +467,8 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       uint32_t t = 0;
       bool ok = true;
       for (int item = cluster; ok && item < p.total_items; item += nclusters, ++t) {
-        const int split = item % p.splits;
-        const int kb_begin = split * p.k_blocks / p.splits;
-        const int kb_end = (split + 1) * p.k_blocks / p.splits;
+        const WorkItem w = decode_item(p, item, kSym);
+        const bool diag = kSym && w.tm == w.tn;
         const uint32_t acc = t & 1u;
         const uint32_t uph = (t >> 1) & 1u;
         if (!mbar_wait_bounded(&tempty[acc], uph ^ 1u)) {
@@ -427,7 +477,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * kTileN;
-        for (int kb = kb_begin; kb < kb_end; ++kb, ++it) {
+        for (int kb = w.kb_begin; kb < w.kb_end; ++kb, ++it) {
           const uint32_t s = it % S;
           const uint32_t ph = (it / S) & 1u;
           if (!mbar_wait_bounded(&full[s], ph)) {
@@ -436,7 +486,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
           }
           tc_fence_after();
           const uint32_t a_base = smem_addr(sA + s * Cfg::kAHalfBytes);
-          const uint32_t b_base = smem_addr(sB + s * Cfg::kBHalfBytes);
+          const uint32_t b_base = diag ? a_base : smem_addr(sB + s * Cfg::kBHalfBytes);
 #pragma unroll
           for (int k = 0; k < Cfg::kBK / 16; ++k) {
             // K-major: K step k lies in swizzle atom k/4 (16 KiB apart), 32
@@ -452,9 +502,9 @@ __global__ void __launch_bounds__(kPairThreads, 1)
               bd = smem_desc_sw128(b_base + koff, 16, 1024);
             }
             if constexpr (PAIR == 2)
-              umma_bf16_pair(d_tmem, ad, bd, idesc, (kb > kb_begin || k > 0) ? 1u : 0u);
+              umma_bf16_pair(d_tmem, ad, bd, idesc, (kb > w.kb_begin || k > 0) ? 1u : 0u);
             else
-              umma_bf16(d_tmem, ad, bd, idesc, (kb > kb_begin || k > 0) ? 1u : 0u);
+              umma_bf16(d_tmem, ad, bd, idesc, (kb > w.kb_begin || k > 0) ? 1u : 0u);
           }
           if constexpr (PAIR == 2) {
             umma_commit_pair(map_to_cta(smem_addr(&empty[s]), 0));
@@ -490,14 +540,13 @@ __global__ void __launch_bounds__(kPairThreads, 1)
     const uint32_t tempty_leader1 = PAIR == 2 ? map_to_cta(smem_addr(&tempty[1]), 0) : 0u;
     bool aux_inflight = false;
     auto load_aux = [&](int item) {
-      const TileCoord tc =
-          decode_tile(item / p.splits, kSym, p.tiles_m, p.tiles_n, p.tiles_per_batch);
+      const WorkItem w = decode_item(p, item, kSym);
       mbar_arrive_expect_tx(aux_full, Cfg::kChunks * Cfg::kOutChunkBytes);
 #pragma unroll
       for (int c = 0; c < Cfg::kChunks; ++c)
         tma_load_3d(sOut + c * Cfg::kOutChunkBytes, &tmap_aux, aux_full,
-                    tc.tn * kTileN + c * kChunkCols,
-                    tc.tm * kTileM + static_cast<int>(rank) * kHalf, tc.b);
+                    w.tn * kTileN + c * kChunkCols,
+                    w.tm * kTileM + static_cast<int>(rank) * kHalf, w.b);
       aux_inflight = true;
     };
     auto release_accumulator = [&](uint32_t acc) {
@@ -515,10 +564,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
     }
     uint32_t t = 0;
     for (int item = cluster; item < p.total_items; item += nclusters, ++t) {
-      const int tile = item / p.splits;
-      const int split = item - tile * p.splits;
-      const TileCoord tc =
-          decode_tile(tile, kSym, p.tiles_m, p.tiles_n, p.tiles_per_batch);
+      const WorkItem tc = decode_item(p, item, kSym);
       const uint32_t acc = t & 1u;
       const uint32_t uph = (t >> 1) & 1u;
       int ok = 1;
@@ -541,50 +587,78 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       const int col0 = tc.tn * kTileN;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * kTileN;
       bool reduce = false;
-      if (p.splits > 1) {
-        // Split-K: publish this split's partial band; the last split of the
-        // tile to arrive (per CTA band) sums all partials in split order --
-        // the same order whichever split arrives last -- and runs the
-        // epilogue.  Nobody waits for anybody.
-        // Partial band layout: float4 slots [chunk][vec 0..15][row 0..127],
-        // so the 32 lanes of a warp (consecutive rows) write 512
-        // contiguous bytes per store.
-        float4* mine = reinterpret_cast<float4*>(
-                           p.partial + (static_cast<size_t>(item) * PAIR + rank) * Cfg::kBandFloats) +
-                       row;
-#pragma unroll 1
-        for (int c = 0; c < Cfg::kChunks; ++c) {
-          uint32_t r0[32];
-          tmem_ld_32x32b_x32(t_row + c * kChunkCols + hc * 32, r0);
-          tmem_wait_ld();
-#pragma unroll
-          for (int u = 0; u < 8; ++u)
-            __stcg(mine + (c * 16 + hc * 8 + u) * kHalf,
-                   make_float4(__uint_as_float(r0[4 * u]), __uint_as_float(r0[4 * u + 1]),
-                               __uint_as_float(r0[4 * u + 2]), __uint_as_float(r0[4 * u + 3])));
+      // Other splits' partial chunks c into buffer c % 2 of the (free)
+      // pipeline stages; issued by the leader of the last split.
+      auto load_parts = [&](int c) {
+        uint64_t* bar = &part_full[c & 1];
+        mbar_arrive_expect_tx(bar, (tc.nsplit - 1) * kPartChunkBytes);
+        int o = 0;
+        for (int i = 0; i < tc.nsplit; ++i) {
+          if (i == tc.split) continue;
+          const float* src =
+              p.partial +
+              (static_cast<size_t>(tc.tile * tc.nsplit + i) * PAIR + rank) * Cfg::kBandFloats +
+              static_cast<size_t>(c) * (kPartChunkBytes / 4);
+          bulk_load(sA + ((c & 1) * (tc.nsplit - 1) + o) * kPartChunkBytes, src, kPartChunkBytes,
+                    bar);
+          ++o;
         }
-        __threadfence();
-        named_barrier(1, kPairEpiThreads);
+      };
+      if (tc.nsplit > 1) {
+        // Split-K.  A launch with splits has one work item per cluster, so
+        // once the accumulator is complete the pipeline stages are free and
+        // serve as staging for partial sums.  The split that arrives last
+        // (per CTA band) takes the others' partial bands and sums all of them
+        // in split order -- the same order whichever split is last -- and
+        // runs the epilogue; the others publish their band and leave.
+        // Partial band layout: float4 slots [chunk][vec 0..15][row 0..127],
+        // 32 KiB per chunk, moved as whole chunks by bulk copies.
+        uint32_t* ctr = p.counters + (static_cast<size_t>(tc.tile) * PAIR + rank) * 2;
         if (leader) {
-          uint32_t* counter = p.counters + static_cast<size_t>(tile) * PAIR + rank;
-          const uint32_t arrived = atomicAdd(counter, 1u) + 1u;
-          const bool last = arrived == static_cast<uint32_t>(p.splits);
-          if (last) atomicExch(counter, 0u);  // ready for the next launch
-          __threadfence();
-          *last_flag = last ? 1u : 0u;
+          if (p.total_items > nclusters) atomicOr(&g_watchdog, MUON_POLAR_WATCHDOG_EPILOGUE);
+          *last_flag = atomicAdd(ctr, 1u) + 1u == static_cast<uint32_t>(tc.nsplit) ? 1u : 0u;
         }
         named_barrier(1, kPairEpiThreads);
         reduce = *last_flag != 0u;
         if (!reduce) {
+          const uint32_t stage = smem_addr(sA) + static_cast<uint32_t>(row) * 16u;
+#pragma unroll 1
+          for (int c = 0; c < Cfg::kChunks; ++c) {
+            uint32_t r0[32];
+            tmem_ld_32x32b_x32(t_row + c * kChunkCols + hc * 32, r0);
+            tmem_wait_ld();
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+              st_shared_v4(stage + static_cast<uint32_t>((c * 16 + hc * 8 + u) * kHalf) * 16u,
+                           make_uint4(r0[4 * u], r0[4 * u + 1], r0[4 * u + 2], r0[4 * u + 3]));
+          }
           release_accumulator(acc);
-          if constexpr (Cfg::kAux) {
-            if (leader) {
-              bulk_wait_group_read<0>();
-              const int next = item + nclusters;
-              if (next < p.total_items) load_aux(next);
-            }
+          fence_proxy_async_smem();
+          named_barrier(1, kPairEpiThreads);
+          if (leader) {
+            float* dst = p.partial + (static_cast<size_t>(item) * PAIR + rank) * Cfg::kBandFloats;
+#pragma unroll
+            for (int c = 0; c < Cfg::kChunks; ++c)
+              bulk_store(dst + c * (kPartChunkBytes / 4), sA + c * kPartChunkBytes,
+                         kPartChunkBytes);
+            bulk_commit_group();
+            bulk_wait_group0();
+            fence_proxy_async_global();
+            __threadfence();
+            red_release_gpu_add(ctr + 1, 1u);
           }
           continue;
+        }
+        if (leader) {
+          // Last split: no other split touches the ticket counter again, and
+          // once every other band has been published, nor the other one.
+          ctr[0] = 0u;
+          if (!wait_counter_bounded(ctr + 1, static_cast<uint32_t>(tc.nsplit - 1)))
+            atomicOr(&g_watchdog, MUON_POLAR_WATCHDOG_EPILOGUE);
+          ctr[1] = 0u;
+          fence_proxy_async_global();
+          load_parts(0);
+          if (Cfg::kChunks > 1) load_parts(1);
         }
       }
 #pragma unroll 1
@@ -606,53 +680,49 @@ __global__ void __launch_bounds__(kPairThreads, 1)
 #pragma unroll
         for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r0[j]);
         if (reduce) {
-          // v <- sum over splits i = 0..splits-1, in that order, of the
-          // split's partial (this split's own from tensor memory); all
-          // splits' loads of a quarter chunk are issued before the adds.
-          const float4* band0 = reinterpret_cast<const float4*>(
-                                    p.partial + static_cast<size_t>(tile) * p.splits * PAIR *
-                                                    Cfg::kBandFloats) +
-                                static_cast<size_t>(rank) * (Cfg::kBandFloats / 4) + row;
-          const size_t split_stride = PAIR * (Cfg::kBandFloats / 4);  // float4 per split item
+          // v <- sum over splits i = 0..nsplit-1, in that order, of the
+          // split's partial (this split's own from tensor memory).
+          if (!mbar_wait_bounded(&part_full[c & 1], (c >> 1) & 1))
+            atomicOr(&g_watchdog, MUON_POLAR_WATCHDOG_EPILOGUE);
+          const uint32_t buf = smem_addr(sA) + (c & 1) * (tc.nsplit - 1) * kPartChunkBytes +
+                               static_cast<uint32_t>(row) * 16u;
 #pragma unroll
-          for (int g = 0; g < 2; ++g) {
-            float4 parts[kMaxSplits][4];
+          for (int u = 0; u < 8; ++u) {
+            const uint32_t off = static_cast<uint32_t>((hc * 8 + u) * kHalf) * 16u;
+            float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
             for (int i = 0; i < kMaxSplits; ++i) {
-#pragma unroll
-              for (int u = 0; u < 4; ++u) {
-                const int j = (g * 4 + u) * 4;
-                if (i < p.splits && i != split)
-                  parts[i][u] = __ldcg(band0 + i * split_stride +
-                                       (c * 16 + hc * 8 + g * 4 + u) * kHalf);
-                else
-                  parts[i][u] = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+              if (i >= tc.nsplit) break;
+              float4 x;
+              if (i == tc.split) {
+                x = make_float4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]);
+              } else {
+                const int o = i < tc.split ? i : i - 1;
+                const uint4 w4 = ld_shared_v4(buf + o * kPartChunkBytes + off);
+                x = make_float4(__uint_as_float(w4.x), __uint_as_float(w4.y),
+                                __uint_as_float(w4.z), __uint_as_float(w4.w));
+              }
+              if (i == 0) {
+                sum = x;
+              } else {
+                sum.x = __fadd_rn(sum.x, x.x);
+                sum.y = __fadd_rn(sum.y, x.y);
+                sum.z = __fadd_rn(sum.z, x.z);
+                sum.w = __fadd_rn(sum.w, x.w);
               }
             }
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-              float4 acc4 = parts[0][u];
-#pragma unroll
-              for (int i = 1; i < kMaxSplits; ++i) {
-                if (i < p.splits) {
-                  acc4.x = __fadd_rn(acc4.x, parts[i][u].x);
-                  acc4.y = __fadd_rn(acc4.y, parts[i][u].y);
-                  acc4.z = __fadd_rn(acc4.z, parts[i][u].z);
-                  acc4.w = __fadd_rn(acc4.w, parts[i][u].w);
-                }
-              }
-              const int j = (g * 4 + u) * 4;
-              v[j] = acc4.x;
-              v[j + 1] = acc4.y;
-              v[j + 2] = acc4.z;
-              v[j + 3] = acc4.w;
-            }
+            v[4 * u] = sum.x;
+            v[4 * u + 1] = sum.y;
+            v[4 * u + 2] = sum.z;
+            v[4 * u + 3] = sum.w;
           }
         }
         pair_epilogue_half<KIND>(p, out, mir, mirror, row, hc, v);
         fence_proxy_async_smem();
         named_barrier(1, kPairEpiThreads);
         if (leader) {
+          // every thread is done with partial buffer c % 2: refill it
+          if (reduce && c + 2 < Cfg::kChunks) load_parts(c + 2);
           const uint8_t* so = sOut + ro * Cfg::kOutChunkBytes;
           const uint8_t* sm = sMir + rm * Cfg::kMirChunkBytes;
 #pragma unroll
@@ -1202,10 +1272,9 @@ constexpr int instance_of() {
 }
 static_assert(instance_of<kApply, 2>() < kNumInstances, "instance slots");
 
-// Kernel choice: 0 = by size (CTA-pair 256x256 tiles when a launch has at
-// least half as many pair tiles as the device runs pairs at once, else
-// single-CTA 128x128 tiles, which keep more SMs busy on small problems),
-// 1 = always CTA pairs, 2 = never.  Initial value from MUON_POLAR_PAIR.
+// Kernel choice: 0 = by size (the engine with the smaller estimated time,
+// see use_pairs), 1 = always CTA pairs, 2 = never.  Initial value from
+// MUON_POLAR_PAIR.
 std::atomic<int> g_policy{[] {
   const char* s = std::getenv("MUON_POLAR_PAIR");
   if (s == nullptr) return 0;
@@ -1213,11 +1282,24 @@ std::atomic<int> g_policy{[] {
   return v == 1 ? 1 : (v == 0 ? 2 : 0);
 }()};
 
-bool use_pairs(int64_t pair_tiles, int capacity) {
+// Estimated time of a launch: rounds of tiles over the device, times the
+// pipeline iterations per tile, times the measured cost of one iteration
+// (B200: a CTA pair's 256 x 256 x 64 step about 0.33 us, a single CTA's
+// 128 x 128 x 128 step about 0.45 us; the latter is bound by shared-memory
+// bandwidth, both operands of every MMA being read from it).
+double engine_cost(int64_t tiles, int units, int64_t k_blocks, int pair) {
+  const int64_t rounds = (tiles + units - 1) / units;
+  return static_cast<double>(rounds) * static_cast<double>(k_blocks) * (pair == 2 ? 1.0 : 1.36);
+}
+
+// Whether a launch runs on CTA pairs, given each engine's tile count, the
+// tiles it works on at once and its pipeline iterations per tile.
+bool use_pairs(int64_t tiles2, int units2, int64_t kb2, int64_t tiles1, int units1,
+               int64_t kb1) {
   const int policy = g_policy.load(std::memory_order_relaxed);
   if (policy == 1) return true;
   if (policy == 2) return false;
-  return 2 * pair_tiles >= capacity;
+  return engine_cost(tiles2, units2, kb2, 2) <= engine_cost(tiles1, units1, kb1, 1);
 }
 
 // Split-K of the symmetric kinds: when a problem has fewer tiles than the
@@ -1233,13 +1315,28 @@ constexpr size_t partial_item_bytes() {
 }
 constexpr size_t kPartialItemBytes = partial_item_bytes<2>();
 
-// `units`: tiles the device works on at once (CTA pairs, or single CTAs).
-template <int PAIR>
+// `units`: tiles the device works on at once (CTA pairs, or single CTAs);
+// at most one work item per cluster (the kernel stages partial sums in its
+// pipeline stages, free only then), two counters per tile and CTA band, and
+// every split gets two k-blocks or more.
+// A split also has to save more pipeline iterations than its partial-sum
+// round trip through L2 costs: measured on B200 about 10 us for a pair band
+// (128 KiB) and 5 us for a single-CTA band (64 KiB), i.e. about 30 and 12
+// iterations.
+// Split mode (muon_polar_set_split_mode): 0 by size, 1 whenever possible,
+// 2 never.
+std::atomic<int> g_split_mode{0};
+
+template <int KIND, int PAIR>
 int choose_splits(int64_t tiles, int64_t k_blocks, int units) {
-  if (tiles <= 0 || tiles * PAIR > static_cast<int64_t>(kCounterBytes / 4)) return 1;
+  const int mode = g_split_mode.load(std::memory_order_relaxed);
+  if (mode == 2) return 1;
+  if (tiles <= 0 || tiles * PAIR * 2 > static_cast<int64_t>(kCounterBytes / 4)) return 1;
   int64_t s = units / tiles;
-  if (s > kMaxSplits) s = kMaxSplits;
+  if (s > PairCfg<KIND, PAIR>::kMaxSplitsHere) s = PairCfg<KIND, PAIR>::kMaxSplitsHere;
   if (s > k_blocks / 2) s = k_blocks / 2;
+  constexpr int64_t kMinSaved = PAIR == 2 ? 30 : 12;
+  while (mode == 0 && s >= 2 && k_blocks - k_blocks / s < kMinSaved) --s;
   return s < 2 ? 1 : static_cast<int>(s);
 }
 
@@ -1258,11 +1355,11 @@ void plan_no_splits(EpiParams& p) {
 }
 
 // Applies split-K to `p` if the scratch buffer allows it.
-template <int PAIR>
+template <int KIND, int PAIR>
 void plan_splits(EpiParams& p, void* scratch, size_t scratch_bytes, int units) {
   plan_no_splits(p);
   if (scratch == nullptr || !aligned16(scratch)) return;
-  const int s = choose_splits<PAIR>(p.total_tiles, p.k_blocks, units);
+  const int s = choose_splits<KIND, PAIR>(p.total_tiles, p.k_blocks, units);
   if (s < 2 || split_scratch_bytes<PAIR>(p.total_tiles, s) > scratch_bytes) return;
   p.splits = s;
   p.total_items = p.total_tiles * s;
@@ -1294,7 +1391,7 @@ int tile_capacity(DeviceState* st, int* capacity) {
   if constexpr (PAIR == 2) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * (st->sms / 2), 1, 1);
-    cfg.blockDim = dim3(kPairThreads, 1, 1);
+    cfg.blockDim = dim3(kTileThreads, 1, 1);
     cfg.dynamicSmemBytes = smem;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -1310,7 +1407,7 @@ int tile_capacity(DeviceState* st, int* capacity) {
     if (units > st->sms / 2) units = st->sms / 2;
   } else {
     int per_sm = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kPairThreads, smem) !=
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kTileThreads, smem) !=
             cudaSuccess ||
         per_sm <= 0) {
       (void)cudaGetLastError();
@@ -1332,7 +1429,7 @@ int launch_tile(DeviceState* st, const TileMaps& maps, const EpiParams& p,
   const int ctas = PAIR * (p.total_items < units ? p.total_items : units);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(ctas, 1, 1);
-  cfg.blockDim = dim3(kPairThreads, 1, 1);
+  cfg.blockDim = dim3(kTileThreads, 1, 1);
   cfg.dynamicSmemBytes = PairCfg<KIND, PAIR>::kSmemBytes;
   cfg.stream = stream;
   cudaLaunchAttribute attr[2];
@@ -1406,13 +1503,13 @@ int gram_launch(DeviceState* st, const void* x, void* gram, int64_t batch, int64
   if (rc != MUON_POLAR_OK) return rc;
   EpiParams p = {};
   sym_grid<PAIR>(p, batch, mp);
-  p.k_blocks = static_cast<int32_t>(pair_k_blocks<KIND>(n));
+  p.k_blocks = static_cast<int32_t>(k_blocks_of<PAIR>(n));
   if (fixed_scratch &&
       split_scratch_bytes<PAIR>(p.total_tiles,
-                                choose_splits<PAIR>(p.total_tiles, p.k_blocks, units)) >
+                                choose_splits<KIND, PAIR>(p.total_tiles, p.k_blocks, units)) >
           scratch_bytes)
     return MUON_POLAR_ERR_STATIC_SCRATCH;
-  plan_splits<PAIR>(p, scratch, scratch_bytes, units);
+  plan_splits<KIND, PAIR>(p, scratch, scratch_bytes, units);
   if (fixed_scratch && p.splits > 1) {
     cudaError_t e = cudaMemsetAsync(scratch, 0, kCounterBytes, stream);
     if (e != cudaSuccess) return static_cast<int>(e);
@@ -1436,10 +1533,13 @@ int gram_impl(const void* x, void* gram, int64_t batch, int64_t m, int64_t n,
   const int64_t d = padded_rows(m) / kHalf;
   if (d * (d + 1) / 2 * batch > INT32_MAX) return MUON_POLAR_ERR_INVALID_ARGUMENT;
   const int64_t dp = padded_rows(m) / kPairM;
-  int pairs = 0;
+  int pairs = 0, ctas = 0;
   rc = tile_capacity<KIND, 2>(st, &pairs);
   if (rc != MUON_POLAR_OK) return rc;
-  if (fixed_scratch || use_pairs(dp * (dp + 1) / 2 * batch, pairs))
+  rc = tile_capacity<KIND, 1>(st, &ctas);
+  if (rc != MUON_POLAR_OK) return rc;
+  if (fixed_scratch || use_pairs(dp * (dp + 1) / 2 * batch, pairs, k_blocks_of<2>(n),
+                                 d * (d + 1) / 2 * batch, ctas, k_blocks_of<1>(n)))
     return gram_launch<KIND, 2>(st, x, gram, batch, m, n, ldx, scratch, scratch_bytes,
                                 fixed_scratch, stream);
   return gram_launch<KIND, 1>(st, x, gram, batch, m, n, ldx, scratch, scratch_bytes,
@@ -1463,10 +1563,10 @@ int poly_launch(DeviceState* st, const void* gram, void* poly, int64_t batch, in
   if (rc != MUON_POLAR_OK) return rc;
   EpiParams p = {};
   sym_grid<PAIR>(p, batch, mp);
-  p.k_blocks = static_cast<int32_t>(pair_k_blocks<kPoly>(mp));
+  p.k_blocks = static_cast<int32_t>(k_blocks_of<PAIR>(mp));
   p.coef_b = b;
   p.coef_c = c;
-  plan_splits<PAIR>(p, scratch, scratch_bytes, units);
+  plan_splits<kPoly, PAIR>(p, scratch, scratch_bytes, units);
   return launch_tile<kPoly, PAIR>(st, tm, p, stream);
 }
 
@@ -1482,10 +1582,13 @@ int poly_impl(const void* gram, void* poly, int64_t batch, int64_t mp, float b,
   const int64_t d = mp / kHalf;
   if (d * (d + 1) / 2 * batch > INT32_MAX) return MUON_POLAR_ERR_INVALID_ARGUMENT;
   const int64_t dp = mp / kPairM;
-  int pairs = 0;
+  int pairs = 0, ctas = 0;
   rc = tile_capacity<kPoly, 2>(st, &pairs);
   if (rc != MUON_POLAR_OK) return rc;
-  if ((mp % kPairM) == 0 && use_pairs(dp * (dp + 1) / 2 * batch, pairs))
+  rc = tile_capacity<kPoly, 1>(st, &ctas);
+  if (rc != MUON_POLAR_OK) return rc;
+  if ((mp % kPairM) == 0 && use_pairs(dp * (dp + 1) / 2 * batch, pairs, k_blocks_of<2>(mp),
+                                      d * (d + 1) / 2 * batch, ctas, k_blocks_of<1>(mp)))
     return poly_launch<2>(st, gram, poly, batch, mp, b, c, scratch, scratch_bytes, stream);
   return poly_launch<1>(st, gram, poly, batch, mp, b, c, scratch, scratch_bytes, stream);
 }
@@ -1532,7 +1635,7 @@ int apply_launch(DeviceState* st, const void* poly, const void* x, void* y, int6
   p.tiles_per_batch = static_cast<int32_t>(tiles_m * tiles_n);
   p.total_tiles = static_cast<int32_t>(tiles_m * tiles_n * batch);
   // P's columns >= m are zero and X's rows >= m read as zero: stop at m.
-  p.k_blocks = static_cast<int32_t>(pair_k_blocks<kApply>(m));
+  p.k_blocks = static_cast<int32_t>(k_blocks_of<PAIR>(m));
   p.alpha = round_to_bf16(a);
   plan_no_splits(p);
   return launch_tile<kApply, PAIR>(st, tm, p, stream);
@@ -1550,10 +1653,15 @@ int apply_impl(const void* poly, const void* x, void* y, int64_t batch,
   DeviceState* st = nullptr;
   rc = current_device_state(&st);
   if (rc != MUON_POLAR_OK) return rc;
-  int pairs = 0;
+  int pairs = 0, ctas = 0;
   rc = tile_capacity<kApply, 2>(st, &pairs);
   if (rc != MUON_POLAR_OK) return rc;
-  if (use_pairs(padded_rows(m) / kPairM * ((n + kPairN - 1) / kPairN) * batch, pairs))
+  rc = tile_capacity<kApply, 1>(st, &ctas);
+  if (rc != MUON_POLAR_OK) return rc;
+  if (use_pairs(padded_rows(m) / kPairM * ((n + kPairN - 1) / kPairN) * batch, pairs,
+                k_blocks_of<2>(m),
+                (m + kHalf - 1) / kHalf * ((n + kHalf - 1) / kHalf) * batch, ctas,
+                k_blocks_of<1>(m)))
     return apply_launch<2>(st, poly, x, y, batch, m, n, ldx, ldy, a, stream);
   return apply_launch<1>(st, poly, x, y, batch, m, n, ldx, ldy, a, stream);
 }
@@ -1862,20 +1970,19 @@ size_t muon_polar_scratch_bytes(int64_t batch, int64_t m, int64_t n) {
     ctas = 1024;
   }
   const int64_t mp = padded_rows(m);
-  const int64_t kb_gram = pair_k_blocks<kGramF32>(n) > pair_k_blocks<kGramBf16>(n)
-                              ? pair_k_blocks<kGramF32>(n)
-                              : pair_k_blocks<kGramBf16>(n);
-  const int64_t kb_poly = pair_k_blocks<kPoly>(mp);
+
   const int64_t d2 = mp / kPairM, d1 = mp / kHalf;
   const int64_t t2 = d2 * (d2 + 1) / 2 * batch, t1 = d1 * (d1 + 1) / 2 * batch;
   // The largest plan either engine makes for kernels (1) and (2); the fused
   // step's dependency counters live in the counter area.
   size_t need = kCounterBytes;
-  const size_t plans[4] = {
-      split_scratch_bytes<2>(t2, choose_splits<2>(t2, kb_gram, pairs)),
-      split_scratch_bytes<2>(t2, choose_splits<2>(t2, kb_poly, pairs)),
-      split_scratch_bytes<1>(t1, choose_splits<1>(t1, kb_gram, ctas)),
-      split_scratch_bytes<1>(t1, choose_splits<1>(t1, kb_poly, ctas))};
+  const size_t plans[6] = {
+      split_scratch_bytes<2>(t2, choose_splits<kGramBf16, 2>(t2, k_blocks_of<2>(n), pairs)),
+      split_scratch_bytes<2>(t2, choose_splits<kGramF32, 2>(t2, k_blocks_of<2>(n), pairs)),
+      split_scratch_bytes<2>(t2, choose_splits<kPoly, 2>(t2, k_blocks_of<2>(mp), pairs)),
+      split_scratch_bytes<1>(t1, choose_splits<kGramBf16, 1>(t1, k_blocks_of<1>(n), ctas)),
+      split_scratch_bytes<1>(t1, choose_splits<kGramF32, 1>(t1, k_blocks_of<1>(n), ctas)),
+      split_scratch_bytes<1>(t1, choose_splits<kPoly, 1>(t1, k_blocks_of<1>(mp), ctas))};
   for (size_t v : plans) need = v > need ? v : need;
   return need;
 }
@@ -1951,6 +2058,11 @@ int muon_polar_set_kernel_policy(int policy) {
 int muon_polar_set_step_mode(int mode) {
   if (mode < 0 || mode > 2) return MUON_POLAR_ERR_INVALID_ARGUMENT;
   return g_step_mode.exchange(mode);
+}
+
+int muon_polar_set_split_mode(int mode) {
+  if (mode < 0 || mode > 2) return MUON_POLAR_ERR_INVALID_ARGUMENT;
+  return g_split_mode.exchange(mode);
 }
 
 int muon_polar_device_pairs(int* pairs) {

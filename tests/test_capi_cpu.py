@@ -77,4 +77,6 @@ def test_argument_validation_without_device(api):
     assert lib.muon_polar_gram_static_scratch_sm100(None, _vp(16), 1, 8, 8, 8, None) == -1
     assert lib.muon_polar_gram_static_scratch_sm100(_vp(16), _vp(24), 1, 8, 8, 8, None) == -3
     assert lib.muon_polar_set_kernel_policy(7) == -1
+    assert lib.muon_polar_set_split_mode(3) == -1
+    assert lib.muon_polar_set_split_mode(-1) == -1
     assert lib.muon_polar_read_device_status(0, None, 0) == -1

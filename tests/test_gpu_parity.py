@@ -83,9 +83,12 @@ def mode_policy(api):
     returns whether the mode passes split-K scratch."""
     def set_mode(mode):
         api.set_kernel_policy(2 if mode.startswith("single") else 1)
-        return mode.endswith("_split")
+        split = mode.endswith("_split")
+        api.set_split_mode(1 if split else 0)
+        return split
     yield set_mode
     api.set_kernel_policy(0)
+    api.set_split_mode(0)
 
 
 def _check_watchdog(api):
@@ -101,7 +104,8 @@ def _counters_zero(scratch):
 # ------------------------------------------------------------------ stages
 @pytest.mark.parametrize("mode", MODES)
 @pytest.mark.parametrize("shape", [(1, 128, 128), (2, 150, 2064), (8, 512, 2048),
-                                   (1, 300, 1000), (3, 64, 72), (1, 640, 640)])
+                                   (1, 300, 1000), (3, 64, 72), (1, 640, 640),
+                                   (1, 256, 8192)])
 def test_gram_stage(api, cuda_device, shape, mode, mode_policy):
     split = mode_policy(mode)
     bsz, m, n = shape
