@@ -55,6 +55,12 @@ struct EpiParams {
   float coef_b;
   float coef_c;
   float alpha;  // kApply: a already rounded to bf16
+  // kApply: X (both its operand and its epilogue input) does not depend on
+  // the previous kernel in the stream, so it is loaded before the grid
+  // dependency wait.  True inside a Polar Express step: the apply follows the
+  // polynomial kernel, which writes only P, and runs only after the Gram
+  // kernel -- whose own dependency wait covers X -- has completed.
+  int32_t x_ready;
   // Split-K (symmetric kinds): each tile's K range is cut into `splits`
   // work items of (nearly) equal length; item = tile * splits + split.
   int32_t splits;
@@ -341,8 +347,8 @@ __global__ void __launch_bounds__(kTileThreads, 1)
   uint64_t* tfull = empty + S;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
-  uint64_t* aux_full = drain + 1;
-  uint64_t* part_full = aux_full + 1;  // split-K partial chunks, two buffers
+  uint64_t* aux_full = drain + 1;      // epilogue input, one per chunk
+  uint64_t* part_full = aux_full + 4;  // split-K partial chunks, two buffers
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(part_full + 2);
   volatile uint32_t* last_flag = tmem_slot + 1;
 
@@ -363,7 +369,7 @@ __global__ void __launch_bounds__(kTileThreads, 1)
       mbar_init(&tempty[a], 8 * PAIR);  // 8 epilogue warps in each CTA
     }
     mbar_init(drain, 1);
-    mbar_init(aux_full, 1);
+    for (int c = 0; c < 4; ++c) mbar_init(&aux_full[c], 1);
     mbar_init(&part_full[0], 1);
     mbar_init(&part_full[1], 1);
     fence_mbar_init();
@@ -388,8 +394,8 @@ __global__ void __launch_bounds__(kTileThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  grid_dependency_wait();
-  grid_launch_dependents();
+  // Every thread passes the grid dependency wait before it touches data the
+  // previous kernel may write, and lets dependents launch only after it.
 
   if (warp == 0 || warp == kProducerWarp2) {
     // (warp kProducerWarp2 idles when the stage count is odd)
@@ -397,6 +403,59 @@ __global__ void __launch_bounds__(kTileThreads, 1)
       // ---------------- TMA producers (both CTAs): producer `pid` fills the
       // stages of the pipeline iterations with it % kProducers == pid.
       const uint32_t pid = warp == 0 ? 0u : 1u;
+      // Loads of one operand into stage s of the pipeline; PAIR = 2 counts
+      // the bytes on the leader's barrier, PAIR = 1 on its own.
+      auto load_a = [&](uint32_t s, const WorkItem& w, int kb) {
+        const uint32_t bar = PAIR == 2 ? map_to_cta(smem_addr(&full[s]), 0) : 0u;
+        const int a_row = w.tm * kTileM + static_cast<int>(rank) * kHalf;
+#pragma unroll
+        for (int j = 0; j < Cfg::kBK / kAtom; ++j) {
+          if constexpr (PAIR == 2)
+            tma_load_3d_pair(sA + s * Cfg::kAHalfBytes + j * kAtomBytes, &tmap_a, bar,
+                             kb * Cfg::kBK + j * kAtom, a_row, w.b);
+          else
+            tma_load_3d(sA + s * Cfg::kAHalfBytes + j * kAtomBytes, &tmap_a, &full[s],
+                        kb * Cfg::kBK + j * kAtom, a_row, w.b);
+        }
+      };
+      auto load_b = [&](uint32_t s, const WorkItem& w, int kb) {
+        const uint32_t bar = PAIR == 2 ? map_to_cta(smem_addr(&full[s]), 0) : 0u;
+        const int b_row = w.tn * kTileN + static_cast<int>(rank) * kHalf;
+        // K-major: [128 n x 64 k] boxes; MN-major: one [kBK k x 64 n] box per
+        // 64-column chunk
+        constexpr int kBoxes = kBmn ? kHalf / kAtom : Cfg::kBK / kAtom;
+#pragma unroll
+        for (int j = 0; j < kBoxes; ++j) {
+          void* dst = sB + s * Cfg::kBHalfBytes + j * (kBmn ? Cfg::kBK * 128 : kAtomBytes);
+          const int c0 = kBmn ? b_row + j * kAtom : kb * Cfg::kBK + j * kAtom;
+          const int c1 = kBmn ? kb * Cfg::kBK : b_row;
+          if constexpr (PAIR == 2)
+            tma_load_3d_pair(dst, &tmap_b, bar, c0, c1, w.b);
+          else
+            tma_load_3d(dst, &tmap_b, &full[s], c0, c1, w.b);
+        }
+      };
+      // The first pipeline iterations' B operand (X) before the dependency
+      // wait, when X does not depend on the previous kernel.  Their stages
+      // are fresh, so no empty-wait is needed.
+      uint32_t n_pre = 0;
+      if constexpr (kBmn) {
+        if (p.x_ready) {
+          uint32_t it = 0;
+          for (int item = cluster; item < p.total_items && it < static_cast<uint32_t>(S);
+               item += nclusters) {
+            const WorkItem w = decode_item(p, item, kSym);
+            for (int kb = w.kb_begin; kb < w.kb_end && it < static_cast<uint32_t>(S); ++kb, ++it) {
+              if (it % Cfg::kProducers != pid) continue;
+              if (rank == 0) mbar_arrive_expect_tx(&full[it], PAIR * Cfg::kStageBytes);
+              load_b(it, w, kb);
+            }
+          }
+          n_pre = it;
+        }
+      }
+      grid_dependency_wait();
+      grid_launch_dependents();
       uint32_t it = 0;
       bool ok = true;
       for (int item = cluster; ok && item < p.total_items; item += nclusters) {
@@ -404,45 +463,21 @@ __global__ void __launch_bounds__(kTileThreads, 1)
         // A diagonal tile of a symmetric kind multiplies a row block by
         // itself: only the A operand is loaded, and the MMA reads it twice.
         const bool diag = kSym && w.tm == w.tn;
-        const int a_row = w.tm * kTileM + static_cast<int>(rank) * kHalf;
-        const int b_row = w.tn * kTileN + static_cast<int>(rank) * kHalf;
         for (int kb = w.kb_begin; kb < w.kb_end; ++kb, ++it) {
           if (it % Cfg::kProducers != pid) continue;
           const uint32_t s = it % S;
           const uint32_t ph = (it / S) & 1u;
-          if (!mbar_wait_bounded(&empty[s], ph ^ 1u)) {
-            ok = false;
-            break;
-          }
-          if (rank == 0)
-            mbar_arrive_expect_tx(&full[s], PAIR * (diag ? Cfg::kAHalfBytes : Cfg::kStageBytes));
-          const uint32_t bar = PAIR == 2 ? map_to_cta(smem_addr(&full[s]), 0) : 0u;
-          // loads into this CTA's stage; PAIR = 2 counts the bytes on the
-          // leader's barrier, PAIR = 1 on its own
-          auto load = [&](void* dst, const CUtensorMap* map, int c0, int c1) {
-            if constexpr (PAIR == 2)
-              tma_load_3d_pair(dst, map, bar, c0, c1, w.b);
-            else
-              tma_load_3d(dst, map, &full[s], c0, c1, w.b);
-          };
-#pragma unroll
-          for (int j = 0; j < Cfg::kBK / kAtom; ++j)
-            load(sA + s * Cfg::kAHalfBytes + j * kAtomBytes, &tmap_a, kb * Cfg::kBK + j * kAtom,
-                 a_row);
-          if constexpr (!kBmn) {
-            if (!diag) {
-#pragma unroll
-              for (int j = 0; j < Cfg::kBK / kAtom; ++j)
-                load(sB + s * Cfg::kBHalfBytes + j * kAtomBytes, &tmap_b,
-                     kb * Cfg::kBK + j * kAtom, b_row);
+          if (it >= n_pre) {
+            if (!mbar_wait_bounded(&empty[s], ph ^ 1u)) {
+              ok = false;
+              break;
             }
-          } else {
-            // MN-major B: one [kBK k-rows x 64 n] box per 64-column chunk
-#pragma unroll
-            for (int j = 0; j < kHalf / kAtom; ++j)
-              load(sB + s * Cfg::kBHalfBytes + j * (Cfg::kBK * 128), &tmap_b, b_row + j * kAtom,
-                   kb * Cfg::kBK);
+            if (rank == 0)
+              mbar_arrive_expect_tx(&full[s],
+                                    PAIR * (diag ? Cfg::kAHalfBytes : Cfg::kStageBytes));
           }
+          load_a(s, w, kb);
+          if (it >= n_pre && !diag) load_b(s, w, kb);
         }
       }
       if (!ok) atomicOr(&g_watchdog, MUON_POLAR_WATCHDOG_PRODUCER);
@@ -458,8 +493,13 @@ __global__ void __launch_bounds__(kTileThreads, 1)
           }
         }
       }
+    } else {
+      grid_dependency_wait();
+      grid_launch_dependents();
     }
   } else if (warp == 1) {
+    grid_dependency_wait();
+    grid_launch_dependents();
     if (lane == 0 && rank == 0) {
       // ---------------- tcgen05 MMA issuer (leader CTA only)
       constexpr uint32_t idesc = idesc_bf16_f32(kTileN, kBmn ? 1u : 0u, kTileM);
@@ -538,16 +578,17 @@ __global__ void __launch_bounds__(kTileThreads, 1)
     const bool leader = threadIdx.x == kEpiLeader;
     const uint32_t tempty_leader0 = PAIR == 2 ? map_to_cta(smem_addr(&tempty[0]), 0) : 0u;
     const uint32_t tempty_leader1 = PAIR == 2 ? map_to_cta(smem_addr(&tempty[1]), 0) : 0u;
-    bool aux_inflight = false;
-    auto load_aux = [&](int item) {
+    // Epilogue input tile (kAux kinds), one region and one barrier per
+    // chunk; the leader reloads chunk c for the next item as soon as the TMA
+    // store of this item's chunk c has read the region.
+    uint32_t aux_issued[4] = {0u, 0u, 0u, 0u};
+    auto load_aux_chunk = [&](int item, int c) {
       const WorkItem w = decode_item(p, item, kSym);
-      mbar_arrive_expect_tx(aux_full, Cfg::kChunks * Cfg::kOutChunkBytes);
-#pragma unroll
-      for (int c = 0; c < Cfg::kChunks; ++c)
-        tma_load_3d(sOut + c * Cfg::kOutChunkBytes, &tmap_aux, aux_full,
-                    w.tn * kTileN + c * kChunkCols,
-                    w.tm * kTileM + static_cast<int>(rank) * kHalf, w.b);
-      aux_inflight = true;
+      mbar_arrive_expect_tx(&aux_full[c], Cfg::kOutChunkBytes);
+      tma_load_3d(sOut + c * Cfg::kOutChunkBytes, &tmap_aux, &aux_full[c],
+                  w.tn * kTileN + c * kChunkCols, w.tm * kTileM + static_cast<int>(rank) * kHalf,
+                  w.b);
+      ++aux_issued[c];
     };
     auto release_accumulator = [&](uint32_t acc) {
       tc_fence_before();
@@ -559,28 +600,32 @@ __global__ void __launch_bounds__(kTileThreads, 1)
           mbar_arrive_cluster(acc ? tempty_leader1 : tempty_leader0);
       }
     };
+    // The apply's input tile is X: before the dependency wait when X does not
+    // depend on the previous kernel.
+    const bool aux_early = kBmn && p.x_ready;
     if constexpr (Cfg::kAux) {
-      if (leader && cluster < p.total_items) load_aux(cluster);
+      if (leader && aux_early && cluster < p.total_items)
+        for (int c = 0; c < Cfg::kChunks; ++c) load_aux_chunk(cluster, c);
+    }
+    grid_dependency_wait();
+    grid_launch_dependents();
+    if constexpr (Cfg::kAux) {
+      if (leader && !aux_early && cluster < p.total_items)
+        for (int c = 0; c < Cfg::kChunks; ++c) load_aux_chunk(cluster, c);
     }
     uint32_t t = 0;
     for (int item = cluster; item < p.total_items; item += nclusters, ++t) {
       const WorkItem tc = decode_item(p, item, kSym);
       const uint32_t acc = t & 1u;
       const uint32_t uph = (t >> 1) & 1u;
+      const int next = item + nclusters;
       int ok = 1;
-      if (lane == 0) {
-        ok = mbar_wait_bounded(&tfull[acc], uph) ? 1 : 0;
-        if (Cfg::kAux && ok) {
-          ok = mbar_wait_bounded(aux_full, t & 1u) ? 1 : 0;
-          if (ok) aux_inflight = false;
-        }
-      }
+      if (lane == 0) ok = mbar_wait_bounded(&tfull[acc], uph) ? 1 : 0;
       ok = __shfl_sync(0xffffffffu, ok, 0);
       if (!ok) {
         if (lane == 0) atomicOr(&g_watchdog, MUON_POLAR_WATCHDOG_EPILOGUE);
         break;
       }
-      if constexpr (Cfg::kAux) (void)mbar_try_wait(aux_full, t & 1u);
       tc_fence_after();
       const bool mirror = kSym && tc.tm != tc.tn;
       const int row0 = tc.tm * kTileM + static_cast<int>(rank) * kHalf;
@@ -626,7 +671,7 @@ __global__ void __launch_bounds__(kTileThreads, 1)
           for (int c = 0; c < Cfg::kChunks; ++c) {
             uint32_t r0[32];
             tmem_ld_32x32b_x32(t_row + c * kChunkCols + hc * 32, r0);
-            tmem_wait_ld();
+            tmem_wait_ld(r0);
 #pragma unroll
             for (int u = 0; u < 8; ++u)
               st_shared_v4(stage + static_cast<uint32_t>((c * 16 + hc * 8 + u) * kHalf) * 16u,
@@ -661,7 +706,11 @@ __global__ void __launch_bounds__(kTileThreads, 1)
           if (Cfg::kChunks > 1) load_parts(1);
         }
       }
-#pragma unroll 1
+      // Accumulator chunk c + 1 is read from tensor memory while chunk c is
+      // processed (two register buffers, loop fully unrolled).
+      uint32_t rbuf[2][32];
+      tmem_ld_32x32b_x32(t_row + hc * 32, rbuf[0]);
+#pragma unroll
       for (int c = 0; c < Cfg::kChunks; ++c) {
         const int ro = c % Cfg::kOutRegions;
         const uint32_t out = out_base + ro * Cfg::kOutChunkBytes;
@@ -672,13 +721,18 @@ __global__ void __launch_bounds__(kTileThreads, 1)
           if (leader) bulk_wait_group_read<Cfg::kPending>();
           named_barrier(1, kPairEpiThreads);
         }
-        uint32_t r0[32];
-        tmem_ld_32x32b_x32(t_row + c * kChunkCols + hc * 32, r0);
-        tmem_wait_ld();
-        if (c == Cfg::kChunks - 1) release_accumulator(acc);
+        tmem_wait_ld(rbuf[c & 1]);
+        if (c + 1 < Cfg::kChunks)
+          tmem_ld_32x32b_x32(t_row + (c + 1) * kChunkCols + hc * 32, rbuf[(c + 1) & 1]);
+        else
+          release_accumulator(acc);
         float v[32];
 #pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r0[j]);
+        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(rbuf[c & 1][j]);
+        if constexpr (Cfg::kAux) {
+          if (!mbar_wait_bounded(&aux_full[c], t & 1u))
+            atomicOr(&g_watchdog, MUON_POLAR_WATCHDOG_EPILOGUE);
+        }
         if (reduce) {
           // v <- sum over splits i = 0..nsplit-1, in that order, of the
           // split's partial (this split's own from tensor memory).
@@ -736,20 +790,30 @@ __global__ void __launch_bounds__(kTileThreads, 1)
                            col0 + c * kChunkCols, tc.b);
           }
           bulk_commit_group();
+          if constexpr (Cfg::kAux) {
+            // region c - 1 has been read by its store: next item's chunk c - 1
+            if (c >= 1 && next < p.total_items) {
+              bulk_wait_group_read<1>();
+              load_aux_chunk(next, c - 1);
+            }
+          }
         }
       }
       if constexpr (Cfg::kAux) {
-        if (leader) {
+        if (leader && next < p.total_items) {
           bulk_wait_group_read<0>();
-          const int next = item + nclusters;
-          if (next < p.total_items) load_aux(next);
+          load_aux_chunk(next, Cfg::kChunks - 1);
         }
       }
     }
     if (leader) {
       bulk_wait_group0();
-      if (aux_inflight && !mbar_wait_bounded(aux_full, t & 1u))
-        atomicOr(&g_watchdog, MUON_POLAR_WATCHDOG_DRAIN);
+      // input chunks still in flight (an item that was not processed) land
+      // before the CTA exits
+      for (int c = 0; c < Cfg::kChunks; ++c) {
+        if (aux_issued[c] > 0u && !mbar_wait_bounded(&aux_full[c], (aux_issued[c] - 1u) & 1u))
+          atomicOr(&g_watchdog, MUON_POLAR_WATCHDOG_DRAIN);
+      }
     }
   }
 
@@ -1606,7 +1670,7 @@ float round_to_bf16(float v) {
 
 template <int PAIR>
 int apply_launch(DeviceState* st, const void* poly, const void* x, void* y, int64_t batch,
-                 int64_t m, int64_t n, int64_t ldx, int64_t ldy, float a,
+                 int64_t m, int64_t n, int64_t ldx, int64_t ldy, float a, bool x_ready,
                  cudaStream_t stream) {
   using Cfg = PairCfg<kApply, PAIR>;
   const int64_t mp = padded_rows(m);
@@ -1637,13 +1701,16 @@ int apply_launch(DeviceState* st, const void* poly, const void* x, void* y, int6
   // P's columns >= m are zero and X's rows >= m read as zero: stop at m.
   p.k_blocks = static_cast<int32_t>(k_blocks_of<PAIR>(m));
   p.alpha = round_to_bf16(a);
+  p.x_ready = x_ready ? 1 : 0;
   plan_no_splits(p);
   return launch_tile<kApply, PAIR>(st, tm, p, stream);
 }
 
+// `x_ready`: X does not depend on the previous kernel in the stream (see
+// EpiParams::x_ready); only muon_polar_step_sm100 knows that.
 int apply_impl(const void* poly, const void* x, void* y, int64_t batch,
                int64_t m, int64_t n, int64_t ldx, int64_t ldy, float a,
-               cudaStream_t stream) {
+               cudaStream_t stream, bool x_ready = false) {
   int rc = check_x_args(x, batch, m, n, ldx);
   if (rc != MUON_POLAR_OK) return rc;
   if (poly == nullptr || y == nullptr || ldy < n)
@@ -1662,8 +1729,8 @@ int apply_impl(const void* poly, const void* x, void* y, int64_t batch,
                 k_blocks_of<2>(m),
                 (m + kHalf - 1) / kHalf * ((n + kHalf - 1) / kHalf) * batch, ctas,
                 k_blocks_of<1>(m)))
-    return apply_launch<2>(st, poly, x, y, batch, m, n, ldx, ldy, a, stream);
-  return apply_launch<1>(st, poly, x, y, batch, m, n, ldx, ldy, a, stream);
+    return apply_launch<2>(st, poly, x, y, batch, m, n, ldx, ldy, a, x_ready, stream);
+  return apply_launch<1>(st, poly, x, y, batch, m, n, ldx, ldy, a, x_ready, stream);
 }
 
 // ---------------------------------------------------------------- fused step
@@ -1955,7 +2022,7 @@ int muon_polar_step_sm100(const void* x, void* y, void* workspace,
   if (rc != MUON_POLAR_OK) return rc;
   rc = poly_impl(gram, poly, batch, mp, b, c, scratch, scratch_bytes, s);
   if (rc != MUON_POLAR_OK) return rc;
-  return apply_impl(poly, x, y, batch, m, n, ldx, ldy, a, s);
+  return apply_impl(poly, x, y, batch, m, n, ldx, ldy, a, s, /*x_ready=*/true);
 }
 
 size_t muon_polar_scratch_bytes(int64_t batch, int64_t m, int64_t n) {

@@ -75,6 +75,7 @@ def _assert_within_ulps(actual, expected64, ulps, what, abs_slack=0.0, max_frac=
 
 
 MODES = ["single", "single_split", "pair", "pair_split"]
+_POLICY = {"single": 2, "pair": 1}
 
 
 @pytest.fixture
@@ -82,7 +83,7 @@ def mode_policy(api):
     """Sets the kernel policy for one test and restores the default after;
     returns whether the mode passes split-K scratch."""
     def set_mode(mode):
-        api.set_kernel_policy(2 if mode.startswith("single") else 1)
+        api.set_kernel_policy(_POLICY[mode.split("_")[0]])
         split = mode.endswith("_split")
         api.set_split_mode(1 if split else 0)
         return split
