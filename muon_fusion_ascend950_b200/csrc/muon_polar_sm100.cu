@@ -155,18 +155,20 @@ constexpr int kAtom = 64;  // bf16 elements per 128-byte swizzle row
 
 constexpr uint32_t kAtomBytes = kHalf * kAtom * 2;  // one [128 x 64] box, 16 KiB
 
-// K depth of one pipeline stage: two 128-byte swizzle atoms for single-CTA
-// tiles, one for CTA pairs.  A 128 x 128 tile's MMAs are short (64 cycles for
-// K = 16), so their per-stage handshake (wait, commit, refill) is only hidden
-// behind eight of them; a pair's 256 x 256 MMAs take twice as long, and four
-// per stage measured as fast as eight.
-template <int PAIR>
+// K depth of one pipeline stage: two 128-byte swizzle atoms (64 KiB stages)
+// for single-CTA tiles and for the bf16 Gram on CTA pairs, one (32 KiB) for
+// the other pair kinds.  Every stage costs the MMA thread a handshake (wait,
+// commit, refill) of about 200 cycles that eight MMAs hide better than four:
+// measured on B200, 64 KiB stages make the pair Gram 7-12% faster at
+// 4096-8192 rows; the polynomial and the apply keep 32 KiB stages, which
+// leave room for four or five of them beside their larger epilogue buffers.
+template <int KIND, int PAIR>
 constexpr int stage_k() {
-  return PAIR == 1 ? 128 : 64;
+  return (PAIR == 1 || KIND == kGramBf16) ? 128 : 64;
 }
-template <int PAIR>
+template <int KIND, int PAIR>
 constexpr int64_t k_blocks_of(int64_t k) {
-  return (k + stage_k<PAIR>() - 1) / stage_k<PAIR>();
+  return (k + stage_k<KIND, PAIR>() - 1) / stage_k<KIND, PAIR>();
 }
 
 // Shared-memory and tensor-memory plan of one CTA of polar_tile_kernel.
@@ -184,7 +186,7 @@ struct PairCfg {
   static constexpr int kChunks = kTileN / kChunkCols;
   static constexpr uint32_t kOutChunkBytes = kHalf * kChunkCols * kElem;
   static constexpr uint32_t kMirChunkBytes = kSym ? kChunkCols * kHalf * kElem : 0;
-  static constexpr int kBK = stage_k<PAIR>();
+  static constexpr int kBK = stage_k<KIND, PAIR>();
   // Output regions: kAux kinds keep the whole 128 x kTileN input band (updated
   // in place, one region per chunk, never reused within a tile); the Gram
   // single-buffers its chunk region.
@@ -1352,12 +1354,19 @@ std::atomic<int> g_policy{[] {
 // 128 x 128 x 128 step about 0.45 us; the latter is bound by shared-memory
 // bandwidth, both operands of every MMA being read from it).
 double engine_cost(int64_t tiles, int units, int64_t k_blocks, int pair) {
+  // (k_blocks: K / 64 on pairs, K / 128 on single CTAs; see cost_blocks)
   const int64_t rounds = (tiles + units - 1) / units;
   return static_cast<double>(rounds) * static_cast<double>(k_blocks) * (pair == 2 ? 1.0 : 1.36);
 }
 
+template <int PAIR>
+int64_t cost_blocks(int64_t k) {
+  return PAIR == 2 ? (k + 63) / 64 : (k + 127) / 128;
+}
+
 // Whether a launch runs on CTA pairs, given each engine's tile count, the
-// tiles it works on at once and its pipeline iterations per tile.
+// tiles it works on at once and its K steps per tile (64 deep on pairs, 128
+// on single CTAs).
 bool use_pairs(int64_t tiles2, int units2, int64_t kb2, int64_t tiles1, int units1,
                int64_t kb1) {
   const int policy = g_policy.load(std::memory_order_relaxed);
@@ -1385,8 +1394,8 @@ constexpr size_t kPartialItemBytes = partial_item_bytes<2>();
 // every split gets two k-blocks or more.
 // A split also has to save more pipeline iterations than its partial-sum
 // round trip through L2 costs: measured on B200 about 10 us for a pair band
-// (128 KiB) and 5 us for a single-CTA band (64 KiB), i.e. about 30 and 12
-// iterations.
+// (128 KiB) and 5 us for a single-CTA band (64 KiB), i.e. about 30 pair
+// iterations of K = 64 (17 of K = 128) and 12 single-CTA iterations.
 // Split mode (muon_polar_set_split_mode): 0 by size, 1 whenever possible,
 // 2 never.
 std::atomic<int> g_split_mode{0};
@@ -1399,7 +1408,8 @@ int choose_splits(int64_t tiles, int64_t k_blocks, int units) {
   int64_t s = units / tiles;
   if (s > PairCfg<KIND, PAIR>::kMaxSplitsHere) s = PairCfg<KIND, PAIR>::kMaxSplitsHere;
   if (s > k_blocks / 2) s = k_blocks / 2;
-  constexpr int64_t kMinSaved = PAIR == 2 ? 30 : 12;
+  constexpr int64_t kMinSaved =
+      PAIR == 1 ? 12 : (PairCfg<KIND, PAIR>::kBK == 128 ? 17 : 30);
   while (mode == 0 && s >= 2 && k_blocks - k_blocks / s < kMinSaved) --s;
   return s < 2 ? 1 : static_cast<int>(s);
 }
@@ -1567,7 +1577,7 @@ int gram_launch(DeviceState* st, const void* x, void* gram, int64_t batch, int64
   if (rc != MUON_POLAR_OK) return rc;
   EpiParams p = {};
   sym_grid<PAIR>(p, batch, mp);
-  p.k_blocks = static_cast<int32_t>(k_blocks_of<PAIR>(n));
+  p.k_blocks = static_cast<int32_t>(k_blocks_of<KIND, PAIR>(n));
   if (fixed_scratch &&
       split_scratch_bytes<PAIR>(p.total_tiles,
                                 choose_splits<KIND, PAIR>(p.total_tiles, p.k_blocks, units)) >
@@ -1602,8 +1612,8 @@ int gram_impl(const void* x, void* gram, int64_t batch, int64_t m, int64_t n,
   if (rc != MUON_POLAR_OK) return rc;
   rc = tile_capacity<KIND, 1>(st, &ctas);
   if (rc != MUON_POLAR_OK) return rc;
-  if (fixed_scratch || use_pairs(dp * (dp + 1) / 2 * batch, pairs, k_blocks_of<2>(n),
-                                 d * (d + 1) / 2 * batch, ctas, k_blocks_of<1>(n)))
+  if (fixed_scratch || use_pairs(dp * (dp + 1) / 2 * batch, pairs, cost_blocks<2>(n),
+                                 d * (d + 1) / 2 * batch, ctas, cost_blocks<1>(n)))
     return gram_launch<KIND, 2>(st, x, gram, batch, m, n, ldx, scratch, scratch_bytes,
                                 fixed_scratch, stream);
   return gram_launch<KIND, 1>(st, x, gram, batch, m, n, ldx, scratch, scratch_bytes,
@@ -1627,7 +1637,7 @@ int poly_launch(DeviceState* st, const void* gram, void* poly, int64_t batch, in
   if (rc != MUON_POLAR_OK) return rc;
   EpiParams p = {};
   sym_grid<PAIR>(p, batch, mp);
-  p.k_blocks = static_cast<int32_t>(k_blocks_of<PAIR>(mp));
+  p.k_blocks = static_cast<int32_t>(k_blocks_of<kPoly, PAIR>(mp));
   p.coef_b = b;
   p.coef_c = c;
   plan_splits<kPoly, PAIR>(p, scratch, scratch_bytes, units);
@@ -1651,8 +1661,9 @@ int poly_impl(const void* gram, void* poly, int64_t batch, int64_t mp, float b,
   if (rc != MUON_POLAR_OK) return rc;
   rc = tile_capacity<kPoly, 1>(st, &ctas);
   if (rc != MUON_POLAR_OK) return rc;
-  if ((mp % kPairM) == 0 && use_pairs(dp * (dp + 1) / 2 * batch, pairs, k_blocks_of<2>(mp),
-                                      d * (d + 1) / 2 * batch, ctas, k_blocks_of<1>(mp)))
+  if ((mp % kPairM) == 0 && use_pairs(dp * (dp + 1) / 2 * batch, pairs,
+                                      cost_blocks<2>(mp), d * (d + 1) / 2 * batch, ctas,
+                                      cost_blocks<1>(mp)))
     return poly_launch<2>(st, gram, poly, batch, mp, b, c, scratch, scratch_bytes, stream);
   return poly_launch<1>(st, gram, poly, batch, mp, b, c, scratch, scratch_bytes, stream);
 }
@@ -1699,7 +1710,7 @@ int apply_launch(DeviceState* st, const void* poly, const void* x, void* y, int6
   p.tiles_per_batch = static_cast<int32_t>(tiles_m * tiles_n);
   p.total_tiles = static_cast<int32_t>(tiles_m * tiles_n * batch);
   // P's columns >= m are zero and X's rows >= m read as zero: stop at m.
-  p.k_blocks = static_cast<int32_t>(k_blocks_of<PAIR>(m));
+  p.k_blocks = static_cast<int32_t>(k_blocks_of<kApply, PAIR>(m));
   p.alpha = round_to_bf16(a);
   p.x_ready = x_ready ? 1 : 0;
   plan_no_splits(p);
@@ -1726,9 +1737,9 @@ int apply_impl(const void* poly, const void* x, void* y, int64_t batch,
   rc = tile_capacity<kApply, 1>(st, &ctas);
   if (rc != MUON_POLAR_OK) return rc;
   if (use_pairs(padded_rows(m) / kPairM * ((n + kPairN - 1) / kPairN) * batch, pairs,
-                k_blocks_of<2>(m),
+                cost_blocks<2>(m),
                 (m + kHalf - 1) / kHalf * ((n + kHalf - 1) / kHalf) * batch, ctas,
-                k_blocks_of<1>(m)))
+                cost_blocks<1>(m)))
     return apply_launch<2>(st, poly, x, y, batch, m, n, ldx, ldy, a, x_ready, stream);
   return apply_launch<1>(st, poly, x, y, batch, m, n, ldx, ldy, a, x_ready, stream);
 }
@@ -2044,12 +2055,14 @@ size_t muon_polar_scratch_bytes(int64_t batch, int64_t m, int64_t n) {
   // step's dependency counters live in the counter area.
   size_t need = kCounterBytes;
   const size_t plans[6] = {
-      split_scratch_bytes<2>(t2, choose_splits<kGramBf16, 2>(t2, k_blocks_of<2>(n), pairs)),
-      split_scratch_bytes<2>(t2, choose_splits<kGramF32, 2>(t2, k_blocks_of<2>(n), pairs)),
-      split_scratch_bytes<2>(t2, choose_splits<kPoly, 2>(t2, k_blocks_of<2>(mp), pairs)),
-      split_scratch_bytes<1>(t1, choose_splits<kGramBf16, 1>(t1, k_blocks_of<1>(n), ctas)),
-      split_scratch_bytes<1>(t1, choose_splits<kGramF32, 1>(t1, k_blocks_of<1>(n), ctas)),
-      split_scratch_bytes<1>(t1, choose_splits<kPoly, 1>(t1, k_blocks_of<1>(mp), ctas))};
+      split_scratch_bytes<2>(
+          t2, choose_splits<kGramBf16, 2>(t2, k_blocks_of<kGramBf16, 2>(n), pairs)),
+      split_scratch_bytes<2>(t2, choose_splits<kGramF32, 2>(t2, k_blocks_of<kGramF32, 2>(n), pairs)),
+      split_scratch_bytes<2>(t2, choose_splits<kPoly, 2>(t2, k_blocks_of<kPoly, 2>(mp), pairs)),
+      split_scratch_bytes<1>(
+          t1, choose_splits<kGramBf16, 1>(t1, k_blocks_of<kGramBf16, 1>(n), ctas)),
+      split_scratch_bytes<1>(t1, choose_splits<kGramF32, 1>(t1, k_blocks_of<kGramF32, 1>(n), ctas)),
+      split_scratch_bytes<1>(t1, choose_splits<kPoly, 1>(t1, k_blocks_of<kPoly, 1>(mp), ctas))};
   for (size_t v : plans) need = v > need ? v : need;
   return need;
 }

@@ -3,7 +3,7 @@ callers that cannot allocate device memory (its split-K scratch is an array
 built into the library instead of a caller buffer).
 
 It is compared with the regular entry point, muon_polar_gram_sm100, run on the
-same CTA-pair split-K path with caller-owned scratch, using the tolerance of
+same CTA-pair split-K path (split-K forced on) with caller-owned scratch, using the tolerance of
 the Gram stage tests (one bf16 ulp), on two calls in a row -- the second call
 finds the array as the first call left it.  This file sorts last so that a
 run stopping at the first failure has already run every other test.
@@ -30,6 +30,7 @@ def test_static_scratch_gram_matches_regular_entry(cuda_device):
 
     api = capi()
     previous = api.set_kernel_policy(1)  # regular entry on the same CTA-pair path
+    previous_split = api.set_split_mode(1)  # split-K (and so the scratch) in use
     try:
         # two calls in a row: a split problem, then a different split problem
         for shape, seed in (((8, 512, 2048), 31), ((2, 300, 1000), 32)):
@@ -47,3 +48,4 @@ def test_static_scratch_gram_matches_regular_entry(cuda_device):
             _within_one_ulp(got, expected)
     finally:
         api.set_kernel_policy(previous)
+        api.set_split_mode(previous_split)
