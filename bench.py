@@ -65,6 +65,9 @@ def parse_args():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--shape", default="8,512,2048",
                    help="B,M,N of the `shape` workload (one polar_step per timed step)")
+    p.add_argument("--poly", choices=["replicated", "sharded"], default="sharded",
+                   help="cfg5 with several GPUs: kernel 2 on every rank (replicated) or "
+                        "split into row slabs and all-gathered (sharded)")
     p.add_argument("--workload", choices=["cfg1", "cfg3", "cfg4", "cfg5", "shape"],
                    default="cfg1",
                    help="cfg1 (default, the headline): one step on [8,512,2048] per GPU; "
@@ -520,7 +523,7 @@ def run_large(args):
         if world > 1:
             dist.all_reduce(sq)
         x_local = (x_local / (sq.sqrt() * 1.01 + 1e-6)).to(torch.bfloat16)
-        driver = ColumnShardedPolar(m, device)
+        driver = ColumnShardedPolar(m, device, shard_poly=args.poly == "sharded")
         job_flops = 5 * nominal_flops(m, n)
 
         def step():
@@ -528,7 +531,10 @@ def run_large(args):
 
         workload = "5-step loop on one [8192,65536] bf16 matrix (BASELINE config 5)"
         parallelism = (f"column-sharded x{world}, one NCCL fp32 all-reduce of the 8192x8192 "
-                       "partial Gram per step" if world > 1 else "single GPU")
+                       "partial Gram per step, kernel 2 "
+                       + ("in row slabs + NCCL bf16 all-gather"
+                          if driver.poly_slab is not None else "replicated")
+                       if world > 1 else "single GPU")
 
     def sync_all():
         torch.cuda.synchronize(device)

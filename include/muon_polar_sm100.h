@@ -158,6 +158,16 @@ int muon_polar_poly_sm100(const void* gram, void* poly, int64_t batch,
                           int64_t mp, float b, float c, void* scratch,
                           size_t scratch_bytes, void* stream);
 
+/* Kernel (2) on a slab of rows: rows [row_begin, row_begin + row_count) of
+ * poly[b], written in place into the full [batch][Mp][Mp] bf16 buffer `poly`
+ * (whole rows: both triangles, no mirror), with the arithmetic of
+ * muon_polar_poly_sm100.  Mp, row_begin and row_count are multiples of 256.
+ * For multi-GPU callers that split kernel (2) by row slabs and then gather
+ * the slabs (the reference runs kernel 2 on one device only). */
+int muon_polar_poly_rows_sm100(const void* gram, void* poly, int64_t batch,
+                               int64_t mp, int64_t row_begin, int64_t row_count,
+                               float b, float c, void* stream);
+
 /* Kernel (3): y[b] = bf16(T) + bf16(alpha_bf16 * x) with T = (poly[b].x[b])
  * accumulated in fp32 and the final add done on bf16 values, as in
  * csrc/muon_polar_unified_ascend950.asc:1472-1476; alpha_bf16 is `a`

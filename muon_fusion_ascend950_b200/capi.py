@@ -34,6 +34,8 @@ SIGNATURES = {
                                                  ctypes.c_size_t, _VP]),
     "muon_polar_poly_sm100": (ctypes.c_int, [_VP, _VP, _I64, _I64, ctypes.c_float,
                                              ctypes.c_float, _VP, ctypes.c_size_t, _VP]),
+    "muon_polar_poly_rows_sm100": (ctypes.c_int, [_VP, _VP, _I64, _I64, _I64, _I64,
+                                                  ctypes.c_float, ctypes.c_float, _VP]),
     "muon_polar_apply_sm100": (ctypes.c_int, [_VP, _VP, _VP, _I64, _I64, _I64, _I64,
                                               _I64, ctypes.c_float, _VP]),
     "muon_polar_step_sm100": (ctypes.c_int, [_VP, _VP, _VP, ctypes.c_size_t, _VP,
@@ -212,6 +214,15 @@ class CAPI:
         self._check("muon_polar_poly_sm100", self.lib.muon_polar_poly_sm100(
             gram.data_ptr(), poly.data_ptr(), bsz, mp, float(b), float(c), sp, sb,
             self._stream(stream)))
+
+    def poly_rows(self, gram, poly, b: float, c: float, row_begin: int, row_count: int,
+                  stream=None) -> None:
+        """Rows [row_begin, row_begin + row_count) of kernel (2)'s output,
+        written into the full buffer `poly`."""
+        bsz, mp, _ = gram.shape
+        self._check("muon_polar_poly_rows_sm100", self.lib.muon_polar_poly_rows_sm100(
+            gram.data_ptr(), poly.data_ptr(), bsz, mp, int(row_begin), int(row_count),
+            float(b), float(c), self._stream(stream)))
 
     def apply(self, poly, x, y, a: float, n: Optional[int] = None, stream=None) -> None:
         bsz, m, ldx = x.shape

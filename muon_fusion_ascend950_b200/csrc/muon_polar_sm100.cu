@@ -61,6 +61,11 @@ struct EpiParams {
   // polynomial kernel, which writes only P, and runs only after the Gram
   // kernel -- whose own dependency wait covers X -- has completed.
   int32_t x_ready;
+  // kPoly only: compute whole rows of tile blocks [row_tile_begin,
+  // row_tile_begin + tiles_m) -- both triangles, no mirror -- instead of the
+  // upper triangle (a row slab of P for a multi-GPU caller).
+  int32_t rows_mode;
+  int32_t row_tile_begin;
   // Split-K (symmetric kinds): each tile's K range is cut into `splits`
   // work items of (nearly) equal length; item = tile * splits + split.
   int32_t splits;
@@ -111,10 +116,11 @@ __host__ __device__ __forceinline__ WorkItem decode_item(const EpiParams& p, int
                                                          bool sym) {
   WorkItem w;
   const int tile = item / p.splits;
-  const TileCoord tc = decode_tile(tile, sym, p.tiles_m, p.tiles_n, p.tiles_per_batch);
+  const TileCoord tc =
+      decode_tile(tile, sym && !p.rows_mode, p.tiles_m, p.tiles_n, p.tiles_per_batch);
   w.tile = tile;
   w.b = tc.b;
-  w.tm = tc.tm;
+  w.tm = tc.tm + p.row_tile_begin;
   w.tn = tc.tn;
   w.split = item - tile * p.splits;
   w.nsplit = p.splits;
@@ -629,7 +635,7 @@ __global__ void __launch_bounds__(kTileThreads, 1)
         break;
       }
       tc_fence_after();
-      const bool mirror = kSym && tc.tm != tc.tn;
+      const bool mirror = kSym && !p.rows_mode && tc.tm != tc.tn;
       const int row0 = tc.tm * kTileM + static_cast<int>(rank) * kHalf;
       const int col0 = tc.tn * kTileN;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * kTileN;
@@ -1668,6 +1674,59 @@ int poly_impl(const void* gram, void* poly, int64_t batch, int64_t mp, float b,
   return poly_launch<1>(st, gram, poly, batch, mp, b, c, scratch, scratch_bytes, stream);
 }
 
+// Rows [row_begin, row_begin + row_count) of P into the full [batch][mp][mp]
+// buffer `poly` (whole rows, both triangles), for callers that split kernel
+// (2) over GPUs by row slabs.
+template <int PAIR>
+int poly_rows_launch(DeviceState* st, const void* gram, void* poly, int64_t batch, int64_t mp,
+                     int64_t row_begin, int64_t row_count, float b, float c,
+                     cudaStream_t stream) {
+  using Cfg = PairCfg<kPoly, PAIR>;
+  TileMaps tm;
+  int rc = encode_square(&tm.a, gram, batch, mp, false, kHalf);
+  if (rc != MUON_POLAR_OK) return rc;
+  tm.b = tm.a;
+  tm.aux = tm.a;
+  rc = encode_square(&tm.out, poly, batch, mp, false, kHalf);
+  if (rc != MUON_POLAR_OK) return rc;
+  tm.mir = tm.out;
+  EpiParams p = {};
+  p.tiles_m = static_cast<int32_t>(row_count / Cfg::kTileM);
+  p.tiles_n = static_cast<int32_t>(mp / Cfg::kTileN);
+  p.tiles_per_batch = p.tiles_m * p.tiles_n;
+  p.total_tiles = static_cast<int32_t>(p.tiles_per_batch * batch);
+  p.rows_mode = 1;
+  p.row_tile_begin = static_cast<int32_t>(row_begin / Cfg::kTileM);
+  p.k_blocks = static_cast<int32_t>(k_blocks_of<kPoly, PAIR>(mp));
+  p.coef_b = b;
+  p.coef_c = c;
+  plan_no_splits(p);
+  return launch_tile<kPoly, PAIR>(st, tm, p, stream);
+}
+
+int poly_rows_impl(const void* gram, void* poly, int64_t batch, int64_t mp, int64_t row_begin,
+                   int64_t row_count, float b, float c, cudaStream_t stream) {
+  if (gram == nullptr || poly == nullptr || batch <= 0 || mp <= 0 || (mp % kPairM) != 0 ||
+      batch > INT32_MAX || mp > (1 << 24) || row_begin < 0 || row_count <= 0 ||
+      (row_begin % kPairM) != 0 || (row_count % kPairM) != 0 || row_begin + row_count > mp)
+    return MUON_POLAR_ERR_INVALID_ARGUMENT;
+  if (!aligned16(gram) || !aligned16(poly)) return MUON_POLAR_ERR_ALIGNMENT;
+  if ((row_count / kHalf) * (mp / kHalf) * batch > INT32_MAX)
+    return MUON_POLAR_ERR_INVALID_ARGUMENT;
+  DeviceState* st = nullptr;
+  int rc = current_device_state(&st);
+  if (rc != MUON_POLAR_OK) return rc;
+  int pairs = 0, ctas = 0;
+  rc = tile_capacity<kPoly, 2>(st, &pairs);
+  if (rc != MUON_POLAR_OK) return rc;
+  rc = tile_capacity<kPoly, 1>(st, &ctas);
+  if (rc != MUON_POLAR_OK) return rc;
+  if (use_pairs(row_count / kPairM * (mp / kPairN) * batch, pairs, cost_blocks<2>(mp),
+                row_count / kHalf * (mp / kHalf) * batch, ctas, cost_blocks<1>(mp)))
+    return poly_rows_launch<2>(st, gram, poly, batch, mp, row_begin, row_count, b, c, stream);
+  return poly_rows_launch<1>(st, gram, poly, batch, mp, row_begin, row_count, b, c, stream);
+}
+
 // Host-side fp32 -> bf16 round-to-nearest-even, the same rule as the
 // reference's FloatToBf16Bits (binding.cpp:156-162).
 float round_to_bf16(float v) {
@@ -2000,6 +2059,13 @@ int muon_polar_poly_sm100(const void* gram, void* poly, int64_t batch,
                           size_t scratch_bytes, void* stream) {
   return poly_impl(gram, poly, batch, mp, b, c, scratch, scratch_bytes,
                    static_cast<cudaStream_t>(stream));
+}
+
+int muon_polar_poly_rows_sm100(const void* gram, void* poly, int64_t batch, int64_t mp,
+                               int64_t row_begin, int64_t row_count, float b, float c,
+                               void* stream) {
+  return poly_rows_impl(gram, poly, batch, mp, row_begin, row_count, b, c,
+                        static_cast<cudaStream_t>(stream));
 }
 
 int muon_polar_apply_sm100(const void* poly, const void* x, void* y,

@@ -11,7 +11,10 @@ workloads it is benchmarked on shard in two ways:
   slab X[:, r*N/G : (r+1)*N/G] for the whole iteration.  Per step:
     1. partial Gram G_r = X_r X_r^T in fp32 (kernel 1, fp32 output),
     2. one all-reduce (sum, fp32, Mp x Mp) over NCCL,
-    3. A = bf16(sum) (cast kernel), P = b A + c A A (kernel 2, replicated),
+    3. A = bf16(sum) (cast kernel), P = b A + c A A (kernel 2), either
+       replicated on every rank or (shard_poly) as row slabs, rank r
+       computing rows [r Mp/G, (r+1) Mp/G) followed by an all-gather of the
+       bf16 slabs,
     4. Y_r = a X_r + P X_r on the local slab (kernel 3).
   The result equals the single-GPU step up to the fp32 summation order of
   the Gram (A is rounded to bf16 once, after the sum, as on one GPU).
@@ -71,9 +74,11 @@ def column_range(n: int, rank: int, world: int, align: int = 8) -> range:
 class ColumnShardedPolar:
     """Polar Express steps on a matrix whose columns are split across the
     ranks of `group` (see the module docstring).  Buffers for the replicated
-    Mp x Mp Gram / polynomial are allocated once per instance."""
+    Mp x Mp Gram / polynomial are allocated once per instance.  With
+    `shard_poly`, kernel 2 is split into row slabs across the ranks (when
+    Mp divides into equal slabs of 256-row multiples; otherwise replicated)."""
 
-    def __init__(self, m: int, device, group=None, backend=None):
+    def __init__(self, m: int, device, group=None, backend=None, shard_poly: bool = False):
         if backend is None:
             from .capi import capi
 
@@ -83,6 +88,12 @@ class ColumnShardedPolar:
         self.m = m
         self.mp = backend.padded_rows(m)
         self.device = torch.device(device)
+        world = dist.get_world_size(group) if dist.is_initialized() else 1
+        rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.poly_slab = None
+        if shard_poly and world > 1 and self.mp % (256 * world) == 0:
+            rows = self.mp // world
+            self.poly_slab = (rank * rows, rows)
         shape = (1, self.mp, self.mp)
         self.gram_f32 = torch.empty(shape, dtype=torch.float32, device=self.device)
         self.gram = torch.empty(shape, dtype=torch.bfloat16, device=self.device)
@@ -100,7 +111,15 @@ class ColumnShardedPolar:
         if dist.is_initialized() and dist.get_world_size(self.group) > 1:
             dist.all_reduce(self.gram_f32, op=dist.ReduceOp.SUM, group=self.group)
         self.backend.cast_f32_bf16(self.gram_f32, self.gram)
-        self.backend.poly(self.gram, self.poly, b, c)
+        if self.poly_slab is None:
+            self.backend.poly(self.gram, self.poly, b, c)
+        else:
+            begin, rows = self.poly_slab
+            self.backend.poly_rows(self.gram, self.poly, b, c, begin, rows)
+            flat = self.poly.view(-1)
+            per = rows * self.mp
+            dist.all_gather_into_tensor(flat, flat[begin * self.mp: begin * self.mp + per],
+                                        group=self.group)
         self.backend.apply(self.poly, x3, y3, a)
         return y3.squeeze(0)
 

@@ -169,6 +169,15 @@ class CpuKernels:
         poly.copy_(((b32 * a32) + (c32 * (a32 @ a32.mT))).to(torch.bfloat16))
 
     @staticmethod
+    def poly_rows(gram, poly, b, c, row_begin, row_count, stream=None):
+        a32 = gram.to(torch.float32)
+        rows = slice(row_begin, row_begin + row_count)
+        b32 = torch.tensor(b, dtype=torch.float32)
+        c32 = torch.tensor(c, dtype=torch.float32)
+        poly[:, rows].copy_(((b32 * a32[:, rows]) + (c32 * (a32[:, rows] @ a32.mT)))
+                            .to(torch.bfloat16))
+
+    @staticmethod
     def apply(poly, x, y, a, n=None, stream=None):
         m = x.shape[1]
         t = poly.to(torch.float32)[:, :m, :m] @ x.to(torch.float32)

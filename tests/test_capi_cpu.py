@@ -77,6 +77,10 @@ def test_argument_validation_without_device(api):
     assert lib.muon_polar_gram_static_scratch_sm100(None, _vp(16), 1, 8, 8, 8, None) == -1
     assert lib.muon_polar_gram_static_scratch_sm100(_vp(16), _vp(24), 1, 8, 8, 8, None) == -3
     assert lib.muon_polar_set_kernel_policy(7) == -1
+    # poly rows: slab not a multiple of 256, or past the end
+    assert lib.muon_polar_poly_rows_sm100(_vp(16), _vp(16), 1, 512, 128, 256, 1.0, 1.0, None) == -1
+    assert lib.muon_polar_poly_rows_sm100(_vp(16), _vp(16), 1, 512, 256, 512, 1.0, 1.0, None) == -1
+    assert lib.muon_polar_poly_rows_sm100(_vp(16), _vp(24), 1, 512, 0, 256, 1.0, 1.0, None) == -3
     assert lib.muon_polar_set_split_mode(3) == -1
     assert lib.muon_polar_set_split_mode(-1) == -1
     assert lib.muon_polar_read_device_status(0, None, 0) == -1

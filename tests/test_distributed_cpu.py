@@ -77,7 +77,7 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _column_worker(rank, world, port, m, n, steps, out_dir):
+def _column_worker(rank, world, port, m, n, steps, out_dir, shard_poly=False):
     import datetime
 
     import torch.distributed as dist
@@ -92,18 +92,23 @@ def _column_worker(rank, world, port, m, n, steps, out_dir):
     x = make_input((m, n), seed=7)
     cols = column_range(n, rank, world)
     x_local = x[:, cols.start:cols.stop].contiguous()
-    driver = ColumnShardedPolar(m, "cpu", backend=CpuKernels())
+    driver = ColumnShardedPolar(m, "cpu", backend=CpuKernels(), shard_poly=shard_poly)
+    if shard_poly:
+        # 2 ranks, Mp = 512: rank r computes polynomial rows [256 r, 256 r + 256)
+        assert driver.poly_slab == (256 * rank, 256)
     y = driver.run(x_local, COEFFICIENTS[:steps])
     torch.save(y, os.path.join(out_dir, f"y{rank}.pt"))
     dist.barrier()
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("m,n,steps", [(96, 200, 1), (130, 256, 2)])
-def test_column_sharded_two_ranks_match_single(tmp_path, m, n, steps):
+@pytest.mark.parametrize("m,n,steps,shard_poly", [(96, 200, 1, False), (130, 256, 2, False),
+                                                (300, 320, 2, True)])
+def test_column_sharded_two_ranks_match_single(tmp_path, m, n, steps, shard_poly):
     ctx = mp.get_context("spawn")
     port = _free_port()
-    procs = [ctx.Process(target=_column_worker, args=(r, 2, port, m, n, steps, str(tmp_path)))
+    procs = [ctx.Process(target=_column_worker,
+                         args=(r, 2, port, m, n, steps, str(tmp_path), shard_poly))
              for r in range(2)]
     for p in procs:
         p.start()

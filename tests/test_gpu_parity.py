@@ -183,6 +183,32 @@ def test_poly_stage(api, cuda_device, shape, mode, mode_policy):
 
 
 @pytest.mark.parametrize("mode", ["single", "pair"])
+@pytest.mark.parametrize("shape,slabs", [((2, 512, 1024), ((0, 256), (256, 256))),
+                                         ((1, 1024, 512), ((256, 512), (0, 1024)))])
+def test_poly_rows_match_full(api, cuda_device, shape, slabs, mode, mode_policy):
+    """Row slabs of kernel (2) (muon_polar_poly_rows_sm100, the multi-GPU
+    split of the polynomial) equal the full kernel's rows bit for bit and
+    leave the other rows untouched."""
+    mode_policy(mode)
+    bsz, m, n = shape
+    x = make_input(shape, seed=10).to(cuda_device)
+    mp = api.padded_rows(m)
+    gram = torch.empty((bsz, mp, mp), dtype=torch.bfloat16, device=cuda_device)
+    full = torch.empty_like(gram)
+    api.gram(x, gram)
+    api.poly(gram, full, B1, C1)
+    for begin, rows in slabs:
+        out = torch.full_like(gram, float("nan"))
+        api.poly_rows(gram, out, B1, C1, begin, rows)
+        torch.cuda.synchronize()
+        _check_watchdog(api)
+        sl = slice(begin, begin + rows)
+        assert torch.equal(out[:, sl].view(torch.int16), full[:, sl].view(torch.int16))
+        rest = torch.cat([out[:, :begin], out[:, begin + rows:]], dim=1)
+        assert bool(torch.isnan(rest.float()).all())
+
+
+@pytest.mark.parametrize("mode", ["single", "pair"])
 @pytest.mark.parametrize("shape", [(1, 128, 256), (2, 150, 2064), (8, 512, 2048),
                                    (1, 200, 1000), (2, 384, 520)])
 def test_apply_stage(api, cuda_device, shape, mode, mode_policy):
