@@ -365,3 +365,18 @@ def test_fused_step_matches_three_kernels(api, cuda_device, shape, step_mode):
     assert torch.equal(outs[1].view(torch.int16), outs[2].view(torch.int16))
     e = error_stats(outs[1], reference_formula(make_input(shape, seed=8).float(), COEFFICIENTS[:1]))
     assert e["rel_fro"] <= 1e-2, e
+
+
+def test_torch_compile_matches_eager(op, cuda_device):
+    """torch.compile (aot_eager backend, full graph) traces the operator with
+    its FakeTensor kernel and runs it; the result equals eager bit for bit."""
+    x = make_input((2, 256, 512), seed=11).to(cuda_device)
+
+    def f(t):
+        return torch.ops.muon_ascend950.polar_step(t, A1, B1, C1)
+
+    compiled = torch.compile(f, backend="aot_eager", fullgraph=True)
+    y_c = compiled(x)
+    y_e = f(x)
+    torch.cuda.synchronize()
+    assert torch.equal(y_c.view(torch.int16), y_e.view(torch.int16))

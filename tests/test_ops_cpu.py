@@ -51,3 +51,17 @@ def test_loader_respects_library_override(tmp_path, monkeypatch):
     monkeypatch.setenv("MUON_ASCEND950_LIBRARY", str(tmp_path / "missing.so"))
     with pytest.raises(RuntimeError, match="does not exist"):
         _loader._library_path()
+
+
+def test_fake_kernel_traces_into_a_graph():
+    """The operator traces through the FakeTensor kernel (no device needed):
+    make_fx in fake mode records one call of the op with the input's shape."""
+    from torch.fx.experimental.proxy_tensor import make_fx
+
+    def f(x):
+        return torch.ops.muon_ascend950.polar_step(x, 1.5, -0.5, 0.25)
+
+    gm = make_fx(f, tracing_mode="fake")(torch.empty(2, 16, 32, dtype=torch.bfloat16))
+    calls = [n for n in gm.graph.nodes if n.op == "call_function"]
+    assert [str(n.target) for n in calls] == ["muon_ascend950.polar_step.default"]
+    assert tuple(calls[0].meta["val"].shape) == (2, 16, 32)
