@@ -190,6 +190,36 @@ int muon_polar_step_sm100(const void* x, void* y, void* workspace,
                           int64_t n, int64_t ldx, int64_t ldy, float a,
                           float b, float c, void* stream);
 
+/* M > N without transposed copies.  The reference's Python wrapper runs a
+ * tall X (M > N) as polar_step(X^T).mT, making two transposed copies
+ * (muon_ascend950/ops.py:27-32).  These entries compute the same result in
+ * X's own layout:
+ *     A = X^T . X          [batch][Np][Np] bf16, Np = muon_polar_padded_rows(n)
+ *     P = b . A + c . A . A
+ *     Y = a . X + X . P    (= (a . X^T + P . X^T)^T, P symmetric)
+ * with the arithmetic of kernels 1-3 (fp32 accumulation, the same epilogue
+ * roundings).  The Gram reads X with M-contiguous ("MN-major") tiles.
+ * x and y are [batch][m][ld] with ldx, ldy % 8 == 0, any m and n.
+ *
+ * muon_polar_gram_t_sm100: kernel (1) on X^T; rows/cols >= n of gram are
+ *   zeros.  scratch as for kernel (1); muon_polar_scratch_bytes(batch, n, m)
+ *   covers it.
+ * muon_polar_apply_t_sm100: kernel (3) on X^T; poly is [batch][Np][Np].
+ *   Columns [n, align(n, 8)) of y (inside the row stride) may be written
+ *   with zeros; later columns are not touched.
+ * muon_polar_step_t_sm100: the three kernels; workspace must hold
+ *   muon_polar_workspace_bytes(batch, n) bytes; y must not alias x. */
+int muon_polar_gram_t_sm100(const void* x, void* gram, int64_t batch, int64_t m,
+                            int64_t n, int64_t ldx, void* scratch, size_t scratch_bytes,
+                            void* stream);
+int muon_polar_apply_t_sm100(const void* poly, const void* x, void* y, int64_t batch,
+                             int64_t m, int64_t n, int64_t ldx, int64_t ldy, float a,
+                             void* stream);
+int muon_polar_step_t_sm100(const void* x, void* y, void* workspace, size_t workspace_bytes,
+                            void* scratch, size_t scratch_bytes, int64_t batch, int64_t m,
+                            int64_t n, int64_t ldx, int64_t ldy, float a, float b, float c,
+                            void* stream);
+
 /* dst[i] = bf16_rne(src[i]) for i < count (fp32 Gram after the cross-rank
  * sum -> bf16 input of kernel 2). No counterpart in the reference, which has
  * no multi-device path. */

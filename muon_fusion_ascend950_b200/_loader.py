@@ -50,9 +50,12 @@ def load_library() -> None:
     def fake_polar_step(x, a: float, b: float, c: float):
         return torch.empty_like(x, memory_format=torch.contiguous_format)
 
-    try:
-        torch.library.register_fake("muon_ascend950::polar_step")(fake_polar_step)
-    except RuntimeError as exc:
-        if "already has" not in str(exc):
-            raise
+    # polar_step_t (an extension: the step of x^T in x's layout) has the same
+    # output contract.
+    for name in ("muon_ascend950::polar_step", "muon_ascend950::polar_step_t"):
+        try:
+            torch.library.register_fake(name)(fake_polar_step)
+        except RuntimeError as exc:
+            if "already has" not in str(exc):
+                raise
     _LOADED = True

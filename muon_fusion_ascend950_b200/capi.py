@@ -42,6 +42,14 @@ SIGNATURES = {
                                              ctypes.c_size_t, _I64, _I64, _I64, _I64, _I64,
                                              ctypes.c_float, ctypes.c_float, ctypes.c_float,
                                              _VP]),
+    "muon_polar_gram_t_sm100": (ctypes.c_int, [_VP, _VP, _I64, _I64, _I64, _I64, _VP,
+                                               ctypes.c_size_t, _VP]),
+    "muon_polar_apply_t_sm100": (ctypes.c_int, [_VP, _VP, _VP, _I64, _I64, _I64, _I64,
+                                                _I64, ctypes.c_float, _VP]),
+    "muon_polar_step_t_sm100": (ctypes.c_int, [_VP, _VP, _VP, ctypes.c_size_t, _VP,
+                                               ctypes.c_size_t, _I64, _I64, _I64, _I64, _I64,
+                                               ctypes.c_float, ctypes.c_float, ctypes.c_float,
+                                               _VP]),
     "muon_polar_cast_f32_bf16_sm100": (ctypes.c_int, [_VP, _VP, _I64, _VP]),
     "muon_polar_read_device_status": (ctypes.c_int, [ctypes.c_int,
                                                      ctypes.POINTER(ctypes.c_uint32),
@@ -237,6 +245,32 @@ class CAPI:
         n = ldx if n is None else n
         sp, sb = _scratch(scratch)
         self._check("muon_polar_step_sm100", self.lib.muon_polar_step_sm100(
+            x.data_ptr(), y.data_ptr(), workspace.data_ptr(), _nbytes(workspace), sp, sb,
+            bsz, m, n, ldx, y.shape[-1], float(a), float(b), float(c),
+            self._stream(stream)))
+
+    # The step of X^T returned in X's layout (M > N without transposed
+    # copies): gram is [B, Np, Np] with Np = padded_rows(n).
+    def gram_t(self, x, gram, n: Optional[int] = None, scratch=None, stream=None) -> None:
+        b, m, ld = x.shape
+        n = ld if n is None else n
+        sp, sb = _scratch(scratch)
+        self._check("muon_polar_gram_t_sm100", self.lib.muon_polar_gram_t_sm100(
+            x.data_ptr(), gram.data_ptr(), b, m, n, ld, sp, sb, self._stream(stream)))
+
+    def apply_t(self, poly, x, y, a: float, n: Optional[int] = None, stream=None) -> None:
+        bsz, m, ldx = x.shape
+        n = ldx if n is None else n
+        self._check("muon_polar_apply_t_sm100", self.lib.muon_polar_apply_t_sm100(
+            poly.data_ptr(), x.data_ptr(), y.data_ptr(), bsz, m, n, ldx, y.shape[-1],
+            float(a), self._stream(stream)))
+
+    def step_t(self, x, y, workspace, a: float, b: float, c: float,
+               n: Optional[int] = None, scratch=None, stream=None) -> None:
+        bsz, m, ldx = x.shape
+        n = ldx if n is None else n
+        sp, sb = _scratch(scratch)
+        self._check("muon_polar_step_t_sm100", self.lib.muon_polar_step_t_sm100(
             x.data_ptr(), y.data_ptr(), workspace.data_ptr(), _nbytes(workspace), sp, sb,
             bsz, m, n, ldx, y.shape[-1], float(a), float(b), float(c),
             self._stream(stream)))

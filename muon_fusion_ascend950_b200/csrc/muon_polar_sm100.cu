@@ -11,6 +11,11 @@
 //   kPoly       A rows tm             A rows tn  (K-major)    bf16(b*A + c*acc), tile + mirror
 //   kApply      P rows tm             X[k, n-block] (MN-major) bf16(bf16(acc) + bf16(alpha*X))
 //
+// and, for M > N without transposed copies (the step of X^T, returned in
+// X's layout: A = X^T.X, Y = a.X + X.P, P symmetric):
+//   kGramT      X[k, tm-block] (MN)   X[k, tn-block] (MN)     as kGramBf16
+//   kApplyT     X rows tm             P rows tn  (K-major)    as kApply
+//
 // Two engines of the same kernel (polar_tile_kernel<KIND, PAIR>): 256 x 256
 // tiles on a tcgen05 CTA pair (PAIR = 2) and 128 x 128 tiles on one CTA
 // (PAIR = 1), chosen by problem size.  CTA layout (320 threads): warp 0 lane
@@ -42,7 +47,19 @@
 
 namespace muon_sm100 {
 
-enum Kind : int { kGramBf16 = 0, kGramF32 = 1, kPoly = 2, kApply = 3 };
+enum Kind : int { kGramBf16 = 0, kGramF32 = 1, kPoly = 2, kApply = 3, kGramT = 4, kApplyT = 5 };
+constexpr int kNumKinds = 6;
+
+// The transposed kinds share the epilogue of their plain counterparts.
+__host__ __device__ constexpr int epi_kind(int kind) {
+  return kind == kGramT ? kGramBf16 : (kind == kApplyT ? kApply : kind);
+}
+// Operand layouts in global memory: K-major unless stated.
+__host__ __device__ constexpr bool a_mn_major(int kind) { return kind == kGramT; }
+__host__ __device__ constexpr bool b_mn_major(int kind) { return kind == kApply || kind == kGramT; }
+// Which operand is X in the apply kinds (1 = A, 2 = B), 0 otherwise: X can
+// be loaded before the grid dependency wait when the launch says so.
+__host__ __device__ constexpr int x_operand(int kind) { return kind == kApplyT ? 1 : (kind == kApply ? 2 : 0); }
 
 __device__ uint32_t g_watchdog = 0;
 
@@ -170,7 +187,7 @@ constexpr uint32_t kAtomBytes = kHalf * kAtom * 2;  // one [128 x 64] box, 16 Ki
 // leave room for four or five of them beside their larger epilogue buffers.
 template <int KIND, int PAIR>
 constexpr int stage_k() {
-  return (PAIR == 1 || KIND == kGramBf16) ? 128 : 64;
+  return (PAIR == 1 || KIND == kGramBf16 || KIND == kGramT) ? 128 : 64;
 }
 template <int KIND, int PAIR>
 constexpr int64_t k_blocks_of(int64_t k) {
@@ -182,8 +199,8 @@ constexpr int64_t k_blocks_of(int64_t k) {
 // band); PAIR = 1: a 128 x 128 tile on one CTA.
 template <int KIND, int PAIR = 2>
 struct PairCfg {
-  static constexpr bool kSym = KIND != kApply;
-  static constexpr bool kAux = KIND == kPoly || KIND == kApply;
+  static constexpr bool kSym = KIND != kApply && KIND != kApplyT;
+  static constexpr bool kAux = KIND == kPoly || KIND == kApply || KIND == kApplyT;
   static constexpr bool kF32 = KIND == kGramF32;
   static constexpr int kTileM = kHalf * PAIR;
   static constexpr int kTileN = PAIR == 2 ? kPairN : kHalf;
@@ -340,7 +357,9 @@ __global__ void __launch_bounds__(kTileThreads, 1)
   constexpr int kTileM = Cfg::kTileM;
   constexpr int kTileN = Cfg::kTileN;
   constexpr int S = Cfg::kStages;
-  constexpr bool kBmn = (KIND == kApply);
+  constexpr bool kAmn = a_mn_major(KIND);
+  constexpr bool kBmn = b_mn_major(KIND);
+  constexpr int kX = x_operand(KIND);
   constexpr bool kSym = Cfg::kSym;
 
   extern __shared__ uint8_t smem_raw[];
@@ -413,17 +432,21 @@ __global__ void __launch_bounds__(kTileThreads, 1)
       const uint32_t pid = warp == 0 ? 0u : 1u;
       // Loads of one operand into stage s of the pipeline; PAIR = 2 counts
       // the bytes on the leader's barrier, PAIR = 1 on its own.
+      // K-major: [128 rows x 64 k] boxes; MN-major: one [kBK k x 64 rows] box
+      // per 64-row chunk.
       auto load_a = [&](uint32_t s, const WorkItem& w, int kb) {
         const uint32_t bar = PAIR == 2 ? map_to_cta(smem_addr(&full[s]), 0) : 0u;
         const int a_row = w.tm * kTileM + static_cast<int>(rank) * kHalf;
+        constexpr int kBoxes = kAmn ? kHalf / kAtom : Cfg::kBK / kAtom;
 #pragma unroll
-        for (int j = 0; j < Cfg::kBK / kAtom; ++j) {
+        for (int j = 0; j < kBoxes; ++j) {
+          void* dst = sA + s * Cfg::kAHalfBytes + j * (kAmn ? Cfg::kBK * 128 : kAtomBytes);
+          const int c0 = kAmn ? a_row + j * kAtom : kb * Cfg::kBK + j * kAtom;
+          const int c1 = kAmn ? kb * Cfg::kBK : a_row;
           if constexpr (PAIR == 2)
-            tma_load_3d_pair(sA + s * Cfg::kAHalfBytes + j * kAtomBytes, &tmap_a, bar,
-                             kb * Cfg::kBK + j * kAtom, a_row, w.b);
+            tma_load_3d_pair(dst, &tmap_a, bar, c0, c1, w.b);
           else
-            tma_load_3d(sA + s * Cfg::kAHalfBytes + j * kAtomBytes, &tmap_a, &full[s],
-                        kb * Cfg::kBK + j * kAtom, a_row, w.b);
+            tma_load_3d(dst, &tmap_a, &full[s], c0, c1, w.b);
         }
       };
       auto load_b = [&](uint32_t s, const WorkItem& w, int kb) {
@@ -443,11 +466,11 @@ __global__ void __launch_bounds__(kTileThreads, 1)
             tma_load_3d(dst, &tmap_b, &full[s], c0, c1, w.b);
         }
       };
-      // The first pipeline iterations' B operand (X) before the dependency
-      // wait, when X does not depend on the previous kernel.  Their stages
-      // are fresh, so no empty-wait is needed.
+      // The first pipeline iterations' X operand before the dependency wait,
+      // when X does not depend on the previous kernel.  Their stages are
+      // fresh, so no empty-wait is needed.
       uint32_t n_pre = 0;
-      if constexpr (kBmn) {
+      if constexpr (kX != 0) {
         if (p.x_ready) {
           uint32_t it = 0;
           for (int item = cluster; item < p.total_items && it < static_cast<uint32_t>(S);
@@ -456,7 +479,10 @@ __global__ void __launch_bounds__(kTileThreads, 1)
             for (int kb = w.kb_begin; kb < w.kb_end && it < static_cast<uint32_t>(S); ++kb, ++it) {
               if (it % Cfg::kProducers != pid) continue;
               if (rank == 0) mbar_arrive_expect_tx(&full[it], PAIR * Cfg::kStageBytes);
-              load_b(it, w, kb);
+              if constexpr (kX == 1)
+                load_a(it, w, kb);
+              else
+                load_b(it, w, kb);
             }
           }
           n_pre = it;
@@ -475,7 +501,8 @@ __global__ void __launch_bounds__(kTileThreads, 1)
           if (it % Cfg::kProducers != pid) continue;
           const uint32_t s = it % S;
           const uint32_t ph = (it / S) & 1u;
-          if (it >= n_pre) {
+          const bool pre = it < n_pre;  // X operand already in flight
+          if (!pre) {
             if (!mbar_wait_bounded(&empty[s], ph ^ 1u)) {
               ok = false;
               break;
@@ -484,8 +511,8 @@ __global__ void __launch_bounds__(kTileThreads, 1)
               mbar_arrive_expect_tx(&full[s],
                                     PAIR * (diag ? Cfg::kAHalfBytes : Cfg::kStageBytes));
           }
-          load_a(s, w, kb);
-          if (it >= n_pre && !diag) load_b(s, w, kb);
+          if (!(pre && kX == 1)) load_a(s, w, kb);
+          if (!diag && !(pre && kX == 2)) load_b(s, w, kb);
         }
       }
       if (!ok) atomicOr(&g_watchdog, MUON_POLAR_WATCHDOG_PRODUCER);
@@ -510,7 +537,7 @@ __global__ void __launch_bounds__(kTileThreads, 1)
     grid_launch_dependents();
     if (lane == 0 && rank == 0) {
       // ---------------- tcgen05 MMA issuer (leader CTA only)
-      constexpr uint32_t idesc = idesc_bf16_f32(kTileN, kBmn ? 1u : 0u, kTileM);
+      constexpr uint32_t idesc = idesc_bf16_f32(kTileN, kBmn ? 1u : 0u, kTileM, kAmn ? 1u : 0u);
       uint32_t it = 0;
       uint32_t t = 0;
       bool ok = true;
@@ -540,15 +567,12 @@ __global__ void __launch_bounds__(kTileThreads, 1)
             // K-major: K step k lies in swizzle atom k/4 (16 KiB apart), 32
             // bytes per step inside the atom's 128-byte rows.
             const uint32_t koff = (k / 4) * kAtomBytes + (k % 4) * 32;
-            const uint64_t ad = smem_desc_sw128(a_base + koff, 16, 1024);
-            uint64_t bd;
-            if constexpr (kBmn) {
-              // MN-major: 16 k-rows of 128 bytes per step; 64-column chunks
-              // are Cfg::kBK*128 bytes apart (leading offset).
-              bd = smem_desc_sw128(b_base + k * 2048, Cfg::kBK * 128, 1024);
-            } else {
-              bd = smem_desc_sw128(b_base + koff, 16, 1024);
-            }
+            // MN-major: 16 k-rows of 128 bytes per step; 64-column chunks are
+            // Cfg::kBK*128 bytes apart (leading offset).
+            const uint64_t ad = kAmn ? smem_desc_sw128(a_base + k * 2048, Cfg::kBK * 128, 1024)
+                                     : smem_desc_sw128(a_base + koff, 16, 1024);
+            const uint64_t bd = kBmn ? smem_desc_sw128(b_base + k * 2048, Cfg::kBK * 128, 1024)
+                                     : smem_desc_sw128(b_base + koff, 16, 1024);
             if constexpr (PAIR == 2)
               umma_bf16_pair(d_tmem, ad, bd, idesc, (kb > w.kb_begin || k > 0) ? 1u : 0u);
             else
@@ -610,7 +634,7 @@ __global__ void __launch_bounds__(kTileThreads, 1)
     };
     // The apply's input tile is X: before the dependency wait when X does not
     // depend on the previous kernel.
-    const bool aux_early = kBmn && p.x_ready;
+    const bool aux_early = kX != 0 && p.x_ready;
     if constexpr (Cfg::kAux) {
       if (leader && aux_early && cluster < p.total_items)
         for (int c = 0; c < Cfg::kChunks; ++c) load_aux_chunk(cluster, c);
@@ -779,7 +803,7 @@ __global__ void __launch_bounds__(kTileThreads, 1)
             v[4 * u + 3] = sum.w;
           }
         }
-        pair_epilogue_half<KIND>(p, out, mir, mirror, row, hc, v);
+        pair_epilogue_half<epi_kind(KIND)>(p, out, mir, mirror, row, hc, v);
         fence_proxy_async_smem();
         named_barrier(1, kPairEpiThreads);
         if (leader) {
@@ -1255,7 +1279,7 @@ namespace {
 std::atomic<uint64_t> g_launch_count{0};
 
 constexpr int kMaxDevices = 64;
-constexpr int kNumInstances = 8;
+constexpr int kNumInstances = 2 * kNumKinds;
 
 struct DeviceState {
   std::once_flag once;
@@ -1340,9 +1364,9 @@ struct TileMaps {
 // Slot of (KIND, PAIR) in the per-device caches.
 template <int KIND, int PAIR>
 constexpr int instance_of() {
-  return (PAIR - 1) * 4 + KIND;
+  return (PAIR - 1) * kNumKinds + KIND;
 }
-static_assert(instance_of<kApply, 2>() < kNumInstances, "instance slots");
+static_assert(instance_of<kNumKinds - 1, 2>() < kNumInstances, "instance slots");
 
 // Kernel choice: 0 = by size (the engine with the smaller estimated time,
 // see use_pairs), 1 = always CTA pairs, 2 = never.  Initial value from
@@ -1562,18 +1586,23 @@ void sym_grid(EpiParams& p, int64_t batch, int64_t mp) {
 // Kernel (1) on one engine.  `fixed_scratch`: the scratch is a fixed buffer
 // that keeps the previous call's contents -- a plan that needs more than it
 // holds is refused, and the arrival counters are cleared before the launch.
+// kGramT: the Gram of X^T, [batch][align(n, 256)]^2, contracting over the m
+// rows of X.
 template <int KIND, int PAIR>
 int gram_launch(DeviceState* st, const void* x, void* gram, int64_t batch, int64_t m,
                 int64_t n, int64_t ldx, void* scratch, size_t scratch_bytes,
                 bool fixed_scratch, cudaStream_t stream) {
-  const int64_t mp = padded_rows(m);
+  constexpr bool kT = KIND == kGramT;
+  const int64_t mp = padded_rows(kT ? n : m);
   int units = 0;
   int rc = tile_capacity<KIND, PAIR>(st, &units);
   if (rc != MUON_POLAR_OK) return rc;
   TileMaps tm;
-  // X: rows beyond m and columns beyond n read as zero.
+  // X: rows beyond m and columns beyond n read as zero.  K-major boxes of
+  // [128 rows x 64 columns]; MN-major (kGramT) boxes of [kBK rows x 64
+  // columns].
   rc = encode_3d(&tm.a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, x, n, m, batch, ldx, m * ldx,
-                 kAtom, kHalf);
+                 kAtom, kT ? PairCfg<KIND, PAIR>::kBK : kHalf);
   if (rc != MUON_POLAR_OK) return rc;
   tm.b = tm.a;
   tm.aux = tm.a;
@@ -1583,7 +1612,7 @@ int gram_launch(DeviceState* st, const void* x, void* gram, int64_t batch, int64
   if (rc != MUON_POLAR_OK) return rc;
   EpiParams p = {};
   sym_grid<PAIR>(p, batch, mp);
-  p.k_blocks = static_cast<int32_t>(k_blocks_of<KIND, PAIR>(n));
+  p.k_blocks = static_cast<int32_t>(k_blocks_of<KIND, PAIR>(kT ? m : n));
   if (fixed_scratch &&
       split_scratch_bytes<PAIR>(p.total_tiles,
                                 choose_splits<KIND, PAIR>(p.total_tiles, p.k_blocks, units)) >
@@ -1607,19 +1636,23 @@ int gram_impl(const void* x, void* gram, int64_t batch, int64_t m, int64_t n,
   if (rc != MUON_POLAR_OK) return rc;
   if (gram == nullptr) return MUON_POLAR_ERR_INVALID_ARGUMENT;
   if (!aligned16(gram)) return MUON_POLAR_ERR_ALIGNMENT;
+  // rows of the Gram and the contraction length
+  const int64_t rows = KIND == kGramT ? n : m;
+  const int64_t depth = KIND == kGramT ? m : n;
+  if (rows > (1 << 24)) return MUON_POLAR_ERR_INVALID_ARGUMENT;
   DeviceState* st = nullptr;
   rc = current_device_state(&st);
   if (rc != MUON_POLAR_OK) return rc;
-  const int64_t d = padded_rows(m) / kHalf;
+  const int64_t d = padded_rows(rows) / kHalf;
   if (d * (d + 1) / 2 * batch > INT32_MAX) return MUON_POLAR_ERR_INVALID_ARGUMENT;
-  const int64_t dp = padded_rows(m) / kPairM;
+  const int64_t dp = padded_rows(rows) / kPairM;
   int pairs = 0, ctas = 0;
   rc = tile_capacity<KIND, 2>(st, &pairs);
   if (rc != MUON_POLAR_OK) return rc;
   rc = tile_capacity<KIND, 1>(st, &ctas);
   if (rc != MUON_POLAR_OK) return rc;
-  if (fixed_scratch || use_pairs(dp * (dp + 1) / 2 * batch, pairs, cost_blocks<2>(n),
-                                 d * (d + 1) / 2 * batch, ctas, cost_blocks<1>(n)))
+  if (fixed_scratch || use_pairs(dp * (dp + 1) / 2 * batch, pairs, cost_blocks<2>(depth),
+                                 d * (d + 1) / 2 * batch, ctas, cost_blocks<1>(depth)))
     return gram_launch<KIND, 2>(st, x, gram, batch, m, n, ldx, scratch, scratch_bytes,
                                 fixed_scratch, stream);
   return gram_launch<KIND, 1>(st, x, gram, batch, m, n, ldx, scratch, scratch_bytes,
@@ -1801,6 +1834,69 @@ int apply_impl(const void* poly, const void* x, void* y, int64_t batch,
                 cost_blocks<1>(m)))
     return apply_launch<2>(st, poly, x, y, batch, m, n, ldx, ldy, a, x_ready, stream);
   return apply_launch<1>(st, poly, x, y, batch, m, n, ldx, ldy, a, x_ready, stream);
+}
+
+// Kernel (3) of the step of X^T returned in X's layout (M > N without
+// transposed copies): y = bf16( bf16(X.P) + bf16(alpha*X) ), X and Y
+// [batch][m][ld], P [batch][align(n, 256)]^2 -- symmetric, so its rows serve
+// as the K-major B operand of X.P.
+template <int PAIR>
+int apply_t_launch(DeviceState* st, const void* poly, const void* x, void* y, int64_t batch,
+                   int64_t m, int64_t n, int64_t ldx, int64_t ldy, float a, bool x_ready,
+                   cudaStream_t stream) {
+  using Cfg = PairCfg<kApplyT, PAIR>;
+  const int64_t np = padded_rows(n);
+  const int64_t tiles_m = (m + Cfg::kTileM - 1) / Cfg::kTileM;
+  const int64_t tiles_n = (n + Cfg::kTileN - 1) / Cfg::kTileN;
+  if (tiles_m * tiles_n * batch > INT32_MAX) return MUON_POLAR_ERR_INVALID_ARGUMENT;
+  TileMaps tm;
+  // X rows: the A operand (K = its columns) and the epilogue input tile.
+  int rc = encode_3d(&tm.a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, x, n, m, batch, ldx, m * ldx,
+                     kAtom, kHalf);
+  if (rc != MUON_POLAR_OK) return rc;
+  tm.aux = tm.a;
+  rc = encode_square(&tm.b, poly, batch, np, false, kHalf);
+  if (rc != MUON_POLAR_OK) return rc;
+  rc = encode_3d(&tm.out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, y, n, m, batch, ldy, m * ldy,
+                 kAtom, kHalf);
+  if (rc != MUON_POLAR_OK) return rc;
+  tm.mir = tm.out;
+  EpiParams p = {};
+  p.tiles_m = static_cast<int32_t>(tiles_m);
+  p.tiles_n = static_cast<int32_t>(tiles_n);
+  p.tiles_per_batch = static_cast<int32_t>(tiles_m * tiles_n);
+  p.total_tiles = static_cast<int32_t>(tiles_m * tiles_n * batch);
+  // X's columns >= n read as zero and P's rows/columns >= n are zero.
+  p.k_blocks = static_cast<int32_t>(k_blocks_of<kApplyT, PAIR>(n));
+  p.alpha = round_to_bf16(a);
+  p.x_ready = x_ready ? 1 : 0;
+  plan_no_splits(p);
+  return launch_tile<kApplyT, PAIR>(st, tm, p, stream);
+}
+
+int apply_t_impl(const void* poly, const void* x, void* y, int64_t batch, int64_t m,
+                 int64_t n, int64_t ldx, int64_t ldy, float a, cudaStream_t stream,
+                 bool x_ready = false) {
+  int rc = check_x_args(x, batch, m, n, ldx);
+  if (rc != MUON_POLAR_OK) return rc;
+  if (poly == nullptr || y == nullptr || ldy < n || n > (1 << 24))
+    return MUON_POLAR_ERR_INVALID_ARGUMENT;
+  if (!aligned16(poly) || !aligned16(y) || (ldy % 8) != 0)
+    return MUON_POLAR_ERR_ALIGNMENT;
+  DeviceState* st = nullptr;
+  rc = current_device_state(&st);
+  if (rc != MUON_POLAR_OK) return rc;
+  int pairs = 0, ctas = 0;
+  rc = tile_capacity<kApplyT, 2>(st, &pairs);
+  if (rc != MUON_POLAR_OK) return rc;
+  rc = tile_capacity<kApplyT, 1>(st, &ctas);
+  if (rc != MUON_POLAR_OK) return rc;
+  if (use_pairs((m + kPairM - 1) / kPairM * ((n + kPairN - 1) / kPairN) * batch, pairs,
+                cost_blocks<2>(n),
+                (m + kHalf - 1) / kHalf * ((n + kHalf - 1) / kHalf) * batch, ctas,
+                cost_blocks<1>(n)))
+    return apply_t_launch<2>(st, poly, x, y, batch, m, n, ldx, ldy, a, x_ready, stream);
+  return apply_t_launch<1>(st, poly, x, y, batch, m, n, ldx, ldy, a, x_ready, stream);
 }
 
 // ---------------------------------------------------------------- fused step
@@ -2100,6 +2196,41 @@ int muon_polar_step_sm100(const void* x, void* y, void* workspace,
   rc = poly_impl(gram, poly, batch, mp, b, c, scratch, scratch_bytes, s);
   if (rc != MUON_POLAR_OK) return rc;
   return apply_impl(poly, x, y, batch, m, n, ldx, ldy, a, s, /*x_ready=*/true);
+}
+
+int muon_polar_gram_t_sm100(const void* x, void* gram, int64_t batch, int64_t m,
+                            int64_t n, int64_t ldx, void* scratch, size_t scratch_bytes,
+                            void* stream) {
+  return gram_impl<kGramT>(x, gram, batch, m, n, ldx, scratch, scratch_bytes,
+                           static_cast<cudaStream_t>(stream));
+}
+
+int muon_polar_apply_t_sm100(const void* poly, const void* x, void* y, int64_t batch,
+                             int64_t m, int64_t n, int64_t ldx, int64_t ldy, float a,
+                             void* stream) {
+  return apply_t_impl(poly, x, y, batch, m, n, ldx, ldy, a, static_cast<cudaStream_t>(stream));
+}
+
+int muon_polar_step_t_sm100(const void* x, void* y, void* workspace, size_t workspace_bytes,
+                            void* scratch, size_t scratch_bytes, int64_t batch, int64_t m,
+                            int64_t n, int64_t ldx, int64_t ldy, float a, float b, float c,
+                            void* stream) {
+  int rc = check_x_args(x, batch, m, n, ldx);
+  if (rc != MUON_POLAR_OK) return rc;
+  if (y == nullptr || y == x || ldy < n || n > (1 << 24)) return MUON_POLAR_ERR_INVALID_ARGUMENT;
+  if (workspace == nullptr || !aligned16(workspace) ||
+      workspace_bytes < muon_polar_workspace_bytes(batch, n))
+    return MUON_POLAR_ERR_WORKSPACE;
+  const int64_t np = padded_rows(n);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  void* gram = ws;
+  void* poly = ws + static_cast<size_t>(batch * np * np * 2);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  rc = gram_impl<kGramT>(x, gram, batch, m, n, ldx, scratch, scratch_bytes, s);
+  if (rc != MUON_POLAR_OK) return rc;
+  rc = poly_impl(gram, poly, batch, np, b, c, scratch, scratch_bytes, s);
+  if (rc != MUON_POLAR_OK) return rc;
+  return apply_t_impl(poly, x, y, batch, m, n, ldx, ldy, a, s, /*x_ready=*/true);
 }
 
 size_t muon_polar_scratch_bytes(int64_t batch, int64_t m, int64_t n) {

@@ -103,8 +103,10 @@ std::pair<void*, size_t> GetScratch(const at::Tensor& like, int device,
   return {fresh.data_ptr(), bytes};
 }
 
-at::Tensor MuonPolarStepCuda(const at::Tensor& x, double a, double b,
-                             double c) {
+// `transposed` = false: the reference operator (M <= N).  true: the step of
+// X^T returned in X's layout, for tall X (M > N), without the two transposed
+// copies the reference's wrapper makes (ops.py:27-32).
+at::Tensor RunPolarStep(const at::Tensor& x, double a, double b, double c, bool transposed) {
   TORCH_CHECK(x.defined(), "muon_polar_step: x must be defined");
   TORCH_CHECK(x.device().is_cuda(), "muon_polar_step: x must be a CUDA tensor");
   TORCH_CHECK(x.scalar_type() == at::kBFloat16,
@@ -112,9 +114,10 @@ at::Tensor MuonPolarStepCuda(const at::Tensor& x, double a, double b,
   TORCH_CHECK(x.dim() == 3, "muon_polar_step: x must have shape [batch, M, N]");
   TORCH_CHECK(x.size(0) > 0 && x.size(1) > 0 && x.size(2) > 0,
               "muon_polar_step: all dimensions must be positive");
-  TORCH_CHECK(x.size(1) <= x.size(2),
-              "muon_polar_step: expects M <= N; transpose policy stays outside "
-              "this op");
+  if (!transposed)
+    TORCH_CHECK(x.size(1) <= x.size(2),
+                "muon_polar_step: expects M <= N; transpose policy stays outside "
+                "this op");
   const c10::cuda::CUDAGuard deviceGuard(x.device());
   at::Tensor input = x.contiguous();
   const int64_t batch = input.size(0);
@@ -132,7 +135,10 @@ at::Tensor MuonPolarStepCuda(const at::Tensor& x, double a, double b,
   }
   const auto stream = c10::cuda::getCurrentCUDAStream(x.device().index());
   void* raw_stream = static_cast<void*>(stream.stream());
-  const size_t wsBytes = muon_polar_workspace_bytes(batch, rows);
+  // The Gram is [batch][g][g]: g = M, or N for the transposed step.
+  const int64_t g = transposed ? cols : rows;
+  const int64_t depth = transposed ? rows : cols;
+  const size_t wsBytes = muon_polar_workspace_bytes(batch, g);
   at::Tensor workspace =
       at::empty({static_cast<int64_t>(wsBytes)}, input.options().dtype(at::kByte));
   at::Tensor out = at::empty({batch, rows, ld}, input.options());
@@ -140,45 +146,74 @@ at::Tensor MuonPolarStepCuda(const at::Tensor& x, double a, double b,
   const float fb = static_cast<float>(b);
   const float fc = static_cast<float>(c);
   const auto scratch = GetScratch(input, x.device().index(), stream.stream(),
-                                  muon_polar_scratch_bytes(batch, rows, cols));
+                                  muon_polar_scratch_bytes(batch, g, depth));
 
   if (!DebugSyncEnabled()) {
-    CheckStatus(muon_polar_step_sm100(input.data_ptr(), out.data_ptr(),
-                                      workspace.data_ptr(), wsBytes, scratch.first,
-                                      scratch.second, batch, rows, cols, ld, ld,
-                                      fa, fb, fc, raw_stream),
-                "polar_step_sm100");
+    if (transposed)
+      CheckStatus(muon_polar_step_t_sm100(input.data_ptr(), out.data_ptr(),
+                                          workspace.data_ptr(), wsBytes, scratch.first,
+                                          scratch.second, batch, rows, cols, ld, ld,
+                                          fa, fb, fc, raw_stream),
+                  "polar_step_t_sm100");
+    else
+      CheckStatus(muon_polar_step_sm100(input.data_ptr(), out.data_ptr(),
+                                        workspace.data_ptr(), wsBytes, scratch.first,
+                                        scratch.second, batch, rows, cols, ld, ld,
+                                        fa, fb, fc, raw_stream),
+                  "polar_step_sm100");
   } else {
     const int device = x.device().index();
-    const int64_t mp = muon_polar_padded_rows(rows);
+    const int64_t mp = muon_polar_padded_rows(g);
     uint8_t* ws = static_cast<uint8_t*>(workspace.data_ptr());
     void* gram = ws;
     void* poly = ws + static_cast<size_t>(batch * mp * mp * 2);
-    CheckStatus(muon_polar_gram_sm100(input.data_ptr(), gram, batch, rows,
-                                      cols, ld, scratch.first, scratch.second,
-                                      raw_stream),
-                "gram_sm100");
+    if (transposed)
+      CheckStatus(muon_polar_gram_t_sm100(input.data_ptr(), gram, batch, rows, cols, ld,
+                                          scratch.first, scratch.second, raw_stream),
+                  "gram_t_sm100");
+    else
+      CheckStatus(muon_polar_gram_sm100(input.data_ptr(), gram, batch, rows,
+                                        cols, ld, scratch.first, scratch.second,
+                                        raw_stream),
+                  "gram_sm100");
     DebugSync(device, "gram_sm100");
     CheckStatus(muon_polar_poly_sm100(gram, poly, batch, mp, fb, fc,
                                       scratch.first, scratch.second, raw_stream),
                 "poly_sm100");
     DebugSync(device, "poly_sm100");
-    CheckStatus(muon_polar_apply_sm100(poly, input.data_ptr(), out.data_ptr(),
-                                       batch, rows, cols, ld, ld, fa,
-                                       raw_stream),
-                "apply_sm100");
+    if (transposed)
+      CheckStatus(muon_polar_apply_t_sm100(poly, input.data_ptr(), out.data_ptr(), batch,
+                                           rows, cols, ld, ld, fa, raw_stream),
+                  "apply_t_sm100");
+    else
+      CheckStatus(muon_polar_apply_sm100(poly, input.data_ptr(), out.data_ptr(),
+                                         batch, rows, cols, ld, ld, fa,
+                                         raw_stream),
+                  "apply_sm100");
     DebugSync(device, "apply_sm100");
   }
   if (aligned) return out;
   return out.narrow(2, 0, cols).contiguous();
 }
 
+at::Tensor MuonPolarStepCuda(const at::Tensor& x, double a, double b, double c) {
+  return RunPolarStep(x, a, b, c, /*transposed=*/false);
+}
+
+at::Tensor MuonPolarStepTCuda(const at::Tensor& x, double a, double b, double c) {
+  return RunPolarStep(x, a, b, c, /*transposed=*/true);
+}
+
 }  // namespace
 
 TORCH_LIBRARY(muon_ascend950, m) {
   m.def("polar_step(Tensor x, float a, float b, float c) -> Tensor");
+  // Extension (no counterpart in the reference): the step of x^T for tall
+  // x, returned in x's layout -- polar_step(x.mT).mT without the copies.
+  m.def("polar_step_t(Tensor x, float a, float b, float c) -> Tensor");
 }
 
 TORCH_LIBRARY_IMPL(muon_ascend950, CUDA, m) {
   m.impl("polar_step", &MuonPolarStepCuda);
+  m.impl("polar_step_t", &MuonPolarStepTCuda);
 }

@@ -389,8 +389,9 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr,
 //   15 A major (0 = K), 16 B major (1 = MN), 17-22 N>>3, 24-28 M>>4.
 __host__ __device__ constexpr uint32_t idesc_bf16_f32(uint32_t n,
                                                       uint32_t b_mn_major,
-                                                      uint32_t m = 128) {
-  return (1u << 4) | (1u << 7) | (1u << 10) | (b_mn_major << 16) |
+                                                      uint32_t m = 128,
+                                                      uint32_t a_mn_major = 0) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | (a_mn_major << 15) | (b_mn_major << 16) |
          ((n >> 3) << 17) | ((m >> 4) << 24);
 }
 

@@ -84,3 +84,22 @@ def test_argument_validation_without_device(api):
     assert lib.muon_polar_set_split_mode(3) == -1
     assert lib.muon_polar_set_split_mode(-1) == -1
     assert lib.muon_polar_read_device_status(0, None, 0) == -1
+
+
+def test_transposed_entry_validation_without_device(api):
+    """The M > N entries check their arguments like the plain ones; the
+    transposed step sizes its workspace by N (the Gram is N x N)."""
+    lib = api.lib
+    assert lib.muon_polar_gram_t_sm100(None, _vp(16), 1, 300, 128, 128, None, 0, None) == -1
+    assert lib.muon_polar_gram_t_sm100(_vp(16), _vp(24), 1, 300, 128, 128, None, 0, None) == -3
+    assert lib.muon_polar_gram_t_sm100(_vp(16), _vp(16), 1, 300, 130, 130, None, 0, None) == -3
+    assert lib.muon_polar_apply_t_sm100(_vp(16), _vp(16), None, 1, 300, 8, 8, 8, 1.0, None) == -1
+    assert lib.muon_polar_apply_t_sm100(_vp(16), _vp(16), _vp(16), 1, 300, 16, 16, 8, 1.0,
+                                        None) == -1
+    # workspace for N = 128 rows of the Gram is enough; for M = 300 it is not
+    # required
+    small = api.workspace_bytes(1, 128) - 1
+    assert lib.muon_polar_step_t_sm100(_vp(16), _vp(32), _vp(16), small, None, 0, 1, 300, 128,
+                                       128, 128, 1.0, 1.0, 1.0, None) == -5
+    assert lib.muon_polar_step_t_sm100(_vp(16), _vp(16), _vp(16), 1 << 30, None, 0, 1, 300, 128,
+                                       128, 128, 1.0, 1.0, 1.0, None) == -1

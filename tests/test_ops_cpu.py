@@ -65,3 +65,17 @@ def test_fake_kernel_traces_into_a_graph():
     calls = [n for n in gm.graph.nodes if n.op == "call_function"]
     assert [str(n.target) for n in calls] == ["muon_ascend950.polar_step.default"]
     assert tuple(calls[0].meta["val"].shape) == (2, 16, 32)
+
+
+def test_fake_kernel_of_the_transposed_op():
+    """polar_step_t (tall X in its own layout) has the same FakeTensor
+    contract as polar_step."""
+    from torch.fx.experimental.proxy_tensor import make_fx
+
+    def f(x):
+        return torch.ops.muon_ascend950.polar_step_t(x, 1.5, -0.5, 0.25)
+
+    gm = make_fx(f, tracing_mode="fake")(torch.empty(2, 48, 16, dtype=torch.bfloat16))
+    calls = [n for n in gm.graph.nodes if n.op == "call_function"]
+    assert [str(n.target) for n in calls] == ["muon_ascend950.polar_step_t.default"]
+    assert tuple(calls[0].meta["val"].shape) == (2, 48, 16)
