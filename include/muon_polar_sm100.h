@@ -220,6 +220,47 @@ int muon_polar_step_t_sm100(const void* x, void* y, void* workspace, size_t work
                             int64_t n, int64_t ldx, int64_t ldy, float a, float b, float c,
                             void* stream);
 
+/* ------------------------------------------------------------------------
+ * The caller side of the step, on the device (no counterpart in the
+ * reference, which leaves the loop, the normalisation and the optimizer
+ * update to its caller: README.md:5, examples/five_steps.py:18-21).
+ *
+ * muon_polar_express_sm100: `steps` Polar Express steps with coefficient rows
+ * coefficients[3*i .. 3*i+2] = (a, b, c) (a host array), optionally after the
+ * normalisation x / (||x||_F * 1.01 + 1e-6) of each matrix (fp32 norm, one
+ * rounding to bf16).  x is [batch][m][ldx] (batch stride m*ldx), fp32
+ * (x_dtype 0) or bf16 (x_dtype 1; without normalisation only bf16 with
+ * ldx % 8 == 0, read in place by the first step).  y is [batch][m][ldy]
+ * bf16 and must not alias x.  Tall x (m > n) runs the
+ * transposed step.  workspace: muon_polar_express_workspace_bytes(batch, m,
+ * n) bytes, 16-byte aligned; scratch as for muon_polar_step_sm100 (or its _t
+ * form for tall x), sized by muon_polar_scratch_bytes(batch, min(m,n),
+ * max(m,n)).  All launches are asynchronous on `stream`.
+ *
+ * muon_polar_update_sm100: one Muon update of a batch of parameter matrices
+ *   buf <- lerp(buf, grad, 1 - momentum)            (momentum buffer, in place)
+ *   v    = nesterov ? lerp(grad, buf, momentum) : buf
+ *   X    = bf16( v / (||v||_F * 1.01 + 1e-6) )
+ *   Y    = `steps` Polar Express steps of X
+ *   p   <- round( p * (1 - lr * weight_decay) - lr * scale * Y )
+ * param, grad and momentum are contiguous [batch][m][n] of one dtype: fp32
+ * (dtype 0) or bf16 (dtype 1), pairwise distinct, 16-byte aligned.  The
+ * arithmetic is fp32 with one rounding per stored value (lerp as torch.lerp
+ * computes it).  workspace and scratch as for muon_polar_express_sm100. */
+size_t muon_polar_express_workspace_bytes(int64_t batch, int64_t m, int64_t n);
+int muon_polar_express_sm100(const void* x, int x_dtype, int64_t ldx, void* y, int64_t ldy,
+                             void* workspace, size_t workspace_bytes, void* scratch,
+                             size_t scratch_bytes, int64_t batch, int64_t m, int64_t n,
+                             const float* coefficients, int steps, int normalize, void* stream);
+int muon_polar_update_sm100(void* param, const void* grad, void* momentum, int dtype, void* workspace,
+                      size_t workspace_bytes, void* scratch, size_t scratch_bytes, int64_t batch,
+                      int64_t m, int64_t n, float lr, float momentum_coef, int nesterov,
+                      float weight_decay, float scale, const float* coefficients, int steps,
+                      void* stream);
+/* Kernels launched by the two entries above (their elementwise stages; the
+ * Polar Express kernels count in muon_polar_launch_count). */
+uint64_t muon_polar_update_launch_count(void);
+
 /* dst[i] = bf16_rne(src[i]) for i < count (fp32 Gram after the cross-rank
  * sum -> bf16 input of kernel 2). No counterpart in the reference, which has
  * no multi-device path. */

@@ -9,8 +9,9 @@ from ._loader import load_library
 
 load_library()
 
-from .ops import polar_step  # noqa: E402
+from .ops import POLAR_EXPRESS_COEFFICIENTS, polar_express, polar_step  # noqa: E402
+from .optim import Muon  # noqa: E402
 
-__all__ = ["polar_step", "load_library"]
+__all__ = ["polar_step", "polar_express", "Muon", "POLAR_EXPRESS_COEFFICIENTS", "load_library"]
 
 __version__ = "0.1.1"

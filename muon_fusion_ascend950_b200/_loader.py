@@ -50,11 +50,23 @@ def load_library() -> None:
     def fake_polar_step(x, a: float, b: float, c: float):
         return torch.empty_like(x, memory_format=torch.contiguous_format)
 
-    # polar_step_t (an extension: the step of x^T in x's layout) has the same
-    # output contract.
-    for name in ("muon_ascend950::polar_step", "muon_ascend950::polar_step_t"):
+    def fake_polar_express(x, coefficients, normalize=True):
+        return torch.empty_like(x, dtype=torch.bfloat16, memory_format=torch.contiguous_format)
+
+    def fake_muon_update(param, grad, momentum_buffer, lr, momentum, nesterov, weight_decay,
+                         scale, coefficients):
+        return None
+
+    # Extensions of this build: polar_step_t (the step of x^T in x's layout)
+    # has polar_step's output contract; polar_express returns bf16 of x's
+    # shape; muon_update_ mutates its arguments and returns nothing.
+    fakes = (("muon_ascend950::polar_step", fake_polar_step),
+             ("muon_ascend950::polar_step_t", fake_polar_step),
+             ("muon_ascend950::polar_express", fake_polar_express),
+             ("muon_ascend950::muon_update_", fake_muon_update))
+    for name, fn in fakes:
         try:
-            torch.library.register_fake(name)(fake_polar_step)
+            torch.library.register_fake(name)(fn)
         except RuntimeError as exc:
             if "already has" not in str(exc):
                 raise

@@ -1,7 +1,9 @@
 """In-tree build of the two native libraries of this package.
 
 * ``libmuon_polar_sm100.so`` -- the sm_100a kernels and the C ABI declared in
-  ``include/muon_polar_sm100.h`` (nvcc, static CUDA runtime, no torch).
+  ``include/muon_polar_sm100.h`` (nvcc, static CUDA runtime, no torch): the
+  Polar Express step (``muon_polar_sm100.cu``) and the Muon update around it
+  (``muon_update_sm100.cu``).
 * ``_C.so`` -- the PyTorch operator ``muon_ascend950::polar_step`` on the CUDA
   dispatch key, linked against the library above (rpath ``$ORIGIN``).
 
@@ -52,14 +54,13 @@ def _run(cmd) -> None:
 def build_library(force: bool = False, verbose_ptxas: bool = False) -> Path:
     """nvcc -> libmuon_polar_sm100.so (kernels + C ABI)."""
     out = PKG / LIB_NAME
-    sources = [CSRC / "muon_polar_sm100.cu", CSRC / "sm100_ptx.cuh",
-               INCLUDE / "muon_polar_sm100.h"]
+    cu = [CSRC / "muon_polar_sm100.cu", CSRC / "muon_update_sm100.cu"]
+    sources = [*cu, CSRC / "sm100_ptx.cuh", INCLUDE / "muon_polar_sm100.h"]
     if not force and _newer(out, sources):
         return out
     nvcc = _cuda_home() / "bin" / "nvcc"
     cmd = [nvcc, *NVCC_ARCH, "-O3", "-std=c++17", "-lineinfo",
-           "-Xcompiler", "-fPIC", "-shared", "-I", INCLUDE,
-           CSRC / "muon_polar_sm100.cu", "-o", out]
+           "-Xcompiler", "-fPIC", "-shared", "-I", INCLUDE, *cu, "-o", out]
     if verbose_ptxas:
         cmd.insert(1, "-Xptxas=-v")
     _run(cmd)

@@ -50,6 +50,17 @@ SIGNATURES = {
                                                ctypes.c_size_t, _I64, _I64, _I64, _I64, _I64,
                                                ctypes.c_float, ctypes.c_float, ctypes.c_float,
                                                _VP]),
+    "muon_polar_express_workspace_bytes": (ctypes.c_size_t, [_I64, _I64, _I64]),
+    "muon_polar_express_sm100": (ctypes.c_int, [_VP, ctypes.c_int, _I64, _VP, _I64, _VP,
+                                                ctypes.c_size_t, _VP, ctypes.c_size_t, _I64,
+                                                _I64, _I64, ctypes.POINTER(ctypes.c_float),
+                                                ctypes.c_int, ctypes.c_int, _VP]),
+    "muon_polar_update_sm100": (ctypes.c_int, [_VP, _VP, _VP, ctypes.c_int, _VP, ctypes.c_size_t,
+                                         _VP, ctypes.c_size_t, _I64, _I64, _I64,
+                                         ctypes.c_float, ctypes.c_float, ctypes.c_int,
+                                         ctypes.c_float, ctypes.c_float,
+                                         ctypes.POINTER(ctypes.c_float), ctypes.c_int, _VP]),
+    "muon_polar_update_launch_count": (ctypes.c_uint64, []),
     "muon_polar_cast_f32_bf16_sm100": (ctypes.c_int, [_VP, _VP, _I64, _VP]),
     "muon_polar_read_device_status": (ctypes.c_int, [ctypes.c_int,
                                                      ctypes.POINTER(ctypes.c_uint32),
@@ -274,6 +285,55 @@ class CAPI:
             x.data_ptr(), y.data_ptr(), workspace.data_ptr(), _nbytes(workspace), sp, sb,
             bsz, m, n, ldx, y.shape[-1], float(a), float(b), float(c),
             self._stream(stream)))
+
+    # The caller side of the step: several steps, normalisation, Muon update.
+    @staticmethod
+    def _coefficients(coefficients):
+        flat = [float(v) for row in coefficients for v in row]
+        return (ctypes.c_float * len(flat))(*flat), len(flat) // 3
+
+    @staticmethod
+    def _dtype_code(t) -> int:
+        import torch
+
+        if t.dtype == torch.float32:
+            return 0
+        if t.dtype == torch.bfloat16:
+            return 1
+        raise TypeError(f"unsupported dtype {t.dtype}")
+
+    def express_workspace_bytes(self, batch: int, m: int, n: int) -> int:
+        return int(self.lib.muon_polar_express_workspace_bytes(int(batch), int(m), int(n)))
+
+    def polar_express(self, x, y, workspace, coefficients, normalize: bool = True,
+                      n: Optional[int] = None, scratch=None, stream=None) -> None:
+        """y = the Polar Express steps of x ([B, M, ld], fp32 or bf16, first n
+        columns valid), after x / (||x||_F * 1.01 + 1e-6) when `normalize`."""
+        bsz, m, ldx = x.shape
+        n = ldx if n is None else n
+        coeffs, steps = self._coefficients(coefficients)
+        sp, sb = _scratch(scratch)
+        self._check("muon_polar_express_sm100", self.lib.muon_polar_express_sm100(
+            x.data_ptr(), self._dtype_code(x), ldx, y.data_ptr(), y.shape[-1],
+            workspace.data_ptr(), _nbytes(workspace), sp, sb, bsz, m, n, coeffs, steps,
+            1 if normalize else 0, self._stream(stream)))
+
+    def muon_update(self, param, grad, momentum, workspace, lr: float, momentum_coef: float,
+                    nesterov: bool, weight_decay: float, scale: float, coefficients,
+                    scratch=None, stream=None) -> None:
+        """One Muon update of contiguous [B, M, N] param / grad / momentum
+        (one dtype, fp32 or bf16), in place on param and momentum."""
+        bsz, m, n = param.shape
+        coeffs, steps = self._coefficients(coefficients)
+        sp, sb = _scratch(scratch)
+        self._check("muon_polar_update_sm100", self.lib.muon_polar_update_sm100(
+            param.data_ptr(), grad.data_ptr(), momentum.data_ptr(), self._dtype_code(param),
+            workspace.data_ptr(), _nbytes(workspace), sp, sb, bsz, m, n, float(lr),
+            float(momentum_coef), 1 if nesterov else 0, float(weight_decay), float(scale),
+            coeffs, steps, self._stream(stream)))
+
+    def update_launch_count(self) -> int:
+        return int(self.lib.muon_polar_update_launch_count())
 
     def cast_f32_bf16(self, src, dst, stream=None) -> None:
         self._check("muon_polar_cast_f32_bf16_sm100", self.lib.muon_polar_cast_f32_bf16_sm100(

@@ -204,6 +204,100 @@ at::Tensor MuonPolarStepTCuda(const at::Tensor& x, double a, double b, double c)
   return RunPolarStep(x, a, b, c, /*transposed=*/true);
 }
 
+std::vector<float> CoefficientRows(at::ArrayRef<double> coefficients, const char* who) {
+  TORCH_CHECK(!coefficients.empty() && coefficients.size() % 3 == 0, who,
+              ": coefficients must hold (a, b, c) rows, got ", coefficients.size(), " values");
+  return std::vector<float>(coefficients.begin(), coefficients.end());
+}
+
+// Several Polar Express steps (one C-ABI call), optionally after the
+// normalisation x / (||x||_F * 1.01 + 1e-6).  x: [B, M, N] fp32 or bf16.
+at::Tensor PolarExpressCuda(const at::Tensor& x, at::ArrayRef<double> coefficients,
+                            bool normalize) {
+  TORCH_CHECK(x.defined() && x.device().is_cuda(), "polar_express: x must be a CUDA tensor");
+  TORCH_CHECK(x.dim() == 3, "polar_express: x must have shape [batch, M, N]");
+  TORCH_CHECK(x.size(0) > 0 && x.size(1) > 0 && x.size(2) > 0,
+              "polar_express: all dimensions must be positive");
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16 || (normalize && x.scalar_type() == at::kFloat),
+              "polar_express: x must be bfloat16 (or float32 with normalize=True)");
+  const std::vector<float> coeffs = CoefficientRows(coefficients, "polar_express");
+  const c10::cuda::CUDAGuard deviceGuard(x.device());
+  at::Tensor input = x.contiguous();
+  const int64_t batch = input.size(0), rows = input.size(1), cols = input.size(2);
+  int64_t ldx = cols;
+  if (!normalize && ((cols % 8) != 0 ||
+                     (reinterpret_cast<uintptr_t>(input.data_ptr()) % 16) != 0)) {
+    // read in place by the first step: the TMA row-stride rule needs a copy
+    ldx = AlignUp(cols, 16);
+    at::Tensor padded = at::zeros({batch, rows, ldx}, input.options());
+    padded.narrow(2, 0, cols).copy_(input);
+    input = padded;
+  } else if ((reinterpret_cast<uintptr_t>(input.data_ptr()) % 16) != 0) {
+    input = input.clone();
+  }
+  const int64_t ld = (cols % 8) == 0 ? cols : AlignUp(cols, 16);
+  const auto stream = c10::cuda::getCurrentCUDAStream(x.device().index());
+  const size_t wsBytes = muon_polar_express_workspace_bytes(batch, rows, cols);
+  at::Tensor workspace =
+      at::empty({static_cast<int64_t>(wsBytes)}, input.options().dtype(at::kByte));
+  at::Tensor out = at::empty({batch, rows, ld}, input.options().dtype(at::kBFloat16));
+  const int64_t g = rows < cols ? rows : cols;
+  const int64_t depth = rows < cols ? cols : rows;
+  const auto scratch = GetScratch(input, x.device().index(), stream.stream(),
+                                  muon_polar_scratch_bytes(batch, g, depth));
+  CheckStatus(muon_polar_express_sm100(input.data_ptr(), input.scalar_type() == at::kFloat ? 0 : 1,
+                                       ldx, out.data_ptr(), ld, workspace.data_ptr(), wsBytes,
+                                       scratch.first, scratch.second, batch, rows, cols,
+                                       coeffs.data(), static_cast<int>(coeffs.size() / 3),
+                                       normalize ? 1 : 0, stream.stream()),
+              "polar_express_sm100");
+  if (ld == cols) return out;
+  return out.narrow(2, 0, cols).contiguous();
+}
+
+// One Muon update, in place on param and momentum_buffer.
+void MuonUpdateCuda(const at::Tensor& param, const at::Tensor& grad,
+                    const at::Tensor& momentum_buffer, double lr, double momentum,
+                    bool nesterov, double weight_decay, double scale,
+                    at::ArrayRef<double> coefficients) {
+  TORCH_CHECK(param.device().is_cuda() && grad.device() == param.device() &&
+                  momentum_buffer.device() == param.device(),
+              "muon_update: tensors must be on one CUDA device");
+  TORCH_CHECK(param.dim() == 2 || param.dim() == 3,
+              "muon_update: param must have shape [M, N] or [batch, M, N]");
+  TORCH_CHECK(grad.sizes() == param.sizes() && momentum_buffer.sizes() == param.sizes(),
+              "muon_update: grad and momentum_buffer must have param's shape");
+  TORCH_CHECK(param.scalar_type() == at::kFloat || param.scalar_type() == at::kBFloat16,
+              "muon_update: param must be float32 or bfloat16");
+  TORCH_CHECK(grad.scalar_type() == param.scalar_type() &&
+                  momentum_buffer.scalar_type() == param.scalar_type(),
+              "muon_update: grad and momentum_buffer must have param's dtype");
+  TORCH_CHECK(param.is_contiguous() && grad.is_contiguous() && momentum_buffer.is_contiguous(),
+              "muon_update: tensors must be contiguous");
+  TORCH_CHECK(param.numel() > 0, "muon_update: empty parameter");
+  const std::vector<float> coeffs = CoefficientRows(coefficients, "muon_update");
+  const c10::cuda::CUDAGuard deviceGuard(param.device());
+  const int64_t batch = param.dim() == 3 ? param.size(0) : 1;
+  const int64_t rows = param.size(-2), cols = param.size(-1);
+  const auto stream = c10::cuda::getCurrentCUDAStream(param.device().index());
+  const size_t wsBytes = muon_polar_express_workspace_bytes(batch, rows, cols);
+  at::Tensor workspace =
+      at::empty({static_cast<int64_t>(wsBytes)}, param.options().dtype(at::kByte));
+  const int64_t g = rows < cols ? rows : cols;
+  const int64_t depth = rows < cols ? cols : rows;
+  const auto scratch = GetScratch(param, param.device().index(), stream.stream(),
+                                  muon_polar_scratch_bytes(batch, g, depth));
+  CheckStatus(muon_polar_update_sm100(param.data_ptr(), grad.data_ptr(), momentum_buffer.data_ptr(),
+                                      param.scalar_type() == at::kFloat ? 0 : 1,
+                                      workspace.data_ptr(), wsBytes, scratch.first, scratch.second,
+                                      batch, rows, cols, static_cast<float>(lr),
+                                      static_cast<float>(momentum), nesterov ? 1 : 0,
+                                      static_cast<float>(weight_decay), static_cast<float>(scale),
+                                      coeffs.data(), static_cast<int>(coeffs.size() / 3),
+                                      stream.stream()),
+              "muon_update_sm100");
+}
+
 }  // namespace
 
 TORCH_LIBRARY(muon_ascend950, m) {
@@ -211,9 +305,17 @@ TORCH_LIBRARY(muon_ascend950, m) {
   // Extension (no counterpart in the reference): the step of x^T for tall
   // x, returned in x's layout -- polar_step(x.mT).mT without the copies.
   m.def("polar_step_t(Tensor x, float a, float b, float c) -> Tensor");
+  // Extensions: the caller side of the step on the device (several steps
+  // with normalisation; a whole Muon update of one parameter).
+  m.def("polar_express(Tensor x, float[] coefficients, bool normalize=True) -> Tensor");
+  m.def("muon_update_(Tensor(a!) param, Tensor grad, Tensor(b!) momentum_buffer, float lr, "
+        "float momentum, bool nesterov, float weight_decay, float scale, "
+        "float[] coefficients) -> ()");
 }
 
 TORCH_LIBRARY_IMPL(muon_ascend950, CUDA, m) {
   m.impl("polar_step", &MuonPolarStepCuda);
   m.impl("polar_step_t", &MuonPolarStepTCuda);
+  m.impl("polar_express", &PolarExpressCuda);
+  m.impl("muon_update_", &MuonUpdateCuda);
 }

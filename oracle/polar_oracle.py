@@ -227,9 +227,47 @@ __all__ = [
     "reference_formula",
     "kernel_dataflow_3d",
     "polar_step_oracle",
+    "normalize_oracle",
+    "polar_express_oracle",
+    "muon_update_oracle",
     "nominal_flops",
     "CpuKernels",
     "error_stats",
     "ulp_bf16",
     "bf16_bits",
 ]
+
+
+# ------------------------------------------------------------------ caller side
+# The reference leaves the loop, the normalisation and the optimizer update to
+# its caller (README.md:5, 130).  Its example caller normalises with
+# x / (||x||_F * 1.01 + 1e-6) and runs one polar_step per coefficient row
+# (examples/five_steps.py:18-21).  These restate that caller, plus the usual
+# Muon momentum / weight-decay / scaled update, in fp32 torch on the CPU:
+# the checker of muon_polar_express_sm100 and muon_polar_update_sm100.
+
+def normalize_oracle(v: torch.Tensor) -> torch.Tensor:
+    """bf16( v / (||v||_F * 1.01 + 1e-6) ) per matrix, fp32 arithmetic."""
+    v32 = v.to(torch.float32)
+    norm = torch.linalg.vector_norm(v32.to(torch.float64), dim=(-2, -1), keepdim=True)
+    s = (norm.to(torch.float32) * 1.01) + 1e-6
+    return (v32 / s).to(torch.bfloat16)
+
+
+def polar_express_oracle(x: torch.Tensor, coefficients, normalize: bool = True) -> torch.Tensor:
+    """examples/five_steps.py:18-21: normalise, then one step per row."""
+    y = normalize_oracle(x) if normalize else x.to(torch.bfloat16)
+    for a, b, c in coefficients:
+        y = polar_step_oracle(y, a, b, c)
+    return y
+
+
+def muon_update_oracle(param, grad, buf, lr, momentum, nesterov, weight_decay, scale,
+                       coefficients):
+    """One Muon update in the tensors' own dtype (torch.lerp semantics), the
+    orthogonalisation through polar_express_oracle; returns (param, buf)."""
+    buf = buf.clone().lerp_(grad, 1.0 - momentum)
+    v = grad.lerp(buf, momentum) if nesterov else buf
+    y = polar_express_oracle(v, coefficients, normalize=True).to(torch.float32)
+    p = param.to(torch.float32) * (1.0 - lr * weight_decay) - (lr * scale) * y
+    return p.to(param.dtype), buf

@@ -103,3 +103,38 @@ def test_transposed_entry_validation_without_device(api):
                                        128, 128, 1.0, 1.0, 1.0, None) == -5
     assert lib.muon_polar_step_t_sm100(_vp(16), _vp(16), _vp(16), 1 << 30, None, 0, 1, 300, 128,
                                        128, 128, 1.0, 1.0, 1.0, None) == -1
+
+
+def test_caller_side_entry_validation_without_device(api):
+    """The multi-step and Muon-update entries reject bad arguments before
+    touching a device."""
+    lib = api.lib
+    coeffs = (ctypes.c_float * 3)(1.0, 1.0, 1.0)
+    ws = api.express_workspace_bytes(1, 128, 256)
+    assert ws > api.workspace_bytes(1, 128)
+    assert api.express_workspace_bytes(0, 128, 256) == 0
+    # x aliases y; zero steps; unknown dtype; fp32 without normalisation
+    assert lib.muon_polar_express_sm100(_vp(16), 1, 256, _vp(16), 256, _vp(16), ws, None, 0, 1,
+                                        128, 256, coeffs, 1, 1, None) == -1
+    assert lib.muon_polar_express_sm100(_vp(16), 1, 256, _vp(32), 256, _vp(16), ws, None, 0, 1,
+                                        128, 256, coeffs, 0, 1, None) == -1
+    assert lib.muon_polar_express_sm100(_vp(16), 2, 256, _vp(32), 256, _vp(16), ws, None, 0, 1,
+                                        128, 256, coeffs, 1, 1, None) == -1
+    assert lib.muon_polar_express_sm100(_vp(16), 0, 256, _vp(32), 256, _vp(16), ws, None, 0, 1,
+                                        128, 256, coeffs, 1, 0, None) == -1
+    # unaligned in-place read; workspace too small
+    assert lib.muon_polar_express_sm100(_vp(16), 1, 130, _vp(32), 256, _vp(16), ws, None, 0, 1,
+                                        128, 130, coeffs, 1, 0, None) == -3
+    assert lib.muon_polar_express_sm100(_vp(16), 1, 256, _vp(32), 256, _vp(16), ws - 1, None, 0,
+                                        1, 128, 256, coeffs, 1, 1, None) == -5
+    # update: aliasing tensors, bad dtype, misalignment, small workspace
+    f32 = ctypes.c_float
+    args = (f32(0.1), f32(0.9), 1, f32(0.0), f32(1.0), coeffs, 1, None)
+    assert lib.muon_polar_update_sm100(_vp(16), _vp(16), _vp(48), 0, _vp(64), ws, None, 0, 1, 128,
+                                       256, *args) == -1
+    assert lib.muon_polar_update_sm100(_vp(16), _vp(32), _vp(48), 3, _vp(64), ws, None, 0, 1, 128,
+                                       256, *args) == -1
+    assert lib.muon_polar_update_sm100(_vp(16), _vp(40), _vp(48), 0, _vp(64), ws, None, 0, 1, 128,
+                                       256, *args) == -3
+    assert lib.muon_polar_update_sm100(_vp(16), _vp(32), _vp(48), 0, _vp(64), ws - 1, None, 0, 1,
+                                       128, 256, *args) == -5

@@ -79,3 +79,53 @@ def test_fake_kernel_of_the_transposed_op():
     calls = [n for n in gm.graph.nodes if n.op == "call_function"]
     assert [str(n.target) for n in calls] == ["muon_ascend950.polar_step_t.default"]
     assert tuple(calls[0].meta["val"].shape) == (2, 48, 16)
+
+
+def test_fake_kernels_of_the_caller_side_ops():
+    """polar_express returns bf16 of x's shape; muon_update_ mutates and
+    returns nothing: both trace in fake mode."""
+    from torch.fx.experimental.proxy_tensor import make_fx
+
+    def f(x):
+        return torch.ops.muon_ascend950.polar_express(x, [1.0, 0.5, 0.25] * 2, True)
+
+    gm = make_fx(f, tracing_mode="fake")(torch.empty(2, 16, 32, dtype=torch.float32))
+    call = [n for n in gm.graph.nodes if n.op == "call_function"][0]
+    assert call.meta["val"].dtype == torch.bfloat16
+    assert tuple(call.meta["val"].shape) == (2, 16, 32)
+
+    def g(p, grad, buf):
+        torch.ops.muon_ascend950.muon_update_(p, grad, buf, 0.02, 0.95, True, 0.0, 1.0,
+                                              [1.0, 0.5, 0.25])
+        return p
+
+    t = torch.empty(16, 32)
+    gm = make_fx(g, tracing_mode="fake")(t, t.clone(), t.clone())
+    targets = [str(n.target) for n in gm.graph.nodes if n.op == "call_function"]
+    assert "muon_ascend950.muon_update_.default" in targets
+
+
+def test_muon_optimizer_argument_checks():
+    import muon_fusion_ascend950_b200 as pkg
+
+    w = torch.nn.Parameter(torch.zeros(4, 4))
+    with pytest.raises(ValueError):
+        pkg.Muon([w], lr=-1.0)
+    with pytest.raises(ValueError):
+        pkg.Muon([w], momentum=1.0)
+    with pytest.raises(ValueError):
+        pkg.Muon([w], coefficients=[(1.0, 2.0)])
+    v = torch.nn.Parameter(torch.zeros(4))
+    opt = pkg.Muon([v])
+    v.grad = torch.zeros(4)
+    with pytest.raises(ValueError, match="matrices"):
+        opt.step()
+
+
+def test_polar_express_argument_checks():
+    import muon_fusion_ascend950_b200 as pkg
+
+    with pytest.raises(TypeError):
+        pkg.polar_express([1.0])
+    with pytest.raises(ValueError):
+        pkg.polar_express(torch.zeros(2, 3, dtype=torch.bfloat16))  # not on CUDA
