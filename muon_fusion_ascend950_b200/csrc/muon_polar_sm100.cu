@@ -335,13 +335,11 @@ __device__ __forceinline__ void pair_epilogue_half(const EpiParams& p, uint32_t 
   }
 }
 
-// Threads of the fused step kernel: warp 0 TMA producer, warp 1 MMA issuer
-// and tensor-memory owner, warps 2..9 epilogue (two per tensor-memory lane
-// quarter, each taking 32 of a chunk's 64 columns).
-constexpr int kPairThreads = 320;
+// Threads of polar_tile_kernel and polar_fused_kernel: warps 0 and 10 TMA
+// producers, warp 1 MMA issuer and tensor-memory owner, warps 2..9 epilogue
+// (two per tensor-memory lane quarter, each taking 32 of a chunk's 64
+// columns).
 constexpr int kPairEpiThreads = 256;
-// Threads of polar_tile_kernel: the same roles plus a second TMA producer,
-// warp 10.
 constexpr int kTileThreads = 352;
 constexpr int kProducerWarp2 = 10;
 
@@ -862,43 +860,65 @@ __global__ void __launch_bounds__(kTileThreads, 1)
 }
 
 // ============================================================ fused step
-// One launch for a whole Polar Express step on CTA pairs.  The work items of
-// the step -- Gram tiles of every matrix, then polynomial tiles, then apply
-// tiles -- are dealt round-robin to the co-resident pairs; an item waits
-// (bounded) until the items it reads are complete:
-//   polynomial tile of matrix b  <- every Gram tile of b
-//   apply tile of matrix b       <- every polynomial tile of b
-// Completion is counted per matrix in scratch (one increment per CTA band
-// and tile, released after the band's TMA stores have completed; acquired
-// with a proxy fence before the TMA loads of the dependent item).  Every
-// dependency has a lower item index than its dependent and items of a pair
-// run in index order, so the wait always ends.  The last CTA to exit resets
-// the counters, so each launch starts from zero.  Phases of different
-// matrices overlap and the three launch/fill/drain overheads become one.
+// One launch for a whole Polar Express step on tcgen05 CTA pairs.  The work
+// items of the step -- Gram regions of every matrix, then polynomial
+// regions, then apply tiles -- are dealt round-robin to the co-resident
+// pairs; an item waits (bounded) until the items it reads are complete:
+//   polynomial region of matrix b  <- every Gram region of b
+//   apply tile of matrix b         <- every polynomial region of b
+// Completion is counted per matrix in scratch (one increment per CTA and
+// item, released after the CTA's TMA stores have completed; acquired with a
+// proxy fence before the TMA loads of the dependent item).  Every dependency
+// has a lower item index than its dependent and items of a pair run in
+// index order, so every wait ends.  The last CTA to exit resets the
+// counters, so each launch starts from zero.
+//
+// Two tile shapes, both cta_group::2 (M = 256):
+//  * Gram and polynomial items: 256 x 128 regions (N = 128).  A region
+//    (I, j) covers 128-row blocks 2I and 2I+1 against 128-column block j,
+//    j >= 2I: every block on or above the diagonal exactly once (block
+//    (2I+1, 2I), below it, is computed and not stored; the mirror of block
+//    (2I, 2I+1) writes it).  Per SM a 128 x 128 x 16 MMA reads 6 KiB of
+//    shared memory (A: 128 rows, B: 64 rows) instead of the single-CTA
+//    engine's 8 KiB, and twice as many SMs work on the Gram.
+//  * Apply items: 256 x 256 tiles (N = 256), as the apply kernel.
+// The stage ring (192 KiB) is cut per item kind: four 48 KiB stages of
+// K = 128 for Gram/polynomial items; four 32 KiB stages of K = 64 for apply
+// items, whose epilogue tile (X, 64 KiB) takes the rest of the ring.  At a
+// change of layout the producers wait until the previous item's MMAs have
+// completed (its accumulator barrier), then restart the ring; each stage's
+// barriers keep their own phase.  The Gram / polynomial epilogue stages its
+// output and mirror chunks in two dedicated 16 KiB regions; the polynomial
+// reads its A tile (the b*A term) straight from global memory into
+// registers before its accumulator is ready.  An apply item's X operand and
+// epilogue tile do not depend on the polynomial: they are loaded before the
+// item waits for it.
 enum FusedKind : int { kFGram = 0, kFPoly = 1, kFApply = 2 };
 
 struct FusedParams {
   int32_t batch;
-  int32_t d;          // Mp / 256
-  int32_t sym_tiles;  // d (d + 1) / 2 per matrix
-  int32_t apply_tn;   // ceil(n / 256)
-  int32_t n_gram;     // batch * sym_tiles
-  int32_t n_poly;     // batch * sym_tiles
-  int32_t total;      // n_gram + n_poly + batch * d * apply_tn
-  int32_t kb_gram;    // 64-deep k-blocks of each kind
-  int32_t kb_poly;
+  int32_t d2;           // Mp / 256: row blocks of a region
+  int32_t regions;      // d2 (d2 + 1): Gram / polynomial regions per matrix
+  int32_t apply_tn;     // ceil(n / 256)
+  int32_t n_gram;       // batch * regions
+  int32_t n_poly;       // batch * regions
+  int32_t total;        // n_gram + n_poly + batch * d2 * apply_tn
+  int32_t kb_gram;      // K-blocks of each kind (128 deep for Gram / poly,
+  int32_t kb_poly;      // 64 for the apply)
   int32_t kb_apply;
   float coef_b;
   float coef_c;
-  float alpha;        // a rounded to bf16
-  uint32_t* counters; // [0, batch): Gram done; [batch, 2 batch): poly done; [2 batch]: exits
+  float alpha;          // a rounded to bf16
+  uint32_t* counters;   // [0, batch): Gram done; [batch, 2 batch): poly done; [2 batch]: exits
+  const uint16_t* gram; // A, [batch][mp][mp] bf16 (the polynomial's epilogue input)
+  int32_t mp;
 };
 
 struct FusedMaps {
-  CUtensorMap x_k;   // X, box {64, 128}: Gram operands, apply epilogue tile
-  CUtensorMap x_mn;  // X, box {64, 64}: apply B operand (MN-major)
-  CUtensorMap a128;  // A, box {64, 128}: Gram output, poly operands and tile
-  CUtensorMap a64;   // A, box {64, 64}: Gram mirror
+  CUtensorMap x_k;   // X, box {64, 128}: Gram A operand, apply epilogue tile
+  CUtensorMap x_mn;  // X, box {64, 64}: Gram B operand (K-major), apply B operand (MN-major)
+  CUtensorMap a128;  // A, box {64, 128}: Gram output, poly A operand and tile
+  CUtensorMap a64;   // A, box {64, 64}: Gram mirror, poly B operand
   CUtensorMap p128;  // P, box {64, 128}: poly output, apply A operand
   CUtensorMap p64;   // P, box {64, 64}: poly mirror
   CUtensorMap y128;  // Y, box {64, 128}: apply output
@@ -910,66 +930,118 @@ struct FusedItem {
 
 __device__ __forceinline__ FusedItem fused_item(int w, const FusedParams& p) {
   FusedItem it;
-  TileCoord tc;
-  if (w < p.n_gram) {
-    it.kind = kFGram;
-    it.k_blocks = p.kb_gram;
-    tc = decode_tile(w, true, p.d, p.d, p.sym_tiles);
-  } else if (w < p.n_gram + p.n_poly) {
-    it.kind = kFPoly;
-    it.k_blocks = p.kb_poly;
-    tc = decode_tile(w - p.n_gram, true, p.d, p.d, p.sym_tiles);
+  int r;
+  if (w < p.n_gram + p.n_poly) {
+    it.kind = w < p.n_gram ? kFGram : kFPoly;
+    it.k_blocks = w < p.n_gram ? p.kb_gram : p.kb_poly;
+    r = w < p.n_gram ? w : w - p.n_gram;
+    it.b = r / p.regions;
+    r -= it.b * p.regions;
+    // row I holds regions (I, 2I .. 2 d2 - 1)
+    int tm = 0;
+    while (r >= 2 * p.d2 - 2 * tm) {
+      r -= 2 * p.d2 - 2 * tm;
+      ++tm;
+    }
+    it.tm = tm;
+    it.tn = 2 * tm + r;
   } else {
     it.kind = kFApply;
     it.k_blocks = p.kb_apply;
-    tc = decode_tile(w - p.n_gram - p.n_poly, false, p.d, p.apply_tn, p.d * p.apply_tn);
+    r = w - p.n_gram - p.n_poly;
+    const int per = p.d2 * p.apply_tn;
+    it.b = r / per;
+    r -= it.b * per;
+    it.tm = r / p.apply_tn;
+    it.tn = r - it.tm * p.apply_tn;
   }
-  it.b = tc.b;
-  it.tm = tc.tm;
-  it.tn = tc.tn;
   return it;
 }
 
-// The item's inputs are complete (bounded wait; false on timeout).
+// Waits (bounded) until the item's inputs from this launch are complete.
 __device__ __forceinline__ bool fused_wait_inputs(const FusedItem& it, const FusedParams& p) {
   bool ok = true;
   if (it.kind == kFPoly)
-    ok = wait_counter_bounded(p.counters + it.b, 2u * p.sym_tiles);
+    ok = wait_counter_bounded(p.counters + it.b, 2u * p.regions);
   else if (it.kind == kFApply)
-    ok = wait_counter_bounded(p.counters + p.batch + it.b, 2u * p.sym_tiles);
+    ok = wait_counter_bounded(p.counters + p.batch + it.b, 2u * p.regions);
   fence_proxy_async_global();
   return ok;
 }
 
-// Smem plan of the fused kernel: 4 output / epilogue-input regions of
-// [128 x 64] bf16, 2 mirror regions of [64 x 128] bf16, 4 stages of 32 KiB.
 struct FusedCfg {
-  static constexpr int kChunks = kPairN / kChunkCols;
-  static constexpr uint32_t kRegionBytes = kHalf * kChunkCols * 2;      // 16 KiB
-  static constexpr uint32_t kEpiBytes = 4 * kRegionBytes + 2 * kRegionBytes;
-  static constexpr uint32_t kAHalfBytes = kHalf * kAtom * 2;
-  static constexpr uint32_t kBHalfBytes = kHalf * kAtom * 2;
-  static constexpr uint32_t kStageBytes = kAHalfBytes + kBHalfBytes;    // 32 KiB
-  static constexpr uint32_t kFixedBytes = 1024 + kEpiBytes + 256;
-  static constexpr int kStages = static_cast<int>((232448u - kFixedBytes) / kStageBytes);
-  static constexpr uint32_t kSmemBytes = kFixedBytes + kStages * kStageBytes;
+  static constexpr uint32_t kRegionBytes = kHalf * kChunkCols * 2;  // 16 KiB
+  static constexpr uint32_t kEpiBytes = 2 * kRegionBytes;           // sym output + mirror
+  static constexpr uint32_t kSymA = kHalf * 128 * 2;                // 32 KiB
+  static constexpr uint32_t kSymB = 64 * 128 * 2;                   // 16 KiB
+  static constexpr uint32_t kSymStage = kSymA + kSymB;
+  static constexpr uint32_t kApA = kHalf * kAtom * 2;               // 16 KiB
+  static constexpr uint32_t kApB = kAtom * kHalf * 2;               // 16 KiB
+  static constexpr uint32_t kApStage = kApA + kApB;
+  static constexpr int kSymStages = 4;
+  static constexpr int kApStages = 4;
+  static constexpr uint32_t kRingBytes = kSymStages * kSymStage;    // 192 KiB
+  static constexpr uint32_t kApAux = kApStages * kApStage;          // apply tile at 128 KiB
+  static constexpr int kMaxStages = 4;
+  static constexpr uint32_t kSmemBytes = 1024 + kEpiBytes + kRingBytes + 256;
   static constexpr uint32_t kTmemCols = 2 * kPairN;
-  static_assert(kStages >= 3, "pipeline depth");
+  static_assert(kApAux + 4 * kRegionBytes <= kRingBytes, "apply layout");
+  static_assert(kSmemBytes <= 232448, "shared memory budget");
 };
 
-__global__ void __launch_bounds__(kPairThreads, 1)
+// Polynomial epilogue of 32 accumulator columns with the A values (the b*A
+// term) from registers: eight bf16 per 16-byte unit, in column order.  The
+// arithmetic and staging are those of pair_epilogue_half<kPoly>.
+__device__ __forceinline__ void fused_poly_half(const EpiParams& p, uint32_t out, uint32_t mir,
+                                                bool mirror, int row, int h,
+                                                const float (&v)[32], const uint4 (&aux)[4]) {
+  uint32_t w[16];
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    const uint32_t in[4] = {aux[u].x, aux[u].y, aux[u].z, aux[u].w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int j = 8 * u + 2 * e;
+      const float2 a2 = __bfloat1622float2(bits_bf162(in[e]));
+      w[4 * u + e] = bf162_bits(__floats2bfloat162_rn(
+          __fadd_rn(__fmul_rn(p.coef_b, a2.x), __fmul_rn(p.coef_c, v[j])),
+          __fadd_rn(__fmul_rn(p.coef_b, a2.y), __fmul_rn(p.coef_c, v[j + 1]))));
+    }
+    st_shared_v4(out + swz_box(row, h * 64 + u * 16),
+                 make_uint4(w[4 * u], w[4 * u + 1], w[4 * u + 2], w[4 * u + 3]));
+  }
+  if (mirror) {
+    const uint32_t mbase = mir + (row / 64) * (kChunkCols * 128);
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const uint16_t hv = static_cast<uint16_t>((j & 1) ? (w[j >> 1] >> 16) : (w[j >> 1] & 0xFFFFu));
+      st_shared_u16(mbase + swz_box(h * 32 + j, (row % 64) * 2), hv);
+    }
+  }
+}
+
+// Stage ring of one role: the current layout (0 none yet, 1 Gram /
+// polynomial, 2 apply), its stage count, the position in it and, per stage,
+// the parity of the barrier phase it waits for next.
+struct FusedRing {
+  int layout;
+  int stages;
+  int pos;
+  uint32_t parity;  // bit s: phases of stage s used so far, mod 2
+};
+
+__global__ void __launch_bounds__(kTileThreads, 1)
     polar_fused_kernel(const __grid_constant__ FusedMaps maps, const FusedParams p) {
   using Cfg = FusedCfg;
-  constexpr int S = Cfg::kStages;
+  constexpr int S = Cfg::kMaxStages;
 
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_addr(smem_raw);
   uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
-  uint8_t* sOut = smem;
-  uint8_t* sMir = sOut + 4 * Cfg::kRegionBytes;
-  uint8_t* sA = smem + Cfg::kEpiBytes;
-  uint8_t* sB = sA + S * Cfg::kAHalfBytes;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sB + S * Cfg::kBHalfBytes);
+  uint8_t* sReg = smem;  // sym epilogue: output chunk, mirror chunk
+  uint8_t* sRing = smem + Cfg::kEpiBytes;
+  uint8_t* sAux = sRing + Cfg::kApAux;  // apply epilogue tile (apply layout only)
+  uint64_t* full = reinterpret_cast<uint64_t*>(sRing + Cfg::kRingBytes);
   uint64_t* empty = full + S;
   uint64_t* tfull = empty + S;
   uint64_t* tempty = tfull + 2;
@@ -991,7 +1063,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], 16);
+      mbar_init(&tempty[a], 16);  // 8 epilogue warps in each CTA
     }
     mbar_init(drain, 1);
     mbar_init(aux_full, 1);
@@ -1017,89 +1089,167 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   grid_dependency_wait();
   grid_launch_dependents();
 
-  if (warp == 0) {
+  if (warp == 0 || warp == kProducerWarp2) {
     if (lane == 0) {
-      // ---------------- TMA producer (both CTAs)
-      uint32_t it = 0;
+      // ---------------- TMA producers (both CTAs): producer `pid` owns the
+      // stages s with s % 2 == pid in either layout.
+      const uint32_t pid = warp == 0 ? 0u : 1u;
+      FusedRing ring = {0, 0, 0, 0u};
+      uint32_t t = 0;
+      int started = 0;  // items whose loads this producer has begun
       bool ok = true;
-      for (int w = cluster; ok && w < p.total; w += nclusters) {
+      for (int w = cluster; ok && w < p.total; w += nclusters, ++t) {
         const FusedItem item = fused_item(w, p);
+        const bool ap = item.kind == kFApply;
+        const int layout = ap ? 2 : 1;
+        if (layout != ring.layout) {
+          // new layout: the previous item's MMAs have read every stage
+          if (t > 0 && !mbar_wait_bounded(&tfull[(t - 1) & 1u], ((t - 1) >> 1) & 1u)) {
+            ok = false;
+            break;
+          }
+          ring.layout = layout;
+          ring.stages = ap ? Cfg::kApStages : Cfg::kSymStages;
+          ring.pos = 0;
+        }
+        started = static_cast<int>(t) + 1;
+        const uint32_t stage_bytes = ap ? Cfg::kApStage : Cfg::kSymStage;
+        const uint32_t a_bytes = ap ? Cfg::kApA : Cfg::kSymA;
+        const int a_row = item.tm * kPairM + static_cast<int>(rank) * kHalf;
+        // Apply: X (B operand) of the first stages before the dependency
+        // wait; Gram: no dependency; polynomial: A only after it.
+        FusedRing pre = ring;
+        int n_pre = 0;
+        if (ap) {
+          for (int kb = 0; kb < item.k_blocks && kb < ring.stages; ++kb, ++n_pre) {
+            const int s = pre.pos;
+            pre.pos = pre.pos + 1 == pre.stages ? 0 : pre.pos + 1;
+            if ((s & 1) != static_cast<int>(pid)) continue;
+            const uint32_t par = (pre.parity >> s) & 1u;
+            if (!mbar_wait_bounded(&empty[s], par ^ 1u)) {
+              ok = false;
+              break;
+            }
+            if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * stage_bytes);
+            const uint32_t bar = map_to_cta(smem_addr(&full[s]), 0);
+            uint8_t* sb = sRing + s * stage_bytes + a_bytes;
+#pragma unroll
+            for (int j = 0; j < kHalf / kAtom; ++j)
+              tma_load_3d_pair(sb + j * (kAtom * 128), &maps.x_mn, bar,
+                               item.tn * kPairN + static_cast<int>(rank) * kHalf + j * kAtom,
+                               kb * kAtom, item.b);
+          }
+          if (!ok) break;
+        }
         if (!fused_wait_inputs(item, p)) {
           atomicOr(&g_watchdog, MUON_POLAR_WATCHDOG_DEPENDENCY);
           ok = false;
           break;
         }
-        const int a_row = item.tm * kPairM + static_cast<int>(rank) * kHalf;
-        const int b_row = item.tn * kPairN + static_cast<int>(rank) * kHalf;
-        const CUtensorMap* ma = item.kind == kFGram ? &maps.x_k
-                                : item.kind == kFPoly ? &maps.a128 : &maps.p128;
-        for (int kb = 0; kb < item.k_blocks; ++kb, ++it) {
-          const uint32_t s = it % S;
-          const uint32_t ph = (it / S) & 1u;
-          if (!mbar_wait_bounded(&empty[s], ph ^ 1u)) {
-            ok = false;
-            break;
-          }
-          if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * Cfg::kStageBytes);
+        for (int kb = 0; kb < item.k_blocks; ++kb) {
+          const int s = ring.pos;
+          ring.pos = ring.pos + 1 == ring.stages ? 0 : ring.pos + 1;
+          if ((s & 1) != static_cast<int>(pid)) continue;
+          const uint32_t par = (ring.parity >> s) & 1u;
+          ring.parity ^= 1u << s;
           const uint32_t bar = map_to_cta(smem_addr(&full[s]), 0);
-          tma_load_3d_pair(sA + s * Cfg::kAHalfBytes, ma, bar, kb * kAtom, a_row, item.b);
-          if (item.kind != kFApply) {
-            tma_load_3d_pair(sB + s * Cfg::kBHalfBytes, ma, bar, kb * kAtom, b_row, item.b);
-          } else {
+          uint8_t* sa = sRing + s * stage_bytes;
+          if (ap) {
+            if (kb >= n_pre) {
+              if (!mbar_wait_bounded(&empty[s], par ^ 1u)) {
+                ok = false;
+                break;
+              }
+              if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * stage_bytes);
 #pragma unroll
-            for (int j = 0; j < kHalf / kAtom; ++j)
-              tma_load_3d_pair(sB + s * Cfg::kBHalfBytes + j * (kAtom * 128), &maps.x_mn, bar,
-                               b_row + j * kAtom, kb * kAtom, item.b);
+              for (int j = 0; j < kHalf / kAtom; ++j)
+                tma_load_3d_pair(sa + a_bytes + j * (kAtom * 128), &maps.x_mn, bar,
+                                 item.tn * kPairN + static_cast<int>(rank) * kHalf + j * kAtom,
+                                 kb * kAtom, item.b);
+            }
+            tma_load_3d_pair(sa, &maps.p128, bar, kb * kAtom, a_row, item.b);
+          } else {
+            if (!mbar_wait_bounded(&empty[s], par ^ 1u)) {
+              ok = false;
+              break;
+            }
+            if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * stage_bytes);
+            const CUtensorMap* ma = item.kind == kFGram ? &maps.x_k : &maps.a128;
+            const CUtensorMap* mb = item.kind == kFGram ? &maps.x_mn : &maps.a64;
+            const int b_row = item.tn * kHalf + static_cast<int>(rank) * 64;
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+              tma_load_3d_pair(sa + j * kAtomBytes, ma, bar, kb * 128 + j * kAtom, a_row, item.b);
+              tma_load_3d_pair(sa + a_bytes + j * (64 * 128), mb, bar, kb * 128 + j * kAtom,
+                               b_row, item.b);
+            }
           }
         }
       }
       if (!ok) atomicOr(&g_watchdog, MUON_POLAR_WATCHDOG_PRODUCER);
-      if (rank == 0) {
-        const uint32_t inflight = it < static_cast<uint32_t>(S) ? it : S;
-        for (uint32_t i = it - inflight; i < it; ++i) {
-          if (!mbar_wait_bounded(&full[i % S], (i / S) & 1u)) {
-            atomicOr(&g_watchdog, MUON_POLAR_WATCHDOG_DRAIN);
-            break;
-          }
-        }
+      if (rank == 0 && started > 0) {
+        // Drain: the pair's last loads land before the CTAs exit (the last
+        // item's accumulator completes only after every one of its stages).
+        const uint32_t last = static_cast<uint32_t>(started - 1);
+        if (!mbar_wait_bounded(&tfull[last & 1u], (last >> 1) & 1u))
+          atomicOr(&g_watchdog, MUON_POLAR_WATCHDOG_DRAIN);
       }
     }
   } else if (warp == 1) {
     if (lane == 0 && rank == 0) {
       // ---------------- tcgen05 MMA issuer (leader CTA only)
-      constexpr uint32_t idesc_k = idesc_bf16_f32(kPairN, 0u, kPairM);
-      constexpr uint32_t idesc_mn = idesc_bf16_f32(kPairN, 1u, kPairM);
-      uint32_t it = 0;
+      constexpr uint32_t idesc_sym = idesc_bf16_f32(kHalf, 0u, kPairM);
+      constexpr uint32_t idesc_ap = idesc_bf16_f32(kPairN, 1u, kPairM);
+      FusedRing ring = {0, 0, 0, 0u};
       uint32_t t = 0;
       bool ok = true;
       for (int w = cluster; ok && w < p.total; w += nclusters, ++t) {
         const FusedItem item = fused_item(w, p);
-        const bool bmn = item.kind == kFApply;
+        const bool ap = item.kind == kFApply;
+        const int layout = ap ? 2 : 1;
+        if (layout != ring.layout) {
+          ring.layout = layout;
+          ring.stages = ap ? Cfg::kApStages : Cfg::kSymStages;
+          ring.pos = 0;
+        }
+        const uint32_t stage_bytes = ap ? Cfg::kApStage : Cfg::kSymStage;
+        const uint32_t a_bytes = ap ? Cfg::kApA : Cfg::kSymA;
         const uint32_t acc = t & 1u;
-        const uint32_t uph = (t >> 1) & 1u;
-        if (!mbar_wait_bounded(&tempty[acc], uph ^ 1u)) {
+        if (!mbar_wait_bounded(&tempty[acc], ((t >> 1) & 1u) ^ 1u)) {
           ok = false;
           break;
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * kPairN;
-        for (int kb = 0; kb < item.k_blocks; ++kb, ++it) {
-          const uint32_t s = it % S;
-          const uint32_t ph = (it / S) & 1u;
-          if (!mbar_wait_bounded(&full[s], ph)) {
+        for (int kb = 0; kb < item.k_blocks; ++kb) {
+          const int s = ring.pos;
+          ring.pos = ring.pos + 1 == ring.stages ? 0 : ring.pos + 1;
+          const uint32_t par = (ring.parity >> s) & 1u;
+          ring.parity ^= 1u << s;
+          if (!mbar_wait_bounded(&full[s], par)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t a_base = smem_addr(sA + s * Cfg::kAHalfBytes);
-          const uint32_t b_base = smem_addr(sB + s * Cfg::kBHalfBytes);
+          const uint32_t a_base = smem_addr(sRing + s * stage_bytes);
+          const uint32_t b_base = a_base + a_bytes;
+          if (ap) {
 #pragma unroll
-          for (int k = 0; k < kAtom / 16; ++k) {
-            const uint64_t ad = smem_desc_sw128(a_base + k * 32, 16, 1024);
-            const uint64_t bd = bmn ? smem_desc_sw128(b_base + k * 2048, kAtom * 128, 1024)
-                                    : smem_desc_sw128(b_base + k * 32, 16, 1024);
-            umma_bf16_pair(d_tmem, ad, bd, bmn ? idesc_mn : idesc_k,
-                           (kb > 0 || k > 0) ? 1u : 0u);
+            for (int k = 0; k < kAtom / 16; ++k)
+              umma_bf16_pair(d_tmem, smem_desc_sw128(a_base + k * 32, 16, 1024),
+                             smem_desc_sw128(b_base + k * 2048, kAtom * 128, 1024), idesc_ap,
+                             (kb > 0 || k > 0) ? 1u : 0u);
+          } else {
+            // K-major: step k lies in swizzle atom k/4 (A atoms of 128 rows,
+            // 16 KiB apart; B atoms of 64 rows, 8 KiB apart)
+#pragma unroll
+            for (int k = 0; k < 128 / 16; ++k)
+              umma_bf16_pair(d_tmem,
+                             smem_desc_sw128(a_base + (k / 4) * kAtomBytes + (k % 4) * 32, 16,
+                                             1024),
+                             smem_desc_sw128(b_base + (k / 4) * (64 * 128) + (k % 4) * 32, 16,
+                                             1024),
+                             idesc_sym, (kb > 0 || k > 0) ? 1u : 0u);
           }
           umma_commit_pair(map_to_cta(smem_addr(&empty[s]), 0));
           umma_commit_pair(map_to_cta(smem_addr(&empty[s]), 1));
@@ -1117,8 +1267,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
     const int q = warp & 3;
     const int hc = (warp - 2) >> 2;
     const int row = q * 32 + lane;
-    const uint32_t out_base = smem_addr(sOut);
-    const uint32_t mir_base = smem_addr(sMir);
+    const uint32_t reg_base = smem_addr(sReg);
     const bool leader = threadIdx.x == kEpiLeader;
     const uint32_t tempty_leader0 = map_to_cta(smem_addr(&tempty[0]), 0);
     const uint32_t tempty_leader1 = map_to_cta(smem_addr(&tempty[1]), 0);
@@ -1127,20 +1276,28 @@ __global__ void __launch_bounds__(kPairThreads, 1)
     ep.coef_c = p.coef_c;
     ep.alpha = p.alpha;
     bool aux_inflight = false;
-    bool dep_failed = false;
-    // Leader: load the epilogue input tile of item w (poly: A; apply: X).
+    // Failures never change the epilogue's control flow: every thread runs
+    // the same named barriers for every item, and after a failed wait it only
+    // skips its waits, reads and stores (the watchdog word records why).
+    bool failed = false;
+    // This CTA's 128-row block of a Gram / polynomial region against its
+    // column block: above the diagonal (stored with its mirror), on it
+    // (stored), or below it (not stored).
+    auto block_rel = [&](const FusedItem& it) {
+      const int br = 2 * it.tm + static_cast<int>(rank);
+      return br < it.tn ? 1 : (br == it.tn ? 0 : -1);
+    };
+    // Leader: the epilogue tile of apply item w (X: no wait), into the
+    // ring's apply tile area -- free once the previous item's MMAs and
+    // stores are done with it.
     auto load_aux = [&](int w) {
       const FusedItem item = fused_item(w, p);
-      if (item.kind == kFGram) return;
-      if (!fused_wait_inputs(item, p)) {
-        atomicOr(&g_watchdog, MUON_POLAR_WATCHDOG_DEPENDENCY);
-        dep_failed = true;
-      }
-      const CUtensorMap* m = item.kind == kFPoly ? &maps.a128 : &maps.x_k;
+      if (item.kind != kFApply) return;
       mbar_arrive_expect_tx(aux_full, 4 * Cfg::kRegionBytes);
 #pragma unroll
       for (int c = 0; c < 4; ++c)
-        tma_load_3d(sOut + c * Cfg::kRegionBytes, m, aux_full, item.tn * kPairN + c * kChunkCols,
+        tma_load_3d(sAux + c * Cfg::kRegionBytes, &maps.x_k, aux_full,
+                    item.tn * kPairN + c * kChunkCols,
                     item.tm * kPairM + static_cast<int>(rank) * kHalf, item.b);
       aux_inflight = true;
     };
@@ -1159,82 +1316,121 @@ __global__ void __launch_bounds__(kPairThreads, 1)
     uint32_t aux_uses = 0;  // completed aux_full phases
     for (int w = cluster; w < p.total; w += nclusters, ++t) {
       const FusedItem item = fused_item(w, p);
-      const bool has_aux = item.kind != kFGram;
+      const bool ap = item.kind == kFApply;
+      const int rel = ap ? 1 : block_rel(item);
+      const bool has_aux = ap;
       const uint32_t acc = t & 1u;
-      const uint32_t uph = (t >> 1) & 1u;
-      int ok = 1;
-      if (lane == 0) {
-        ok = mbar_wait_bounded(&tfull[acc], uph) ? 1 : 0;
-        if (has_aux && ok) {
-          ok = mbar_wait_bounded(aux_full, aux_uses & 1u) ? 1 : 0;
-          if (ok) aux_inflight = false;
+      const int row0 = item.tm * kPairM + static_cast<int>(rank) * kHalf;
+      const int col0 = item.tn * (ap ? kPairN : kHalf);
+      // Polynomial: this thread's A values (row `row`, columns hc*32.. of
+      // each chunk) from global memory, requested before the accumulator is
+      // ready.  The Gram of the matrix is complete (acquired per warp).
+      uint4 pa[2][4];
+      if (item.kind == kFPoly && rel >= 0 && !failed) {
+        int dep = 1;
+        if (lane == 0) dep = wait_counter_bounded(p.counters + item.b, 2u * p.regions) ? 1 : 0;
+        dep = __shfl_sync(0xffffffffu, dep, 0);
+        if (!dep) {
+          if (lane == 0) atomicOr(&g_watchdog, MUON_POLAR_WATCHDOG_DEPENDENCY);
+          failed = true;
+        } else {
+          const uint16_t* src = p.gram +
+                                (static_cast<size_t>(item.b) * p.mp + row0 + row) * p.mp + col0 +
+                                hc * 32;
+#pragma unroll
+          for (int c = 0; c < 2; ++c)
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+              pa[c][u] = __ldcg(reinterpret_cast<const uint4*>(src + c * kChunkCols + u * 8));
         }
       }
-      ok = __shfl_sync(0xffffffffu, ok, 0);
-      if (!ok) {
-        if (lane == 0) atomicOr(&g_watchdog, MUON_POLAR_WATCHDOG_EPILOGUE);
-        break;
+      int ok = failed ? 0 : 1;
+      if (lane == 0 && ok) {
+        ok = mbar_wait_bounded(&tfull[acc], (t >> 1) & 1u) ? 1 : 0;
+        if (has_aux && ok) ok = mbar_wait_bounded(aux_full, aux_uses & 1u) ? 1 : 0;
+        if (!ok) atomicOr(&g_watchdog, MUON_POLAR_WATCHDOG_EPILOGUE);
       }
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) failed = true;
       if (has_aux) {
-        (void)mbar_try_wait(aux_full, aux_uses & 1u);
+        // every thread acquires the epilogue input the TMA wrote
+        if (!failed) (void)mbar_try_wait(aux_full, aux_uses & 1u);
         ++aux_uses;
+        if (leader) aux_inflight = false;
       }
       tc_fence_after();
-      const bool mirror = item.kind != kFApply && item.tm != item.tn;
-      const int row0 = item.tm * kPairM + static_cast<int>(rank) * kHalf;
-      const int col0 = item.tn * kPairN;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * kPairN;
+      const bool store = rel >= 0;
+      const bool mirror = !ap && rel > 0;
       const CUtensorMap* m_out = item.kind == kFGram ? &maps.a128
                                  : item.kind == kFPoly ? &maps.p128 : &maps.y128;
       const CUtensorMap* m_mir = item.kind == kFGram ? &maps.a64 : &maps.p64;
-#pragma unroll 1
-      for (int c = 0; c < Cfg::kChunks; ++c) {
-        const uint32_t out = out_base + c * Cfg::kRegionBytes;
-        const uint32_t mir = mir_base + (c & 1) * Cfg::kRegionBytes;
-        if (item.kind != kFApply) {
-          if (leader) bulk_wait_group_read<1>();
+      const int chunks = !store ? 0 : (ap ? kPairN / kChunkCols : kHalf / kChunkCols);
+      if (chunks == 0) release_accumulator(acc);
+      // Accumulator chunk c + 1 is read from tensor memory while chunk c is
+      // processed.  Apply: chunk c in place of its X chunk in the tile area.
+      // Gram / polynomial: output chunk in region 0, mirror chunk in region
+      // 1, reused by chunk 1 once chunk 0's stores have read them.
+      const uint32_t aux_base = smem_addr(sAux);
+      uint32_t rbuf[2][32];
+      if (chunks > 0 && !failed) tmem_ld_32x32b_x32(t_row + hc * 32, rbuf[0]);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        if (c >= chunks) break;
+        const uint32_t out = ap ? aux_base + c * Cfg::kRegionBytes : reg_base;
+        const uint32_t mir = reg_base + Cfg::kRegionBytes;
+        if (!ap && c > 0) {
+          if (leader) bulk_wait_group_read<0>();
           named_barrier(1, kPairEpiThreads);
         }
-        uint32_t r0[32];
-        tmem_ld_32x32b_x32(t_row + c * kChunkCols + hc * 32, r0);
-        tmem_wait_ld();
-        if (c == Cfg::kChunks - 1) release_accumulator(acc);
-        float v[32];
+        if (!failed) {
+          tmem_wait_ld(rbuf[c & 1]);
+          if (c + 1 < chunks)
+            tmem_ld_32x32b_x32(t_row + (c + 1) * kChunkCols + hc * 32, rbuf[(c + 1) & 1]);
+        }
+        if (c + 1 == chunks) release_accumulator(acc);
+        if (!failed) {
+          float v[32];
 #pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r0[j]);
-        if (item.kind == kFGram)
-          pair_epilogue_half<kGramBf16>(ep, out, mir, mirror, row, hc, v);
-        else if (item.kind == kFPoly)
-          pair_epilogue_half<kPoly>(ep, out, mir, mirror, row, hc, v);
-        else
-          pair_epilogue_half<kApply>(ep, out, mir, false, row, hc, v);
+          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(rbuf[c & 1][j]);
+          if (item.kind == kFGram)
+            pair_epilogue_half<kGramBf16>(ep, out, mir, mirror, row, hc, v);
+          else if (item.kind == kFPoly)
+            fused_poly_half(ep, out, mir, mirror, row, hc, v, pa[c & 1]);
+          else
+            pair_epilogue_half<kApply>(ep, out, mir, false, row, hc, v);
+        }
         fence_proxy_async_smem();
         named_barrier(1, kPairEpiThreads);
-        if (leader) {
-          tma_store_3d(m_out, sOut + c * Cfg::kRegionBytes, col0 + c * kChunkCols, row0, item.b);
+        if (leader && !failed) {
+          tma_store_3d(m_out, ap ? sAux + c * Cfg::kRegionBytes : sReg, col0 + c * kChunkCols,
+                       row0, item.b);
           if (mirror) {
 #pragma unroll
             for (int h = 0; h < kHalf / kChunkCols; ++h)
-              tma_store_3d(m_mir, sMir + (c & 1) * Cfg::kRegionBytes + h * (kChunkCols * 128),
+              tma_store_3d(m_mir, sReg + Cfg::kRegionBytes + h * (kChunkCols * 128),
                            row0 + h * kChunkCols, col0 + c * kChunkCols, item.b);
           }
           bulk_commit_group();
         }
       }
       if (leader) {
-        if (item.kind != kFApply) {
-          // Publish this band of the tile: its stores must have landed.
+        if (!ap) {
+          // Publish this CTA's part of the region once its stores have
+          // landed (also when it stored nothing or gave up: the count is
+          // per CTA and item).
           bulk_wait_group0();
           fence_proxy_async_global();
-          __threadfence();
           red_release_gpu_add(p.counters + (item.kind == kFGram ? 0 : p.batch) + item.b, 1u);
         } else {
           bulk_wait_group_read<0>();
         }
         const int next = w + nclusters;
-        if (next < p.total && !dep_failed) load_aux(next);
+        if (next < p.total && !failed) load_aux(next);
       }
-      if (dep_failed) break;
+      // the regions are free (stores have read them) before the next item
+      // writes them
+      named_barrier(1, kPairEpiThreads);
     }
     if (leader) {
       bulk_wait_group0();
@@ -1900,9 +2096,8 @@ int apply_t_impl(const void* poly, const void* x, void* y, int64_t batch, int64_
 }
 
 // ---------------------------------------------------------------- fused step
-// Step mode: 0 = by size (the fused kernel when the Gram has fewer pair tiles
-// than the device runs pairs at once, else three kernels), 1 = always fused,
-// 2 = never.  Initial value from MUON_POLAR_FUSED (1 -> 1, 0 -> 2).
+// Step mode: 0 = by size (see step_fused_impl), 1 = always fused, 2 = never.
+// Initial value from MUON_POLAR_FUSED (1 -> 1, 0 -> 2).
 std::atomic<int> g_step_mode{[] {
   const char* s = std::getenv("MUON_POLAR_FUSED");
   if (s == nullptr) return 0;
@@ -1926,7 +2121,7 @@ int fused_capacity(DeviceState* st, int dev, int* capacity) {
     if (fs.err != cudaSuccess) return;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * (st->sms / 2), 1, 1);
-    cfg.blockDim = dim3(kPairThreads, 1, 1);
+    cfg.blockDim = dim3(kTileThreads, 1, 1);
     cfg.dynamicSmemBytes = FusedCfg::kSmemBytes;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -1969,14 +2164,18 @@ int step_fused_impl(const void* x, void* y, void* gram, void* poly, void* scratc
   rc = fused_capacity(st, dev, &capacity);
   if (rc != MUON_POLAR_OK) return rc;
   const int64_t mp = padded_rows(m);
-  const int64_t d = mp / kPairM;
-  const int64_t sym = d * (d + 1) / 2;
+  const int64_t d2 = mp / kPairM;
+  const int64_t regions = d2 * (d2 + 1);
   const int64_t tn = (n + kPairN - 1) / kPairN;
-  const int64_t total = 2 * batch * sym + batch * d * tn;
+  const int64_t total = 2 * batch * regions + batch * d2 * tn;
   if (total > INT32_MAX) return MUON_POLAR_OK;
-  // By size: not yet faster than the three kernels on any measured shape
-  // (the stages of all matrices still run in lockstep), so only on request.
-  if (mode == 0) return MUON_POLAR_OK;
+  // By size, from measurements on B200 (muon_polar_step_sm100, 15 shapes):
+  // the fused launch wins for many small matrices -- more Gram regions than
+  // pairs and Mp <= 768: 4-21% faster at [16|32,512,2048], [8|16,768,3072],
+  // [64,256,1024] -- and loses where the three kernels run a Gram of one
+  // round (config 1 [8,512,2048]: 38.5 vs 36.8 us) or a large one on 256 x
+  // 256 pair tiles (Mp >= 1024, N >= 4096: up to 12% slower).
+  if (mode == 0 && !(batch * regions > capacity && mp <= 768)) return MUON_POLAR_OK;
 
   FusedMaps maps;
   rc = encode_3d(&maps.x_k, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, x, n, m, batch, ldx,
@@ -1999,24 +2198,26 @@ int step_fused_impl(const void* x, void* y, void* gram, void* poly, void* scratc
 
   FusedParams p = {};
   p.batch = static_cast<int32_t>(batch);
-  p.d = static_cast<int32_t>(d);
-  p.sym_tiles = static_cast<int32_t>(sym);
+  p.d2 = static_cast<int32_t>(d2);
+  p.regions = static_cast<int32_t>(regions);
   p.apply_tn = static_cast<int32_t>(tn);
-  p.n_gram = static_cast<int32_t>(batch * sym);
-  p.n_poly = static_cast<int32_t>(batch * sym);
+  p.n_gram = static_cast<int32_t>(batch * regions);
+  p.n_poly = static_cast<int32_t>(batch * regions);
   p.total = static_cast<int32_t>(total);
-  p.kb_gram = static_cast<int32_t>((n + kAtom - 1) / kAtom);
-  p.kb_poly = static_cast<int32_t>(mp / kAtom);
+  p.kb_gram = static_cast<int32_t>((n + 127) / 128);
+  p.kb_poly = static_cast<int32_t>(mp / 128);
   p.kb_apply = static_cast<int32_t>((m + kAtom - 1) / kAtom);
   p.coef_b = b;
   p.coef_c = c;
   p.alpha = round_to_bf16(a);
   p.counters = static_cast<uint32_t*>(scratch);
+  p.gram = static_cast<const uint16_t*>(gram);
+  p.mp = static_cast<int32_t>(mp);
 
   const int pairs = total < capacity ? static_cast<int>(total) : capacity;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * pairs, 1, 1);
-  cfg.blockDim = dim3(kPairThreads, 1, 1);
+  cfg.blockDim = dim3(kTileThreads, 1, 1);
   cfg.dynamicSmemBytes = FusedCfg::kSmemBytes;
   cfg.stream = stream;
   cudaLaunchAttribute attr[2];

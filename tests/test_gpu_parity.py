@@ -337,13 +337,16 @@ def step_mode(api):
 
 
 @pytest.mark.parametrize("shape", [(8, 512, 2048), (2, 150, 2064), (1, 128, 256),
-                                   (3, 640, 1000), (1, 1024, 1024)])
+                                   (3, 640, 1000), (1, 1024, 1024), (16, 256, 1024),
+                                   (32, 256, 512), (16, 512, 2048)])
 def test_fused_step_matches_three_kernels(api, cuda_device, shape, step_mode):
     """One fused persistent launch gives the bits of the three kernels, and
     repeated launches reuse the scratch counters correctly (they are reset by
     the last CTA of each launch).  The three kernels run without scratch, so
     without split-K: the fused kernel does not split K, and a split changes
-    the fp32 summation order of the Gram and the polynomial."""
+    the fp32 summation order of the Gram and the polynomial.  [16|32,256,*]
+    run polynomial items first on some pairs and then apply items with fewer
+    polynomial K-blocks than stages (a change of stage layout mid-ring)."""
     bsz, m, n = shape
     x = make_input(shape, seed=8).to(cuda_device)
     ws = torch.empty(api.workspace_bytes(bsz, m), dtype=torch.uint8, device=cuda_device)
@@ -365,6 +368,30 @@ def test_fused_step_matches_three_kernels(api, cuda_device, shape, step_mode):
     assert torch.equal(outs[1].view(torch.int16), outs[2].view(torch.int16))
     e = error_stats(outs[1], reference_formula(make_input(shape, seed=8).float(), COEFFICIENTS[:1]))
     assert e["rel_fro"] <= 1e-2, e
+
+
+@pytest.mark.parametrize("shape,fused", [((16, 512, 2048), True), ((64, 256, 1024), True),
+                                         ((8, 512, 2048), False), ((4, 1024, 4096), False)])
+def test_step_by_size_choice(api, cuda_device, shape, fused, step_mode):
+    """The default step mode picks one fused launch for many small matrices
+    and three kernels otherwise, with the bits of the forced mode."""
+    bsz, m, n = shape
+    x = make_input(shape, seed=12).to(cuda_device)
+    ws = torch.empty(api.workspace_bytes(bsz, m), dtype=torch.uint8, device=cuda_device)
+    scratch = api.new_scratch(bsz, m, n)
+    step_mode(0)
+    y0 = torch.empty_like(x)
+    before = api.launch_count()
+    api.step(x, y0, ws, A1, B1, C1, scratch=scratch)
+    launches = api.launch_count() - before
+    step_mode(1 if fused else 2)
+    y1 = torch.empty_like(x)
+    api.step(x, y1, ws, A1, B1, C1, scratch=scratch)
+    torch.cuda.synchronize()
+    _check_watchdog(api)
+    _counters_zero(scratch)
+    assert launches == (1 if fused else 3)
+    assert torch.equal(y0.view(torch.int16), y1.view(torch.int16))
 
 
 def test_torch_compile_matches_eager(op, cuda_device):
