@@ -293,7 +293,14 @@ int muon_polar_set_kernel_policy(int policy);
  *      <= 768), where it measured 4-21% faster on B200; else three kernels;
  *   1  one fused persistent launch for all three stages, with per-matrix
  *      dependencies tracked in the scratch counter area (needs scratch);
- *   2  always three kernels.
+ *   2  always three kernels, each waiting for the whole previous grid
+ *      (programmatic dependent launch);
+ *   3  always three kernels handing over per matrix: the polynomial kernel
+ *      starts on a matrix as soon as that matrix's Gram tiles are stored,
+ *      the apply kernel likewise after the polynomial (needs scratch;
+ *      counters in the upper half of the scratch counter area, batch <= 42,
+ *      split-K then keeps to the lower half; otherwise as mode 2).  Same
+ *      bits as mode 2; measured no faster on B200.
  * Initial value from MUON_POLAR_FUSED (1 -> 1, 0 -> 2).  Results are the
  * same in every mode (identical bits). */
 int muon_polar_set_step_mode(int mode);

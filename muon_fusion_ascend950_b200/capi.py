@@ -152,8 +152,9 @@ class CAPI:
         return prev
 
     def set_step_mode(self, mode: int) -> int:
-        """0 = by size, 1 = always one fused launch, 2 = always three kernels;
-        returns the previous mode."""
+        """0 = by size, 1 = always one fused launch, 2 = always three kernels,
+        3 = three kernels handing over per matrix; returns the previous
+        mode."""
         prev = int(self.lib.muon_polar_set_step_mode(int(mode)))
         if prev < 0:
             raise MuonPolarError("muon_polar_set_step_mode", prev, self.status_string(prev))

@@ -89,6 +89,21 @@ struct EpiParams {
   int32_t total_items;
   float* partial;      // [total_items][PAIR][128][tile width] fp32 partial sums
   uint32_t* counters;  // [total_tiles][PAIR] arrivals, zero between launches
+  // Chained step: the three kernels of muon_polar_step_sm100 hand over per
+  // matrix through counters chain[0..3*batch) = [Gram][poly][apply] instead
+  // of each waiting for the whole previous grid.  Role 1 (Gram): each CTA
+  // band of a finished tile adds one to Gram[b] once its stores have landed.
+  // Role 2 (poly): waits (bounded) for Gram[b] == chain_wait_target before it
+  // loads A of matrix b; signals poly[b] like the Gram.  Role 3 (apply):
+  // waits for poly[b] before loading P; each finished band adds one to
+  // apply[b], and the last (chain_ticket_target) resets the matrix's three
+  // counters to zero.  Roles 2 and 3 do their grid dependency wait at the
+  // end, so a grid still completes only after its predecessor.
+  uint32_t* chain;
+  int32_t chain_role;
+  int32_t chain_batch;
+  uint32_t chain_wait_target;
+  uint32_t chain_ticket_target;
 };
 
 struct TileCoord {
@@ -383,6 +398,15 @@ __global__ void __launch_bounds__(kTileThreads, 1)
   const int cluster = static_cast<int>(blockIdx.x) / PAIR;
   const int nclusters = static_cast<int>(gridDim.x) / PAIR;
   constexpr int kEpiLeader = 64;
+  // Chained step, roles 2 and 3: per-matrix waits replace the grid
+  // dependency wait (see EpiParams::chain).
+  const bool chain_wait = p.chain != nullptr && p.chain_role >= 2;
+  auto wait_chain = [&](int b) {
+    const bool ok = wait_counter_bounded(
+        p.chain + (p.chain_role == 2 ? 0 : p.chain_batch) + b, p.chain_wait_target);
+    fence_proxy_async_global();
+    return ok;
+  };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -486,7 +510,7 @@ __global__ void __launch_bounds__(kTileThreads, 1)
           n_pre = it;
         }
       }
-      grid_dependency_wait();
+      if (!chain_wait) grid_dependency_wait();
       grid_launch_dependents();
       uint32_t it = 0;
       bool ok = true;
@@ -495,6 +519,11 @@ __global__ void __launch_bounds__(kTileThreads, 1)
         // A diagonal tile of a symmetric kind multiplies a row block by
         // itself: only the A operand is loaded, and the MMA reads it twice.
         const bool diag = kSym && w.tm == w.tn;
+        if (chain_wait && !wait_chain(w.b)) {
+          atomicOr(&g_watchdog, MUON_POLAR_WATCHDOG_DEPENDENCY);
+          ok = false;
+          break;
+        }
         for (int kb = w.kb_begin; kb < w.kb_end; ++kb, ++it) {
           if (it % Cfg::kProducers != pid) continue;
           const uint32_t s = it % S;
@@ -527,11 +556,11 @@ __global__ void __launch_bounds__(kTileThreads, 1)
         }
       }
     } else {
-      grid_dependency_wait();
+      if (!chain_wait) grid_dependency_wait();
       grid_launch_dependents();
     }
   } else if (warp == 1) {
-    grid_dependency_wait();
+    if (!chain_wait) grid_dependency_wait();
     grid_launch_dependents();
     if (lane == 0 && rank == 0) {
       // ---------------- tcgen05 MMA issuer (leader CTA only)
@@ -614,6 +643,10 @@ __global__ void __launch_bounds__(kTileThreads, 1)
     uint32_t aux_issued[4] = {0u, 0u, 0u, 0u};
     auto load_aux_chunk = [&](int item, int c) {
       const WorkItem w = decode_item(p, item, kSym);
+      // the polynomial's input tile is A: in a chained step, after the Gram
+      // of its matrix
+      if (KIND == kPoly && chain_wait && !wait_chain(w.b))
+        atomicOr(&g_watchdog, MUON_POLAR_WATCHDOG_DEPENDENCY);
       mbar_arrive_expect_tx(&aux_full[c], Cfg::kOutChunkBytes);
       tma_load_3d(sOut + c * Cfg::kOutChunkBytes, &tmap_aux, &aux_full[c],
                   w.tn * kTileN + c * kChunkCols, w.tm * kTileM + static_cast<int>(rank) * kHalf,
@@ -637,7 +670,7 @@ __global__ void __launch_bounds__(kTileThreads, 1)
       if (leader && aux_early && cluster < p.total_items)
         for (int c = 0; c < Cfg::kChunks; ++c) load_aux_chunk(cluster, c);
     }
-    grid_dependency_wait();
+    if (!chain_wait) grid_dependency_wait();
     grid_launch_dependents();
     if constexpr (Cfg::kAux) {
       if (leader && !aux_early && cluster < p.total_items)
@@ -835,6 +868,23 @@ __global__ void __launch_bounds__(kTileThreads, 1)
           load_aux_chunk(next, Cfg::kChunks - 1);
         }
       }
+      if (leader && p.chain != nullptr) {
+        const int bt = p.chain_batch;
+        if (p.chain_role == 1 || p.chain_role == 2) {
+          // this band of the tile is stored: publish it
+          bulk_wait_group0();
+          fence_proxy_async_global();
+          red_release_gpu_add(p.chain + (p.chain_role == 1 ? 0 : bt) + tc.b, 1u);
+        } else if (p.chain_role == 3) {
+          uint32_t* tk = p.chain + 2 * bt + tc.b;
+          if (atomicAdd(tk, 1u) + 1u == p.chain_ticket_target) {
+            // every band of matrix b has passed its waits: zero its counters
+            p.chain[tc.b] = 0u;
+            p.chain[bt + tc.b] = 0u;
+            *tk = 0u;
+          }
+        }
+      }
     }
     if (leader) {
       bulk_wait_group0();
@@ -847,6 +897,9 @@ __global__ void __launch_bounds__(kTileThreads, 1)
     }
   }
 
+  // A chained grid completes only after its predecessor (its waits were
+  // on counters).
+  if (chain_wait) grid_dependency_wait();
   tc_fence_before();
   __syncthreads();
   if constexpr (PAIR == 2) cluster_sync();  // the leader's MMAs are done with both CTAs
@@ -1627,10 +1680,11 @@ constexpr size_t kPartialItemBytes = partial_item_bytes<2>();
 std::atomic<int> g_split_mode{0};
 
 template <int KIND, int PAIR>
-int choose_splits(int64_t tiles, int64_t k_blocks, int units) {
+int choose_splits(int64_t tiles, int64_t k_blocks, int units,
+                  int64_t max_counters = static_cast<int64_t>(kCounterBytes / 4)) {
   const int mode = g_split_mode.load(std::memory_order_relaxed);
   if (mode == 2) return 1;
-  if (tiles <= 0 || tiles * PAIR * 2 > static_cast<int64_t>(kCounterBytes / 4)) return 1;
+  if (tiles <= 0 || tiles * PAIR * 2 > max_counters) return 1;
   int64_t s = units / tiles;
   if (s > PairCfg<KIND, PAIR>::kMaxSplitsHere) s = PairCfg<KIND, PAIR>::kMaxSplitsHere;
   if (s > k_blocks / 2) s = k_blocks / 2;
@@ -1655,11 +1709,35 @@ void plan_no_splits(EpiParams& p) {
 }
 
 // Applies split-K to `p` if the scratch buffer allows it.
+// Chained step (EpiParams::chain): its per-matrix counters take the upper
+// half of the counter area, so split-K keeps to the lower half.
+constexpr size_t kChainCounterOffset = kCounterBytes / 2;
+
+struct ChainArgs {
+  uint32_t* base;          // scratch + kChainCounterOffset
+  int32_t role;            // 1 Gram, 2 poly, 3 apply
+  int32_t batch;
+  uint32_t wait_target;    // bands per matrix of the stage waited on
+  uint32_t ticket_target;  // apply: its own bands per matrix
+};
+
+void apply_chain(EpiParams& p, const ChainArgs* chain) {
+  if (chain == nullptr) return;
+  p.chain = chain->base;
+  p.chain_role = chain->role;
+  p.chain_batch = chain->batch;
+  p.chain_wait_target = chain->wait_target;
+  p.chain_ticket_target = chain->ticket_target;
+}
+
 template <int KIND, int PAIR>
-void plan_splits(EpiParams& p, void* scratch, size_t scratch_bytes, int units) {
+void plan_splits(EpiParams& p, void* scratch, size_t scratch_bytes, int units,
+                 bool chained = false) {
   plan_no_splits(p);
   if (scratch == nullptr || !aligned16(scratch)) return;
-  const int s = choose_splits<KIND, PAIR>(p.total_tiles, p.k_blocks, units);
+  const int64_t max_counters =
+      static_cast<int64_t>((chained ? kChainCounterOffset : kCounterBytes) / 4);
+  const int s = choose_splits<KIND, PAIR>(p.total_tiles, p.k_blocks, units, max_counters);
   if (s < 2 || split_scratch_bytes<PAIR>(p.total_tiles, s) > scratch_bytes) return;
   p.splits = s;
   p.total_items = p.total_tiles * s;
@@ -1787,7 +1865,7 @@ void sym_grid(EpiParams& p, int64_t batch, int64_t mp) {
 template <int KIND, int PAIR>
 int gram_launch(DeviceState* st, const void* x, void* gram, int64_t batch, int64_t m,
                 int64_t n, int64_t ldx, void* scratch, size_t scratch_bytes,
-                bool fixed_scratch, cudaStream_t stream) {
+                bool fixed_scratch, cudaStream_t stream, const ChainArgs* chain = nullptr) {
   constexpr bool kT = KIND == kGramT;
   const int64_t mp = padded_rows(kT ? n : m);
   int units = 0;
@@ -1814,11 +1892,12 @@ int gram_launch(DeviceState* st, const void* x, void* gram, int64_t batch, int64
                                 choose_splits<KIND, PAIR>(p.total_tiles, p.k_blocks, units)) >
           scratch_bytes)
     return MUON_POLAR_ERR_STATIC_SCRATCH;
-  plan_splits<KIND, PAIR>(p, scratch, scratch_bytes, units);
+  plan_splits<KIND, PAIR>(p, scratch, scratch_bytes, units, chain != nullptr);
   if (fixed_scratch && p.splits > 1) {
     cudaError_t e = cudaMemsetAsync(scratch, 0, kCounterBytes, stream);
     if (e != cudaSuccess) return static_cast<int>(e);
   }
+  apply_chain(p, chain);
   return launch_tile<KIND, PAIR>(st, tm, p, stream);
 }
 
@@ -1827,7 +1906,8 @@ int gram_launch(DeviceState* st, const void* x, void* gram, int64_t batch, int64
 template <int KIND>
 int gram_impl(const void* x, void* gram, int64_t batch, int64_t m, int64_t n,
               int64_t ldx, void* scratch, size_t scratch_bytes,
-              cudaStream_t stream, bool fixed_scratch = false) {
+              cudaStream_t stream, bool fixed_scratch = false,
+              const ChainArgs* chain = nullptr) {
   int rc = check_x_args(x, batch, m, n, ldx);
   if (rc != MUON_POLAR_OK) return rc;
   if (gram == nullptr) return MUON_POLAR_ERR_INVALID_ARGUMENT;
@@ -1850,14 +1930,15 @@ int gram_impl(const void* x, void* gram, int64_t batch, int64_t m, int64_t n,
   if (fixed_scratch || use_pairs(dp * (dp + 1) / 2 * batch, pairs, cost_blocks<2>(depth),
                                  d * (d + 1) / 2 * batch, ctas, cost_blocks<1>(depth)))
     return gram_launch<KIND, 2>(st, x, gram, batch, m, n, ldx, scratch, scratch_bytes,
-                                fixed_scratch, stream);
+                                fixed_scratch, stream, chain);
   return gram_launch<KIND, 1>(st, x, gram, batch, m, n, ldx, scratch, scratch_bytes,
-                              fixed_scratch, stream);
+                              fixed_scratch, stream, chain);
 }
 
 template <int PAIR>
 int poly_launch(DeviceState* st, const void* gram, void* poly, int64_t batch, int64_t mp,
-                float b, float c, void* scratch, size_t scratch_bytes, cudaStream_t stream) {
+                float b, float c, void* scratch, size_t scratch_bytes, cudaStream_t stream,
+                const ChainArgs* chain = nullptr) {
   int units = 0;
   int rc = tile_capacity<kPoly, PAIR>(st, &units);
   if (rc != MUON_POLAR_OK) return rc;
@@ -1875,12 +1956,14 @@ int poly_launch(DeviceState* st, const void* gram, void* poly, int64_t batch, in
   p.k_blocks = static_cast<int32_t>(k_blocks_of<kPoly, PAIR>(mp));
   p.coef_b = b;
   p.coef_c = c;
-  plan_splits<kPoly, PAIR>(p, scratch, scratch_bytes, units);
+  plan_splits<kPoly, PAIR>(p, scratch, scratch_bytes, units, chain != nullptr);
+  apply_chain(p, chain);
   return launch_tile<kPoly, PAIR>(st, tm, p, stream);
 }
 
 int poly_impl(const void* gram, void* poly, int64_t batch, int64_t mp, float b,
-              float c, void* scratch, size_t scratch_bytes, cudaStream_t stream) {
+              float c, void* scratch, size_t scratch_bytes, cudaStream_t stream,
+              const ChainArgs* chain = nullptr) {
   if (gram == nullptr || poly == nullptr || batch <= 0 || mp <= 0 ||
       (mp % kHalf) != 0 || batch > INT32_MAX || mp > (1 << 24))
     return MUON_POLAR_ERR_INVALID_ARGUMENT;
@@ -1899,8 +1982,8 @@ int poly_impl(const void* gram, void* poly, int64_t batch, int64_t mp, float b,
   if ((mp % kPairM) == 0 && use_pairs(dp * (dp + 1) / 2 * batch, pairs,
                                       cost_blocks<2>(mp), d * (d + 1) / 2 * batch, ctas,
                                       cost_blocks<1>(mp)))
-    return poly_launch<2>(st, gram, poly, batch, mp, b, c, scratch, scratch_bytes, stream);
-  return poly_launch<1>(st, gram, poly, batch, mp, b, c, scratch, scratch_bytes, stream);
+    return poly_launch<2>(st, gram, poly, batch, mp, b, c, scratch, scratch_bytes, stream, chain);
+  return poly_launch<1>(st, gram, poly, batch, mp, b, c, scratch, scratch_bytes, stream, chain);
 }
 
 // Rows [row_begin, row_begin + row_count) of P into the full [batch][mp][mp]
@@ -1970,7 +2053,7 @@ float round_to_bf16(float v) {
 template <int PAIR>
 int apply_launch(DeviceState* st, const void* poly, const void* x, void* y, int64_t batch,
                  int64_t m, int64_t n, int64_t ldx, int64_t ldy, float a, bool x_ready,
-                 cudaStream_t stream) {
+                 cudaStream_t stream, const ChainArgs* chain = nullptr) {
   using Cfg = PairCfg<kApply, PAIR>;
   const int64_t mp = padded_rows(m);
   const int64_t tiles_m = (m + Cfg::kTileM - 1) / Cfg::kTileM;
@@ -2002,6 +2085,7 @@ int apply_launch(DeviceState* st, const void* poly, const void* x, void* y, int6
   p.alpha = round_to_bf16(a);
   p.x_ready = x_ready ? 1 : 0;
   plan_no_splits(p);
+  apply_chain(p, chain);
   return launch_tile<kApply, PAIR>(st, tm, p, stream);
 }
 
@@ -2009,7 +2093,7 @@ int apply_launch(DeviceState* st, const void* poly, const void* x, void* y, int6
 // EpiParams::x_ready); only muon_polar_step_sm100 knows that.
 int apply_impl(const void* poly, const void* x, void* y, int64_t batch,
                int64_t m, int64_t n, int64_t ldx, int64_t ldy, float a,
-               cudaStream_t stream, bool x_ready = false) {
+               cudaStream_t stream, bool x_ready = false, const ChainArgs* chain = nullptr) {
   int rc = check_x_args(x, batch, m, n, ldx);
   if (rc != MUON_POLAR_OK) return rc;
   if (poly == nullptr || y == nullptr || ldy < n)
@@ -2028,8 +2112,8 @@ int apply_impl(const void* poly, const void* x, void* y, int64_t batch,
                 cost_blocks<2>(m),
                 (m + kHalf - 1) / kHalf * ((n + kHalf - 1) / kHalf) * batch, ctas,
                 cost_blocks<1>(m)))
-    return apply_launch<2>(st, poly, x, y, batch, m, n, ldx, ldy, a, x_ready, stream);
-  return apply_launch<1>(st, poly, x, y, batch, m, n, ldx, ldy, a, x_ready, stream);
+    return apply_launch<2>(st, poly, x, y, batch, m, n, ldx, ldy, a, x_ready, stream, chain);
+  return apply_launch<1>(st, poly, x, y, batch, m, n, ldx, ldy, a, x_ready, stream, chain);
 }
 
 // Kernel (3) of the step of X^T returned in X's layout (M > N without
@@ -2096,8 +2180,12 @@ int apply_t_impl(const void* poly, const void* x, void* y, int64_t batch, int64_
 }
 
 // ---------------------------------------------------------------- fused step
-// Step mode: 0 = by size (see step_fused_impl), 1 = always fused, 2 = never.
-// Initial value from MUON_POLAR_FUSED (1 -> 1, 0 -> 2).
+// Step mode: 0 = by size (see step_fused_impl), 1 = always fused, 2 = three
+// kernels, each waiting for the whole previous grid, 3 = three kernels
+// handing over per matrix (see plan_chain; measured on B200 no faster than
+// mode 2: 37.5 vs 37.0 us at [8,512,2048], 0.3-2% slower on five other
+// shapes -- the per-tile store completion and release cost what the earlier
+// start saves).  Initial value from MUON_POLAR_FUSED (1 -> 1, 0 -> 2).
 std::atomic<int> g_step_mode{[] {
   const char* s = std::getenv("MUON_POLAR_FUSED");
   if (s == nullptr) return 0;
@@ -2151,7 +2239,7 @@ int step_fused_impl(const void* x, void* y, void* gram, void* poly, void* scratc
                     cudaStream_t stream, bool* done) {
   *done = false;
   const int mode = g_step_mode.load(std::memory_order_relaxed);
-  if (mode == 2 || scratch == nullptr || !aligned16(scratch) ||
+  if (mode >= 2 || scratch == nullptr || !aligned16(scratch) ||
       static_cast<size_t>(2 * batch + 1) * 4 > kCounterBytes || scratch_bytes < kCounterBytes)
     return MUON_POLAR_OK;
   DeviceState* st = nullptr;
@@ -2233,6 +2321,50 @@ int step_fused_impl(const void* x, void* y, void* gram, void* poly, void* scratc
   if (e != cudaSuccess) return static_cast<int>(e);
   g_launch_count.fetch_add(1, std::memory_order_relaxed);
   *done = true;
+  return MUON_POLAR_OK;
+}
+
+// Chained three-kernel step (EpiParams::chain, step mode 3): whether the
+// scratch allows it, and each kernel's role and counts.  The engines are chosen here exactly
+// as gram_impl / poly_impl / apply_impl choose them, since the counts are
+// CTA bands per matrix of the producing kernel.
+int plan_chain(int64_t batch, int64_t m, int64_t n, void* scratch, size_t scratch_bytes,
+               ChainArgs (&chain)[3], bool* chained) {
+  *chained = false;
+  const int mode = g_step_mode.load(std::memory_order_relaxed);
+  if (mode != 3 || scratch == nullptr || !aligned16(scratch) || scratch_bytes < kCounterBytes ||
+      static_cast<size_t>(3 * batch) * 4 > kCounterBytes - kChainCounterOffset)
+    return MUON_POLAR_OK;
+  DeviceState* st = nullptr;
+  int rc = current_device_state(&st);
+  if (rc != MUON_POLAR_OK) return rc;
+  int gp = 0, gc = 0, pp = 0, pc = 0, ap = 0, ac = 0;
+  if ((rc = tile_capacity<kGramBf16, 2>(st, &gp)) != MUON_POLAR_OK) return rc;
+  if ((rc = tile_capacity<kGramBf16, 1>(st, &gc)) != MUON_POLAR_OK) return rc;
+  if ((rc = tile_capacity<kPoly, 2>(st, &pp)) != MUON_POLAR_OK) return rc;
+  if ((rc = tile_capacity<kPoly, 1>(st, &pc)) != MUON_POLAR_OK) return rc;
+  if ((rc = tile_capacity<kApply, 2>(st, &ap)) != MUON_POLAR_OK) return rc;
+  if ((rc = tile_capacity<kApply, 1>(st, &ac)) != MUON_POLAR_OK) return rc;
+  const int64_t mp = padded_rows(m);
+  const int64_t d = mp / kHalf, dp = mp / kPairM;
+  const int64_t sym1 = d * (d + 1) / 2, sym2 = dp * (dp + 1) / 2;
+  const bool gram_pairs = use_pairs(sym2 * batch, gp, cost_blocks<2>(n), sym1 * batch, gc,
+                                    cost_blocks<1>(n));
+  const bool poly_pairs = use_pairs(sym2 * batch, pp, cost_blocks<2>(mp), sym1 * batch, pc,
+                                    cost_blocks<1>(mp));
+  const int64_t at2 = (m + kPairM - 1) / kPairM * ((n + kPairN - 1) / kPairN);
+  const int64_t at1 = (m + kHalf - 1) / kHalf * ((n + kHalf - 1) / kHalf);
+  const bool apply_pairs = use_pairs(dp * ((n + kPairN - 1) / kPairN) * batch, ap,
+                                     cost_blocks<2>(m), at1 * batch, ac, cost_blocks<1>(m));
+  const uint32_t gram_bands = static_cast<uint32_t>(gram_pairs ? 2 * sym2 : sym1);
+  const uint32_t poly_bands = static_cast<uint32_t>(poly_pairs ? 2 * sym2 : sym1);
+  const uint32_t apply_bands = static_cast<uint32_t>(apply_pairs ? 2 * at2 : at1);
+  uint32_t* base = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(scratch) + kChainCounterOffset);
+  const int32_t bt = static_cast<int32_t>(batch);
+  chain[0] = {base, 1, bt, 0u, 0u};
+  chain[1] = {base, 2, bt, gram_bands, 0u};
+  chain[2] = {base, 3, bt, poly_bands, apply_bands};
+  *chained = true;
   return MUON_POLAR_OK;
 }
 
@@ -2392,11 +2524,18 @@ int muon_polar_step_sm100(const void* x, void* y, void* workspace,
   rc = step_fused_impl(x, y, gram, poly, scratch, scratch_bytes, batch, m, n, ldx, ldy, a, b,
                        c, s, &fused);
   if (rc != MUON_POLAR_OK || fused) return rc;
-  rc = gram_impl<kGramBf16>(x, gram, batch, m, n, ldx, scratch, scratch_bytes, s);
+  ChainArgs chain[3];
+  bool chained = false;
+  rc = plan_chain(batch, m, n, scratch, scratch_bytes, chain, &chained);
   if (rc != MUON_POLAR_OK) return rc;
-  rc = poly_impl(gram, poly, batch, mp, b, c, scratch, scratch_bytes, s);
+  rc = gram_impl<kGramBf16>(x, gram, batch, m, n, ldx, scratch, scratch_bytes, s, false,
+                            chained ? &chain[0] : nullptr);
   if (rc != MUON_POLAR_OK) return rc;
-  return apply_impl(poly, x, y, batch, m, n, ldx, ldy, a, s, /*x_ready=*/true);
+  rc = poly_impl(gram, poly, batch, mp, b, c, scratch, scratch_bytes, s,
+                 chained ? &chain[1] : nullptr);
+  if (rc != MUON_POLAR_OK) return rc;
+  return apply_impl(poly, x, y, batch, m, n, ldx, ldy, a, s, /*x_ready=*/true,
+                    chained ? &chain[2] : nullptr);
 }
 
 int muon_polar_gram_t_sm100(const void* x, void* gram, int64_t batch, int64_t m,
@@ -2534,7 +2673,7 @@ int muon_polar_set_kernel_policy(int policy) {
 }
 
 int muon_polar_set_step_mode(int mode) {
-  if (mode < 0 || mode > 2) return MUON_POLAR_ERR_INVALID_ARGUMENT;
+  if (mode < 0 || mode > 3) return MUON_POLAR_ERR_INVALID_ARGUMENT;
   return g_step_mode.exchange(mode);
 }
 

@@ -394,6 +394,38 @@ def test_step_by_size_choice(api, cuda_device, shape, fused, step_mode):
     assert torch.equal(y0.view(torch.int16), y1.view(torch.int16))
 
 
+@pytest.mark.parametrize("shape", [(8, 512, 2048), (1, 128, 256), (3, 640, 1000),
+                                   (2, 150, 2064), (40, 256, 512), (2, 1024, 1024)])
+def test_chained_step_matches_grid_waits(api, cuda_device, shape, step_mode):
+    """The three kernels handing over per matrix (step mode 3 with scratch)
+    give the bits of the three kernels each waiting for the whole previous
+    grid (mode 2), over repeated steps that reuse the counters (the last
+    apply band of each matrix zeroes them)."""
+    bsz, m, n = shape
+    x = make_input(shape, seed=13).to(cuda_device)
+    ws = torch.empty(api.workspace_bytes(bsz, m), dtype=torch.uint8, device=cuda_device)
+    scratch = api.new_scratch(bsz, m, n)
+    prev = api.set_split_mode(2)  # the same (unsplit) K order in both modes
+    try:
+        outs = {}
+        for mode in (3, 2):
+            step_mode(mode)
+            ys = []
+            for _ in range(3):
+                y = torch.full_like(x, float("nan"))
+                api.step(x, y, ws, A1, B1, C1, scratch=scratch)
+                ys.append(y)
+            torch.cuda.synchronize()
+            _check_watchdog(api)
+            _counters_zero(scratch)
+            for y in ys[1:]:
+                assert torch.equal(y.view(torch.int16), ys[0].view(torch.int16))
+            outs[mode] = ys[0]
+        assert torch.equal(outs[2].view(torch.int16), outs[3].view(torch.int16))
+    finally:
+        api.set_split_mode(prev)
+
+
 def test_torch_compile_matches_eager(op, cuda_device):
     """torch.compile (aot_eager backend, full graph) traces the operator with
     its FakeTensor kernel and runs it; the result equals eager bit for bit."""
