@@ -68,6 +68,7 @@ SIGNATURES = {
     "muon_polar_set_kernel_policy": (ctypes.c_int, [ctypes.c_int]),
     "muon_polar_set_step_mode": (ctypes.c_int, [ctypes.c_int]),
     "muon_polar_set_split_mode": (ctypes.c_int, [ctypes.c_int]),
+    "muon_polar_set_storage_mode": (ctypes.c_int, [ctypes.c_int]),
     "muon_polar_device_pairs": (ctypes.c_int, [ctypes.POINTER(ctypes.c_int)]),
     "muon_polar_launch_count": (ctypes.c_uint64, []),
 }
@@ -166,6 +167,14 @@ class CAPI:
         prev = int(self.lib.muon_polar_set_split_mode(int(mode)))
         if prev < 0:
             raise MuonPolarError("muon_polar_set_split_mode", prev, self.status_string(prev))
+        return prev
+
+    def set_storage_mode(self, mode: int) -> int:
+        """A and P inside the step: 0 = upper-only, 1 = full symmetric;
+        returns the previous mode."""
+        prev = int(self.lib.muon_polar_set_storage_mode(int(mode)))
+        if prev < 0:
+            raise MuonPolarError("muon_polar_set_storage_mode", prev, self.status_string(prev))
         return prev
 
     def device_pairs(self) -> int:
