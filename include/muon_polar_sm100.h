@@ -293,32 +293,10 @@ int muon_polar_set_kernel_policy(int policy);
  *      <= 768), where it measured 4-21% faster on B200; else three kernels;
  *   1  one fused persistent launch for all three stages, with per-matrix
  *      dependencies tracked in the scratch counter area (needs scratch);
- *   2  always three kernels, each waiting for the whole previous grid
- *      (programmatic dependent launch);
- *   3  always three kernels handing over per matrix: the polynomial kernel
- *      starts on a matrix as soon as that matrix's Gram tiles are stored,
- *      the apply kernel likewise after the polynomial (needs scratch;
- *      counters in the upper half of the scratch counter area, batch <= 42,
- *      split-K then keeps to the lower half; otherwise as mode 2).  Same
- *      bits as mode 2; measured no faster on B200.
+ *   2  always three kernels.
  * Initial value from MUON_POLAR_FUSED (1 -> 1, 0 -> 2).  Results are the
  * same in every mode (identical bits). */
 int muon_polar_set_step_mode(int mode);
-
-/* Storage of A and P between the three kernels of muon_polar_step_sm100,
- * process-wide; returns the previous mode (or
- * MUON_POLAR_ERR_INVALID_ARGUMENT).
- *   0  upper-only where it measured faster (default): when the Gram and
- *      the polynomial each run one round of tiles, no mirror tiles are
- *      written -- only the blocks on and above the diagonal -- and the
- *      polynomial and apply kernels read a block below it as the transpose
- *      of its mirror (M-contiguous tensor-map loads, transposed-operand
- *      MMAs), halving the Gram's and the polynomial's output stores (1-2%
- *      faster steps at [8,512,2048]); larger problems keep full storage;
- *   1  full symmetric matrices, as the per-kernel entry points write them.
- * Both give identical Y.  The initial value comes from MUON_POLAR_UPPER
- * (0 -> mode 1).  The per-kernel entry points always write full matrices. */
-int muon_polar_set_storage_mode(int mode);
 
 /* Split-K of kernels (1) and (2) when scratch is given, process-wide;
  * returns the previous mode (or MUON_POLAR_ERR_INVALID_ARGUMENT).

@@ -68,7 +68,6 @@ SIGNATURES = {
     "muon_polar_set_kernel_policy": (ctypes.c_int, [ctypes.c_int]),
     "muon_polar_set_step_mode": (ctypes.c_int, [ctypes.c_int]),
     "muon_polar_set_split_mode": (ctypes.c_int, [ctypes.c_int]),
-    "muon_polar_set_storage_mode": (ctypes.c_int, [ctypes.c_int]),
     "muon_polar_device_pairs": (ctypes.c_int, [ctypes.POINTER(ctypes.c_int)]),
     "muon_polar_launch_count": (ctypes.c_uint64, []),
 }
@@ -153,9 +152,8 @@ class CAPI:
         return prev
 
     def set_step_mode(self, mode: int) -> int:
-        """0 = by size, 1 = always one fused launch, 2 = always three kernels,
-        3 = three kernels handing over per matrix; returns the previous
-        mode."""
+        """0 = by size, 1 = always one fused launch, 2 = always three kernels;
+        returns the previous mode."""
         prev = int(self.lib.muon_polar_set_step_mode(int(mode)))
         if prev < 0:
             raise MuonPolarError("muon_polar_set_step_mode", prev, self.status_string(prev))
@@ -167,14 +165,6 @@ class CAPI:
         prev = int(self.lib.muon_polar_set_split_mode(int(mode)))
         if prev < 0:
             raise MuonPolarError("muon_polar_set_split_mode", prev, self.status_string(prev))
-        return prev
-
-    def set_storage_mode(self, mode: int) -> int:
-        """A and P inside the step: 0 = upper-only, 1 = full symmetric;
-        returns the previous mode."""
-        prev = int(self.lib.muon_polar_set_storage_mode(int(mode)))
-        if prev < 0:
-            raise MuonPolarError("muon_polar_set_storage_mode", prev, self.status_string(prev))
         return prev
 
     def device_pairs(self) -> int:

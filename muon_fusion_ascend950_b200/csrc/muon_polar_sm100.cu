@@ -89,33 +89,6 @@ struct EpiParams {
   int32_t total_items;
   float* partial;      // [total_items][PAIR][128][tile width] fp32 partial sums
   uint32_t* counters;  // [total_tiles][PAIR] arrivals, zero between launches
-  // Chained step: the three kernels of muon_polar_step_sm100 hand over per
-  // matrix through counters chain[0..3*batch) = [Gram][poly][apply] instead
-  // of each waiting for the whole previous grid.  Role 1 (Gram): each CTA
-  // band of a finished tile adds one to Gram[b] once its stores have landed.
-  // Role 2 (poly): waits (bounded) for Gram[b] == chain_wait_target before it
-  // loads A of matrix b; signals poly[b] like the Gram.  Role 3 (apply):
-  // waits for poly[b] before loading P; each finished band adds one to
-  // apply[b], and the last (chain_ticket_target) resets the matrix's three
-  // counters to zero.  Roles 2 and 3 do their grid dependency wait at the
-  // end, so a grid still completes only after its predecessor.
-  uint32_t* chain;
-  int32_t chain_role;
-  int32_t chain_batch;
-  uint32_t chain_wait_target;
-  uint32_t chain_ticket_target;
-  // Upper-only storage of A and P inside muon_polar_step_sm100: the Gram and
-  // polynomial kernels write no mirror tiles, only blocks on and above the
-  // diagonal.  A single-CTA launch whose reader needs every 256 x 256 block
-  // on or above the diagonal also stores the 128 x 128 blocks (2q+1, 2q):
-  // as extra tiles computed directly (the tile list ends with them), or as
-  // the mirrors of the tiles (2q, 2q+1) (mirror_sub).  t_rule (polynomial,
-  // apply): operand blocks below the diagonal, at the tile-height
-  // granularity, are read as the transpose of their stored mirror block
-  // through an M-contiguous map (polynomial: tmap_b; apply: tmap_mir).
-  int32_t upper_only;
-  int32_t mirror_sub;
-  int32_t t_rule;
 };
 
 struct TileCoord {
@@ -160,23 +133,8 @@ __host__ __device__ __forceinline__ WorkItem decode_item(const EpiParams& p, int
                                                          bool sym) {
   WorkItem w;
   const int tile = item / p.splits;
-  TileCoord tc;
-  const int sym_tiles = p.tiles_m * (p.tiles_m + 1) / 2;
-  if (sym && p.upper_only && p.tiles_per_batch > sym_tiles) {
-    // upper tiles of each matrix, then its sub-diagonal tiles (2q+1, 2q)
-    tc.b = tile / p.tiles_per_batch;
-    const int r = tile - tc.b * p.tiles_per_batch;
-    if (r < sym_tiles) {
-      const TileCoord u = decode_tile(r, true, p.tiles_m, p.tiles_n, sym_tiles);
-      tc.tm = u.tm;
-      tc.tn = u.tn;
-    } else {
-      tc.tm = 2 * (r - sym_tiles) + 1;
-      tc.tn = tc.tm - 1;
-    }
-  } else {
-    tc = decode_tile(tile, sym && !p.rows_mode, p.tiles_m, p.tiles_n, p.tiles_per_batch);
-  }
+  const TileCoord tc =
+      decode_tile(tile, sym && !p.rows_mode, p.tiles_m, p.tiles_n, p.tiles_per_batch);
   w.tile = tile;
   w.b = tc.b;
   w.tm = tc.tm + p.row_tile_begin;
@@ -425,23 +383,6 @@ __global__ void __launch_bounds__(kTileThreads, 1)
   const int cluster = static_cast<int>(blockIdx.x) / PAIR;
   const int nclusters = static_cast<int>(gridDim.x) / PAIR;
   constexpr int kEpiLeader = 64;
-  // Upper-only storage (EpiParams::upper_only): the polynomial reads both
-  // operands, the apply its A operand, as the transpose of the stored block
-  // when the block (tile-height granularity) lies below the diagonal.
-  constexpr bool kTransA = KIND == kPoly || KIND == kApply;
-  constexpr bool kTransB = KIND == kPoly;
-  auto trans_at = [&](int tile_row, int kb) {
-    return p.t_rule != 0 && tile_row > kb * Cfg::kBK / kTileM;
-  };
-  // Chained step, roles 2 and 3: per-matrix waits replace the grid
-  // dependency wait (see EpiParams::chain).
-  const bool chain_wait = p.chain != nullptr && p.chain_role >= 2;
-  auto wait_chain = [&](int b) {
-    const bool ok = wait_counter_bounded(
-        p.chain + (p.chain_role == 2 ? 0 : p.chain_batch) + b, p.chain_wait_target);
-    fence_proxy_async_global();
-    return ok;
-  };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -491,51 +432,24 @@ __global__ void __launch_bounds__(kTileThreads, 1)
       // the bytes on the leader's barrier, PAIR = 1 on its own.
       // K-major: [128 rows x 64 k] boxes; MN-major: one [kBK k x 64 rows] box
       // per 64-row chunk.
-      // Operand rows [row0, row0 + 128) x k-block kb into dst: K-major boxes
-      // from kmap, or M-contiguous boxes from mnmap when `mn`.
-      auto load_op = [&](uint8_t* dst, uint32_t s, const CUtensorMap* kmap,
-                         const CUtensorMap* mnmap, bool mn, int row0, int kb, int b) {
-        const uint32_t bar = PAIR == 2 ? map_to_cta(smem_addr(&full[s]), 0) : 0u;
-        if (mn) {
-#pragma unroll
-          for (int j = 0; j < kHalf / kAtom; ++j) {
-            if constexpr (PAIR == 2)
-              tma_load_3d_pair(dst + j * (Cfg::kBK * 128), mnmap, bar, row0 + j * kAtom,
-                               kb * Cfg::kBK, b);
-            else
-              tma_load_3d(dst + j * (Cfg::kBK * 128), mnmap, &full[s], row0 + j * kAtom,
-                          kb * Cfg::kBK, b);
-          }
-        } else {
-#pragma unroll
-          for (int j = 0; j < Cfg::kBK / kAtom; ++j) {
-            if constexpr (PAIR == 2)
-              tma_load_3d_pair(dst + j * kAtomBytes, kmap, bar, kb * Cfg::kBK + j * kAtom, row0,
-                               b);
-            else
-              tma_load_3d(dst + j * kAtomBytes, kmap, &full[s], kb * Cfg::kBK + j * kAtom, row0,
-                          b);
-          }
-        }
-      };
-      // M-contiguous map of a transposed operand read (polynomial: A in the
-      // B slot; apply: P in the mirror slot; kGramT: its own A map)
-      const CUtensorMap* tmap_t = kAmn ? &tmap_a : (KIND == kPoly ? &tmap_b : &tmap_mir);
       auto load_a = [&](uint32_t s, const WorkItem& w, int kb) {
+        const uint32_t bar = PAIR == 2 ? map_to_cta(smem_addr(&full[s]), 0) : 0u;
         const int a_row = w.tm * kTileM + static_cast<int>(rank) * kHalf;
-        const bool mn = kAmn || (kTransA && trans_at(w.tm, kb));
-        load_op(sA + s * Cfg::kAHalfBytes, s, &tmap_a, tmap_t, mn, a_row, kb, w.b);
+        constexpr int kBoxes = kAmn ? kHalf / kAtom : Cfg::kBK / kAtom;
+#pragma unroll
+        for (int j = 0; j < kBoxes; ++j) {
+          void* dst = sA + s * Cfg::kAHalfBytes + j * (kAmn ? Cfg::kBK * 128 : kAtomBytes);
+          const int c0 = kAmn ? a_row + j * kAtom : kb * Cfg::kBK + j * kAtom;
+          const int c1 = kAmn ? kb * Cfg::kBK : a_row;
+          if constexpr (PAIR == 2)
+            tma_load_3d_pair(dst, &tmap_a, bar, c0, c1, w.b);
+          else
+            tma_load_3d(dst, &tmap_a, &full[s], c0, c1, w.b);
+        }
       };
       auto load_b = [&](uint32_t s, const WorkItem& w, int kb) {
         const uint32_t bar = PAIR == 2 ? map_to_cta(smem_addr(&full[s]), 0) : 0u;
         const int b_row = w.tn * kTileN + static_cast<int>(rank) * kHalf;
-        if (kTransB && trans_at(w.tn, kb)) {
-          load_op(sB + s * Cfg::kBHalfBytes, s, &tmap_a, tmap_t, true, b_row, kb, w.b);
-          return;
-        }
-        // the polynomial's B rows are A rows: the A map (its B slot may hold
-        // the M-contiguous map)
-        const CUtensorMap* kmap_b = KIND == kPoly ? &tmap_a : &tmap_b;
         // K-major: [128 n x 64 k] boxes; MN-major: one [kBK k x 64 n] box per
         // 64-column chunk
         constexpr int kBoxes = kBmn ? kHalf / kAtom : Cfg::kBK / kAtom;
@@ -545,9 +459,9 @@ __global__ void __launch_bounds__(kTileThreads, 1)
           const int c0 = kBmn ? b_row + j * kAtom : kb * Cfg::kBK + j * kAtom;
           const int c1 = kBmn ? kb * Cfg::kBK : b_row;
           if constexpr (PAIR == 2)
-            tma_load_3d_pair(dst, kmap_b, bar, c0, c1, w.b);
+            tma_load_3d_pair(dst, &tmap_b, bar, c0, c1, w.b);
           else
-            tma_load_3d(dst, kmap_b, &full[s], c0, c1, w.b);
+            tma_load_3d(dst, &tmap_b, &full[s], c0, c1, w.b);
         }
       };
       // The first pipeline iterations' X operand before the dependency wait,
@@ -572,7 +486,7 @@ __global__ void __launch_bounds__(kTileThreads, 1)
           n_pre = it;
         }
       }
-      if (!chain_wait) grid_dependency_wait();
+      grid_dependency_wait();
       grid_launch_dependents();
       uint32_t it = 0;
       bool ok = true;
@@ -581,21 +495,8 @@ __global__ void __launch_bounds__(kTileThreads, 1)
         // A diagonal tile of a symmetric kind multiplies a row block by
         // itself: only the A operand is loaded, and the MMA reads it twice.
         const bool diag = kSym && w.tm == w.tn;
-        if (chain_wait && !wait_chain(w.b)) {
-          atomicOr(&g_watchdog, MUON_POLAR_WATCHDOG_DEPENDENCY);
-          ok = false;
-          break;
-        }
         for (int kb = w.kb_begin; kb < w.kb_end; ++kb, ++it) {
           if (it % Cfg::kProducers != pid) continue;
-          // Single CTA: the second producer issues its first stage only once
-          // the first has landed, so the first MMA does not wait for both
-          // (measured on B200: the polynomial kernel at [8,512,2048] 11.5 ->
-          // 8.8 us alone, the step 0.5 us shorter).
-          if (PAIR == 1 && pid == 1 && it == 1 && !mbar_wait_bounded(&full[0], 0u)) {
-            ok = false;
-            break;
-          }
           const uint32_t s = it % S;
           const uint32_t ph = (it / S) & 1u;
           const bool pre = it < n_pre;  // X operand already in flight
@@ -626,15 +527,15 @@ __global__ void __launch_bounds__(kTileThreads, 1)
         }
       }
     } else {
-      if (!chain_wait) grid_dependency_wait();
+      grid_dependency_wait();
       grid_launch_dependents();
     }
   } else if (warp == 1) {
-    if (!chain_wait) grid_dependency_wait();
+    grid_dependency_wait();
     grid_launch_dependents();
     if (lane == 0 && rank == 0) {
       // ---------------- tcgen05 MMA issuer (leader CTA only)
-      constexpr uint32_t idesc_base = idesc_bf16_f32(kTileN, kBmn ? 1u : 0u, kTileM, kAmn ? 1u : 0u);
+      constexpr uint32_t idesc = idesc_bf16_f32(kTileN, kBmn ? 1u : 0u, kTileM, kAmn ? 1u : 0u);
       uint32_t it = 0;
       uint32_t t = 0;
       bool ok = true;
@@ -659,11 +560,6 @@ __global__ void __launch_bounds__(kTileThreads, 1)
           tc_fence_after();
           const uint32_t a_base = smem_addr(sA + s * Cfg::kAHalfBytes);
           const uint32_t b_base = diag ? a_base : smem_addr(sB + s * Cfg::kBHalfBytes);
-          // operands read as the transpose of their stored block this stage
-          const bool a_mn = kAmn || (kTransA && trans_at(w.tm, kb));
-          const bool b_mn = kBmn || (kTransB && (diag ? a_mn : trans_at(w.tn, kb)));
-          const uint32_t idesc = (idesc_base & ~(3u << 15)) | ((a_mn ? 1u : 0u) << 15) |
-                                 ((b_mn ? 1u : 0u) << 16);
 #pragma unroll
           for (int k = 0; k < Cfg::kBK / 16; ++k) {
             // K-major: K step k lies in swizzle atom k/4 (16 KiB apart), 32
@@ -671,9 +567,9 @@ __global__ void __launch_bounds__(kTileThreads, 1)
             const uint32_t koff = (k / 4) * kAtomBytes + (k % 4) * 32;
             // MN-major: 16 k-rows of 128 bytes per step; 64-column chunks are
             // Cfg::kBK*128 bytes apart (leading offset).
-            const uint64_t ad = a_mn ? smem_desc_sw128(a_base + k * 2048, Cfg::kBK * 128, 1024)
+            const uint64_t ad = kAmn ? smem_desc_sw128(a_base + k * 2048, Cfg::kBK * 128, 1024)
                                      : smem_desc_sw128(a_base + koff, 16, 1024);
-            const uint64_t bd = b_mn ? smem_desc_sw128(b_base + k * 2048, Cfg::kBK * 128, 1024)
+            const uint64_t bd = kBmn ? smem_desc_sw128(b_base + k * 2048, Cfg::kBK * 128, 1024)
                                      : smem_desc_sw128(b_base + koff, 16, 1024);
             if constexpr (PAIR == 2)
               umma_bf16_pair(d_tmem, ad, bd, idesc, (kb > w.kb_begin || k > 0) ? 1u : 0u);
@@ -718,10 +614,6 @@ __global__ void __launch_bounds__(kTileThreads, 1)
     uint32_t aux_issued[4] = {0u, 0u, 0u, 0u};
     auto load_aux_chunk = [&](int item, int c) {
       const WorkItem w = decode_item(p, item, kSym);
-      // the polynomial's input tile is A: in a chained step, after the Gram
-      // of its matrix
-      if (KIND == kPoly && chain_wait && !wait_chain(w.b))
-        atomicOr(&g_watchdog, MUON_POLAR_WATCHDOG_DEPENDENCY);
       mbar_arrive_expect_tx(&aux_full[c], Cfg::kOutChunkBytes);
       tma_load_3d(sOut + c * Cfg::kOutChunkBytes, &tmap_aux, &aux_full[c],
                   w.tn * kTileN + c * kChunkCols, w.tm * kTileM + static_cast<int>(rank) * kHalf,
@@ -745,7 +637,7 @@ __global__ void __launch_bounds__(kTileThreads, 1)
       if (leader && aux_early && cluster < p.total_items)
         for (int c = 0; c < Cfg::kChunks; ++c) load_aux_chunk(cluster, c);
     }
-    if (!chain_wait) grid_dependency_wait();
+    grid_dependency_wait();
     grid_launch_dependents();
     if constexpr (Cfg::kAux) {
       if (leader && !aux_early && cluster < p.total_items)
@@ -765,9 +657,7 @@ __global__ void __launch_bounds__(kTileThreads, 1)
         break;
       }
       tc_fence_after();
-      const bool mirror =
-          kSym && !p.rows_mode && tc.tm != tc.tn &&
-          (!p.upper_only || (p.mirror_sub && (tc.tm & 1) == 0 && tc.tn == tc.tm + 1));
+      const bool mirror = kSym && !p.rows_mode && tc.tm != tc.tn;
       const int row0 = tc.tm * kTileM + static_cast<int>(rank) * kHalf;
       const int col0 = tc.tn * kTileN;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * kTileN;
@@ -945,23 +835,6 @@ __global__ void __launch_bounds__(kTileThreads, 1)
           load_aux_chunk(next, Cfg::kChunks - 1);
         }
       }
-      if (leader && p.chain != nullptr) {
-        const int bt = p.chain_batch;
-        if (p.chain_role == 1 || p.chain_role == 2) {
-          // this band of the tile is stored: publish it
-          bulk_wait_group0();
-          fence_proxy_async_global();
-          red_release_gpu_add(p.chain + (p.chain_role == 1 ? 0 : bt) + tc.b, 1u);
-        } else if (p.chain_role == 3) {
-          uint32_t* tk = p.chain + 2 * bt + tc.b;
-          if (atomicAdd(tk, 1u) + 1u == p.chain_ticket_target) {
-            // every band of matrix b has passed its waits: zero its counters
-            p.chain[tc.b] = 0u;
-            p.chain[bt + tc.b] = 0u;
-            *tk = 0u;
-          }
-        }
-      }
     }
     if (leader) {
       bulk_wait_group0();
@@ -974,9 +847,6 @@ __global__ void __launch_bounds__(kTileThreads, 1)
     }
   }
 
-  // A chained grid completes only after its predecessor (its waits were
-  // on counters).
-  if (chain_wait) grid_dependency_wait();
   tc_fence_before();
   __syncthreads();
   if constexpr (PAIR == 2) cluster_sync();  // the leader's MMAs are done with both CTAs
@@ -1757,11 +1627,10 @@ constexpr size_t kPartialItemBytes = partial_item_bytes<2>();
 std::atomic<int> g_split_mode{0};
 
 template <int KIND, int PAIR>
-int choose_splits(int64_t tiles, int64_t k_blocks, int units,
-                  int64_t max_counters = static_cast<int64_t>(kCounterBytes / 4)) {
+int choose_splits(int64_t tiles, int64_t k_blocks, int units) {
   const int mode = g_split_mode.load(std::memory_order_relaxed);
   if (mode == 2) return 1;
-  if (tiles <= 0 || tiles * PAIR * 2 > max_counters) return 1;
+  if (tiles <= 0 || tiles * PAIR * 2 > static_cast<int64_t>(kCounterBytes / 4)) return 1;
   int64_t s = units / tiles;
   if (s > PairCfg<KIND, PAIR>::kMaxSplitsHere) s = PairCfg<KIND, PAIR>::kMaxSplitsHere;
   if (s > k_blocks / 2) s = k_blocks / 2;
@@ -1786,35 +1655,11 @@ void plan_no_splits(EpiParams& p) {
 }
 
 // Applies split-K to `p` if the scratch buffer allows it.
-// Chained step (EpiParams::chain): its per-matrix counters take the upper
-// half of the counter area, so split-K keeps to the lower half.
-constexpr size_t kChainCounterOffset = kCounterBytes / 2;
-
-struct ChainArgs {
-  uint32_t* base;          // scratch + kChainCounterOffset
-  int32_t role;            // 1 Gram, 2 poly, 3 apply
-  int32_t batch;
-  uint32_t wait_target;    // bands per matrix of the stage waited on
-  uint32_t ticket_target;  // apply: its own bands per matrix
-};
-
-void apply_chain(EpiParams& p, const ChainArgs* chain) {
-  if (chain == nullptr) return;
-  p.chain = chain->base;
-  p.chain_role = chain->role;
-  p.chain_batch = chain->batch;
-  p.chain_wait_target = chain->wait_target;
-  p.chain_ticket_target = chain->ticket_target;
-}
-
 template <int KIND, int PAIR>
-void plan_splits(EpiParams& p, void* scratch, size_t scratch_bytes, int units,
-                 bool chained = false) {
+void plan_splits(EpiParams& p, void* scratch, size_t scratch_bytes, int units) {
   plan_no_splits(p);
   if (scratch == nullptr || !aligned16(scratch)) return;
-  const int64_t max_counters =
-      static_cast<int64_t>((chained ? kChainCounterOffset : kCounterBytes) / 4);
-  const int s = choose_splits<KIND, PAIR>(p.total_tiles, p.k_blocks, units, max_counters);
+  const int s = choose_splits<KIND, PAIR>(p.total_tiles, p.k_blocks, units);
   if (s < 2 || split_scratch_bytes<PAIR>(p.total_tiles, s) > scratch_bytes) return;
   p.splits = s;
   p.total_items = p.total_tiles * s;
@@ -1934,22 +1779,6 @@ void sym_grid(EpiParams& p, int64_t batch, int64_t mp) {
   p.total_tiles = static_cast<int32_t>(d * (d + 1) / 2 * batch);
 }
 
-// Upper-only storage (EpiParams::upper_only): no mirror tiles; single-CTA
-// launches also compute the tiles (2q+1, 2q), so that every 256 x 256 block
-// on or above the diagonal is stored whichever engine wrote it.
-// `upper`: 1 = upper-only, 2 = plus the extra tiles (2q+1, 2q), 3 = plus the
-// mirrors of the tiles (2q, 2q+1); 2 and 3 only matter on single CTAs (CTA
-// pairs store whole 256 x 256 blocks).
-template <int PAIR>
-void upper_grid(EpiParams& p, int64_t batch, int upper) {
-  p.upper_only = 1;
-  if (PAIR == 1 && upper == 2) {
-    p.tiles_per_batch += p.tiles_m / 2;
-    p.total_tiles = static_cast<int32_t>(static_cast<int64_t>(p.tiles_per_batch) * batch);
-  }
-  if (PAIR == 1 && upper == 3) p.mirror_sub = 1;
-}
-
 // Kernel (1) on one engine.  `fixed_scratch`: the scratch is a fixed buffer
 // that keeps the previous call's contents -- a plan that needs more than it
 // holds is refused, and the arrival counters are cleared before the launch.
@@ -1958,8 +1787,7 @@ void upper_grid(EpiParams& p, int64_t batch, int upper) {
 template <int KIND, int PAIR>
 int gram_launch(DeviceState* st, const void* x, void* gram, int64_t batch, int64_t m,
                 int64_t n, int64_t ldx, void* scratch, size_t scratch_bytes,
-                bool fixed_scratch, cudaStream_t stream, const ChainArgs* chain = nullptr,
-                int upper = 0) {
+                bool fixed_scratch, cudaStream_t stream) {
   constexpr bool kT = KIND == kGramT;
   const int64_t mp = padded_rows(kT ? n : m);
   int units = 0;
@@ -1980,19 +1808,17 @@ int gram_launch(DeviceState* st, const void* x, void* gram, int64_t batch, int64
   if (rc != MUON_POLAR_OK) return rc;
   EpiParams p = {};
   sym_grid<PAIR>(p, batch, mp);
-  if (upper) upper_grid<PAIR>(p, batch, upper);
   p.k_blocks = static_cast<int32_t>(k_blocks_of<KIND, PAIR>(kT ? m : n));
   if (fixed_scratch &&
       split_scratch_bytes<PAIR>(p.total_tiles,
                                 choose_splits<KIND, PAIR>(p.total_tiles, p.k_blocks, units)) >
           scratch_bytes)
     return MUON_POLAR_ERR_STATIC_SCRATCH;
-  plan_splits<KIND, PAIR>(p, scratch, scratch_bytes, units, chain != nullptr);
+  plan_splits<KIND, PAIR>(p, scratch, scratch_bytes, units);
   if (fixed_scratch && p.splits > 1) {
     cudaError_t e = cudaMemsetAsync(scratch, 0, kCounterBytes, stream);
     if (e != cudaSuccess) return static_cast<int>(e);
   }
-  apply_chain(p, chain);
   return launch_tile<KIND, PAIR>(st, tm, p, stream);
 }
 
@@ -2001,8 +1827,7 @@ int gram_launch(DeviceState* st, const void* x, void* gram, int64_t batch, int64
 template <int KIND>
 int gram_impl(const void* x, void* gram, int64_t batch, int64_t m, int64_t n,
               int64_t ldx, void* scratch, size_t scratch_bytes,
-              cudaStream_t stream, bool fixed_scratch = false,
-              const ChainArgs* chain = nullptr, int upper = 0) {
+              cudaStream_t stream, bool fixed_scratch = false) {
   int rc = check_x_args(x, batch, m, n, ldx);
   if (rc != MUON_POLAR_OK) return rc;
   if (gram == nullptr) return MUON_POLAR_ERR_INVALID_ARGUMENT;
@@ -2025,28 +1850,21 @@ int gram_impl(const void* x, void* gram, int64_t batch, int64_t m, int64_t n,
   if (fixed_scratch || use_pairs(dp * (dp + 1) / 2 * batch, pairs, cost_blocks<2>(depth),
                                  d * (d + 1) / 2 * batch, ctas, cost_blocks<1>(depth)))
     return gram_launch<KIND, 2>(st, x, gram, batch, m, n, ldx, scratch, scratch_bytes,
-                                fixed_scratch, stream, chain, upper);
+                                fixed_scratch, stream);
   return gram_launch<KIND, 1>(st, x, gram, batch, m, n, ldx, scratch, scratch_bytes,
-                              fixed_scratch, stream, chain, upper);
+                              fixed_scratch, stream);
 }
 
 template <int PAIR>
 int poly_launch(DeviceState* st, const void* gram, void* poly, int64_t batch, int64_t mp,
-                float b, float c, void* scratch, size_t scratch_bytes, cudaStream_t stream,
-                const ChainArgs* chain = nullptr, int upper = 0) {
+                float b, float c, void* scratch, size_t scratch_bytes, cudaStream_t stream) {
   int units = 0;
   int rc = tile_capacity<kPoly, PAIR>(st, &units);
   if (rc != MUON_POLAR_OK) return rc;
   TileMaps tm;
   rc = encode_square(&tm.a, gram, batch, mp, false, kHalf);
   if (rc != MUON_POLAR_OK) return rc;
-  // upper-only: A blocks below the diagonal are read through an M-contiguous
-  // map of A in the B slot (the B operand's K-major loads use the A map)
   tm.b = tm.a;
-  if (upper) {
-    rc = encode_square(&tm.b, gram, batch, mp, false, PairCfg<kPoly, PAIR>::kBK);
-    if (rc != MUON_POLAR_OK) return rc;
-  }
   tm.aux = tm.a;
   rc = encode_square(&tm.out, poly, batch, mp, false, kHalf);
   if (rc != MUON_POLAR_OK) return rc;
@@ -2054,21 +1872,15 @@ int poly_launch(DeviceState* st, const void* gram, void* poly, int64_t batch, in
   if (rc != MUON_POLAR_OK) return rc;
   EpiParams p = {};
   sym_grid<PAIR>(p, batch, mp);
-  if (upper) {
-    upper_grid<PAIR>(p, batch, upper);
-    p.t_rule = 1;
-  }
   p.k_blocks = static_cast<int32_t>(k_blocks_of<kPoly, PAIR>(mp));
   p.coef_b = b;
   p.coef_c = c;
-  plan_splits<kPoly, PAIR>(p, scratch, scratch_bytes, units, chain != nullptr);
-  apply_chain(p, chain);
+  plan_splits<kPoly, PAIR>(p, scratch, scratch_bytes, units);
   return launch_tile<kPoly, PAIR>(st, tm, p, stream);
 }
 
 int poly_impl(const void* gram, void* poly, int64_t batch, int64_t mp, float b,
-              float c, void* scratch, size_t scratch_bytes, cudaStream_t stream,
-              const ChainArgs* chain = nullptr, int upper = 0) {
+              float c, void* scratch, size_t scratch_bytes, cudaStream_t stream) {
   if (gram == nullptr || poly == nullptr || batch <= 0 || mp <= 0 ||
       (mp % kHalf) != 0 || batch > INT32_MAX || mp > (1 << 24))
     return MUON_POLAR_ERR_INVALID_ARGUMENT;
@@ -2087,10 +1899,8 @@ int poly_impl(const void* gram, void* poly, int64_t batch, int64_t mp, float b,
   if ((mp % kPairM) == 0 && use_pairs(dp * (dp + 1) / 2 * batch, pairs,
                                       cost_blocks<2>(mp), d * (d + 1) / 2 * batch, ctas,
                                       cost_blocks<1>(mp)))
-    return poly_launch<2>(st, gram, poly, batch, mp, b, c, scratch, scratch_bytes, stream, chain,
-                          upper);
-  return poly_launch<1>(st, gram, poly, batch, mp, b, c, scratch, scratch_bytes, stream, chain,
-                        upper);
+    return poly_launch<2>(st, gram, poly, batch, mp, b, c, scratch, scratch_bytes, stream);
+  return poly_launch<1>(st, gram, poly, batch, mp, b, c, scratch, scratch_bytes, stream);
 }
 
 // Rows [row_begin, row_begin + row_count) of P into the full [batch][mp][mp]
@@ -2160,7 +1970,7 @@ float round_to_bf16(float v) {
 template <int PAIR>
 int apply_launch(DeviceState* st, const void* poly, const void* x, void* y, int64_t batch,
                  int64_t m, int64_t n, int64_t ldx, int64_t ldy, float a, bool x_ready,
-                 cudaStream_t stream, const ChainArgs* chain = nullptr, bool upper = false) {
+                 cudaStream_t stream) {
   using Cfg = PairCfg<kApply, PAIR>;
   const int64_t mp = padded_rows(m);
   const int64_t tiles_m = (m + Cfg::kTileM - 1) / Cfg::kTileM;
@@ -2182,13 +1992,7 @@ int apply_launch(DeviceState* st, const void* poly, const void* x, void* y, int6
                  kAtom, kHalf);
   if (rc != MUON_POLAR_OK) return rc;
   tm.mir = tm.out;
-  if (upper) {
-    // P upper-only: blocks below the diagonal through an M-contiguous map
-    rc = encode_square(&tm.mir, poly, batch, mp, false, Cfg::kBK);
-    if (rc != MUON_POLAR_OK) return rc;
-  }
   EpiParams p = {};
-  p.t_rule = upper ? 1 : 0;
   p.tiles_m = static_cast<int32_t>(tiles_m);
   p.tiles_n = static_cast<int32_t>(tiles_n);
   p.tiles_per_batch = static_cast<int32_t>(tiles_m * tiles_n);
@@ -2198,7 +2002,6 @@ int apply_launch(DeviceState* st, const void* poly, const void* x, void* y, int6
   p.alpha = round_to_bf16(a);
   p.x_ready = x_ready ? 1 : 0;
   plan_no_splits(p);
-  apply_chain(p, chain);
   return launch_tile<kApply, PAIR>(st, tm, p, stream);
 }
 
@@ -2206,8 +2009,7 @@ int apply_launch(DeviceState* st, const void* poly, const void* x, void* y, int6
 // EpiParams::x_ready); only muon_polar_step_sm100 knows that.
 int apply_impl(const void* poly, const void* x, void* y, int64_t batch,
                int64_t m, int64_t n, int64_t ldx, int64_t ldy, float a,
-               cudaStream_t stream, bool x_ready = false, const ChainArgs* chain = nullptr,
-               bool upper = false) {
+               cudaStream_t stream, bool x_ready = false) {
   int rc = check_x_args(x, batch, m, n, ldx);
   if (rc != MUON_POLAR_OK) return rc;
   if (poly == nullptr || y == nullptr || ldy < n)
@@ -2226,10 +2028,8 @@ int apply_impl(const void* poly, const void* x, void* y, int64_t batch,
                 cost_blocks<2>(m),
                 (m + kHalf - 1) / kHalf * ((n + kHalf - 1) / kHalf) * batch, ctas,
                 cost_blocks<1>(m)))
-    return apply_launch<2>(st, poly, x, y, batch, m, n, ldx, ldy, a, x_ready, stream, chain,
-                           upper);
-  return apply_launch<1>(st, poly, x, y, batch, m, n, ldx, ldy, a, x_ready, stream, chain,
-                         upper);
+    return apply_launch<2>(st, poly, x, y, batch, m, n, ldx, ldy, a, x_ready, stream);
+  return apply_launch<1>(st, poly, x, y, batch, m, n, ldx, ldy, a, x_ready, stream);
 }
 
 // Kernel (3) of the step of X^T returned in X's layout (M > N without
@@ -2297,24 +2097,12 @@ int apply_t_impl(const void* poly, const void* x, void* y, int64_t batch, int64_
 
 // ---------------------------------------------------------------- fused step
 // Step mode: 0 = by size (see step_fused_impl), 1 = always fused, 2 = three
-// kernels, each waiting for the whole previous grid, 3 = three kernels
-// handing over per matrix (see plan_chain; measured on B200 no faster than
-// mode 2: 37.5 vs 37.0 us at [8,512,2048], 0.3-2% slower on five other
-// shapes -- the per-tile store completion and release cost what the earlier
-// start saves).  Initial value from MUON_POLAR_FUSED (1 -> 1, 0 -> 2).
+// kernels.  Initial value from MUON_POLAR_FUSED (1 -> 1, 0 -> 2).
 std::atomic<int> g_step_mode{[] {
   const char* s = std::getenv("MUON_POLAR_FUSED");
   if (s == nullptr) return 0;
   const int v = std::atoi(s);
   return v == 1 ? 1 : (v == 0 ? 2 : 0);
-}()};
-
-// Storage of A and P inside muon_polar_step_sm100's three kernels: 1 =
-// upper-only (EpiParams::upper_only; no mirror tiles), 0 = full symmetric
-// matrices.  Initial value from MUON_POLAR_UPPER (default 1).
-std::atomic<int> g_upper_only{[] {
-  const char* s = std::getenv("MUON_POLAR_UPPER");
-  return (s != nullptr && std::atoi(s) == 0) ? 0 : 1;
 }()};
 
 struct FusedDeviceState {
@@ -2363,7 +2151,7 @@ int step_fused_impl(const void* x, void* y, void* gram, void* poly, void* scratc
                     cudaStream_t stream, bool* done) {
   *done = false;
   const int mode = g_step_mode.load(std::memory_order_relaxed);
-  if (mode >= 2 || scratch == nullptr || !aligned16(scratch) ||
+  if (mode == 2 || scratch == nullptr || !aligned16(scratch) ||
       static_cast<size_t>(2 * batch + 1) * 4 > kCounterBytes || scratch_bytes < kCounterBytes)
     return MUON_POLAR_OK;
   DeviceState* st = nullptr;
@@ -2445,91 +2233,6 @@ int step_fused_impl(const void* x, void* y, void* gram, void* poly, void* scratc
   if (e != cudaSuccess) return static_cast<int>(e);
   g_launch_count.fetch_add(1, std::memory_order_relaxed);
   *done = true;
-  return MUON_POLAR_OK;
-}
-
-// Engines of muon_polar_step_sm100's three kernels, chosen here exactly as
-// gram_impl / poly_impl / apply_impl choose them, and what the step derives
-// from them (band counts for chaining, the storage of A and P).
-struct StepEngines {
-  bool gram_pairs, poly_pairs, apply_pairs;
-  int64_t sym1, sym2, d;           // tiles per matrix (single / pair), 128-blocks
-  int gram_ctas, poly_ctas;        // single-CTA units of the Gram / polynomial
-  uint32_t gram_bands, poly_bands, apply_bands;  // CTA bands per matrix
-  bool one_round;  // the Gram and the polynomial each fit the device at once
-};
-
-int step_engines(int64_t batch, int64_t m, int64_t n, StepEngines* e) {
-  DeviceState* st = nullptr;
-  int rc = current_device_state(&st);
-  if (rc != MUON_POLAR_OK) return rc;
-  int gp = 0, gc = 0, pp = 0, pc = 0, ap = 0, ac = 0;
-  if ((rc = tile_capacity<kGramBf16, 2>(st, &gp)) != MUON_POLAR_OK) return rc;
-  if ((rc = tile_capacity<kGramBf16, 1>(st, &gc)) != MUON_POLAR_OK) return rc;
-  if ((rc = tile_capacity<kPoly, 2>(st, &pp)) != MUON_POLAR_OK) return rc;
-  if ((rc = tile_capacity<kPoly, 1>(st, &pc)) != MUON_POLAR_OK) return rc;
-  if ((rc = tile_capacity<kApply, 2>(st, &ap)) != MUON_POLAR_OK) return rc;
-  if ((rc = tile_capacity<kApply, 1>(st, &ac)) != MUON_POLAR_OK) return rc;
-  const int64_t mp = padded_rows(m);
-  const int64_t d = mp / kHalf, dp = mp / kPairM;
-  e->d = d;
-  e->sym1 = d * (d + 1) / 2;
-  e->sym2 = dp * (dp + 1) / 2;
-  e->gram_ctas = gc;
-  e->poly_ctas = pc;
-  e->gram_pairs = use_pairs(e->sym2 * batch, gp, cost_blocks<2>(n), e->sym1 * batch, gc,
-                            cost_blocks<1>(n));
-  e->poly_pairs = use_pairs(e->sym2 * batch, pp, cost_blocks<2>(mp), e->sym1 * batch, pc,
-                            cost_blocks<1>(mp));
-  const int64_t at2 = (m + kPairM - 1) / kPairM * ((n + kPairN - 1) / kPairN);
-  const int64_t at1 = (m + kHalf - 1) / kHalf * ((n + kHalf - 1) / kHalf);
-  e->apply_pairs = use_pairs(dp * ((n + kPairN - 1) / kPairN) * batch, ap, cost_blocks<2>(m),
-                             at1 * batch, ac, cost_blocks<1>(m));
-  e->one_round = (e->gram_pairs ? e->sym2 * batch <= gp : e->sym1 * batch <= gc) &&
-                 (e->poly_pairs ? e->sym2 * batch <= pp : e->sym1 * batch <= pc);
-  e->gram_bands = static_cast<uint32_t>(e->gram_pairs ? 2 * e->sym2 : e->sym1);
-  e->poly_bands = static_cast<uint32_t>(e->poly_pairs ? 2 * e->sym2 : e->sym1);
-  e->apply_bands = static_cast<uint32_t>(e->apply_pairs ? 2 * at2 : at1);
-  return MUON_POLAR_OK;
-}
-
-// Storage modes (gram_launch / poly_launch `upper`) of the step's Gram and
-// polynomial.  A CTA-pair reader (256-row tiles) reads a whole 256 x 256
-// block as stored or transposed, so it needs every 256 x 256 block on or
-// above the diagonal stored; a single-CTA writer then adds the 128 x 128
-// blocks (2q+1, 2q) -- as extra tiles when they fit in the same rounds of
-// tiles, else as the mirrors of (2q, 2q+1).  A single-CTA reader needs the
-// 128 x 128 blocks on and above the diagonal only, and the extra tiles of a
-// single-CTA polynomial read their A blocks (2q+1, 2q) as epilogue input.
-void step_storage(const StepEngines& e, int64_t batch, int* gram_upper, int* poly_upper) {
-  auto single_mode = [&](int units) {
-    const int64_t base = e.sym1 * batch, more = (e.sym1 + e.d / 2) * batch;
-    return (more + units - 1) / units == (base + units - 1) / units ? 2 : 3;
-  };
-  *poly_upper = (e.poly_pairs || !e.apply_pairs) ? 1 : single_mode(e.poly_ctas);
-  const bool a_blocks256 = e.poly_pairs || *poly_upper == 2;
-  *gram_upper = (e.gram_pairs || !a_blocks256) ? 1 : single_mode(e.gram_ctas);
-}
-
-// Chained three-kernel step (EpiParams::chain, step mode 3): whether the
-// scratch allows it, and each kernel's role and counts (CTA bands per
-// matrix of the producing kernel).
-int plan_chain(int64_t batch, int64_t m, int64_t n, void* scratch, size_t scratch_bytes,
-               ChainArgs (&chain)[3], bool* chained) {
-  *chained = false;
-  const int mode = g_step_mode.load(std::memory_order_relaxed);
-  if (mode != 3 || scratch == nullptr || !aligned16(scratch) || scratch_bytes < kCounterBytes ||
-      static_cast<size_t>(3 * batch) * 4 > kCounterBytes - kChainCounterOffset)
-    return MUON_POLAR_OK;
-  StepEngines e;
-  int rc = step_engines(batch, m, n, &e);
-  if (rc != MUON_POLAR_OK) return rc;
-  uint32_t* base = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(scratch) + kChainCounterOffset);
-  const int32_t bt = static_cast<int32_t>(batch);
-  chain[0] = {base, 1, bt, 0u, 0u};
-  chain[1] = {base, 2, bt, e.gram_bands, 0u};
-  chain[2] = {base, 3, bt, e.poly_bands, e.apply_bands};
-  *chained = true;
   return MUON_POLAR_OK;
 }
 
@@ -2689,32 +2392,11 @@ int muon_polar_step_sm100(const void* x, void* y, void* workspace,
   rc = step_fused_impl(x, y, gram, poly, scratch, scratch_bytes, batch, m, n, ldx, ldy, a, b,
                        c, s, &fused);
   if (rc != MUON_POLAR_OK || fused) return rc;
-  ChainArgs chain[3];
-  bool chained = false;
-  rc = plan_chain(batch, m, n, scratch, scratch_bytes, chain, &chained);
+  rc = gram_impl<kGramBf16>(x, gram, batch, m, n, ldx, scratch, scratch_bytes, s);
   if (rc != MUON_POLAR_OK) return rc;
-  // A and P are internal here: upper-only storage (EpiParams::upper_only)
-  // when the Gram and the polynomial each run one round of tiles.  Measured
-  // on B200 (step, warm): 1-2% faster at [8,512,2048], [1,512,2048],
-  // [8,384,1536]; 4-7% slower at [16,1024,4096] and [2,2048,8192], where the
-  // transposed block reads cost more than the halved output stores save.
-  bool upper = g_upper_only.load(std::memory_order_relaxed) != 0;
-  int gram_upper = 0, poly_upper = 0;
-  if (upper) {
-    StepEngines e;
-    rc = step_engines(batch, m, n, &e);
-    if (rc != MUON_POLAR_OK) return rc;
-    upper = e.one_round;
-    if (upper) step_storage(e, batch, &gram_upper, &poly_upper);
-  }
-  rc = gram_impl<kGramBf16>(x, gram, batch, m, n, ldx, scratch, scratch_bytes, s, false,
-                            chained ? &chain[0] : nullptr, gram_upper);
+  rc = poly_impl(gram, poly, batch, mp, b, c, scratch, scratch_bytes, s);
   if (rc != MUON_POLAR_OK) return rc;
-  rc = poly_impl(gram, poly, batch, mp, b, c, scratch, scratch_bytes, s,
-                 chained ? &chain[1] : nullptr, poly_upper);
-  if (rc != MUON_POLAR_OK) return rc;
-  return apply_impl(poly, x, y, batch, m, n, ldx, ldy, a, s, /*x_ready=*/true,
-                    chained ? &chain[2] : nullptr, upper);
+  return apply_impl(poly, x, y, batch, m, n, ldx, ldy, a, s, /*x_ready=*/true);
 }
 
 int muon_polar_gram_t_sm100(const void* x, void* gram, int64_t batch, int64_t m,
@@ -2852,13 +2534,8 @@ int muon_polar_set_kernel_policy(int policy) {
 }
 
 int muon_polar_set_step_mode(int mode) {
-  if (mode < 0 || mode > 3) return MUON_POLAR_ERR_INVALID_ARGUMENT;
+  if (mode < 0 || mode > 2) return MUON_POLAR_ERR_INVALID_ARGUMENT;
   return g_step_mode.exchange(mode);
-}
-
-int muon_polar_set_storage_mode(int mode) {
-  if (mode < 0 || mode > 1) return MUON_POLAR_ERR_INVALID_ARGUMENT;
-  return g_upper_only.exchange(mode == 0 ? 1 : 0) != 0 ? 0 : 1;
 }
 
 int muon_polar_set_split_mode(int mode) {

@@ -328,48 +328,6 @@ def test_kernel_paths_agree_bitwise(api, cuda_device, shape, mode_policy):
 
 
 @pytest.fixture
-def storage_mode(api):
-    """Sets the step's storage of A and P for one test, restores upper-only."""
-    def set_mode(mode):
-        api.set_storage_mode(mode)
-    yield set_mode
-    api.set_storage_mode(0)
-
-
-@pytest.mark.parametrize("mode", ["single", "pair"])
-@pytest.mark.parametrize("shape", [(8, 512, 2048), (2, 150, 2064), (1, 1024, 1024),
-                                   (3, 640, 1000), (2, 768, 512), (4, 256, 4096),
-                                   (4, 1024, 4096), (1, 512, 2048)])
-def test_upper_only_storage_matches_full(api, cuda_device, shape, mode, mode_policy,
-                                         storage_mode, step_mode):
-    """The step with upper-only A and P (no mirror tiles; blocks below the
-    diagonal read as transposes) agrees with full symmetric storage: the same
-    products in the same K order, read through transposed-operand MMAs, so
-    nearly every bit is equal and the rest within the apply stage's bound,
-    and both meet the oracle."""
-    mode_policy(mode)
-    step_mode(2)
-    bsz, m, n = shape
-    x = make_input(shape, seed=14).to(cuda_device)
-    ws = torch.empty(api.workspace_bytes(bsz, m), dtype=torch.uint8, device=cuda_device)
-    scratch = api.new_scratch(bsz, m, n)
-    ys = {}
-    for smode in (1, 0):
-        storage_mode(smode)
-        y = torch.full_like(x, float("nan"))
-        api.step(x, y, ws, A1, B1, C1, scratch=scratch)
-        torch.cuda.synchronize()
-        _check_watchdog(api)
-        ys[smode] = y.cpu()
-    same = (ys[0].view(torch.int16) == ys[1].view(torch.int16)).double().mean()
-    assert float(same) >= 0.95, float(same)
-    e = error_stats(ys[0], ys[1])
-    assert e["rel_fro"] <= 2e-3, e
-    e0 = error_stats(ys[0], reference_formula(make_input(shape, seed=14).float(), COEFFICIENTS[:1]))
-    assert e0["rel_fro"] <= 1e-2, e0
-
-
-@pytest.fixture
 def step_mode(api):
     """Sets the step mode for one test and restores the default after."""
     def set_mode(mode):
@@ -381,7 +339,7 @@ def step_mode(api):
 @pytest.mark.parametrize("shape", [(8, 512, 2048), (2, 150, 2064), (1, 128, 256),
                                    (3, 640, 1000), (1, 1024, 1024), (16, 256, 1024),
                                    (32, 256, 512), (16, 512, 2048)])
-def test_fused_step_matches_three_kernels(api, cuda_device, shape, step_mode, storage_mode):
+def test_fused_step_matches_three_kernels(api, cuda_device, shape, step_mode):
     """One fused persistent launch gives the bits of the three kernels, and
     repeated launches reuse the scratch counters correctly (they are reset by
     the last CTA of each launch).  The three kernels run without scratch, so
@@ -394,9 +352,6 @@ def test_fused_step_matches_three_kernels(api, cuda_device, shape, step_mode, st
     ws = torch.empty(api.workspace_bytes(bsz, m), dtype=torch.uint8, device=cuda_device)
     scratch = api.new_scratch(bsz, m, n)
     outs = {}
-    # the three kernels with full symmetric A and P, as the fused launch
-    # reads them (no transposed operand loads)
-    storage_mode(1)
     for mode in (2, 1):
         step_mode(mode)
         ys = []
@@ -437,38 +392,6 @@ def test_step_by_size_choice(api, cuda_device, shape, fused, step_mode):
     _counters_zero(scratch)
     assert launches == (1 if fused else 3)
     assert torch.equal(y0.view(torch.int16), y1.view(torch.int16))
-
-
-@pytest.mark.parametrize("shape", [(8, 512, 2048), (1, 128, 256), (3, 640, 1000),
-                                   (2, 150, 2064), (40, 256, 512), (2, 1024, 1024)])
-def test_chained_step_matches_grid_waits(api, cuda_device, shape, step_mode):
-    """The three kernels handing over per matrix (step mode 3 with scratch)
-    give the bits of the three kernels each waiting for the whole previous
-    grid (mode 2), over repeated steps that reuse the counters (the last
-    apply band of each matrix zeroes them)."""
-    bsz, m, n = shape
-    x = make_input(shape, seed=13).to(cuda_device)
-    ws = torch.empty(api.workspace_bytes(bsz, m), dtype=torch.uint8, device=cuda_device)
-    scratch = api.new_scratch(bsz, m, n)
-    prev = api.set_split_mode(2)  # the same (unsplit) K order in both modes
-    try:
-        outs = {}
-        for mode in (3, 2):
-            step_mode(mode)
-            ys = []
-            for _ in range(3):
-                y = torch.full_like(x, float("nan"))
-                api.step(x, y, ws, A1, B1, C1, scratch=scratch)
-                ys.append(y)
-            torch.cuda.synchronize()
-            _check_watchdog(api)
-            _counters_zero(scratch)
-            for y in ys[1:]:
-                assert torch.equal(y.view(torch.int16), ys[0].view(torch.int16))
-            outs[mode] = ys[0]
-        assert torch.equal(outs[2].view(torch.int16), outs[3].view(torch.int16))
-    finally:
-        api.set_split_mode(prev)
 
 
 def test_torch_compile_matches_eager(op, cuda_device):
