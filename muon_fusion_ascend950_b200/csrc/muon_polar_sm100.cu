@@ -343,7 +343,11 @@ constexpr int kPairEpiThreads = 256;
 constexpr int kTileThreads = 352;
 constexpr int kProducerWarp2 = 10;
 
-template <int KIND, int PAIR>
+// SPLIT: the launch has split-K items (symmetric kinds only).  Compiling the
+// split-K paths out of the other launches cuts the kernel's registers (the
+// single-CTA Gram from 145 to 77, the pair apply from 158 to 101); measured
+// on B200 the config-1 step 38.9 -> 37.5 us.
+template <int KIND, int PAIR, bool SPLIT>
 __global__ void __launch_bounds__(kTileThreads, 1)
     polar_tile_kernel(const __grid_constant__ CUtensorMap tmap_a,
                       const __grid_constant__ CUtensorMap tmap_b,
@@ -679,7 +683,7 @@ __global__ void __launch_bounds__(kTileThreads, 1)
           ++o;
         }
       };
-      if (tc.nsplit > 1) {
+      if (SPLIT && tc.nsplit > 1) {
         // Split-K.  A launch with splits has one work item per cluster, so
         // once the accumulator is complete the pipeline stages are free and
         // serve as staging for partial sums.  The split that arrives last
@@ -763,7 +767,7 @@ __global__ void __launch_bounds__(kTileThreads, 1)
           if (!mbar_wait_bounded(&aux_full[c], t & 1u))
             atomicOr(&g_watchdog, MUON_POLAR_WATCHDOG_EPILOGUE);
         }
-        if (reduce) {
+        if (SPLIT && reduce) {
           // v <- sum over splits i = 0..nsplit-1, in that order, of the
           // split's partial (this split's own from tensor memory).
           if (!mbar_wait_bounded(&part_full[c & 1], (c >> 1) & 1))
@@ -806,7 +810,7 @@ __global__ void __launch_bounds__(kTileThreads, 1)
         named_barrier(1, kPairEpiThreads);
         if (leader) {
           // every thread is done with partial buffer c % 2: refill it
-          if (reduce && c + 2 < Cfg::kChunks) load_parts(c + 2);
+          if (SPLIT && reduce && c + 2 < Cfg::kChunks) load_parts(c + 2);
           const uint8_t* so = sOut + ro * Cfg::kOutChunkBytes;
           const uint8_t* sm = sMir + rm * Cfg::kMirChunkBytes;
 #pragma unroll
@@ -1680,11 +1684,16 @@ int tile_capacity(DeviceState* st, int* capacity) {
     *capacity = st->capacity[inst];
     return MUON_POLAR_OK;
   }
-  auto kern = polar_tile_kernel<KIND, PAIR>;
+  auto kern = polar_tile_kernel<KIND, PAIR, false>;
   const uint32_t smem = PairCfg<KIND, PAIR>::kSmemBytes;
   if (!st->smem_attr_set[inst]) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return static_cast<int>(e);
+    if constexpr (PairCfg<KIND, PAIR>::kSym) {
+      e = cudaFuncSetAttribute(polar_tile_kernel<KIND, PAIR, true>,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+      if (e != cudaSuccess) return static_cast<int>(e);
+    }
     st->smem_attr_set[inst] = true;
   }
   int units = 0;
@@ -1741,8 +1750,18 @@ int launch_tile(DeviceState* st, const TileMaps& maps, const EpiParams& p,
   attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = PAIR == 2 ? 2 : 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, polar_tile_kernel<KIND, PAIR>, maps.a, maps.b,
-                                     maps.aux, maps.out, maps.mir, p);
+  cudaError_t e;
+  if constexpr (PairCfg<KIND, PAIR>::kSym) {
+    if (p.splits > 1)
+      e = cudaLaunchKernelEx(&cfg, polar_tile_kernel<KIND, PAIR, true>, maps.a, maps.b, maps.aux,
+                             maps.out, maps.mir, p);
+    else
+      e = cudaLaunchKernelEx(&cfg, polar_tile_kernel<KIND, PAIR, false>, maps.a, maps.b,
+                             maps.aux, maps.out, maps.mir, p);
+  } else {
+    e = cudaLaunchKernelEx(&cfg, polar_tile_kernel<KIND, PAIR, false>, maps.a, maps.b, maps.aux,
+                           maps.out, maps.mir, p);
+  }
   if (e != cudaSuccess) return static_cast<int>(e);
   g_launch_count.fetch_add(1, std::memory_order_relaxed);
   return MUON_POLAR_OK;
