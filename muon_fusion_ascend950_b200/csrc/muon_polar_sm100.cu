@@ -57,9 +57,6 @@ __host__ __device__ constexpr int epi_kind(int kind) {
 // Operand layouts in global memory: K-major unless stated.
 __host__ __device__ constexpr bool a_mn_major(int kind) { return kind == kGramT; }
 __host__ __device__ constexpr bool b_mn_major(int kind) { return kind == kApply || kind == kGramT; }
-// Which operand is X in the apply kinds (1 = A, 2 = B), 0 otherwise: X can
-// be loaded before the grid dependency wait when the launch says so.
-__host__ __device__ constexpr int x_operand(int kind) { return kind == kApplyT ? 1 : (kind == kApply ? 2 : 0); }
 
 __device__ uint32_t g_watchdog = 0;
 
@@ -72,12 +69,6 @@ struct EpiParams {
   float coef_b;
   float coef_c;
   float alpha;  // kApply: a already rounded to bf16
-  // kApply: X (both its operand and its epilogue input) does not depend on
-  // the previous kernel in the stream, so it is loaded before the grid
-  // dependency wait.  True inside a Polar Express step: the apply follows the
-  // polynomial kernel, which writes only P, and runs only after the Gram
-  // kernel -- whose own dependency wait covers X -- has completed.
-  int32_t x_ready;
   // kPoly only: compute whole rows of tile blocks [row_tile_begin,
   // row_tile_begin + tiles_m) -- both triangles, no mirror -- instead of the
   // upper triangle (a row slab of P for a multi-GPU caller).
@@ -361,7 +352,6 @@ __global__ void __launch_bounds__(kTileThreads, 1)
   constexpr int S = Cfg::kStages;
   constexpr bool kAmn = a_mn_major(KIND);
   constexpr bool kBmn = b_mn_major(KIND);
-  constexpr int kX = x_operand(KIND);
   constexpr bool kSym = Cfg::kSym;
 
   extern __shared__ uint8_t smem_raw[];
@@ -468,28 +458,6 @@ __global__ void __launch_bounds__(kTileThreads, 1)
             tma_load_3d(dst, &tmap_b, &full[s], c0, c1, w.b);
         }
       };
-      // The first pipeline iterations' X operand before the dependency wait,
-      // when X does not depend on the previous kernel.  Their stages are
-      // fresh, so no empty-wait is needed.
-      uint32_t n_pre = 0;
-      if constexpr (kX != 0) {
-        if (p.x_ready) {
-          uint32_t it = 0;
-          for (int item = cluster; item < p.total_items && it < static_cast<uint32_t>(S);
-               item += nclusters) {
-            const WorkItem w = decode_item(p, item, kSym);
-            for (int kb = w.kb_begin; kb < w.kb_end && it < static_cast<uint32_t>(S); ++kb, ++it) {
-              if (it % Cfg::kProducers != pid) continue;
-              if (rank == 0) mbar_arrive_expect_tx(&full[it], PAIR * Cfg::kStageBytes);
-              if constexpr (kX == 1)
-                load_a(it, w, kb);
-              else
-                load_b(it, w, kb);
-            }
-          }
-          n_pre = it;
-        }
-      }
       grid_dependency_wait();
       grid_launch_dependents();
       uint32_t it = 0;
@@ -503,18 +471,14 @@ __global__ void __launch_bounds__(kTileThreads, 1)
           if (it % Cfg::kProducers != pid) continue;
           const uint32_t s = it % S;
           const uint32_t ph = (it / S) & 1u;
-          const bool pre = it < n_pre;  // X operand already in flight
-          if (!pre) {
-            if (!mbar_wait_bounded(&empty[s], ph ^ 1u)) {
-              ok = false;
-              break;
-            }
-            if (rank == 0)
-              mbar_arrive_expect_tx(&full[s],
-                                    PAIR * (diag ? Cfg::kAHalfBytes : Cfg::kStageBytes));
+          if (!mbar_wait_bounded(&empty[s], ph ^ 1u)) {
+            ok = false;
+            break;
           }
-          if (!(pre && kX == 1)) load_a(s, w, kb);
-          if (!diag && !(pre && kX == 2)) load_b(s, w, kb);
+          if (rank == 0)
+            mbar_arrive_expect_tx(&full[s], PAIR * (diag ? Cfg::kAHalfBytes : Cfg::kStageBytes));
+          load_a(s, w, kb);
+          if (!diag) load_b(s, w, kb);
         }
       }
       if (!ok) atomicOr(&g_watchdog, MUON_POLAR_WATCHDOG_PRODUCER);
@@ -634,17 +598,14 @@ __global__ void __launch_bounds__(kTileThreads, 1)
           mbar_arrive_cluster(acc ? tempty_leader1 : tempty_leader0);
       }
     };
-    // The apply's input tile is X: before the dependency wait when X does not
-    // depend on the previous kernel.
-    const bool aux_early = kX != 0 && p.x_ready;
-    if constexpr (Cfg::kAux) {
-      if (leader && aux_early && cluster < p.total_items)
-        for (int c = 0; c < Cfg::kChunks; ++c) load_aux_chunk(cluster, c);
-    }
+    // Everything, X included, is loaded after the grid dependency wait:
+    // measured on B200, loading the apply's X (operand stages and epilogue
+    // tile) before it delayed the P loads queued behind it and made the
+    // config-1 step 0.6 us slower.
     grid_dependency_wait();
     grid_launch_dependents();
     if constexpr (Cfg::kAux) {
-      if (leader && !aux_early && cluster < p.total_items)
+      if (leader && cluster < p.total_items)
         for (int c = 0; c < Cfg::kChunks; ++c) load_aux_chunk(cluster, c);
     }
     uint32_t t = 0;
@@ -1988,7 +1949,7 @@ float round_to_bf16(float v) {
 
 template <int PAIR>
 int apply_launch(DeviceState* st, const void* poly, const void* x, void* y, int64_t batch,
-                 int64_t m, int64_t n, int64_t ldx, int64_t ldy, float a, bool x_ready,
+                 int64_t m, int64_t n, int64_t ldx, int64_t ldy, float a,
                  cudaStream_t stream) {
   using Cfg = PairCfg<kApply, PAIR>;
   const int64_t mp = padded_rows(m);
@@ -2019,16 +1980,13 @@ int apply_launch(DeviceState* st, const void* poly, const void* x, void* y, int6
   // P's columns >= m are zero and X's rows >= m read as zero: stop at m.
   p.k_blocks = static_cast<int32_t>(k_blocks_of<kApply, PAIR>(m));
   p.alpha = round_to_bf16(a);
-  p.x_ready = x_ready ? 1 : 0;
   plan_no_splits(p);
   return launch_tile<kApply, PAIR>(st, tm, p, stream);
 }
 
-// `x_ready`: X does not depend on the previous kernel in the stream (see
-// EpiParams::x_ready); only muon_polar_step_sm100 knows that.
 int apply_impl(const void* poly, const void* x, void* y, int64_t batch,
                int64_t m, int64_t n, int64_t ldx, int64_t ldy, float a,
-               cudaStream_t stream, bool x_ready = false) {
+               cudaStream_t stream) {
   int rc = check_x_args(x, batch, m, n, ldx);
   if (rc != MUON_POLAR_OK) return rc;
   if (poly == nullptr || y == nullptr || ldy < n)
@@ -2047,8 +2005,8 @@ int apply_impl(const void* poly, const void* x, void* y, int64_t batch,
                 cost_blocks<2>(m),
                 (m + kHalf - 1) / kHalf * ((n + kHalf - 1) / kHalf) * batch, ctas,
                 cost_blocks<1>(m)))
-    return apply_launch<2>(st, poly, x, y, batch, m, n, ldx, ldy, a, x_ready, stream);
-  return apply_launch<1>(st, poly, x, y, batch, m, n, ldx, ldy, a, x_ready, stream);
+    return apply_launch<2>(st, poly, x, y, batch, m, n, ldx, ldy, a, stream);
+  return apply_launch<1>(st, poly, x, y, batch, m, n, ldx, ldy, a, stream);
 }
 
 // Kernel (3) of the step of X^T returned in X's layout (M > N without
@@ -2057,7 +2015,7 @@ int apply_impl(const void* poly, const void* x, void* y, int64_t batch,
 // as the K-major B operand of X.P.
 template <int PAIR>
 int apply_t_launch(DeviceState* st, const void* poly, const void* x, void* y, int64_t batch,
-                   int64_t m, int64_t n, int64_t ldx, int64_t ldy, float a, bool x_ready,
+                   int64_t m, int64_t n, int64_t ldx, int64_t ldy, float a,
                    cudaStream_t stream) {
   using Cfg = PairCfg<kApplyT, PAIR>;
   const int64_t np = padded_rows(n);
@@ -2084,14 +2042,12 @@ int apply_t_launch(DeviceState* st, const void* poly, const void* x, void* y, in
   // X's columns >= n read as zero and P's rows/columns >= n are zero.
   p.k_blocks = static_cast<int32_t>(k_blocks_of<kApplyT, PAIR>(n));
   p.alpha = round_to_bf16(a);
-  p.x_ready = x_ready ? 1 : 0;
   plan_no_splits(p);
   return launch_tile<kApplyT, PAIR>(st, tm, p, stream);
 }
 
 int apply_t_impl(const void* poly, const void* x, void* y, int64_t batch, int64_t m,
-                 int64_t n, int64_t ldx, int64_t ldy, float a, cudaStream_t stream,
-                 bool x_ready = false) {
+                 int64_t n, int64_t ldx, int64_t ldy, float a, cudaStream_t stream) {
   int rc = check_x_args(x, batch, m, n, ldx);
   if (rc != MUON_POLAR_OK) return rc;
   if (poly == nullptr || y == nullptr || ldy < n || n > (1 << 24))
@@ -2110,8 +2066,8 @@ int apply_t_impl(const void* poly, const void* x, void* y, int64_t batch, int64_
                 cost_blocks<2>(n),
                 (m + kHalf - 1) / kHalf * ((n + kHalf - 1) / kHalf) * batch, ctas,
                 cost_blocks<1>(n)))
-    return apply_t_launch<2>(st, poly, x, y, batch, m, n, ldx, ldy, a, x_ready, stream);
-  return apply_t_launch<1>(st, poly, x, y, batch, m, n, ldx, ldy, a, x_ready, stream);
+    return apply_t_launch<2>(st, poly, x, y, batch, m, n, ldx, ldy, a, stream);
+  return apply_t_launch<1>(st, poly, x, y, batch, m, n, ldx, ldy, a, stream);
 }
 
 // ---------------------------------------------------------------- fused step
@@ -2415,7 +2371,7 @@ int muon_polar_step_sm100(const void* x, void* y, void* workspace,
   if (rc != MUON_POLAR_OK) return rc;
   rc = poly_impl(gram, poly, batch, mp, b, c, scratch, scratch_bytes, s);
   if (rc != MUON_POLAR_OK) return rc;
-  return apply_impl(poly, x, y, batch, m, n, ldx, ldy, a, s, /*x_ready=*/true);
+  return apply_impl(poly, x, y, batch, m, n, ldx, ldy, a, s);
 }
 
 int muon_polar_gram_t_sm100(const void* x, void* gram, int64_t batch, int64_t m,
@@ -2450,7 +2406,7 @@ int muon_polar_step_t_sm100(const void* x, void* y, void* workspace, size_t work
   if (rc != MUON_POLAR_OK) return rc;
   rc = poly_impl(gram, poly, batch, np, b, c, scratch, scratch_bytes, s);
   if (rc != MUON_POLAR_OK) return rc;
-  return apply_t_impl(poly, x, y, batch, m, n, ldx, ldy, a, s, /*x_ready=*/true);
+  return apply_t_impl(poly, x, y, batch, m, n, ldx, ldy, a, s);
 }
 
 size_t muon_polar_scratch_bytes(int64_t batch, int64_t m, int64_t n) {
