@@ -220,6 +220,27 @@ int muon_polar_step_t_sm100(const void* x, void* y, void* workspace, size_t work
                             int64_t n, int64_t ldx, int64_t ldy, float a, float b, float c,
                             void* stream);
 
+/* `steps` Polar Express steps (the reference's caller loop,
+ * examples/five_steps.py:18-21, over polar_step) with coefficient rows
+ * coefficients[3*i .. 3*i+2] = (a, b, c) (a host array).  Step 0 reads x
+ * (row stride ldx); step i > 0 reads the previous step's output, kept in
+ * buf0 / buf1 ([batch][m][ldb] bf16, ldb % 8 == 0; step i writes
+ * buf[i % 2], the last step y).  buf0 may not be x, and y may not be the
+ * last step's input (buf[(steps - 2) % 2]); buf0/buf1 may be NULL when
+ * steps == 1.  workspace: muon_polar_workspace_bytes(batch, min(m, n)).
+ * With m <= n and the step mode (muon_polar_set_step_mode) choosing the
+ * fused kernel, up to 8 steps run as ONE persistent launch (per-matrix
+ * dependencies across steps in the scratch counter area: the next step's
+ * Gram of a matrix starts once the previous step's apply of that matrix is
+ * complete); otherwise each step runs as muon_polar_step_sm100 (or its _t
+ * form for m > n).  The result has the same bits either way when kernels
+ * (1) and (2) do not split K. */
+int muon_polar_steps_sm100(const void* x, void* y, void* buf0, void* buf1, int64_t ldb,
+                           void* workspace, size_t workspace_bytes, void* scratch,
+                           size_t scratch_bytes, int64_t batch, int64_t m, int64_t n,
+                           int64_t ldx, int64_t ldy, const float* coefficients, int steps,
+                           void* stream);
+
 /* ------------------------------------------------------------------------
  * The caller side of the step, on the device (no counterpart in the
  * reference, which leaves the loop, the normalisation and the optimizer
@@ -295,7 +316,8 @@ int muon_polar_set_kernel_policy(int policy);
  *      dependencies tracked in the scratch counter area (needs scratch);
  *   2  always three kernels.
  * Initial value from MUON_POLAR_FUSED (1 -> 1, 0 -> 2).  Results are the
- * same in every mode (identical bits). */
+ * same in every mode; the bits are identical when kernels (1) and (2) do not
+ * split K (the fused launch never does; see muon_polar_set_split_mode). */
 int muon_polar_set_step_mode(int mode);
 
 /* Split-K of kernels (1) and (2) when scratch is given, process-wide;

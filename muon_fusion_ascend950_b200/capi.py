@@ -50,6 +50,10 @@ SIGNATURES = {
                                                ctypes.c_size_t, _I64, _I64, _I64, _I64, _I64,
                                                ctypes.c_float, ctypes.c_float, ctypes.c_float,
                                                _VP]),
+    "muon_polar_steps_sm100": (ctypes.c_int, [_VP, _VP, _VP, _VP, _I64, _VP, ctypes.c_size_t,
+                                              _VP, ctypes.c_size_t, _I64, _I64, _I64, _I64,
+                                              _I64, ctypes.POINTER(ctypes.c_float),
+                                              ctypes.c_int, _VP]),
     "muon_polar_express_workspace_bytes": (ctypes.c_size_t, [_I64, _I64, _I64]),
     "muon_polar_express_sm100": (ctypes.c_int, [_VP, ctypes.c_int, _I64, _VP, _I64, _VP,
                                                 ctypes.c_size_t, _VP, ctypes.c_size_t, _I64,
@@ -301,6 +305,22 @@ class CAPI:
         if t.dtype == torch.bfloat16:
             return 1
         raise TypeError(f"unsupported dtype {t.dtype}")
+
+    def steps(self, x, y, buf0, buf1, workspace, coefficients, n: Optional[int] = None,
+              scratch=None, stream=None) -> None:
+        """len(coefficients) Polar Express steps of bf16 x ([B, M, ld]) into y,
+        the intermediate iterates in buf0 / buf1 ([B, M, ldb]; None for one
+        step)."""
+        bsz, m, ldx = x.shape
+        n = ldx if n is None else n
+        coeffs, steps = self._coefficients(coefficients)
+        sp, sb = _scratch(scratch)
+        b0 = 0 if buf0 is None else buf0.data_ptr()
+        b1 = 0 if buf1 is None else buf1.data_ptr()
+        ldb = 0 if buf0 is None else buf0.shape[-1]
+        self._check("muon_polar_steps_sm100", self.lib.muon_polar_steps_sm100(
+            x.data_ptr(), y.data_ptr(), b0, b1, ldb, workspace.data_ptr(), _nbytes(workspace),
+            sp, sb, bsz, m, n, ldx, y.shape[-1], coeffs, steps, self._stream(stream)))
 
     def express_workspace_bytes(self, batch: int, m: int, n: int) -> int:
         return int(self.lib.muon_polar_express_workspace_bytes(int(batch), int(m), int(n)))

@@ -860,6 +860,15 @@ __global__ void __launch_bounds__(kTileThreads, 1)
 // item waits for it.
 enum FusedKind : int { kFGram = 0, kFPoly = 1, kFApply = 2 };
 
+// Several Polar Express steps in one launch (muon_polar_express_sm100): the
+// items of step s+1 follow those of step s, and a Gram region of matrix b in
+// step s+1 waits for every apply tile of b in step s (its input).  X of step
+// s is the launch input for s = 0, else one of two ping-pong buffers; Y of
+// the last step is the launch output.  A, P and the buffers are per matrix,
+// and every write to one of them waits (through the chain of per-matrix
+// dependencies) until the previous step's readers of that matrix are done.
+constexpr int kMaxFusedSteps = 8;
+
 struct FusedParams {
   int32_t batch;
   int32_t d2;           // Mp / 256: row blocks of a region
@@ -871,30 +880,45 @@ struct FusedParams {
   int32_t kb_gram;      // K-blocks of each kind (128 deep for Gram / poly,
   int32_t kb_poly;      // 64 for the apply)
   int32_t kb_apply;
-  float coef_b;
-  float coef_c;
-  float alpha;          // a rounded to bf16
-  uint32_t* counters;   // [0, batch): Gram done; [batch, 2 batch): poly done; [2 batch]: exits
+  int32_t steps;        // Polar Express steps of this launch
+  int32_t per_step;     // items of one step
+  uint32_t apply_bands; // apply CTA bands per matrix (two per tile)
+  float coef[kMaxFusedSteps][3];  // per step: b, c, a rounded to bf16
+  // per matrix, counted over all steps: [0, batch) Gram, [batch, 2 batch)
+  // poly, [2 batch, 3 batch) apply CTA parts done; [3 batch]: exits.  A
+  // step's items of a matrix start only after the previous step's apply of
+  // it is complete, so after step s the Gram and poly counts of the matrix
+  // are exactly 2 regions (s + 1) and the apply count apply_bands (s + 1).
+  uint32_t* counters;
   const uint16_t* gram; // A, [batch][mp][mp] bf16 (the polynomial's epilogue input)
   int32_t mp;
 };
 
+// X of a step (index 0: the launch input; 1, 2: ping-pong buffers) and Y
+// (index 0: the launch output; 1, 2: the same buffers).
 struct FusedMaps {
-  CUtensorMap x_k;   // X, box {64, 128}: Gram A operand, apply epilogue tile
-  CUtensorMap x_mn;  // X, box {64, 64}: Gram B operand (K-major), apply B operand (MN-major)
-  CUtensorMap a128;  // A, box {64, 128}: Gram output, poly A operand and tile
-  CUtensorMap a64;   // A, box {64, 64}: Gram mirror, poly B operand
-  CUtensorMap p128;  // P, box {64, 128}: poly output, apply A operand
-  CUtensorMap p64;   // P, box {64, 64}: poly mirror
-  CUtensorMap y128;  // Y, box {64, 128}: apply output
+  CUtensorMap x_k[3];   // X, box {64, 128}: Gram A operand, apply epilogue tile
+  CUtensorMap x_mn[3];  // X, box {64, 64}: Gram B operand (K-major), apply B operand (MN-major)
+  CUtensorMap a128;     // A, box {64, 128}: Gram output, poly A operand and tile
+  CUtensorMap a64;      // A, box {64, 64}: Gram mirror, poly B operand
+  CUtensorMap p128;     // P, box {64, 128}: poly output, apply A operand
+  CUtensorMap p64;      // P, box {64, 64}: poly mirror
+  CUtensorMap y128[3];  // Y, box {64, 128}: apply output
 };
+
+__device__ __forceinline__ int fused_src(int step) { return step == 0 ? 0 : 1 + ((step - 1) & 1); }
+__device__ __forceinline__ int fused_dst(int step, int steps) {
+  return step == steps - 1 ? 0 : 1 + (step & 1);
+}
 
 struct FusedItem {
-  int kind, b, tm, tn, k_blocks;
+  int kind, b, tm, tn, k_blocks, step;
 };
 
-__device__ __forceinline__ FusedItem fused_item(int w, const FusedParams& p) {
+__device__ __forceinline__ FusedItem fused_item(int w_all, const FusedParams& p) {
   FusedItem it;
+  it.step = w_all / p.per_step;
+  const int w = w_all - it.step * p.per_step;
   int r;
   if (w < p.n_gram + p.n_poly) {
     it.kind = w < p.n_gram ? kFGram : kFPoly;
@@ -923,13 +947,32 @@ __device__ __forceinline__ FusedItem fused_item(int w, const FusedParams& p) {
   return it;
 }
 
+// Count of a matrix's Gram or poly CTA parts once `step` is complete.
+__device__ __forceinline__ uint32_t fused_sym_done(const FusedParams& p, int step) {
+  return 2u * static_cast<uint32_t>(p.regions) * static_cast<uint32_t>(step + 1);
+}
+
+// Waits (bounded) until X of the item's step -- the previous step's output
+// for steps after the first -- is complete.
+__device__ __forceinline__ bool fused_wait_x(const FusedItem& it, const FusedParams& p) {
+  bool ok = true;
+  if (it.step > 0) {
+    ok = wait_counter_bounded(p.counters + 2 * p.batch + it.b,
+                              p.apply_bands * static_cast<uint32_t>(it.step));
+    fence_proxy_async_global();
+  }
+  return ok;
+}
+
 // Waits (bounded) until the item's inputs from this launch are complete.
 __device__ __forceinline__ bool fused_wait_inputs(const FusedItem& it, const FusedParams& p) {
   bool ok = true;
+  if (it.kind == kFGram)
+    return fused_wait_x(it, p);
   if (it.kind == kFPoly)
-    ok = wait_counter_bounded(p.counters + it.b, 2u * p.regions);
-  else if (it.kind == kFApply)
-    ok = wait_counter_bounded(p.counters + p.batch + it.b, 2u * p.regions);
+    ok = wait_counter_bounded(p.counters + it.b, fused_sym_done(p, it.step));
+  else
+    ok = wait_counter_bounded(p.counters + p.batch + it.b, fused_sym_done(p, it.step));
   fence_proxy_async_global();
   return ok;
 }
@@ -1013,6 +1056,9 @@ __global__ void __launch_bounds__(kTileThreads, 1)
   uint64_t* drain = tempty + 2;
   uint64_t* aux_full = drain + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(aux_full + 1);
+  // Items of this cluster whose epilogue is finished with the apply tile
+  // area (the epilogue leader writes it, the producers poll it).
+  uint32_t* epi_done = tmem_slot + 1;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -1032,14 +1078,17 @@ __global__ void __launch_bounds__(kTileThreads, 1)
     }
     mbar_init(drain, 1);
     mbar_init(aux_full, 1);
+    *epi_done = 0u;
     fence_mbar_init();
-    prefetch_tensor_map(&maps.x_k);
-    prefetch_tensor_map(&maps.x_mn);
+    for (int i = 0; i < 3; ++i) {
+      prefetch_tensor_map(&maps.x_k[i]);
+      prefetch_tensor_map(&maps.x_mn[i]);
+      prefetch_tensor_map(&maps.y128[i]);
+    }
     prefetch_tensor_map(&maps.a128);
     prefetch_tensor_map(&maps.a64);
     prefetch_tensor_map(&maps.p128);
     prefetch_tensor_map(&maps.p64);
-    prefetch_tensor_map(&maps.y128);
   }
   if (warp == 1) {
     tmem_alloc_pair(tmem_slot, Cfg::kTmemCols);
@@ -1062,6 +1111,9 @@ __global__ void __launch_bounds__(kTileThreads, 1)
       FusedRing ring = {0, 0, 0, 0u};
       uint32_t t = 0;
       int started = 0;  // items whose loads this producer has begun
+      // Sym stages 2 and 3 overlap the apply tile area: after an apply item
+      // they are loaded only once the epilogue is done with items < aux_wait.
+      uint32_t aux_wait = 0;
       bool ok = true;
       for (int w = cluster; ok && w < p.total; w += nclusters, ++t) {
         const FusedItem item = fused_item(w, p);
@@ -1073,6 +1125,7 @@ __global__ void __launch_bounds__(kTileThreads, 1)
             ok = false;
             break;
           }
+          if (!ap && ring.layout == 2) aux_wait = t;
           ring.layout = layout;
           ring.stages = ap ? Cfg::kApStages : Cfg::kSymStages;
           ring.pos = 0;
@@ -1083,9 +1136,16 @@ __global__ void __launch_bounds__(kTileThreads, 1)
         const int a_row = item.tm * kPairM + static_cast<int>(rank) * kHalf;
         // Apply: X (B operand) of the first stages before the dependency
         // wait; Gram: no dependency; polynomial: A only after it.
+        const int src = fused_src(item.step);
         FusedRing pre = ring;
         int n_pre = 0;
         if (ap) {
+          // X of a later step is the previous step's output
+          if (!fused_wait_x(item, p)) {
+            atomicOr(&g_watchdog, MUON_POLAR_WATCHDOG_DEPENDENCY);
+            ok = false;
+            break;
+          }
           for (int kb = 0; kb < item.k_blocks && kb < ring.stages; ++kb, ++n_pre) {
             const int s = pre.pos;
             pre.pos = pre.pos + 1 == pre.stages ? 0 : pre.pos + 1;
@@ -1100,7 +1160,7 @@ __global__ void __launch_bounds__(kTileThreads, 1)
             uint8_t* sb = sRing + s * stage_bytes + a_bytes;
 #pragma unroll
             for (int j = 0; j < kHalf / kAtom; ++j)
-              tma_load_3d_pair(sb + j * (kAtom * 128), &maps.x_mn, bar,
+              tma_load_3d_pair(sb + j * (kAtom * 128), &maps.x_mn[src], bar,
                                item.tn * kPairN + static_cast<int>(rank) * kHalf + j * kAtom,
                                kb * kAtom, item.b);
           }
@@ -1128,19 +1188,26 @@ __global__ void __launch_bounds__(kTileThreads, 1)
               if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * stage_bytes);
 #pragma unroll
               for (int j = 0; j < kHalf / kAtom; ++j)
-                tma_load_3d_pair(sa + a_bytes + j * (kAtom * 128), &maps.x_mn, bar,
+                tma_load_3d_pair(sa + a_bytes + j * (kAtom * 128), &maps.x_mn[src], bar,
                                  item.tn * kPairN + static_cast<int>(rank) * kHalf + j * kAtom,
                                  kb * kAtom, item.b);
             }
             tma_load_3d_pair(sa, &maps.p128, bar, kb * kAtom, a_row, item.b);
           } else {
+            if (aux_wait > 0 && s >= 2) {
+              if (!wait_shared_bounded(smem_addr(epi_done), aux_wait)) {
+                ok = false;
+                break;
+              }
+              aux_wait = 0;
+            }
             if (!mbar_wait_bounded(&empty[s], par ^ 1u)) {
               ok = false;
               break;
             }
             if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * stage_bytes);
-            const CUtensorMap* ma = item.kind == kFGram ? &maps.x_k : &maps.a128;
-            const CUtensorMap* mb = item.kind == kFGram ? &maps.x_mn : &maps.a64;
+            const CUtensorMap* ma = item.kind == kFGram ? &maps.x_k[src] : &maps.a128;
+            const CUtensorMap* mb = item.kind == kFGram ? &maps.x_mn[src] : &maps.a64;
             const int b_row = item.tn * kHalf + static_cast<int>(rank) * 64;
 #pragma unroll
             for (int j = 0; j < 2; ++j) {
@@ -1237,9 +1304,6 @@ __global__ void __launch_bounds__(kTileThreads, 1)
     const uint32_t tempty_leader0 = map_to_cta(smem_addr(&tempty[0]), 0);
     const uint32_t tempty_leader1 = map_to_cta(smem_addr(&tempty[1]), 0);
     EpiParams ep = {};
-    ep.coef_b = p.coef_b;
-    ep.coef_c = p.coef_c;
-    ep.alpha = p.alpha;
     bool aux_inflight = false;
     // Failures never change the epilogue's control flow: every thread runs
     // the same named barriers for every item, and after a failed wait it only
@@ -1258,10 +1322,14 @@ __global__ void __launch_bounds__(kTileThreads, 1)
     auto load_aux = [&](int w) {
       const FusedItem item = fused_item(w, p);
       if (item.kind != kFApply) return;
+      if (!fused_wait_x(item, p)) {
+        atomicOr(&g_watchdog, MUON_POLAR_WATCHDOG_DEPENDENCY);
+        failed = true;
+      }
       mbar_arrive_expect_tx(aux_full, 4 * Cfg::kRegionBytes);
 #pragma unroll
       for (int c = 0; c < 4; ++c)
-        tma_load_3d(sAux + c * Cfg::kRegionBytes, &maps.x_k, aux_full,
+        tma_load_3d(sAux + c * Cfg::kRegionBytes, &maps.x_k[fused_src(item.step)], aux_full,
                     item.tn * kPairN + c * kChunkCols,
                     item.tm * kPairM + static_cast<int>(rank) * kHalf, item.b);
       aux_inflight = true;
@@ -1285,6 +1353,9 @@ __global__ void __launch_bounds__(kTileThreads, 1)
       const int rel = ap ? 1 : block_rel(item);
       const bool has_aux = ap;
       const uint32_t acc = t & 1u;
+      ep.coef_b = p.coef[item.step][0];
+      ep.coef_c = p.coef[item.step][1];
+      ep.alpha = p.coef[item.step][2];
       const int row0 = item.tm * kPairM + static_cast<int>(rank) * kHalf;
       const int col0 = item.tn * (ap ? kPairN : kHalf);
       // Polynomial: this thread's A values (row `row`, columns hc*32.. of
@@ -1293,7 +1364,8 @@ __global__ void __launch_bounds__(kTileThreads, 1)
       uint4 pa[2][4];
       if (item.kind == kFPoly && rel >= 0 && !failed) {
         int dep = 1;
-        if (lane == 0) dep = wait_counter_bounded(p.counters + item.b, 2u * p.regions) ? 1 : 0;
+        if (lane == 0)
+          dep = wait_counter_bounded(p.counters + item.b, fused_sym_done(p, item.step)) ? 1 : 0;
         dep = __shfl_sync(0xffffffffu, dep, 0);
         if (!dep) {
           if (lane == 0) atomicOr(&g_watchdog, MUON_POLAR_WATCHDOG_DEPENDENCY);
@@ -1327,8 +1399,9 @@ __global__ void __launch_bounds__(kTileThreads, 1)
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * kPairN;
       const bool store = rel >= 0;
       const bool mirror = !ap && rel > 0;
-      const CUtensorMap* m_out = item.kind == kFGram ? &maps.a128
-                                 : item.kind == kFPoly ? &maps.p128 : &maps.y128;
+      const CUtensorMap* m_out = item.kind == kFGram   ? &maps.a128
+                                 : item.kind == kFPoly ? &maps.p128
+                                                       : &maps.y128[fused_dst(item.step, p.steps)];
       const CUtensorMap* m_mir = item.kind == kFGram ? &maps.a64 : &maps.p64;
       const int chunks = !store ? 0 : (ap ? kPairN / kChunkCols : kHalf / kChunkCols);
       if (chunks == 0) release_accumulator(acc);
@@ -1380,16 +1453,20 @@ __global__ void __launch_bounds__(kTileThreads, 1)
         }
       }
       if (leader) {
-        if (!ap) {
-          // Publish this CTA's part of the region once its stores have
-          // landed (also when it stored nothing or gave up: the count is
-          // per CTA and item).
+        if (!ap || item.step + 1 < p.steps) {
+          // Publish this CTA's part of the item once its stores have landed
+          // (also when it stored nothing or gave up: the count is per CTA
+          // and item).  An apply tile is waited for only by the next step.
           bulk_wait_group0();
           fence_proxy_async_global();
-          red_release_gpu_add(p.counters + (item.kind == kFGram ? 0 : p.batch) + item.b, 1u);
+          const int slot = item.kind == kFGram ? 0 : (item.kind == kFPoly ? 1 : 2);
+          red_release_gpu_add(p.counters + slot * p.batch + item.b, 1u);
         } else {
           bulk_wait_group_read<0>();
         }
+        // every epilogue thread has read the apply tile (named barrier before
+        // the last store) and the stores have read it
+        st_release_cta_shared(smem_addr(epi_done), t + 1);
         const int next = w + nclusters;
         if (next < p.total && !failed) load_aux(next);
       }
@@ -1414,9 +1491,10 @@ __global__ void __launch_bounds__(kTileThreads, 1)
   // The last CTA out resets the dependency counters for the next launch.
   if (threadIdx.x == 0) {
     __threadfence();
-    const uint32_t exits = atomicAdd(p.counters + 2 * p.batch, 1u);
+    const int n_ctr = 3 * p.batch;
+    const uint32_t exits = atomicAdd(p.counters + n_ctr, 1u);
     if (exits == gridDim.x - 1) {
-      for (int i = 0; i <= 2 * p.batch; ++i) p.counters[i] = 0u;
+      for (int i = 0; i <= n_ctr; ++i) p.counters[i] = 0u;
       __threadfence();
     }
   }
@@ -2142,17 +2220,23 @@ int fused_capacity(DeviceState* st, int dev, int* capacity) {
   return MUON_POLAR_OK;
 }
 
-// Runs the whole step as one fused launch if the mode and sizes allow it;
-// *done = false means the caller should run the three kernels instead.
-int step_fused_impl(const void* x, void* y, void* gram, void* poly, void* scratch,
-                    size_t scratch_bytes, int64_t batch, int64_t m, int64_t n,
-                    int64_t ldx, int64_t ldy, float a, float b, float c,
-                    cudaStream_t stream, bool* done) {
+// Runs `steps` Polar Express steps (coefficient rows coefs[3 s .. 3 s + 2] =
+// a, b, c) as one fused launch if the mode and sizes allow it; *done = false
+// means the caller should run the three kernels instead.  Step 0 reads x
+// (row stride ldx), step s > 0 reads the previous step's output in buffer
+// buf[(s - 1) % 2] (row stride ldb), the last step writes y (ldy), the
+// others buf[s % 2].  buf may be null when steps == 1.
+int fused_steps_impl(const void* x, void* y, void* const* buf, int64_t ldb, void* gram,
+                     void* poly, void* scratch, size_t scratch_bytes, int64_t batch, int64_t m,
+                     int64_t n, int64_t ldx, int64_t ldy, const float* coefs, int steps,
+                     cudaStream_t stream, bool* done) {
   *done = false;
   const int mode = g_step_mode.load(std::memory_order_relaxed);
-  if (mode == 2 || scratch == nullptr || !aligned16(scratch) ||
-      static_cast<size_t>(2 * batch + 1) * 4 > kCounterBytes || scratch_bytes < kCounterBytes)
+  if (mode == 2 || steps < 1 || steps > kMaxFusedSteps || scratch == nullptr ||
+      !aligned16(scratch) ||
+      static_cast<size_t>(3 * batch + 1) * 4 > kCounterBytes || scratch_bytes < kCounterBytes)
     return MUON_POLAR_OK;
+  if (steps > 1 && (buf == nullptr || buf[0] == nullptr || buf[1] == nullptr)) return MUON_POLAR_OK;
   DeviceState* st = nullptr;
   int rc = current_device_state(&st);
   if (rc != MUON_POLAR_OK) return rc;
@@ -2166,8 +2250,8 @@ int step_fused_impl(const void* x, void* y, void* gram, void* poly, void* scratc
   const int64_t d2 = mp / kPairM;
   const int64_t regions = d2 * (d2 + 1);
   const int64_t tn = (n + kPairN - 1) / kPairN;
-  const int64_t total = 2 * batch * regions + batch * d2 * tn;
-  if (total > INT32_MAX) return MUON_POLAR_OK;
+  const int64_t per_step = 2 * batch * regions + batch * d2 * tn;
+  if (per_step * steps > INT32_MAX) return MUON_POLAR_OK;
   // By size, from measurements on B200 (muon_polar_step_sm100, 15 shapes):
   // the fused launch wins for many small matrices -- more Gram regions than
   // pairs and Mp <= 768: 4-21% faster at [16|32,512,2048], [8|16,768,3072],
@@ -2177,12 +2261,22 @@ int step_fused_impl(const void* x, void* y, void* gram, void* poly, void* scratc
   if (mode == 0 && !(batch * regions > capacity && mp <= 768)) return MUON_POLAR_OK;
 
   FusedMaps maps;
-  rc = encode_3d(&maps.x_k, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, x, n, m, batch, ldx,
-                 m * ldx, kAtom, kHalf);
-  if (rc != MUON_POLAR_OK) return rc;
-  rc = encode_3d(&maps.x_mn, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, x, n, m, batch, ldx,
-                 m * ldx, kAtom, kAtom);
-  if (rc != MUON_POLAR_OK) return rc;
+  // X of each step and Y: the input / output and the two buffers
+  const void* xs[3] = {x, steps > 1 ? buf[0] : x, steps > 1 ? buf[1] : x};
+  void* ys[3] = {y, steps > 1 ? buf[0] : y, steps > 1 ? buf[1] : y};
+  const int64_t lds_x[3] = {ldx, steps > 1 ? ldb : ldx, steps > 1 ? ldb : ldx};
+  const int64_t lds_y[3] = {ldy, steps > 1 ? ldb : ldy, steps > 1 ? ldb : ldy};
+  for (int k = 0; k < 3; ++k) {
+    rc = encode_3d(&maps.x_k[k], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, xs[k], n, m, batch,
+                   lds_x[k], m * lds_x[k], kAtom, kHalf);
+    if (rc != MUON_POLAR_OK) return rc;
+    rc = encode_3d(&maps.x_mn[k], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, xs[k], n, m, batch,
+                   lds_x[k], m * lds_x[k], kAtom, kAtom);
+    if (rc != MUON_POLAR_OK) return rc;
+    rc = encode_3d(&maps.y128[k], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, ys[k], n, m, batch,
+                   lds_y[k], m * lds_y[k], kAtom, kHalf);
+    if (rc != MUON_POLAR_OK) return rc;
+  }
   rc = encode_square(&maps.a128, gram, batch, mp, false, kHalf);
   if (rc != MUON_POLAR_OK) return rc;
   rc = encode_square(&maps.a64, gram, batch, mp, false, kChunkCols);
@@ -2190,9 +2284,6 @@ int step_fused_impl(const void* x, void* y, void* gram, void* poly, void* scratc
   rc = encode_square(&maps.p128, poly, batch, mp, false, kHalf);
   if (rc != MUON_POLAR_OK) return rc;
   rc = encode_square(&maps.p64, poly, batch, mp, false, kChunkCols);
-  if (rc != MUON_POLAR_OK) return rc;
-  rc = encode_3d(&maps.y128, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, y, n, m, batch, ldy,
-                 m * ldy, kAtom, kHalf);
   if (rc != MUON_POLAR_OK) return rc;
 
   FusedParams p = {};
@@ -2202,18 +2293,23 @@ int step_fused_impl(const void* x, void* y, void* gram, void* poly, void* scratc
   p.apply_tn = static_cast<int32_t>(tn);
   p.n_gram = static_cast<int32_t>(batch * regions);
   p.n_poly = static_cast<int32_t>(batch * regions);
-  p.total = static_cast<int32_t>(total);
+  p.per_step = static_cast<int32_t>(per_step);
+  p.steps = steps;
+  p.total = static_cast<int32_t>(per_step * steps);
+  p.apply_bands = static_cast<uint32_t>(2 * d2 * tn);
   p.kb_gram = static_cast<int32_t>((n + 127) / 128);
   p.kb_poly = static_cast<int32_t>(mp / 128);
   p.kb_apply = static_cast<int32_t>((m + kAtom - 1) / kAtom);
-  p.coef_b = b;
-  p.coef_c = c;
-  p.alpha = round_to_bf16(a);
+  for (int k = 0; k < steps; ++k) {
+    p.coef[k][0] = coefs[3 * k + 1];
+    p.coef[k][1] = coefs[3 * k + 2];
+    p.coef[k][2] = round_to_bf16(coefs[3 * k]);
+  }
   p.counters = static_cast<uint32_t*>(scratch);
   p.gram = static_cast<const uint16_t*>(gram);
   p.mp = static_cast<int32_t>(mp);
 
-  const int pairs = total < capacity ? static_cast<int>(total) : capacity;
+  const int pairs = p.total < capacity ? p.total : capacity;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * pairs, 1, 1);
   cfg.blockDim = dim3(kTileThreads, 1, 1);
@@ -2388,8 +2484,9 @@ int muon_polar_step_sm100(const void* x, void* y, void* workspace,
   void* poly = ws + static_cast<size_t>(batch * mp * mp * 2);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   bool fused = false;
-  rc = step_fused_impl(x, y, gram, poly, scratch, scratch_bytes, batch, m, n, ldx, ldy, a, b,
-                       c, s, &fused);
+  const float coefs[3] = {a, b, c};
+  rc = fused_steps_impl(x, y, nullptr, 0, gram, poly, scratch, scratch_bytes, batch, m, n, ldx,
+                        ldy, coefs, 1, s, &fused);
   if (rc != MUON_POLAR_OK || fused) return rc;
   rc = gram_impl<kGramBf16>(x, gram, batch, m, n, ldx, scratch, scratch_bytes, s);
   if (rc != MUON_POLAR_OK) return rc;
@@ -2431,6 +2528,69 @@ int muon_polar_step_t_sm100(const void* x, void* y, void* workspace, size_t work
   rc = poly_impl(gram, poly, batch, np, b, c, scratch, scratch_bytes, s);
   if (rc != MUON_POLAR_OK) return rc;
   return apply_t_impl(poly, x, y, batch, m, n, ldx, ldy, a, s);
+}
+
+int muon_polar_steps_sm100(const void* x, void* y, void* buf0, void* buf1, int64_t ldb,
+                           void* workspace, size_t workspace_bytes, void* scratch,
+                           size_t scratch_bytes, int64_t batch, int64_t m, int64_t n,
+                           int64_t ldx, int64_t ldy, const float* coefficients, int steps,
+                           void* stream) {
+  int rc = check_x_args(x, batch, m, n, ldx);
+  if (rc != MUON_POLAR_OK) return rc;
+  if (y == nullptr || y == x || ldy < n || coefficients == nullptr || steps < 1 ||
+      n > (1 << 24))
+    return MUON_POLAR_ERR_INVALID_ARGUMENT;
+  if (steps > 1) {
+    // step 0 must not overwrite its input, nor the last step its own input
+    if (buf0 == nullptr || buf1 == nullptr || buf0 == buf1 || ldb < n || buf0 == x ||
+        y == ((steps & 1) ? buf1 : buf0))
+      return MUON_POLAR_ERR_INVALID_ARGUMENT;
+    if (!aligned16(buf0) || !aligned16(buf1) || (ldb % 8) != 0) return MUON_POLAR_ERR_ALIGNMENT;
+  }
+  const bool tall = m > n;
+  const int64_t g = tall ? n : m;
+  if (workspace == nullptr || !aligned16(workspace) ||
+      workspace_bytes < muon_polar_workspace_bytes(batch, g))
+    return MUON_POLAR_ERR_WORKSPACE;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  void* buf[2] = {buf0, buf1};
+  // step i reads x (i = 0) or buf[(i - 1) % 2] and writes buf[i % 2], the
+  // last step y
+  int i = 0;
+  while (i < steps) {
+    const void* in = i == 0 ? x : buf[(i - 1) & 1];
+    const int64_t ld_in = i == 0 ? ldx : ldb;
+    if (!tall) {
+      // as many steps as one fused launch takes
+      const int cnt = steps - i < kMaxFusedSteps ? steps - i : kMaxFusedSteps;
+      const bool last = i + cnt == steps;
+      void* out = last ? y : buf[(i + cnt - 1) & 1];
+      void* local[2] = {buf[i & 1], buf[(i + 1) & 1]};
+      const int64_t mp = padded_rows(m);
+      uint8_t* ws = static_cast<uint8_t*>(workspace);
+      bool fused = false;
+      rc = fused_steps_impl(in, out, local, ldb, ws, ws + static_cast<size_t>(batch * mp * mp * 2),
+                            scratch, scratch_bytes, batch, m, n, ld_in, last ? ldy : ldb,
+                            coefficients + 3 * i, cnt, s, &fused);
+      if (rc != MUON_POLAR_OK) return rc;
+      if (fused) {
+        i += cnt;
+        continue;
+      }
+    }
+    const bool last = i == steps - 1;
+    void* out = last ? y : buf[i & 1];
+    const float* cf = coefficients + 3 * i;
+    rc = tall ? muon_polar_step_t_sm100(in, out, workspace, workspace_bytes, scratch,
+                                        scratch_bytes, batch, m, n, ld_in, last ? ldy : ldb,
+                                        cf[0], cf[1], cf[2], stream)
+              : muon_polar_step_sm100(in, out, workspace, workspace_bytes, scratch, scratch_bytes,
+                                      batch, m, n, ld_in, last ? ldy : ldb, cf[0], cf[1], cf[2],
+                                      stream);
+    if (rc != MUON_POLAR_OK) return rc;
+    ++i;
+  }
+  return MUON_POLAR_OK;
 }
 
 size_t muon_polar_scratch_bytes(int64_t batch, int64_t m, int64_t n) {

@@ -323,33 +323,19 @@ ExpressPlan express_plan(int64_t batch, int64_t m, int64_t n) {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-// `steps` Polar Express steps from the bf16 iterate `src` (row stride ld)
-// into `dst`, ping-ponging through the two iterate buffers; tall X runs the
-// transposed step (its Gram is N x N).
+// `steps` Polar Express steps from the bf16 iterate `src` (row stride
+// ld_src) into `dst` through the two iterate buffers (muon_polar_steps_sm100:
+// one fused launch for small matrices, else three kernels a step; tall X
+// runs the transposed step, whose Gram is N x N).  When src is iterate 0
+// the first step writes iterate 1.
 int run_steps(const void* src, int64_t ld_src, void* dst, int64_t ld_dst, uint8_t* ws,
               const ExpressPlan& pl, void* scratch, size_t scratch_bytes, int64_t batch,
               int64_t m, int64_t n, const float* coefficients, int steps, cudaStream_t stream) {
   void* iter[2] = {ws + pl.polar_bytes, ws + pl.polar_bytes + pl.iter_bytes};
-  const int64_t ld_it = iterate_ld(n);
-  const void* cur = src;
-  int64_t ld_cur = ld_src;
-  int next = (src == iter[0]) ? 1 : 0;
-  for (int i = 0; i < steps; ++i) {
-    const bool last = i == steps - 1;
-    void* out = last ? dst : iter[next];
-    const int64_t ld_out = last ? ld_dst : ld_it;
-    const float a = coefficients[3 * i], b = coefficients[3 * i + 1], c = coefficients[3 * i + 2];
-    const int rc =
-        m > n ? muon_polar_step_t_sm100(cur, out, ws, pl.polar_bytes, scratch, scratch_bytes, batch,
-                                        m, n, ld_cur, ld_out, a, b, c, stream)
-              : muon_polar_step_sm100(cur, out, ws, pl.polar_bytes, scratch, scratch_bytes, batch,
-                                      m, n, ld_cur, ld_out, a, b, c, stream);
-    if (rc != MUON_POLAR_OK) return rc;
-    cur = out;
-    ld_cur = ld_out;
-    next ^= 1;
-  }
-  return MUON_POLAR_OK;
+  const int first = (src == iter[0]) ? 1 : 0;
+  return muon_polar_steps_sm100(src, dst, iter[first], iter[first ^ 1], iterate_ld(n), ws,
+                                pl.polar_bytes, scratch, scratch_bytes, batch, m, n, ld_src,
+                                ld_dst, coefficients, steps, stream);
 }
 
 // input (and momentum) rows of stride ldg -> normalised bf16 x (stride ldx).

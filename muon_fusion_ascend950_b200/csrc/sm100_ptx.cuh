@@ -152,6 +152,16 @@ __device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
 __device__ __forceinline__ void red_release_gpu_add(uint32_t* p, uint32_t v) {
   asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
+// A counter in this CTA's shared memory, written by one thread and polled by
+// another of the same CTA.
+__device__ __forceinline__ void st_release_cta_shared(uint32_t addr, uint32_t v) {
+  asm volatile("st.release.cta.shared::cta.u32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_cta_shared(uint32_t addr) {
+  uint32_t v;
+  asm volatile("ld.acquire.cta.shared::cta.u32 %0, [%1];" : "=r"(v) : "r"(addr) : "memory");
+  return v;
+}
 // Waits until *p >= target (written by other CTAs with release semantics).
 // Returns false once kWaitLimitNs of wall-clock time have passed.
 __device__ __forceinline__ bool wait_counter_bounded(const uint32_t* p, uint32_t target) {
@@ -160,6 +170,17 @@ __device__ __forceinline__ bool wait_counter_bounded(const uint32_t* p, uint32_t
   while (true) {
     __nanosleep(64);
     if (ld_acquire_gpu(p) >= target) return true;
+    if (global_timer_ns() - t0 > kWaitLimitNs) return false;
+  }
+}
+// Waits until the shared counter at `addr` is >= target; false after
+// kWaitLimitNs.
+__device__ __forceinline__ bool wait_shared_bounded(uint32_t addr, uint32_t target) {
+  if (ld_acquire_cta_shared(addr) >= target) return true;
+  const uint64_t t0 = global_timer_ns();
+  while (true) {
+    __nanosleep(32);
+    if (ld_acquire_cta_shared(addr) >= target) return true;
     if (global_timer_ns() - t0 > kWaitLimitNs) return false;
   }
 }

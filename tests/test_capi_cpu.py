@@ -138,3 +138,32 @@ def test_caller_side_entry_validation_without_device(api):
                                        256, *args) == -3
     assert lib.muon_polar_update_sm100(_vp(16), _vp(32), _vp(48), 0, _vp(64), ws - 1, None, 0, 1,
                                        128, 256, *args) == -5
+
+
+def test_steps_entry_validation_without_device(api):
+    """muon_polar_steps_sm100 refuses, before touching a device: no
+    coefficients or steps, missing or equal buffers for several steps, a
+    first step that would overwrite its input (buf0 == x), a last step that
+    would overwrite its own input (y == buf[(steps - 2) % 2]), misaligned
+    buffers and a small workspace."""
+    lib = api.lib
+    coeffs = (ctypes.c_float * 15)(*([1.0] * 15))
+    ws = api.workspace_bytes(1, 128)
+    x, y, b0, b1 = _vp(16), _vp(32), _vp(48), _vp(64)
+
+    def call(x_, y_, b0_, b1_, ldb, steps, wsb=ws, cf=coeffs):
+        return lib.muon_polar_steps_sm100(x_, y_, b0_, b1_, ldb, _vp(16), wsb, None, 0, 1, 128,
+                                          256, 256, 256, cf, steps, None)
+
+    assert call(x, y, b0, b1, 256, 0) == -1
+    assert call(x, y, b0, b1, 256, 2, cf=None) == -1
+    assert call(x, x, b0, b1, 256, 1) == -1
+    assert call(x, y, None, b1, 256, 2) == -1
+    assert call(x, y, b0, b0, 256, 2) == -1
+    assert call(x, y, x, b1, 256, 2) == -1
+    assert call(x, y, b0, b1, 128, 2) == -1          # ldb < n
+    assert call(x, b0, b0, b1, 256, 2) == -1         # last (2nd) step reads buf0
+    assert call(x, b1, b0, b1, 256, 3) == -1         # last (3rd) step reads buf1
+    assert call(x, y, _vp(40), b1, 256, 2) == -3
+    assert call(x, y, b0, b1, 260, 2) == -3
+    assert call(x, y, b0, b1, 256, 2, wsb=ws - 1) == -5

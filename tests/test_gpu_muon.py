@@ -187,3 +187,81 @@ def test_muon_tall_and_batched_parameters(pkg, api, cuda_device):
     d = (tall.detach() - t0).cpu() / (-0.01 * 2.0)  # scale = sqrt(1024 / 256)
     assert error_stats(d.to(torch.bfloat16), y)["rel_fro"] <= 0.05
     assert not torch.equal(batched.detach(), b0)
+
+
+def _steps_fused_vs_chain(api, x, coeffs, mode):
+    """muon_polar_steps_sm100 in step mode `mode`, split-K off (the fused
+    kernel never splits K; a split changes the fp32 summation order) ->
+    (y, counters after)."""
+    bsz, m, n = x.shape
+    ws = torch.empty(api.workspace_bytes(bsz, m), dtype=torch.uint8, device=x.device)
+    scratch = torch.zeros(api.scratch_bytes(bsz, m, n), dtype=torch.uint8, device=x.device)
+    y = torch.full_like(x, float("nan"))
+    bufs = [torch.full_like(x, float("nan")) for _ in range(2)]
+    prev = api.lib.muon_polar_set_step_mode(mode)
+    prev_split = api.lib.muon_polar_set_split_mode(2)
+    try:
+        api.steps(x, y, bufs[0], bufs[1], ws, coeffs, scratch=scratch)
+        torch.cuda.synchronize()
+    finally:
+        api.lib.muon_polar_set_step_mode(prev)
+        api.lib.muon_polar_set_split_mode(prev_split)
+    return y, scratch[:1024].clone()
+
+
+@pytest.mark.parametrize("steps", [1, 2, 5, 9])
+@pytest.mark.parametrize("shape", [(16, 256, 1024), (8, 512, 2048), (32, 384, 1024),
+                                   (3, 200, 704), (1, 768, 3072)])
+def test_steps_single_launch_matches_three_kernel_chain(api, cuda_device, shape, steps):
+    """Up to 8 steps in ONE fused persistent launch (9 steps: a launch of 8
+    and one of 1) give the bits of the three-kernel chain, and the launch
+    leaves its dependency counters zeroed for the next call."""
+    x = make_input(shape, seed=41).to(cuda_device)
+    # past the five rows, the last (convergent, p(1) = 1) row repeats, as
+    # Polar Express schedules do; cycling back to the first row diverges
+    coeffs = [COEFFICIENTS[min(i, len(COEFFICIENTS) - 1)] for i in range(steps)]
+    before = api.launch_count()
+    y_f, ctr = _steps_fused_vs_chain(api, x, coeffs, 1)
+    launches = api.launch_count() - before
+    assert launches == (steps + 7) // 8
+    y_c, _ = _steps_fused_vs_chain(api, x, coeffs, 2)
+    _watchdog_clear(api)
+    assert not torch.isnan(y_f.float()).any()
+    assert torch.equal(y_f.view(torch.int16), y_c.view(torch.int16))
+    assert int(ctr.count_nonzero()) == 0
+
+
+def test_steps_match_step_calls_and_oracle(pkg, api, cuda_device):
+    """The five-step fused launch equals five polar_step calls and the
+    oracle's loop of the reference's example at the reference tolerance."""
+    x = make_input((16, 256, 1024), seed=42).to(cuda_device)
+    y, _ = _steps_fused_vs_chain(api, x, COEFFICIENTS, 1)
+    ref = x
+    for a, b, c in COEFFICIENTS:
+        ref = pkg.polar_step(ref, a, b, c)
+    assert torch.equal(y.view(torch.int16), ref.view(torch.int16))
+    want = polar_express_oracle(x.cpu(), COEFFICIENTS, normalize=False)
+    torch.testing.assert_close(y.cpu().float(), want.float(), rtol=6e-2, atol=6e-2)
+
+
+def test_steps_in_place_ping_pong(api, cuda_device):
+    """x may be buf1 (the caller's iterate is overwritten by step 1) and y
+    may be the buffer the last step would write: the Muon update's layout."""
+    x = make_input((8, 256, 1024), seed=43).to(cuda_device)
+    bsz, m, n = x.shape
+    ws = torch.empty(api.workspace_bytes(bsz, m), dtype=torch.uint8, device=cuda_device)
+    scratch = torch.zeros(api.scratch_bytes(bsz, m, n), dtype=torch.uint8, device=cuda_device)
+    want, _ = _steps_fused_vs_chain(api, x, COEFFICIENTS, 2)
+    for mode in (1, 2):
+        it0, it1 = x.clone(), torch.empty_like(x)
+        prev = api.lib.muon_polar_set_step_mode(mode)
+        prev_split = api.lib.muon_polar_set_split_mode(2)
+        try:
+            # five steps: it0 -> it1 -> it0 -> it1 -> it0 -> y = it1
+            api.steps(it0, it1, it1, it0, ws, COEFFICIENTS, scratch=scratch)
+            torch.cuda.synchronize()
+        finally:
+            api.lib.muon_polar_set_step_mode(prev)
+            api.lib.muon_polar_set_split_mode(prev_split)
+        assert torch.equal(it1.view(torch.int16), want.view(torch.int16)), mode
+    _watchdog_clear(api)
