@@ -73,14 +73,16 @@ def parse_args():
     p.add_argument("--poly", choices=["replicated", "sharded"], default="sharded",
                    help="cfg5 with several GPUs: kernel 2 on every rank (replicated) or "
                         "split into row slabs and all-gathered (sharded)")
-    p.add_argument("--workload", choices=["cfg1", "cfg3", "cfg4", "cfg5", "shape"],
+    p.add_argument("--workload", choices=["cfg1", "cfg3", "cfg4", "cfg5", "shape", "express"],
                    default="cfg1",
                    help="cfg1 (default, the headline): one step on [8,512,2048] per GPU; "
                         "cfg3: the 5-step loop on [8,512,2048] per GPU; cfg4: 5-step Muon "
                         "update of a 32-layer 7B model's matrices, batch-sharded over the "
                         "GPUs; cfg5: 5 steps on one [8192,65536] matrix, column-sharded "
                         "with an NCCL all-reduce of the fp32 Gram per step; shape: one "
-                        "step on --shape per GPU (config 2 shapes, profiling cases)")
+                        "step on --shape per GPU (config 2 shapes, profiling cases); "
+                        "express: the five steps on --shape as one polar_express call "
+                        "(a single fused launch for small matrices)")
     return p.parse_args()
 
 
@@ -248,13 +250,17 @@ def run_ours(args):
         dist.init_process_group("nccl", device_id=device, timeout=timedelta(seconds=120))
     api = capi()
     global BATCH, M, N
-    if args.workload == "shape":
+    if args.workload in ("shape", "express"):
         BATCH, M, N = (int(v) for v in args.shape.split(","))
     a, b, c = COEFFICIENTS[0]
-    rows = COEFFICIENTS if args.workload == "cfg3" else COEFFICIENTS[:1]
+    rows = COEFFICIENTS if args.workload in ("cfg3", "express") else COEFFICIENTS[:1]
     flops_step = len(rows) * BATCH * nominal_flops_per_matrix(M, N)
 
     def full_step(x):
+        if args.workload == "express":
+            # the five steps as one call (muon_polar_steps_sm100: one fused
+            # launch for small matrices)
+            return pkg.polar_express(x, rows, normalize=False)
         for ra, rb, rc in rows:
             x = pkg.polar_step(x, ra, rb, rc)
         return x
@@ -515,9 +521,13 @@ def run_ours(args):
         return
     cfg3 = args.workload == "cfg3"
     shape_str = f"[{BATCH},{M},{N}]"
+    metric = f"polar_step effective TFLOP/s at {shape_str} bf16"
+    if cfg3:
+        metric = f"5-step Polar Express loop effective TFLOP/s at {shape_str} bf16"
+    elif args.workload == "express":
+        metric = f"5-step polar_express call effective TFLOP/s at {shape_str} bf16"
     line = {
-        "metric": (f"5-step Polar Express loop effective TFLOP/s at {shape_str} bf16" if cfg3
-                   else f"polar_step effective TFLOP/s at {shape_str} bf16"),
+        "metric": metric,
         "value": value,
         "unit": "TFLOP/s",
         "n_gpus": world,
@@ -534,6 +544,8 @@ def run_ours(args):
         "config": {
             "workload": ("5-step polar_step loop on [8,512,2048] bf16 (BASELINE config 3) per GPU"
                          if cfg3 else
+                         f"polar_express (5 steps, one call) on {shape_str} bf16 per GPU"
+                         if args.workload == "express" else
                          f"polar_step {shape_str} bf16 single step per GPU" +
                          (" (BASELINE config 1)" if args.workload == "cfg1" else "")),
             "global_batch": BATCH * world, "m": M, "n": N,
