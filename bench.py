@@ -73,6 +73,11 @@ def parse_args():
     p.add_argument("--poly", choices=["replicated", "sharded"], default="sharded",
                    help="cfg5 with several GPUs: kernel 2 on every rank (replicated) or "
                         "split into row slabs and all-gathered (sharded)")
+    p.add_argument("--overlap-bands", type=int, default=0,
+                   help="cfg5 with several GPUs: run the Gram in this many row bands and "
+                        "all-reduce each band while the next one computes (0: one all-reduce)")
+    p.add_argument("--sm-reserve", type=int, default=16,
+                   help="cfg5 with --overlap-bands: SMs the Gram bands leave to NCCL")
     p.add_argument("--workload", choices=["cfg1", "cfg3", "cfg4", "cfg5", "shape", "express"],
                    default="cfg1",
                    help="cfg1 (default, the headline): one step on [8,512,2048] per GPU; "
@@ -632,15 +637,19 @@ def run_large(args):
         if world > 1:
             dist.all_reduce(sq)
         x_local = (x_local / (sq.sqrt() * 1.01 + 1e-6)).to(torch.bfloat16)
-        driver = ColumnShardedPolar(m, device, shard_poly=args.poly == "sharded")
+        driver = ColumnShardedPolar(m, device, shard_poly=args.poly == "sharded",
+                                    overlap_bands=args.overlap_bands, sm_reserve=args.sm_reserve)
         job_flops = 5 * nominal_flops(m, n)
 
         def step():
             driver.run(x_local, COEFFICIENTS)
 
         workload = "5-step loop on one [8192,65536] bf16 matrix (BASELINE config 5)"
-        parallelism = (f"column-sharded x{world}, one NCCL fp32 all-reduce of the 8192x8192 "
-                       "partial Gram per step, kernel 2 "
+        reduce = ("one NCCL fp32 all-reduce of the 8192x8192 partial Gram per step"
+                  if not driver.bands else
+                  f"the partial Gram in {len(driver.bands)} row bands, each NCCL fp32 "
+                  f"all-reduced while the next computes ({args.sm_reserve} SMs left to NCCL)")
+        parallelism = (f"column-sharded x{world}, {reduce}, kernel 2 "
                        + ("in row slabs + NCCL bf16 all-gather"
                           if driver.poly_slab is not None else "replicated")
                        if world > 1 else "single GPU")

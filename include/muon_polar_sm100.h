@@ -148,6 +148,20 @@ int muon_polar_gram_f32_sm100(const void* x, void* gram_f32, int64_t batch,
                               int64_t m, int64_t n, int64_t ldx, void* scratch,
                               size_t scratch_bytes, void* stream);
 
+/* Kernel (1), fp32 output, on a band of rows: the upper tiles of rows
+ * [row_begin, row_begin + row_count) of gram_f32 (both multiples of 256,
+ * inside muon_polar_padded_rows(m)), each stored with its mirror.  Run for
+ * consecutive bands from row 0 on, the rows of a band are complete (both
+ * triangles) as soon as its call has run, so a column-sharded caller can
+ * all-reduce band i while band i + 1 computes; after the last band the
+ * buffer equals muon_polar_gram_f32_sm100's.  `sm_reserve` SMs are left
+ * free (rounded up to whole clusters of two) for kernels on other streams,
+ * such as the collective.  No counterpart in the reference (single device). */
+int muon_polar_gram_f32_band_sm100(const void* x, void* gram_f32, int64_t batch, int64_t m,
+                                   int64_t n, int64_t ldx, int64_t row_begin, int64_t row_count,
+                                   int sm_reserve, void* scratch, size_t scratch_bytes,
+                                   void* stream);
+
 /* Kernel (2): poly[b] = bf16( b*f32(gram[b]) + c*(gram[b].gram[b])_f32 ),
  * both [batch][Mp][Mp] bf16, Mp a multiple of 128 (256 for the CTA-pair
  * kernels; muon_polar_padded_rows gives 256-multiples).  Products and the

@@ -32,6 +32,9 @@ SIGNATURES = {
                                                             _VP]),
     "muon_polar_gram_f32_sm100": (ctypes.c_int, [_VP, _VP, _I64, _I64, _I64, _I64, _VP,
                                                  ctypes.c_size_t, _VP]),
+    "muon_polar_gram_f32_band_sm100": (ctypes.c_int, [_VP, _VP, _I64, _I64, _I64, _I64, _I64,
+                                                      _I64, ctypes.c_int, _VP, ctypes.c_size_t,
+                                                      _VP]),
     "muon_polar_poly_sm100": (ctypes.c_int, [_VP, _VP, _I64, _I64, ctypes.c_float,
                                              ctypes.c_float, _VP, ctypes.c_size_t, _VP]),
     "muon_polar_poly_rows_sm100": (ctypes.c_int, [_VP, _VP, _I64, _I64, _I64, _I64,
@@ -230,6 +233,18 @@ class CAPI:
         sp, sb = _scratch(scratch)
         self._check("muon_polar_gram_f32_sm100", self.lib.muon_polar_gram_f32_sm100(
             x.data_ptr(), gram_f32.data_ptr(), b, m, n, ld, sp, sb, self._stream(stream)))
+
+    def gram_f32_band(self, x, gram_f32, row_begin: int, row_count: int, sm_reserve: int = 0,
+                      n: Optional[int] = None, scratch=None, stream=None) -> None:
+        """Upper tiles of rows [row_begin, row_begin + row_count) of the fp32
+        Gram, mirrored; run band by band from row 0, each band's rows are
+        complete once it has run."""
+        b, m, ld = x.shape
+        n = ld if n is None else n
+        sp, sb = _scratch(scratch)
+        self._check("muon_polar_gram_f32_band_sm100", self.lib.muon_polar_gram_f32_band_sm100(
+            x.data_ptr(), gram_f32.data_ptr(), b, m, n, ld, int(row_begin), int(row_count),
+            int(sm_reserve), sp, sb, self._stream(stream)))
 
     def poly(self, gram, poly, b: float, c: float, scratch=None, stream=None) -> None:
         bsz, mp, _ = gram.shape

@@ -73,7 +73,13 @@ struct EpiParams {
   // row_tile_begin + tiles_m) -- both triangles, no mirror -- instead of the
   // upper triangle (a row slab of P for a multi-GPU caller).
   int32_t rows_mode;
+  // Without rows_mode, symmetric kinds compute the upper tiles of the tile
+  // rows from row_tile_begin on (tiles_per_batch of them: a band of rows,
+  // each tile stored with its mirror); 0 for the whole triangle.
   int32_t row_tile_begin;
+  // At most this many clusters (0: as many as fit), leaving SMs free for
+  // kernels that run beside this one (a collective on another stream).
+  int32_t max_units;
   // Split-K (symmetric kinds): each tile's K range is cut into `splits`
   // work items of (nearly) equal length; item = tile * splits + split.
   int32_t splits;
@@ -92,7 +98,8 @@ struct TileCoord {
 __host__ __device__ __forceinline__ TileCoord decode_tile(int tile, bool sym,
                                                           int tiles_m,
                                                           int tiles_n,
-                                                          int tiles_per_batch) {
+                                                          int tiles_per_batch,
+                                                          int first_row = 0) {
   TileCoord t;
   t.b = tile / tiles_per_batch;
   int r = tile - t.b * tiles_per_batch;
@@ -101,7 +108,7 @@ __host__ __device__ __forceinline__ TileCoord decode_tile(int tile, bool sym,
     t.tn = r - t.tm * tiles_n;
   } else {
     const int d = tiles_m;
-    int tm = 0;
+    int tm = first_row;
     while (r >= d - tm) {
       r -= d - tm;
       ++tm;
@@ -124,11 +131,12 @@ __host__ __device__ __forceinline__ WorkItem decode_item(const EpiParams& p, int
                                                          bool sym) {
   WorkItem w;
   const int tile = item / p.splits;
-  const TileCoord tc =
-      decode_tile(tile, sym && !p.rows_mode, p.tiles_m, p.tiles_n, p.tiles_per_batch);
+  const bool walk = sym && !p.rows_mode;
+  const TileCoord tc = decode_tile(tile, walk, p.tiles_m, p.tiles_n, p.tiles_per_batch,
+                                   walk ? p.row_tile_begin : 0);
   w.tile = tile;
   w.b = tc.b;
-  w.tm = tc.tm + p.row_tile_begin;
+  w.tm = walk ? tc.tm : tc.tm + p.row_tile_begin;
   w.tn = tc.tn;
   w.split = item - tile * p.splits;
   w.nsplit = p.splits;
@@ -1793,6 +1801,7 @@ int launch_tile(DeviceState* st, const TileMaps& maps, const EpiParams& p,
   int units = 0;
   int rc = tile_capacity<KIND, PAIR>(st, &units);
   if (rc != MUON_POLAR_OK) return rc;
+  if (p.max_units > 0 && units > p.max_units) units = p.max_units;
   int ctas = PAIR * (p.total_items < units ? p.total_items : units);
   // Single-CTA tiles launch as clusters of two independent CTAs as well, so
   // they occupy whole TPCs and leave whole TPCs free for the CTA pairs of
@@ -1869,12 +1878,16 @@ void sym_grid(EpiParams& p, int64_t batch, int64_t mp) {
 template <int KIND, int PAIR>
 int gram_launch(DeviceState* st, const void* x, void* gram, int64_t batch, int64_t m,
                 int64_t n, int64_t ldx, void* scratch, size_t scratch_bytes,
-                bool fixed_scratch, cudaStream_t stream) {
+                bool fixed_scratch, cudaStream_t stream, int64_t band_begin = 0,
+                int64_t band_rows = 0, int sm_reserve = 0) {
   constexpr bool kT = KIND == kGramT;
   const int64_t mp = padded_rows(kT ? n : m);
   int units = 0;
   int rc = tile_capacity<KIND, PAIR>(st, &units);
   if (rc != MUON_POLAR_OK) return rc;
+  // SMs left free: whole clusters of two
+  const int keep_units = units - (sm_reserve + 1) / 2 * (PAIR == 2 ? 1 : 2);
+  if (sm_reserve > 0) units = keep_units > 0 ? keep_units : 1;
   TileMaps tm;
   // X: rows beyond m and columns beyond n read as zero.  K-major boxes of
   // [128 rows x 64 columns]; MN-major (kGramT) boxes of [kBK rows x 64
@@ -1890,6 +1903,16 @@ int gram_launch(DeviceState* st, const void* x, void* gram, int64_t batch, int64
   if (rc != MUON_POLAR_OK) return rc;
   EpiParams p = {};
   sym_grid<PAIR>(p, batch, mp);
+  if (band_rows > 0) {
+    // the upper tiles of tile rows [t0, t0 + nt)
+    const int64_t th = kHalf * PAIR;
+    const int64_t d = mp / th, t0 = band_begin / th, nt = band_rows / th;
+    const int64_t count = nt * d - (2 * t0 + nt - 1) * nt / 2;
+    p.tiles_per_batch = static_cast<int32_t>(count);
+    p.total_tiles = static_cast<int32_t>(count * batch);
+    p.row_tile_begin = static_cast<int32_t>(t0);
+  }
+  if (sm_reserve > 0) p.max_units = units;
   p.k_blocks = static_cast<int32_t>(k_blocks_of<KIND, PAIR>(kT ? m : n));
   if (fixed_scratch &&
       split_scratch_bytes<PAIR>(p.total_tiles,
@@ -1935,6 +1958,42 @@ int gram_impl(const void* x, void* gram, int64_t batch, int64_t m, int64_t n,
                                 fixed_scratch, stream);
   return gram_launch<KIND, 1>(st, x, gram, batch, m, n, ldx, scratch, scratch_bytes,
                               fixed_scratch, stream);
+}
+
+// Kernel (1), fp32 output, on the upper tiles of the rows [row_begin,
+// row_begin + row_count) of the Gram (multiples of 256), each stored with its
+// mirror; `sm_reserve` SMs stay free.  Run for consecutive bands in order,
+// the rows of a band are complete (both triangles) once it has run.
+int gram_f32_band_impl(const void* x, void* gram, int64_t batch, int64_t m, int64_t n,
+                       int64_t ldx, int64_t row_begin, int64_t row_count, int sm_reserve,
+                       void* scratch, size_t scratch_bytes, cudaStream_t stream) {
+  int rc = check_x_args(x, batch, m, n, ldx);
+  if (rc != MUON_POLAR_OK) return rc;
+  if (gram == nullptr) return MUON_POLAR_ERR_INVALID_ARGUMENT;
+  if (!aligned16(gram)) return MUON_POLAR_ERR_ALIGNMENT;
+  const int64_t mp = padded_rows(m);
+  if (row_begin < 0 || row_count <= 0 || row_begin % kPairM != 0 || row_count % kPairM != 0 ||
+      row_begin + row_count > mp || sm_reserve < 0 || sm_reserve > 1024)
+    return MUON_POLAR_ERR_INVALID_ARGUMENT;
+  DeviceState* st = nullptr;
+  rc = current_device_state(&st);
+  if (rc != MUON_POLAR_OK) return rc;
+  int pairs = 0, ctas = 0;
+  rc = tile_capacity<kGramF32, 2>(st, &pairs);
+  if (rc != MUON_POLAR_OK) return rc;
+  rc = tile_capacity<kGramF32, 1>(st, &ctas);
+  if (rc != MUON_POLAR_OK) return rc;
+  auto band_tiles = [&](int64_t th) {
+    const int64_t d = mp / th, t0 = row_begin / th, nt = row_count / th;
+    return (nt * d - (2 * t0 + nt - 1) * nt / 2) * batch;
+  };
+  if (band_tiles(kHalf) > INT32_MAX) return MUON_POLAR_ERR_INVALID_ARGUMENT;
+  if (use_pairs(band_tiles(kPairM), pairs, cost_blocks<2>(n), band_tiles(kHalf), ctas,
+                cost_blocks<1>(n)))
+    return gram_launch<kGramF32, 2>(st, x, gram, batch, m, n, ldx, scratch, scratch_bytes, false,
+                                    stream, row_begin, row_count, sm_reserve);
+  return gram_launch<kGramF32, 1>(st, x, gram, batch, m, n, ldx, scratch, scratch_bytes, false,
+                                  stream, row_begin, row_count, sm_reserve);
 }
 
 template <int PAIR>
@@ -2437,6 +2496,14 @@ int muon_polar_gram_sm100(const void* x, void* gram, int64_t batch, int64_t m,
                           size_t scratch_bytes, void* stream) {
   return gram_impl<kGramBf16>(x, gram, batch, m, n, ldx, scratch, scratch_bytes,
                               static_cast<cudaStream_t>(stream));
+}
+
+int muon_polar_gram_f32_band_sm100(const void* x, void* gram_f32, int64_t batch, int64_t m,
+                                   int64_t n, int64_t ldx, int64_t row_begin, int64_t row_count,
+                                   int sm_reserve, void* scratch, size_t scratch_bytes,
+                                   void* stream) {
+  return gram_f32_band_impl(x, gram_f32, batch, m, n, ldx, row_begin, row_count, sm_reserve,
+                            scratch, scratch_bytes, static_cast<cudaStream_t>(stream));
 }
 
 int muon_polar_gram_f32_sm100(const void* x, void* gram_f32, int64_t batch,

@@ -10,7 +10,11 @@ workloads it is benchmarked on shard in two ways:
 * **Column sharding** (one large matrix: config 5).  Rank r owns the column
   slab X[:, r*N/G : (r+1)*N/G] for the whole iteration.  Per step:
     1. partial Gram G_r = X_r X_r^T in fp32 (kernel 1, fp32 output),
-    2. one all-reduce (sum, fp32, Mp x Mp) over NCCL,
+    2. one all-reduce (sum, fp32, Mp x Mp) over NCCL -- or, with
+       `overlap_bands`, kernel 1 runs band by band over the rows
+       (muon_polar_gram_f32_band_sm100, leaving `sm_reserve` SMs free) and
+       each band's rows are all-reduced on a second stream while the next
+       band computes,
     3. A = bf16(sum) (cast kernel), P = b A + c A A (kernel 2), either
        replicated on every rank or (shard_poly) as row slabs, rank r
        computing rows [r Mp/G, (r+1) Mp/G) followed by an all-gather of the
@@ -71,14 +75,33 @@ def column_range(n: int, rank: int, world: int, align: int = 8) -> range:
     return range(start, stop)
 
 
+def gram_bands(mp: int, bands: int) -> List[tuple]:
+    """Row bands (begin, count) covering [0, mp), multiples of 256 rows, as
+    equal as the 256-row granularity allows (at most `bands` of them)."""
+    tiles = mp // 256
+    bands = max(1, min(bands, tiles))
+    out = []
+    begin = 0
+    for i in range(bands):
+        end = (i + 1) * tiles // bands
+        if end > begin:
+            out.append((begin * 256, (end - begin) * 256))
+        begin = end
+    return out
+
+
 class ColumnShardedPolar:
     """Polar Express steps on a matrix whose columns are split across the
     ranks of `group` (see the module docstring).  Buffers for the replicated
     Mp x Mp Gram / polynomial are allocated once per instance.  With
     `shard_poly`, kernel 2 is split into row slabs across the ranks (when
-    Mp divides into equal slabs of 256-row multiples; otherwise replicated)."""
+    Mp divides into equal slabs of 256-row multiples; otherwise replicated).
+    With `overlap_bands` > 1 the Gram's all-reduce runs band by band beside
+    the computation of the next band (the bands' kernels leave `sm_reserve`
+    SMs to the collective)."""
 
-    def __init__(self, m: int, device, group=None, backend=None, shard_poly: bool = False):
+    def __init__(self, m: int, device, group=None, backend=None, shard_poly: bool = False,
+                 overlap_bands: int = 0, sm_reserve: int = 16):
         if backend is None:
             from .capi import capi
 
@@ -94,6 +117,10 @@ class ColumnShardedPolar:
         if shard_poly and world > 1 and self.mp % (256 * world) == 0:
             rows = self.mp // world
             self.poly_slab = (rank * rows, rows)
+        self.bands = gram_bands(self.mp, overlap_bands) if overlap_bands > 1 and world > 1 else []
+        self.sm_reserve = sm_reserve
+        self.comm = (torch.cuda.Stream(self.device)
+                     if self.bands and self.device.type == "cuda" else None)
         shape = (1, self.mp, self.mp)
         self.gram_f32 = torch.empty(shape, dtype=torch.float32, device=self.device)
         self.gram = torch.empty(shape, dtype=torch.bfloat16, device=self.device)
@@ -107,9 +134,12 @@ class ColumnShardedPolar:
             raise ValueError(f"x_local must be [{self.m}, n_local], got {tuple(x_local.shape)}")
         x3 = x_local.contiguous().unsqueeze(0)
         y3 = torch.empty_like(x3) if out is None else out.view(1, *out.shape[-2:])
-        self.backend.gram_f32(x3, self.gram_f32)
-        if dist.is_initialized() and dist.get_world_size(self.group) > 1:
-            dist.all_reduce(self.gram_f32, op=dist.ReduceOp.SUM, group=self.group)
+        if self.bands:
+            self._gram_reduce_bands(x3)
+        else:
+            self.backend.gram_f32(x3, self.gram_f32)
+            if dist.is_initialized() and dist.get_world_size(self.group) > 1:
+                dist.all_reduce(self.gram_f32, op=dist.ReduceOp.SUM, group=self.group)
         self.backend.cast_f32_bf16(self.gram_f32, self.gram)
         if self.poly_slab is None:
             self.backend.poly(self.gram, self.poly, b, c)
@@ -122,6 +152,25 @@ class ColumnShardedPolar:
                                         group=self.group)
         self.backend.apply(self.poly, x3, y3, a)
         return y3.squeeze(0)
+
+    def _gram_reduce_bands(self, x3: torch.Tensor) -> None:
+        """Kernel 1 band by band; band i's rows are complete after its call
+        and are summed across the ranks while band i + 1 computes.  Every
+        rank issues the same all-reduces in the same order."""
+        cur = torch.cuda.current_stream(self.device) if self.comm is not None else None
+        for begin, count in self.bands:
+            self.backend.gram_f32_band(x3, self.gram_f32, begin, count, self.sm_reserve)
+            rows = self.gram_f32[:, begin:begin + count]  # contiguous rows
+            if self.comm is None:
+                dist.all_reduce(rows, op=dist.ReduceOp.SUM, group=self.group)
+                continue
+            done = torch.cuda.Event()
+            done.record(cur)
+            with torch.cuda.stream(self.comm):
+                self.comm.wait_event(done)
+                dist.all_reduce(rows, op=dist.ReduceOp.SUM, group=self.group)
+        if self.comm is not None:
+            cur.wait_stream(self.comm)
 
     def run(self, x_local: torch.Tensor, coefficients) -> torch.Tensor:
         """The caller-side loop over (a, b, c) rows, slab kept local."""
@@ -156,5 +205,6 @@ __all__ = [
     "partition_items",
     "column_range",
     "ColumnShardedPolar",
+    "gram_bands",
     "batch_sharded_steps",
 ]

@@ -158,6 +158,20 @@ class CpuKernels:
         out[:, :m, :m] = xf @ xf.mT
 
     @staticmethod
+    def gram_f32_band(x, out, row_begin, row_count, sm_reserve=0, n=None, scratch=None,
+                      stream=None):
+        """Rows [row_begin, row_begin + row_count) of the upper triangle
+        (columns >= row_begin) and their mirror, as the banded kernel 1."""
+        m = x.shape[1]
+        xf = x.to(torch.float32)
+        mp = out.shape[-1]
+        r1 = row_begin + row_count
+        full = torch.zeros((x.shape[0], mp, mp), dtype=torch.float32)
+        full[:, :m, :m] = xf @ xf.mT
+        out[:, row_begin:r1, row_begin:] = full[:, row_begin:r1, row_begin:]
+        out[:, row_begin:, row_begin:r1] = full[:, row_begin:, row_begin:r1]
+
+    @staticmethod
     def cast_f32_bf16(src, dst, stream=None):
         dst.copy_(src.to(torch.bfloat16))
 

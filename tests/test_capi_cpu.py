@@ -167,3 +167,21 @@ def test_steps_entry_validation_without_device(api):
     assert call(x, y, _vp(40), b1, 256, 2) == -3
     assert call(x, y, b0, b1, 260, 2) == -3
     assert call(x, y, b0, b1, 256, 2, wsb=ws - 1) == -5
+
+
+def test_gram_band_validation_without_device(api):
+    """The banded fp32 Gram refuses, before touching a device, bands that are
+    not 256-row multiples inside the padded rows, and a negative reserve."""
+    lib = api.lib
+
+    def call(begin, count, reserve=0, x=_vp(16), m=600):
+        return lib.muon_polar_gram_f32_band_sm100(x, _vp(32), 1, m, 512, 512, begin, count,
+                                                  reserve, None, 0, None)
+
+    assert call(0, 256, x=None) == -1
+    assert call(128, 256) == -1      # not a multiple of 256
+    assert call(0, 100) == -1
+    assert call(0, 0) == -1
+    assert call(512, 512) == -1      # past Mp = 768
+    assert call(-256, 256) == -1
+    assert call(0, 256, reserve=-1) == -1

@@ -77,7 +77,7 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _column_worker(rank, world, port, m, n, steps, out_dir, shard_poly=False):
+def _column_worker(rank, world, port, m, n, steps, out_dir, shard_poly=False, overlap=0):
     import datetime
 
     import torch.distributed as dist
@@ -92,7 +92,9 @@ def _column_worker(rank, world, port, m, n, steps, out_dir, shard_poly=False):
     x = make_input((m, n), seed=7)
     cols = column_range(n, rank, world)
     x_local = x[:, cols.start:cols.stop].contiguous()
-    driver = ColumnShardedPolar(m, "cpu", backend=CpuKernels(), shard_poly=shard_poly)
+    driver = ColumnShardedPolar(m, "cpu", backend=CpuKernels(), shard_poly=shard_poly,
+                                overlap_bands=overlap)
+    assert len(driver.bands) == (min(overlap, driver.mp // 256) if overlap > 1 else 0)
     if shard_poly:
         # 2 ranks, Mp = 512: rank r computes polynomial rows [256 r, 256 r + 256)
         assert driver.poly_slab == (256 * rank, 256)
@@ -102,13 +104,18 @@ def _column_worker(rank, world, port, m, n, steps, out_dir, shard_poly=False):
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("m,n,steps,shard_poly", [(96, 200, 1, False), (130, 256, 2, False),
-                                                (300, 320, 2, True)])
-def test_column_sharded_two_ranks_match_single(tmp_path, m, n, steps, shard_poly):
+@pytest.mark.parametrize("m,n,steps,shard_poly,overlap", [(96, 200, 1, False, 0),
+                                                        (130, 256, 2, False, 0),
+                                                        (300, 320, 2, True, 0),
+                                                        (600, 640, 2, False, 3)])
+def test_column_sharded_two_ranks_match_single(tmp_path, m, n, steps, shard_poly, overlap):
+    """Two gloo ranks, each owning a column slab, against the single-process
+    dataflow; `overlap` runs the Gram in row bands, each band all-reduced
+    on its own."""
     ctx = mp.get_context("spawn")
     port = _free_port()
     procs = [ctx.Process(target=_column_worker,
-                         args=(r, 2, port, m, n, steps, str(tmp_path), shard_poly))
+                         args=(r, 2, port, m, n, steps, str(tmp_path), shard_poly, overlap))
              for r in range(2)]
     for p in procs:
         p.start()
@@ -125,6 +132,17 @@ def test_column_sharded_two_ranks_match_single(tmp_path, m, n, steps, shard_poly
     # only the fp32 order of the Gram sum differs from the single-process run
     assert float(d.max()) <= 2e-2 * steps
     assert float(d.mean()) <= 1e-4 * steps
+
+
+def test_gram_bands_cover_rows():
+    from muon_fusion_ascend950_b200.distributed import gram_bands
+
+    for mp_rows, bands in [(256, 4), (1024, 4), (8192, 4), (8192, 5), (2048, 3)]:
+        got = gram_bands(mp_rows, bands)
+        assert got[0][0] == 0 and sum(c for _, c in got) == mp_rows
+        assert all(b % 256 == 0 and c % 256 == 0 and c > 0 for b, c in got)
+        assert all(got[i][0] + got[i][1] == got[i + 1][0] for i in range(len(got) - 1))
+        assert len(got) == min(bands, mp_rows // 256)
 
 
 def _dying_worker(rank, world, port, out_dir):

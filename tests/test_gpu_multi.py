@@ -28,7 +28,7 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, m, n, steps, out_dir, shard_poly=False):
+def _worker(rank, world, port, m, n, steps, out_dir, shard_poly=False, overlap=0):
     import datetime
 
     import torch
@@ -48,7 +48,7 @@ def _worker(rank, world, port, m, n, steps, out_dir, shard_poly=False):
     x = make_input((m, n), seed=9)
     cols = column_range(n, rank, world)
     x_local = x[:, cols.start:cols.stop].contiguous().to(device)
-    driver = ColumnShardedPolar(m, device, shard_poly=shard_poly)
+    driver = ColumnShardedPolar(m, device, shard_poly=shard_poly, overlap_bands=overlap)
     assert (driver.poly_slab is not None) == shard_poly
     y = driver.run(x_local, COEFFICIENTS[:steps])
     torch.cuda.synchronize()
@@ -58,15 +58,18 @@ def _worker(rank, world, port, m, n, steps, out_dir, shard_poly=False):
 
 
 @pytest.mark.skipif(_gpus() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("m,n,steps,shard_poly", [(512, 4096, 1, False), (1024, 8192, 5, False),
-                                                (1024, 8192, 5, True)])
-def test_column_sharded_nccl_matches_single_gpu(tmp_path, m, n, steps, shard_poly):
+@pytest.mark.parametrize("m,n,steps,shard_poly,overlap", [(512, 4096, 1, False, 0),
+                                                        (1024, 8192, 5, False, 0),
+                                                        (1024, 8192, 5, True, 0),
+                                                        (1024, 8192, 5, True, 4)])
+def test_column_sharded_nccl_matches_single_gpu(tmp_path, m, n, steps, shard_poly, overlap):
     import muon_fusion_ascend950_b200 as pkg
     from oracle.polar_oracle import COEFFICIENTS, error_stats, make_input, reference_formula
 
     ctx = mp.get_context("spawn")
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, m, n, steps, str(tmp_path), shard_poly))
+    procs = [ctx.Process(target=_worker,
+                         args=(r, 2, port, m, n, steps, str(tmp_path), shard_poly, overlap))
              for r in range(2)]
     for p in procs:
         p.start()

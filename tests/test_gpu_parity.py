@@ -407,3 +407,30 @@ def test_torch_compile_matches_eager(op, cuda_device):
     y_e = f(x)
     torch.cuda.synchronize()
     assert torch.equal(y_c.view(torch.int16), y_e.view(torch.int16))
+
+
+@pytest.mark.parametrize("shape,bands", [((1, 1024, 4096), 3), ((2, 768, 2048), 3),
+                                         ((1, 2048, 1024), 4)])
+@pytest.mark.parametrize("reserve", [0, 16])
+def test_gram_f32_bands_assemble_the_gram(api, cuda_device, shape, bands, reserve):
+    """Band by band from row 0, each band's rows are complete right after its
+    call, and the last band leaves the fp32 Gram of muon_polar_gram_f32_sm100
+    (split-K off on both sides: same tiles, same K order, same bits)."""
+    from muon_fusion_ascend950_b200.distributed import gram_bands
+
+    bsz, m, n = shape
+    x = make_input(shape, seed=51).to(cuda_device)
+    mp = api.padded_rows(m)
+    full = torch.empty((bsz, mp, mp), dtype=torch.float32, device=cuda_device)
+    banded = torch.full_like(full, float("nan"))
+    prev = api.lib.muon_polar_set_split_mode(2)
+    try:
+        api.gram_f32(x, full)
+        for begin, count in gram_bands(mp, bands):
+            api.gram_f32_band(x, banded, begin, count, reserve)
+            torch.cuda.synchronize()
+            rows = slice(0, begin + count)
+            assert torch.equal(banded[:, rows], full[:, rows]), (begin, count)
+    finally:
+        api.lib.muon_polar_set_split_mode(prev)
+    assert torch.equal(banded, full)
