@@ -880,7 +880,9 @@ constexpr int kMaxFusedSteps = 8;
 struct FusedParams {
   int32_t batch;
   int32_t d2;           // Mp / 256: row blocks of a region
-  int32_t regions;      // d2 (d2 + 1): Gram / polynomial regions per matrix
+  int32_t regions;      // Gram / polynomial items per matrix: d2 (d2 + 1)
+                        // regions, or d2 (d2 + 1) / 2 wide 256 x 256 tiles
+                        // (polar_fused_kernel<true>)
   int32_t apply_tn;     // ceil(n / 256)
   int32_t n_gram;       // batch * regions
   int32_t n_poly;       // batch * regions
@@ -923,6 +925,7 @@ struct FusedItem {
   int kind, b, tm, tn, k_blocks, step;
 };
 
+template <bool WIDE>
 __device__ __forceinline__ FusedItem fused_item(int w_all, const FusedParams& p) {
   FusedItem it;
   it.step = w_all / p.per_step;
@@ -934,14 +937,23 @@ __device__ __forceinline__ FusedItem fused_item(int w_all, const FusedParams& p)
     r = w < p.n_gram ? w : w - p.n_gram;
     it.b = r / p.regions;
     r -= it.b * p.regions;
-    // row I holds regions (I, 2I .. 2 d2 - 1)
     int tm = 0;
-    while (r >= 2 * p.d2 - 2 * tm) {
-      r -= 2 * p.d2 - 2 * tm;
-      ++tm;
+    if (WIDE) {
+      // row I holds tiles (I, I .. d2 - 1)
+      while (r >= p.d2 - tm) {
+        r -= p.d2 - tm;
+        ++tm;
+      }
+      it.tn = tm + r;
+    } else {
+      // row I holds regions (I, 2I .. 2 d2 - 1)
+      while (r >= 2 * p.d2 - 2 * tm) {
+        r -= 2 * p.d2 - 2 * tm;
+        ++tm;
+      }
+      it.tn = 2 * tm + r;
     }
     it.tm = tm;
-    it.tn = 2 * tm + r;
   } else {
     it.kind = kFApply;
     it.k_blocks = p.kb_apply;
@@ -991,6 +1003,9 @@ struct FusedCfg {
   static constexpr uint32_t kSymA = kHalf * 128 * 2;                // 32 KiB
   static constexpr uint32_t kSymB = 64 * 128 * 2;                   // 16 KiB
   static constexpr uint32_t kSymStage = kSymA + kSymB;
+  static constexpr uint32_t kSymBW = 128 * 128 * 2;                 // 32 KiB, wide tiles
+  static constexpr uint32_t kSymStageW = kSymA + kSymBW;            // 64 KiB
+  static constexpr int kSymStagesW = 3;
   static constexpr uint32_t kApA = kHalf * kAtom * 2;               // 16 KiB
   static constexpr uint32_t kApB = kAtom * kHalf * 2;               // 16 KiB
   static constexpr uint32_t kApStage = kApA + kApB;
@@ -1002,6 +1017,7 @@ struct FusedCfg {
   static constexpr uint32_t kSmemBytes = 1024 + kEpiBytes + kRingBytes + 256;
   static constexpr uint32_t kTmemCols = 2 * kPairN;
   static_assert(kApAux + 4 * kRegionBytes <= kRingBytes, "apply layout");
+  static_assert(kSymStagesW * kSymStageW <= kRingBytes, "wide layout");
   static_assert(kSmemBytes <= 232448, "shared memory budget");
 };
 
@@ -1046,6 +1062,7 @@ struct FusedRing {
   uint32_t parity;  // bit s: phases of stage s used so far, mod 2
 };
 
+template <bool WIDE>
 __global__ void __launch_bounds__(kTileThreads, 1)
     polar_fused_kernel(const __grid_constant__ FusedMaps maps, const FusedParams p) {
   using Cfg = FusedCfg;
@@ -1124,7 +1141,7 @@ __global__ void __launch_bounds__(kTileThreads, 1)
       uint32_t aux_wait = 0;
       bool ok = true;
       for (int w = cluster; ok && w < p.total; w += nclusters, ++t) {
-        const FusedItem item = fused_item(w, p);
+        const FusedItem item = fused_item<WIDE>(w, p);
         const bool ap = item.kind == kFApply;
         const int layout = ap ? 2 : 1;
         if (layout != ring.layout) {
@@ -1135,11 +1152,12 @@ __global__ void __launch_bounds__(kTileThreads, 1)
           }
           if (!ap && ring.layout == 2) aux_wait = t;
           ring.layout = layout;
-          ring.stages = ap ? Cfg::kApStages : Cfg::kSymStages;
+          ring.stages = ap ? Cfg::kApStages : (WIDE ? Cfg::kSymStagesW : Cfg::kSymStages);
           ring.pos = 0;
         }
         started = static_cast<int>(t) + 1;
-        const uint32_t stage_bytes = ap ? Cfg::kApStage : Cfg::kSymStage;
+        const uint32_t stage_bytes =
+            ap ? Cfg::kApStage : (WIDE ? Cfg::kSymStageW : Cfg::kSymStage);
         const uint32_t a_bytes = ap ? Cfg::kApA : Cfg::kSymA;
         const int a_row = item.tm * kPairM + static_cast<int>(rank) * kHalf;
         // Apply: X (B operand) of the first stages before the dependency
@@ -1215,13 +1233,18 @@ __global__ void __launch_bounds__(kTileThreads, 1)
             }
             if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * stage_bytes);
             const CUtensorMap* ma = item.kind == kFGram ? &maps.x_k[src] : &maps.a128;
-            const CUtensorMap* mb = item.kind == kFGram ? &maps.x_mn[src] : &maps.a64;
-            const int b_row = item.tn * kHalf + static_cast<int>(rank) * 64;
+            // B: this CTA's half of the item's columns -- 64 rows of a
+            // region, 128 of a wide tile (the same maps as A)
+            const CUtensorMap* mb =
+                WIDE ? ma : (item.kind == kFGram ? &maps.x_mn[src] : &maps.a64);
+            const int b_row = WIDE ? item.tn * kPairN + static_cast<int>(rank) * kHalf
+                                     : item.tn * kHalf + static_cast<int>(rank) * 64;
+            const uint32_t b_atom = WIDE ? kAtomBytes : 64 * 128;
 #pragma unroll
             for (int j = 0; j < 2; ++j) {
               tma_load_3d_pair(sa + j * kAtomBytes, ma, bar, kb * 128 + j * kAtom, a_row, item.b);
-              tma_load_3d_pair(sa + a_bytes + j * (64 * 128), mb, bar, kb * 128 + j * kAtom,
-                               b_row, item.b);
+              tma_load_3d_pair(sa + a_bytes + j * b_atom, mb, bar, kb * 128 + j * kAtom, b_row,
+                               item.b);
             }
           }
         }
@@ -1239,20 +1262,24 @@ __global__ void __launch_bounds__(kTileThreads, 1)
     if (lane == 0 && rank == 0) {
       // ---------------- tcgen05 MMA issuer (leader CTA only)
       constexpr uint32_t idesc_sym = idesc_bf16_f32(kHalf, 0u, kPairM);
+      constexpr uint32_t idesc_sym_w = idesc_bf16_f32(kPairN, 0u, kPairM);
       constexpr uint32_t idesc_ap = idesc_bf16_f32(kPairN, 1u, kPairM);
+      const uint32_t idesc_s = WIDE ? idesc_sym_w : idesc_sym;
+      const uint32_t b_atom = WIDE ? kAtomBytes : 64 * 128;
       FusedRing ring = {0, 0, 0, 0u};
       uint32_t t = 0;
       bool ok = true;
       for (int w = cluster; ok && w < p.total; w += nclusters, ++t) {
-        const FusedItem item = fused_item(w, p);
+        const FusedItem item = fused_item<WIDE>(w, p);
         const bool ap = item.kind == kFApply;
         const int layout = ap ? 2 : 1;
         if (layout != ring.layout) {
           ring.layout = layout;
-          ring.stages = ap ? Cfg::kApStages : Cfg::kSymStages;
+          ring.stages = ap ? Cfg::kApStages : (WIDE ? Cfg::kSymStagesW : Cfg::kSymStages);
           ring.pos = 0;
         }
-        const uint32_t stage_bytes = ap ? Cfg::kApStage : Cfg::kSymStage;
+        const uint32_t stage_bytes =
+            ap ? Cfg::kApStage : (WIDE ? Cfg::kSymStageW : Cfg::kSymStage);
         const uint32_t a_bytes = ap ? Cfg::kApA : Cfg::kSymA;
         const uint32_t acc = t & 1u;
         if (!mbar_wait_bounded(&tempty[acc], ((t >> 1) & 1u) ^ 1u)) {
@@ -1281,15 +1308,16 @@ __global__ void __launch_bounds__(kTileThreads, 1)
                              (kb > 0 || k > 0) ? 1u : 0u);
           } else {
             // K-major: step k lies in swizzle atom k/4 (A atoms of 128 rows,
-            // 16 KiB apart; B atoms of 64 rows, 8 KiB apart)
+            // 16 KiB apart; B atoms of 64 rows, 8 KiB apart, or of 128 rows
+            // for wide tiles)
 #pragma unroll
             for (int k = 0; k < 128 / 16; ++k)
               umma_bf16_pair(d_tmem,
                              smem_desc_sw128(a_base + (k / 4) * kAtomBytes + (k % 4) * 32, 16,
                                              1024),
-                             smem_desc_sw128(b_base + (k / 4) * (64 * 128) + (k % 4) * 32, 16,
+                             smem_desc_sw128(b_base + (k / 4) * b_atom + (k % 4) * 32, 16,
                                              1024),
-                             idesc_sym, (kb > 0 || k > 0) ? 1u : 0u);
+                             idesc_s, (kb > 0 || k > 0) ? 1u : 0u);
           }
           umma_commit_pair(map_to_cta(smem_addr(&empty[s]), 0));
           umma_commit_pair(map_to_cta(smem_addr(&empty[s]), 1));
@@ -1317,18 +1345,20 @@ __global__ void __launch_bounds__(kTileThreads, 1)
     // the same named barriers for every item, and after a failed wait it only
     // skips its waits, reads and stores (the watchdog word records why).
     bool failed = false;
-    // This CTA's 128-row block of a Gram / polynomial region against its
-    // column block: above the diagonal (stored with its mirror), on it
-    // (stored), or below it (not stored).
-    auto block_rel = [&](const FusedItem& it) {
+    // This CTA's 128-row block of a Gram / polynomial item against the
+    // 128-column block of chunk c: above the diagonal (stored with its
+    // mirror), on it (stored), or below it (not stored).  Along an item's
+    // chunks the relation never decreases.
+    auto chunk_rel = [&](const FusedItem& it, int c) {
       const int br = 2 * it.tm + static_cast<int>(rank);
-      return br < it.tn ? 1 : (br == it.tn ? 0 : -1);
+      const int bc = WIDE ? 2 * it.tn + (c >> 1) : it.tn;
+      return br < bc ? 1 : (br == bc ? 0 : -1);
     };
     // Leader: the epilogue tile of apply item w (X: no wait), into the
     // ring's apply tile area -- free once the previous item's MMAs and
     // stores are done with it.
     auto load_aux = [&](int w) {
-      const FusedItem item = fused_item(w, p);
+      const FusedItem item = fused_item<WIDE>(w, p);
       if (item.kind != kFApply) return;
       if (!fused_wait_x(item, p)) {
         atomicOr(&g_watchdog, MUON_POLAR_WATCHDOG_DEPENDENCY);
@@ -1356,21 +1386,27 @@ __global__ void __launch_bounds__(kTileThreads, 1)
     uint32_t t = 0;
     uint32_t aux_uses = 0;  // completed aux_full phases
     for (int w = cluster; w < p.total; w += nclusters, ++t) {
-      const FusedItem item = fused_item(w, p);
+      const FusedItem item = fused_item<WIDE>(w, p);
       const bool ap = item.kind == kFApply;
-      const int rel = ap ? 1 : block_rel(item);
+      // chunks [c_first, chunks) of this CTA's band are stored
+      const int chunks = (ap || WIDE) ? 4 : 2;
+      int c_first = 0;
+      if (!ap)
+        while (c_first < chunks && chunk_rel(item, c_first) < 0) ++c_first;
       const bool has_aux = ap;
       const uint32_t acc = t & 1u;
       ep.coef_b = p.coef[item.step][0];
       ep.coef_c = p.coef[item.step][1];
       ep.alpha = p.coef[item.step][2];
       const int row0 = item.tm * kPairM + static_cast<int>(rank) * kHalf;
-      const int col0 = item.tn * (ap ? kPairN : kHalf);
+      const int col0 = item.tn * ((ap || WIDE) ? kPairN : kHalf);
       // Polynomial: this thread's A values (row `row`, columns hc*32.. of
-      // each chunk) from global memory, requested before the accumulator is
-      // ready.  The Gram of the matrix is complete (acquired per warp).
+      // a chunk) from global memory, the first two chunks' requested before
+      // the accumulator is ready, chunk c + 2's once chunk c is done.  The
+      // Gram of the matrix is complete (acquired per warp).
       uint4 pa[2][4];
-      if (item.kind == kFPoly && rel >= 0 && !failed) {
+      const uint16_t* psrc = nullptr;
+      if (item.kind == kFPoly && c_first < chunks && !failed) {
         int dep = 1;
         if (lane == 0)
           dep = wait_counter_bounded(p.counters + item.b, fused_sym_done(p, item.step)) ? 1 : 0;
@@ -1379,14 +1415,17 @@ __global__ void __launch_bounds__(kTileThreads, 1)
           if (lane == 0) atomicOr(&g_watchdog, MUON_POLAR_WATCHDOG_DEPENDENCY);
           failed = true;
         } else {
-          const uint16_t* src = p.gram +
-                                (static_cast<size_t>(item.b) * p.mp + row0 + row) * p.mp + col0 +
-                                hc * 32;
+          psrc = p.gram + (static_cast<size_t>(item.b) * p.mp + row0 + row) * p.mp + col0 +
+                 hc * 32;
+          // (constant indices into pa: it stays in registers)
 #pragma unroll
-          for (int c = 0; c < 2; ++c)
+          for (int c = 0; c < 4; ++c) {
+            if (c >= c_first && c < c_first + 2 && c < chunks) {
 #pragma unroll
-            for (int u = 0; u < 4; ++u)
-              pa[c][u] = __ldcg(reinterpret_cast<const uint4*>(src + c * kChunkCols + u * 8));
+              for (int u = 0; u < 4; ++u)
+                pa[c & 1][u] = __ldcg(reinterpret_cast<const uint4*>(psrc + c * kChunkCols + u * 8));
+            }
+          }
         }
       }
       int ok = failed ? 0 : 1;
@@ -1405,27 +1444,31 @@ __global__ void __launch_bounds__(kTileThreads, 1)
       }
       tc_fence_after();
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * kPairN;
-      const bool store = rel >= 0;
-      const bool mirror = !ap && rel > 0;
       const CUtensorMap* m_out = item.kind == kFGram   ? &maps.a128
                                  : item.kind == kFPoly ? &maps.p128
                                                        : &maps.y128[fused_dst(item.step, p.steps)];
       const CUtensorMap* m_mir = item.kind == kFGram ? &maps.a64 : &maps.p64;
-      const int chunks = !store ? 0 : (ap ? kPairN / kChunkCols : kHalf / kChunkCols);
-      if (chunks == 0) release_accumulator(acc);
+      if (c_first >= chunks) release_accumulator(acc);
       // Accumulator chunk c + 1 is read from tensor memory while chunk c is
       // processed.  Apply: chunk c in place of its X chunk in the tile area.
       // Gram / polynomial: output chunk in region 0, mirror chunk in region
       // 1, reused by chunk 1 once chunk 0's stores have read them.
       const uint32_t aux_base = smem_addr(sAux);
       uint32_t rbuf[2][32];
-      if (chunks > 0 && !failed) tmem_ld_32x32b_x32(t_row + hc * 32, rbuf[0]);
+      if (c_first < chunks && !failed) {
+        if (c_first & 1)
+          tmem_ld_32x32b_x32(t_row + c_first * kChunkCols + hc * 32, rbuf[1]);
+        else
+          tmem_ld_32x32b_x32(t_row + c_first * kChunkCols + hc * 32, rbuf[0]);
+      }
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
+        if (c < c_first) continue;
         if (c >= chunks) break;
+        const bool mirror = !ap && chunk_rel(item, c) > 0;
         const uint32_t out = ap ? aux_base + c * Cfg::kRegionBytes : reg_base;
         const uint32_t mir = reg_base + Cfg::kRegionBytes;
-        if (!ap && c > 0) {
+        if (!ap && c > c_first) {
           if (leader) bulk_wait_group_read<0>();
           named_barrier(1, kPairEpiThreads);
         }
@@ -1445,6 +1488,12 @@ __global__ void __launch_bounds__(kTileThreads, 1)
             fused_poly_half(ep, out, mir, mirror, row, hc, v, pa[c & 1]);
           else
             pair_epilogue_half<kApply>(ep, out, mir, false, row, hc, v);
+          if (item.kind == kFPoly && psrc != nullptr && c + 2 < chunks) {
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+              pa[c & 1][u] =
+                  __ldcg(reinterpret_cast<const uint4*>(psrc + (c + 2) * kChunkCols + u * 8));
+          }
         }
         fence_proxy_async_smem();
         named_barrier(1, kPairEpiThreads);
@@ -2251,7 +2300,11 @@ FusedDeviceState g_fused_state[kMaxDevices];
 int fused_capacity(DeviceState* st, int dev, int* capacity) {
   FusedDeviceState& fs = g_fused_state[dev];
   std::call_once(fs.once, [&fs, st] {
-    fs.err = cudaFuncSetAttribute(polar_fused_kernel,
+    fs.err = cudaFuncSetAttribute(polar_fused_kernel<false>,
+                                  cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  FusedCfg::kSmemBytes);
+    if (fs.err != cudaSuccess) return;
+    fs.err = cudaFuncSetAttribute(polar_fused_kernel<true>,
                                   cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   FusedCfg::kSmemBytes);
     if (fs.err != cudaSuccess) return;
@@ -2267,7 +2320,8 @@ int fused_capacity(DeviceState* st, int dev, int* capacity) {
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     int clusters = 0;
-    if (cudaOccupancyMaxActiveClusters(&clusters, polar_fused_kernel, &cfg) != cudaSuccess ||
+    if (cudaOccupancyMaxActiveClusters(&clusters, polar_fused_kernel<false>, &cfg) !=
+            cudaSuccess ||
         clusters <= 0) {
       (void)cudaGetLastError();
       clusters = st->sms / 2;
@@ -2307,7 +2361,17 @@ int fused_steps_impl(const void* x, void* y, void* const* buf, int64_t ldb, void
   if (rc != MUON_POLAR_OK) return rc;
   const int64_t mp = padded_rows(m);
   const int64_t d2 = mp / kPairM;
-  const int64_t regions = d2 * (d2 + 1);
+  const int64_t regions_r = d2 * (d2 + 1);  // 256 x 128 regions per matrix
+  const int64_t regions_w = regions_r / 2;  // 256 x 256 tiles per matrix
+  // Item shape of the Gram and the polynomial.  Wide tiles halve the items
+  // but run a 3-stage ring and a 4-chunk epilogue; measured on B200 (five
+  // steps in one launch) they win only when regions would take about three
+  // rounds of the pairs: [32,512,2048] 418.5 -> 403.7 us, [16,768,3072]
+  // 565.8 -> 529.6 us, [32,384,1024] even; and lose at two rounds:
+  // [16,512,2048] 231.5 -> 261.8 us, [8,768,3072] 296.6 -> 327.3 us,
+  // [64,256,1024] 203.2 -> 207.6 us.
+  const bool wide = 2 * batch * regions_r >= 5 * static_cast<int64_t>(capacity);
+  const int64_t regions = wide ? regions_w : regions_r;
   const int64_t tn = (n + kPairN - 1) / kPairN;
   const int64_t per_step = 2 * batch * regions + batch * d2 * tn;
   if (per_step * steps > INT32_MAX) return MUON_POLAR_OK;
@@ -2317,7 +2381,7 @@ int fused_steps_impl(const void* x, void* y, void* const* buf, int64_t ldb, void
   // [64,256,1024] -- and loses where the three kernels run a Gram of one
   // round (config 1 [8,512,2048]: 38.5 vs 36.8 us) or a large one on 256 x
   // 256 pair tiles (Mp >= 1024, N >= 4096: up to 12% slower).
-  if (mode == 0 && !(batch * regions > capacity && mp <= 768)) return MUON_POLAR_OK;
+  if (mode == 0 && !(batch * regions_r > capacity && mp <= 768)) return MUON_POLAR_OK;
 
   FusedMaps maps;
   // X of each step and Y: the input / output and the two buffers
@@ -2383,7 +2447,8 @@ int fused_steps_impl(const void* x, void* y, void* const* buf, int64_t ldb, void
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
-  e = cudaLaunchKernelEx(&cfg, polar_fused_kernel, maps, p);
+  e = wide ? cudaLaunchKernelEx(&cfg, polar_fused_kernel<true>, maps, p)
+           : cudaLaunchKernelEx(&cfg, polar_fused_kernel<false>, maps, p);
   if (e != cudaSuccess) return static_cast<int>(e);
   g_launch_count.fetch_add(1, std::memory_order_relaxed);
   *done = true;
