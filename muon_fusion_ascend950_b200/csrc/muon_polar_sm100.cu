@@ -846,7 +846,7 @@ __global__ void __launch_bounds__(kTileThreads, 1)
 // index order, so every wait ends.  The last CTA to exit resets the
 // counters, so each launch starts from zero.
 //
-// Two tile shapes, both cta_group::2 (M = 256):
+// Tile shapes, all cta_group::2 (M = 256):
 //  * Gram and polynomial items: 256 x 128 regions (N = 128).  A region
 //    (I, j) covers 128-row blocks 2I and 2I+1 against 128-column block j,
 //    j >= 2I: every block on or above the diagonal exactly once (block
@@ -854,10 +854,15 @@ __global__ void __launch_bounds__(kTileThreads, 1)
 //    (2I, 2I+1) writes it).  Per SM a 128 x 128 x 16 MMA reads 6 KiB of
 //    shared memory (A: 128 rows, B: 64 rows) instead of the single-CTA
 //    engine's 8 KiB, and twice as many SMs work on the Gram.
+//  * Or (polar_fused_kernel<true>, when regions would take about three
+//    rounds of the pairs) 256 x 256 tiles (N = 256) of the upper triangle:
+//    half as many items; the blocks below the diagonal of a diagonal tile
+//    are computed and not stored.
 //  * Apply items: 256 x 256 tiles (N = 256), as the apply kernel.
 // The stage ring (192 KiB) is cut per item kind: four 48 KiB stages of
-// K = 128 for Gram/polynomial items; four 32 KiB stages of K = 64 for apply
-// items, whose epilogue tile (X, 64 KiB) takes the rest of the ring.  At a
+// K = 128 for regions (three 64 KiB ones for wide tiles); four 32 KiB
+// stages of K = 64 for apply items, whose epilogue tile (X, 64 KiB) takes
+// the rest of the ring.  At a
 // change of layout the producers wait until the previous item's MMAs have
 // completed (its accumulator barrier), then restart the ring; each stage's
 // barriers keep their own phase.  The Gram / polynomial epilogue stages its
