@@ -324,8 +324,9 @@ int muon_polar_set_kernel_policy(int policy);
 /* How muon_polar_step_sm100 runs a step, process-wide; returns the previous
  * mode (or MUON_POLAR_ERR_INVALID_ARGUMENT).
  *   0  by size (default): one fused launch for many small matrices (more
- *      256 x 128 Gram regions than CTA pairs, and muon_polar_padded_rows(m)
- *      <= 768), where it measured 4-21% faster on B200; else three kernels;
+ *      256 x 128 Gram regions than CTA pairs, at most three times as many,
+ *      and muon_polar_padded_rows(m) <= 768), where it measured 4-21% faster
+ *      on B200; else three kernels;
  *   1  one fused persistent launch for all three stages, with per-matrix
  *      dependencies tracked in the scratch counter area (needs scratch);
  *   2  always three kernels.

@@ -2380,13 +2380,18 @@ int fused_steps_impl(const void* x, void* y, void* const* buf, int64_t ldb, void
   const int64_t tn = (n + kPairN - 1) / kPairN;
   const int64_t per_step = 2 * batch * regions + batch * d2 * tn;
   if (per_step * steps > INT32_MAX) return MUON_POLAR_OK;
-  // By size, from measurements on B200 (muon_polar_step_sm100, 15 shapes):
-  // the fused launch wins for many small matrices -- more Gram regions than
-  // pairs and Mp <= 768: 4-21% faster at [16|32,512,2048], [8|16,768,3072],
+  // By size, from measurements on B200 (muon_polar_step_sm100, 15 shapes;
+  // muon_polar_steps_sm100, 7 more): the fused launch wins for many small
+  // matrices -- more Gram regions than pairs, up to three rounds of them, and
+  // Mp <= 768: 4-21% faster at [16|32,512,2048], [8,768,3072],
   // [64,256,1024] -- and loses where the three kernels run a Gram of one
-  // round (config 1 [8,512,2048]: 38.5 vs 36.8 us) or a large one on 256 x
-  // 256 pair tiles (Mp >= 1024, N >= 4096: up to 12% slower).
-  if (mode == 0 && !(batch * regions_r > capacity && mp <= 768)) return MUON_POLAR_OK;
+  // round (config 1 [8,512,2048]: 38.5 vs 36.8 us), a large one on 256 x
+  // 256 pair tiles (Mp >= 1024, N >= 4096: up to 12% slower) or many rounds
+  // of items (five steps at [64,512,2048]: 896 vs 740 us).
+  const int64_t sym_items = batch * regions_r;
+  if (mode == 0 && !(sym_items > capacity && sym_items <= 3 * static_cast<int64_t>(capacity) &&
+                     mp <= 768))
+    return MUON_POLAR_OK;
 
   FusedMaps maps;
   // X of each step and Y: the input / output and the two buffers

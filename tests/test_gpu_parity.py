@@ -371,7 +371,8 @@ def test_fused_step_matches_three_kernels(api, cuda_device, shape, step_mode):
 
 
 @pytest.mark.parametrize("shape,fused", [((16, 512, 2048), True), ((64, 256, 1024), True),
-                                         ((8, 512, 2048), False), ((4, 1024, 4096), False)])
+                                         ((8, 512, 2048), False), ((4, 1024, 4096), False),
+                                         ((64, 512, 2048), False)])
 def test_step_by_size_choice(api, cuda_device, shape, fused, step_mode):
     """The default step mode picks one fused launch for many small matrices
     and three kernels otherwise, with the bits of the forced mode."""
