@@ -870,7 +870,8 @@ __global__ void __launch_bounds__(kTileThreads, 1)
 // reads its A tile (the b*A term) straight from global memory into
 // registers before its accumulator is ready.  An apply item's X operand and
 // epilogue tile do not depend on the polynomial: they are loaded before the
-// item waits for it.
+// item waits for it (in steps after the first, once X -- the previous
+// step's output for the matrix -- is complete).
 enum FusedKind : int { kFGram = 0, kFPoly = 1, kFApply = 2 };
 
 // Several Polar Express steps in one launch (muon_polar_express_sm100): the
@@ -2286,7 +2287,7 @@ int apply_t_impl(const void* poly, const void* x, void* y, int64_t batch, int64_
 }
 
 // ---------------------------------------------------------------- fused step
-// Step mode: 0 = by size (see step_fused_impl), 1 = always fused, 2 = three
+// Step mode: 0 = by size (see fused_steps_impl), 1 = always fused, 2 = three
 // kernels.  Initial value from MUON_POLAR_FUSED (1 -> 1, 0 -> 2).
 std::atomic<int> g_step_mode{[] {
   const char* s = std::getenv("MUON_POLAR_FUSED");
