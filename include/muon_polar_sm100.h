@@ -110,9 +110,8 @@ int muon_polar_gram_sm100(const void* x, void* gram, int64_t batch, int64_t m,
                           int64_t n, int64_t ldx, void* scratch,
                           size_t scratch_bytes, void* stream);
 
-/* Kernel (1) for callers that cannot allocate device memory.  No
- * counterpart in the reference, whose binding allocates its buffers with
- * at::empty on every call (binding.cpp:646-663).
+/* Kernel (1) for callers that cannot allocate device memory.  It has no
+ * counterpart in the reference.
  *
  * Some callers have no way to hand this library scratch memory: a plugin
  * or real-time host that works inside a fixed device-memory budget, code
@@ -121,20 +120,23 @@ int muon_polar_gram_sm100(const void* x, void* gram, int64_t batch, int64_t m,
  * or a hot path that must not call cudaMalloc/cudaFree because they can
  * synchronise the device.  For them this entry computes exactly what
  * muon_polar_gram_sm100 computes on its CTA-pair path with split-K -- same
- * tiles, same split plan, same reduction order -- but takes its split-K
- * scratch from an array compiled into the library
+ * tiles, same split plan, same reduction order, so the same bits -- but
+ * takes its split-K scratch from an array compiled into the library
  * (MUON_POLAR_STATIC_SCRATCH_BYTES per GPU, held until the process exits).
  * The caller still passes x and gram; nothing is allocated.
  *
  *  - The first call on each device looks up the array's device address
  *    (cudaGetSymbolAddress, with that device current); make that first call
- *    before starting any stream capture.
+ *    before starting any stream capture.  A lookup that fails is returned
+ *    as its cudaError_t and is tried again by the next call; only a
+ *    successful lookup is kept.
  *  - The array is shared by every call on a device and keeps the previous
  *    call's contents; each call clears the counter part itself
  *    (cudaMemsetAsync on `stream`).  Calls whose executions overlap on the
  *    GPU (different streams, not ordered) race on the array and produce
  *    wrong results: order them.
- *  - A problem whose split plan needs more than the array returns
+ *  - A problem whose split plan needs more than the array (or than the
+ *    budget set by muon_polar_set_static_scratch_limit) returns
  *    MUON_POLAR_ERR_STATIC_SCRATCH and launches nothing.
  * Arguments and layout as for muon_polar_gram_sm100. */
 int muon_polar_gram_static_scratch_sm100(const void* x, void* gram, int64_t batch,
@@ -352,6 +354,38 @@ int muon_polar_device_pairs(int* pairs);
 /* Number of kernels the library has launched in this process (all entry
  * points, all devices).  Used by benchmarks to report launch counts. */
 uint64_t muon_polar_launch_count(void);
+
+/* Sets the limit of every bounded wait inside this library's kernels on the
+ * current device (default 2 s): a wait that has not ended after `limit_ns`
+ * nanoseconds of wall-clock time gives up, sets its watchdog bit
+ * (muon_polar_read_device_status) and the kernel drains and returns.  The
+ * previous limit is stored in *previous (may be NULL).  1000 <= limit_ns <=
+ * 6e10.  Synchronous with respect to the host (cudaMemcpyToSymbol); call it
+ * while no kernel of this library runs on the device.  No counterpart in the
+ * reference, whose kernels have no bounded waits. */
+int muon_polar_set_wait_limit_ns(uint64_t limit_ns, uint64_t* previous);
+
+/* Budget of muon_polar_gram_static_scratch_sm100 in bytes of its built-in
+ * array, process-wide: plans needing more are refused with
+ * MUON_POLAR_ERR_STATIC_SCRATCH.  0 (or anything above the array's size)
+ * means the whole array, the default.  Returns the previous budget. */
+size_t muon_polar_set_static_scratch_limit(size_t bytes);
+
+/* Host-side checks (no GPU needed), used by the test suite.
+ *
+ * muon_polar_decode_tile: the work-item enumeration the kernels use, run on
+ *   the host: linear tile index -> out[0..2] = (batch, tile row, tile col).
+ *   symmetric != 0: the upper-triangle tiles (tm <= tn) of tile rows
+ *   first_row .. tiles_m - 1, row by row (tiles_per_batch of them; the
+ *   reference enumerates the same set, asc:129-146 and 609-630); else the
+ *   tiles_m x tiles_n grid in row-major order.
+ * muon_polar_check_address_cache: exercises the per-device address cache of
+ *   muon_polar_gram_static_scratch_sm100 with a stand-in lookup that fails
+ *   once and then succeeds; returns 0 when a failure was reported and not
+ *   kept, the retry succeeded and later calls reuse the cached address. */
+int muon_polar_decode_tile(int64_t tile, int symmetric, int64_t tiles_m, int64_t tiles_n,
+                           int64_t tiles_per_batch, int64_t first_row, int64_t* out);
+int muon_polar_check_address_cache(void);
 
 #ifdef __cplusplus
 }

@@ -77,12 +77,19 @@ SIGNATURES = {
     "muon_polar_set_split_mode": (ctypes.c_int, [ctypes.c_int]),
     "muon_polar_device_pairs": (ctypes.c_int, [ctypes.POINTER(ctypes.c_int)]),
     "muon_polar_launch_count": (ctypes.c_uint64, []),
+    "muon_polar_set_wait_limit_ns": (ctypes.c_int, [ctypes.c_uint64,
+                                                    ctypes.POINTER(ctypes.c_uint64)]),
+    "muon_polar_set_static_scratch_limit": (ctypes.c_size_t, [ctypes.c_size_t]),
+    "muon_polar_decode_tile": (ctypes.c_int, [_I64, ctypes.c_int, _I64, _I64, _I64, _I64,
+                                              ctypes.POINTER(_I64)]),
+    "muon_polar_check_address_cache": (ctypes.c_int, []),
 }
 
 WATCHDOG_PRODUCER = 0x1
 WATCHDOG_MMA = 0x2
 WATCHDOG_EPILOGUE = 0x4
 WATCHDOG_DRAIN = 0x8
+WATCHDOG_DEPENDENCY = 0x10
 
 
 class MuonPolarError(RuntimeError):
@@ -188,6 +195,32 @@ class CAPI:
                     self.lib.muon_polar_read_device_status(int(device), ctypes.byref(flags),
                                                            1 if clear else 0))
         return int(flags.value)
+
+    def set_wait_limit_ns(self, limit_ns: int) -> int:
+        """Limit of the kernels' bounded waits on the current device; returns
+        the previous limit."""
+        prev = ctypes.c_uint64(0)
+        self._check("muon_polar_set_wait_limit_ns",
+                    self.lib.muon_polar_set_wait_limit_ns(int(limit_ns), ctypes.byref(prev)))
+        return int(prev.value)
+
+    def set_static_scratch_limit(self, nbytes: int) -> int:
+        """Budget of gram_static_scratch in bytes of the built-in array (0:
+        all of it); returns the previous budget."""
+        return int(self.lib.muon_polar_set_static_scratch_limit(int(nbytes)))
+
+    def decode_tile(self, tile: int, symmetric: bool, tiles_m: int, tiles_n: int,
+                    tiles_per_batch: int, first_row: int = 0):
+        """(batch, tile row, tile col) of linear tile index `tile` in the
+        kernels' work-item order (host copy of the device enumeration)."""
+        out = (_I64 * 3)()
+        self._check("muon_polar_decode_tile", self.lib.muon_polar_decode_tile(
+            int(tile), 1 if symmetric else 0, int(tiles_m), int(tiles_n), int(tiles_per_batch),
+            int(first_row), out))
+        return int(out[0]), int(out[1]), int(out[2])
+
+    def check_address_cache(self) -> int:
+        return int(self.lib.muon_polar_check_address_cache())
 
     def scratch_bytes(self, batch: int, m: int, n: int) -> int:
         return int(self.lib.muon_polar_scratch_bytes(int(batch), int(m), int(n)))

@@ -1362,13 +1362,16 @@ __global__ void __launch_bounds__(kTileThreads, 1)
     };
     // Leader: the epilogue tile of apply item w (X: no wait), into the
     // ring's apply tile area -- free once the previous item's MMAs and
-    // stores are done with it.
+    // stores are done with it.  If X's wait gives up, nothing is loaded:
+    // the epilogue skips every later wait and load, so no copy is left in
+    // flight when the CTA exits.
     auto load_aux = [&](int w) {
       const FusedItem item = fused_item<WIDE>(w, p);
       if (item.kind != kFApply) return;
       if (!fused_wait_x(item, p)) {
         atomicOr(&g_watchdog, MUON_POLAR_WATCHDOG_DEPENDENCY);
         failed = true;
+        return;
       }
       mbar_arrive_expect_tx(aux_full, 4 * Cfg::kRegionBytes);
 #pragma unroll
@@ -2487,24 +2490,45 @@ static_assert(kStaticScratchBytes == MUON_POLAR_STATIC_SCRATCH_BYTES,
 static __device__ __align__(256) uint8_t g_static_scratch[kStaticScratchBytes];
 
 namespace {
-struct StaticScratchAddress {
-  std::once_flag once;
+// A device address looked up once per device.  Only a successful lookup is
+// kept: a failed one (say, made during a stream capture, or with another
+// error pending) is reported to that caller and tried again by the next.
+struct AddressSlot {
+  std::mutex mu;
   void* ptr = nullptr;
-  cudaError_t err = cudaSuccess;
 };
-StaticScratchAddress g_static_scratch_address[muon_sm100::kMaxDevices];
 
-// Device address of g_static_scratch on the current device `dev`, looked up
-// once per device (with that device current).
-int static_scratch_address(int dev, void** out) {
-  StaticScratchAddress& sa = g_static_scratch_address[dev];
-  std::call_once(sa.once, [&sa] {
-    sa.err = cudaGetSymbolAddress(&sa.ptr, g_static_scratch);
-  });
-  if (sa.err != cudaSuccess) return static_cast<int>(sa.err);
-  *out = sa.ptr;
+typedef cudaError_t (*AddressLookup)(void** out);
+
+int cached_address(AddressSlot& slot, AddressLookup lookup, void** out) {
+  std::lock_guard<std::mutex> lock(slot.mu);
+  if (slot.ptr == nullptr) {
+    void* p = nullptr;
+    const cudaError_t e = lookup(&p);
+    if (e != cudaSuccess || p == nullptr) {
+      (void)cudaGetLastError();  // leave no error behind for later calls
+      return e != cudaSuccess ? static_cast<int>(e) : MUON_POLAR_ERR_DRIVER;
+    }
+    slot.ptr = p;
+  }
+  *out = slot.ptr;
   return MUON_POLAR_OK;
 }
+
+cudaError_t lookup_static_scratch(void** out) {
+  return cudaGetSymbolAddress(out, g_static_scratch);
+}
+
+AddressSlot g_static_scratch_address[muon_sm100::kMaxDevices];
+
+// Device address of g_static_scratch on the current device `dev` (looked up
+// with that device current).
+int static_scratch_address(int dev, void** out) {
+  return cached_address(g_static_scratch_address[dev], lookup_static_scratch, out);
+}
+
+// Bytes of the array a plan may use (muon_polar_set_static_scratch_limit).
+std::atomic<size_t> g_static_scratch_limit{kStaticScratchBytes};
 
 int gram_static_scratch_impl(const void* x, void* gram, int64_t batch, int64_t m,
                              int64_t n, int64_t ldx, cudaStream_t stream) {
@@ -2523,7 +2547,8 @@ int gram_static_scratch_impl(const void* x, void* gram, int64_t batch, int64_t m
   // scratch; a plan that needs more than the static array is refused, and the
   // array's arrival counters (left as the previous call left them) are
   // cleared before the launch.
-  return gram_impl<kGramBf16>(x, gram, batch, m, n, ldx, scratch, kStaticScratchBytes, stream,
+  return gram_impl<kGramBf16>(x, gram, batch, m, n, ldx, scratch,
+                              g_static_scratch_limit.load(std::memory_order_relaxed), stream,
                               /*fixed_scratch=*/true);
 }
 }  // namespace
@@ -2855,6 +2880,76 @@ int muon_polar_device_pairs(int* pairs) {
 
 uint64_t muon_polar_launch_count(void) {
   return g_launch_count.load(std::memory_order_relaxed);
+}
+
+int muon_polar_set_wait_limit_ns(uint64_t limit_ns, uint64_t* previous) {
+  if (limit_ns < 1000ull || limit_ns > 60000000000ull) return MUON_POLAR_ERR_INVALID_ARGUMENT;
+  DeviceState* st = nullptr;
+  int rc = current_device_state(&st);
+  if (rc != MUON_POLAR_OK) return rc;
+  uint64_t old = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&old, g_wait_limit_ns, sizeof(old));
+  if (e == cudaSuccess) e = cudaMemcpyToSymbol(g_wait_limit_ns, &limit_ns, sizeof(limit_ns));
+  if (e != cudaSuccess) return static_cast<int>(e);
+  if (previous != nullptr) *previous = old;
+  return MUON_POLAR_OK;
+}
+
+size_t muon_polar_set_static_scratch_limit(size_t bytes) {
+  const size_t v = (bytes == 0 || bytes > kStaticScratchBytes) ? kStaticScratchBytes : bytes;
+  return g_static_scratch_limit.exchange(v);
+}
+
+int muon_polar_decode_tile(int64_t tile, int symmetric, int64_t tiles_m, int64_t tiles_n,
+                           int64_t tiles_per_batch, int64_t first_row, int64_t* out) {
+  if (out == nullptr || tile < 0 || tiles_m <= 0 || tiles_n <= 0 || tiles_per_batch <= 0 ||
+      first_row < 0 || first_row >= tiles_m || tile > INT32_MAX || tiles_m > INT32_MAX ||
+      tiles_n > INT32_MAX || tiles_per_batch > INT32_MAX)
+    return MUON_POLAR_ERR_INVALID_ARGUMENT;
+  if (symmetric) {
+    // the tiles (tm, tn >= tm) of rows first_row .. tiles_m - 1
+    const int64_t rows = tiles_m - first_row;
+    if (tiles_per_batch > rows * (rows + 1) / 2) return MUON_POLAR_ERR_INVALID_ARGUMENT;
+  } else if (tiles_per_batch != tiles_m * tiles_n) {
+    return MUON_POLAR_ERR_INVALID_ARGUMENT;
+  }
+  const TileCoord t = decode_tile(static_cast<int>(tile), symmetric != 0,
+                                  static_cast<int>(tiles_m), static_cast<int>(tiles_n),
+                                  static_cast<int>(tiles_per_batch), static_cast<int>(first_row));
+  out[0] = t.b;
+  out[1] = t.tm;
+  out[2] = t.tn;
+  return MUON_POLAR_OK;
+}
+
+namespace {
+int g_fake_lookups = 0;
+cudaError_t fake_lookup_fails_once(void** out) {
+  static char target;
+  if (g_fake_lookups++ == 0) return cudaErrorStreamCaptureUnsupported;
+  *out = &target;
+  return cudaSuccess;
+}
+}  // namespace
+
+int muon_polar_check_address_cache(void) {
+  AddressSlot slot;
+  g_fake_lookups = 0;
+  void* p = nullptr;
+  // 1: the first lookup fails and is reported; nothing is cached
+  if (cached_address(slot, fake_lookup_fails_once, &p) != cudaErrorStreamCaptureUnsupported ||
+      p != nullptr || slot.ptr != nullptr)
+    return 1;
+  // 2: the next call looks up again and succeeds
+  if (cached_address(slot, fake_lookup_fails_once, &p) != MUON_POLAR_OK || p == nullptr ||
+      g_fake_lookups != 2)
+    return 2;
+  // 3: a later call uses the cached address without another lookup
+  void* q = nullptr;
+  if (cached_address(slot, fake_lookup_fails_once, &q) != MUON_POLAR_OK || q != p ||
+      g_fake_lookups != 2)
+    return 3;
+  return 0;
 }
 
 }  // extern "C"

@@ -13,9 +13,13 @@
 namespace muon_sm100 {
 
 // A bounded wait gives up after this many nanoseconds of %globaltimer.  No
-// legitimate wait in these kernels is longer than a few microseconds; two
-// seconds only ever trips on a real deadlock.
-constexpr uint64_t kWaitLimitNs = 2000000000ull;
+// legitimate wait in these kernels is longer than a few microseconds; the
+// default of two seconds only ever trips on a real deadlock.  The host may
+// change it per device (muon_polar_set_wait_limit_ns), e.g. to make a test's
+// wait on a flag that nothing sets give up quickly.  Each translation unit
+// has its own copy; the one the host sets is muon_polar_sm100.cu's.
+constexpr uint64_t kDefaultWaitLimitNs = 2000000000ull;
+static __device__ uint64_t g_wait_limit_ns = kDefaultWaitLimitNs;
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -64,7 +68,7 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Waits until the phase with the given parity has completed.  Returns false
-// (and waits no longer) once kWaitLimitNs of wall-clock time have passed.
+// (and waits no longer) once g_wait_limit_ns of wall-clock time have passed.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar,
                                                   uint32_t parity) {
   if (mbar_try_wait(bar, parity)) return true;
@@ -72,7 +76,7 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar,
   uint32_t spins = 0;
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((++spins & 63u) == 0u && global_timer_ns() - t0 > kWaitLimitNs)
+    if ((++spins & 63u) == 0u && global_timer_ns() - t0 > g_wait_limit_ns)
       return false;
   }
 }
@@ -163,25 +167,25 @@ __device__ __forceinline__ uint32_t ld_acquire_cta_shared(uint32_t addr) {
   return v;
 }
 // Waits until *p >= target (written by other CTAs with release semantics).
-// Returns false once kWaitLimitNs of wall-clock time have passed.
+// Returns false once g_wait_limit_ns of wall-clock time have passed.
 __device__ __forceinline__ bool wait_counter_bounded(const uint32_t* p, uint32_t target) {
   if (ld_acquire_gpu(p) >= target) return true;
   const uint64_t t0 = global_timer_ns();
   while (true) {
     __nanosleep(64);
     if (ld_acquire_gpu(p) >= target) return true;
-    if (global_timer_ns() - t0 > kWaitLimitNs) return false;
+    if (global_timer_ns() - t0 > g_wait_limit_ns) return false;
   }
 }
 // Waits until the shared counter at `addr` is >= target; false after
-// kWaitLimitNs.
+// g_wait_limit_ns.
 __device__ __forceinline__ bool wait_shared_bounded(uint32_t addr, uint32_t target) {
   if (ld_acquire_cta_shared(addr) >= target) return true;
   const uint64_t t0 = global_timer_ns();
   while (true) {
     __nanosleep(32);
     if (ld_acquire_cta_shared(addr) >= target) return true;
-    if (global_timer_ns() - t0 > kWaitLimitNs) return false;
+    if (global_timer_ns() - t0 > g_wait_limit_ns) return false;
   }
 }
 // Named barrier over `count` threads (id 0 is __syncthreads).

@@ -10,7 +10,7 @@ module as a whole calls ``pytest.importorskip("torch_npu")`` at import time.
 Usage (build container only; the reference tree is not present on GPU
 boxes, which use the committed .npz):
 
-    python tests/golden/make_golden.py [path/to/reference/tests/test_polar_step.py]
+    python tests/golden/make_golden.py <reference>/tests/test_polar_step.py
 """
 from __future__ import annotations
 
@@ -28,7 +28,9 @@ sys.path.insert(0, str(REPO))
 
 from oracle.polar_oracle import make_input  # noqa: E402
 
-DEFAULT_SOURCE = Path("/root/reference/tests/test_polar_step.py")
+# The reference test file: first command-line argument, else the
+# MUON_REFERENCE_TEST environment variable (no default path).
+SOURCE_ENV = "MUON_REFERENCE_TEST"
 
 # (name, shape, seed, number of Polar Express steps)
 CASES = (
@@ -64,7 +66,13 @@ def bits(t: torch.Tensor) -> np.ndarray:
 
 
 def main() -> None:
-    source = Path(sys.argv[1]) if len(sys.argv) > 1 else DEFAULT_SOURCE
+    import os
+
+    arg = sys.argv[1] if len(sys.argv) > 1 else os.environ.get(SOURCE_ENV)
+    if not arg:
+        raise SystemExit(f"usage: make_golden.py <reference tests/test_polar_step.py> "
+                         f"(or set {SOURCE_ENV})")
+    source = Path(arg)
     reference, coefficients = load_reference_oracle(source)
     arrays = {}
     meta = {"source": "tests/test_polar_step.py:_reference", "torch": torch.__version__,

@@ -185,3 +185,74 @@ def test_gram_band_validation_without_device(api):
     assert call(512, 512) == -1      # past Mp = 768
     assert call(-256, 256) == -1
     assert call(0, 256, reserve=-1) == -1
+
+
+# ---------------------------------------------------------------- host logic
+@pytest.mark.parametrize("d", [1, 2, 3, 4, 7, 16, 32])
+def test_kernel_tile_enumeration_matches_oracle(api, d):
+    """The kernels' symmetric work-item order (decode_tile, run on the host)
+    visits exactly the oracle's upper-triangle tiles, in its row-major order,
+    matrix after matrix (the set the reference enumerates, asc:129-146)."""
+    from oracle.polar_oracle import upper_tiles
+
+    per = d * (d + 1) // 2
+    expected = upper_tiles(d)
+    for batch in (1, 3):
+        got = [api.decode_tile(t, True, d, d, per) for t in range(per * batch)]
+        assert got == [(b, tm, tn) for b in range(batch) for tm, tn in expected]
+
+
+@pytest.mark.parametrize("d,first,rows", [(4, 1, 2), (8, 3, 5), (8, 0, 8), (6, 5, 1)])
+def test_kernel_band_enumeration_matches_oracle(api, d, first, rows):
+    """A band of tile rows [first, first + rows): the upper tiles of those
+    rows, in the oracle's order (the row-band Gram of the column-sharded
+    driver)."""
+    from oracle.polar_oracle import upper_tiles
+
+    expected = [(tm, tn) for tm, tn in upper_tiles(d) if first <= tm < first + rows]
+    per = len(expected)
+    assert per == rows * d - (2 * first + rows - 1) * rows // 2
+    got = [api.decode_tile(t, True, d, d, per, first) for t in range(2 * per)]
+    assert got == [(b, tm, tn) for b in range(2) for tm, tn in expected]
+
+
+def test_kernel_grid_enumeration(api):
+    got = [api.decode_tile(t, False, 3, 5, 15) for t in range(30)]
+    assert got == [(b, r, c) for b in range(2) for r in range(3) for c in range(5)]
+
+
+def test_tile_decoder_rejects_bad_arguments(api):
+    from muon_fusion_ascend950_b200.capi import MuonPolarError
+
+    with pytest.raises(MuonPolarError):
+        api.decode_tile(-1, True, 4, 4, 10)
+    with pytest.raises(MuonPolarError):
+        api.decode_tile(0, True, 4, 4, 11)  # more tiles than the triangle holds
+    with pytest.raises(MuonPolarError):
+        api.decode_tile(0, False, 3, 5, 14)
+
+
+def test_static_scratch_address_cache_keeps_only_success(api):
+    """A failed device-address lookup is reported and not cached; the next
+    call looks up again, and a success is reused without a new lookup."""
+    assert api.check_address_cache() == 0
+
+
+def test_static_scratch_limit_setter(api):
+    full = 1024 + 80 * 262144
+    prev = api.set_static_scratch_limit(4096)
+    try:
+        assert prev == full
+        assert api.set_static_scratch_limit(0) == 4096
+        assert api.set_static_scratch_limit(10 * full) == full  # clamped to the array
+    finally:
+        api.set_static_scratch_limit(prev)
+    assert api.set_static_scratch_limit(0) == full
+
+
+def test_wait_limit_setter_validation_without_device(api):
+    from muon_fusion_ascend950_b200.capi import MuonPolarError
+
+    for bad in (0, 999, 60_000_000_001):
+        with pytest.raises(MuonPolarError):
+            api.set_wait_limit_ns(bad)

@@ -15,6 +15,18 @@ def test_drop_in_alias():
     assert pkg.__version__ == "0.1.1"
 
 
+def test_drop_in_alias_submodules():
+    """The reference's module paths (muon_ascend950/ops.py, _loader.py)
+    resolve to this build's modules of the same role."""
+    import importlib
+
+    ops = importlib.import_module("muon_ascend950.ops")
+    loader = importlib.import_module("muon_ascend950._loader")
+    assert ops is pkg.ops and ops.polar_step is pkg.polar_step
+    assert loader.load_library is pkg.load_library
+    from muon_ascend950.ops import polar_step  # noqa: F401  (the reference's import form)
+
+
 def test_rejects_non_tensor():
     with pytest.raises(TypeError):
         pkg.polar_step([[1.0]], 1.0, 1.0, 1.0)

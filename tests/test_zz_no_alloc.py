@@ -1,28 +1,32 @@
 """GPU test of muon_polar_gram_static_scratch_sm100, the Gram entry point for
-callers that cannot allocate device memory (its split-K scratch is an array
-built into the library instead of a caller buffer).
+callers that cannot allocate device memory: a plugin inside a fixed memory
+budget, code next to a framework allocator that has reserved the GPU, or a
+hot path that must not call cudaMalloc.  Its split-K scratch is an array
+built into the library instead of a caller buffer.
 
-It is compared with the regular entry point, muon_polar_gram_sm100, run on the
-same CTA-pair split-K path (split-K forced on) with caller-owned scratch, using the tolerance of
-the Gram stage tests (one bf16 ulp), on two calls in a row -- the second call
-finds the array as the first call left it.  This file sorts last so that a
-run stopping at the first failure has already run every other test.
+It is compared through the C ABI with the regular entry point,
+muon_polar_gram_sm100, run on the same CTA-pair split-K path (split-K forced
+on) with caller-owned scratch.  The header promises the same tiles, split
+plan and reduction order, so the bits must be identical, on two calls in a
+row -- the second call finds the array as the first call left it.  A plan
+larger than the array's budget must be refused without a launch.  This file
+sorts last so that a run stopping at the first failure has already run every
+other test.
 """
 from __future__ import annotations
 
 import pytest
 import torch
 
-from oracle.polar_oracle import make_input, ulp_bf16
+from oracle.polar_oracle import make_input
 
 pytestmark = pytest.mark.gpu
 
 
-def _within_one_ulp(actual, expected):
-    a = actual.cpu().to(torch.float64)
-    e = expected.cpu().to(torch.float64)
-    assert bool(torch.isfinite(a).all())
-    assert bool(((a - e).abs() <= ulp_bf16(e)).all()), float((a - e).abs().max())
+def _same_bits(actual, expected):
+    assert actual.shape == expected.shape
+    assert torch.equal(actual.view(torch.int16), expected.view(torch.int16)), (
+        int((actual.view(torch.int16) != expected.view(torch.int16)).sum()))
 
 
 def test_static_scratch_gram_matches_regular_entry(cuda_device):
@@ -45,7 +49,30 @@ def test_static_scratch_gram_matches_regular_entry(cuda_device):
             api.gram_static_scratch(x, got)
             torch.cuda.synchronize()
             assert api.read_device_status(torch.cuda.current_device()) == 0
-            _within_one_ulp(got, expected)
+            _same_bits(got, expected)
     finally:
         api.set_kernel_policy(previous)
+        api.set_split_mode(previous_split)
+
+
+def test_static_scratch_refuses_plans_over_budget(cuda_device):
+    from muon_fusion_ascend950_b200.capi import MuonPolarError, capi
+
+    api = capi()
+    previous_split = api.set_split_mode(1)
+    previous_limit = api.set_static_scratch_limit(2 * 2 ** 20)  # 2 MiB: 7 split items
+    try:
+        x = make_input((8, 512, 2048), 33).to(cuda_device)
+        mp = api.padded_rows(512)
+        got = torch.zeros((8, mp, mp), dtype=torch.bfloat16, device=cuda_device)
+        torch.cuda.synchronize()
+        launches = api.launch_count()
+        with pytest.raises(MuonPolarError) as err:
+            api.gram_static_scratch(x, got)
+        assert err.value.status == -7  # MUON_POLAR_ERR_STATIC_SCRATCH
+        assert api.launch_count() == launches  # nothing was launched
+        torch.cuda.synchronize()
+        assert int(got.view(torch.int16).abs().sum()) == 0  # nothing was written
+    finally:
+        api.set_static_scratch_limit(previous_limit)
         api.set_split_mode(previous_split)
