@@ -86,11 +86,25 @@ struct EpiParams {
   int32_t total_items;
   float* partial;      // [total_items][PAIR][128][tile width] fp32 partial sums
   uint32_t* counters;  // [total_tiles][PAIR] arrivals, zero between launches
+  // Packed output (kGramF32, kPoly): the upper-triangle 256 x 256 units of
+  // each matrix stored one after another in row-major upper order, unit
+  // (I, J >= I) at index upper_index(I, J, packed_d); no mirror.  Tiles are
+  // visited from index tile_offset of the upper enumeration on.
+  int32_t packed;
+  int32_t packed_d;      // units per side: mp / 256
+  int32_t packed_units;  // units per matrix: packed_d (packed_d + 1) / 2
+  int32_t tile_offset;
 };
 
 struct TileCoord {
   int b, tm, tn;
 };
+
+// Index of unit (i, j), i <= j, in the row-major walk of the upper triangle
+// of a d x d grid (row i holds (i, i .. d - 1)).
+__host__ __device__ __forceinline__ int upper_index(int i, int j, int d) {
+  return i * d - i * (i - 1) / 2 + (j - i);
+}
 
 // Linear tile index -> (batch, tile row, tile col).  Symmetric kinds walk the
 // upper triangle row by row: row tm holds tiles (tm, tm..d-1) (the
@@ -99,10 +113,11 @@ __host__ __device__ __forceinline__ TileCoord decode_tile(int tile, bool sym,
                                                           int tiles_m,
                                                           int tiles_n,
                                                           int tiles_per_batch,
-                                                          int first_row = 0) {
+                                                          int first_row = 0,
+                                                          int offset = 0) {
   TileCoord t;
   t.b = tile / tiles_per_batch;
-  int r = tile - t.b * tiles_per_batch;
+  int r = tile - t.b * tiles_per_batch + offset;
   if (!sym) {
     t.tm = r / tiles_n;
     t.tn = r - t.tm * tiles_n;
@@ -133,7 +148,7 @@ __host__ __device__ __forceinline__ WorkItem decode_item(const EpiParams& p, int
   const int tile = item / p.splits;
   const bool walk = sym && !p.rows_mode;
   const TileCoord tc = decode_tile(tile, walk, p.tiles_m, p.tiles_n, p.tiles_per_batch,
-                                   walk ? p.row_tile_begin : 0);
+                                   walk ? p.row_tile_begin : 0, walk ? p.tile_offset : 0);
   w.tile = tile;
   w.b = tc.b;
   w.tm = walk ? tc.tm : tc.tm + p.row_tile_begin;
@@ -229,12 +244,13 @@ struct PairCfg {
   static constexpr int kStagesFit =
       static_cast<int>((232448u - kFixedBytes) / kStageBytes);
   static constexpr int kStages = kStagesFit > 8 ? 8 : kStagesFit;
-  // TMA producers: two warps fill alternate stages when the stage count is
-  // even (each stage then always has the same producer, which fills it in
-  // order).  Measured on B200, one thread's loads into successive mbarrier
-  // phases reach about 90 GB/s per SM with 32 KiB phases, two threads about
-  // 150 GB/s, the per-SM limit.
-  static constexpr int kProducers = kStages % 2 == 0 ? 2 : 1;
+  // TMA producers: two threads fill every stage together, one the A
+  // operand's boxes, the other the B operand's (a diagonal tile's A boxes
+  // are shared out between them), each arriving on the stage's full barrier
+  // with its own byte count.  Measured on B200, one thread's loads into
+  // successive mbarrier phases reach about 90 GB/s per SM with 32 KiB
+  // phases, two threads about 150 GB/s, the per-SM limit.
+  static constexpr int kProducers = 2;
   static constexpr uint32_t kSmemBytes = kFixedBytes + kStages * kStageBytes;
   // Split-K stages partial sums in the pipeline stages: a whole band to
   // publish, or two buffers of (splits - 1) chunks to reduce.
@@ -388,7 +404,7 @@ __global__ void __launch_bounds__(kTileThreads, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
-      mbar_init(&full[s], 1);
+      mbar_init(&full[s], Cfg::kProducers);  // the leader CTA's producers
       mbar_init(&empty[s], 1);
     }
     for (int a = 0; a < 2; ++a) {
@@ -425,21 +441,24 @@ __global__ void __launch_bounds__(kTileThreads, 1)
   // previous kernel may write, and lets dependents launch only after it.
 
   if (warp == 0 || warp == kProducerWarp2) {
-    // (warp kProducerWarp2 idles when the stage count is odd)
-    if (lane == 0 && (warp == 0 || Cfg::kProducers == 2)) {
-      // ---------------- TMA producers (both CTAs): producer `pid` fills the
-      // stages of the pipeline iterations with it % kProducers == pid.
+    if (lane == 0) {
+      // ---------------- TMA producers (both CTAs): producer 0 loads the A
+      // operand of every stage, producer 1 the B operand; on a diagonal
+      // tile of a symmetric kind (A only) they split A's boxes.
       const uint32_t pid = warp == 0 ? 0u : 1u;
-      // Loads of one operand into stage s of the pipeline; PAIR = 2 counts
-      // the bytes on the leader's barrier, PAIR = 1 on its own.
+      // Boxes [j0, j1) of one operand into stage s; PAIR = 2 counts the
+      // bytes on the leader's barrier, PAIR = 1 on its own.
       // K-major: [128 rows x 64 k] boxes; MN-major: one [kBK k x 64 rows] box
       // per 64-row chunk.
-      auto load_a = [&](uint32_t s, const WorkItem& w, int kb) {
+      constexpr int kBoxesA = kAmn ? kHalf / kAtom : Cfg::kBK / kAtom;
+      constexpr int kBoxesB = kBmn ? kHalf / kAtom : Cfg::kBK / kAtom;
+      constexpr uint32_t kBoxBytesA = Cfg::kAHalfBytes / kBoxesA;
+      auto load_a = [&](uint32_t s, const WorkItem& w, int kb, int j0, int j1) {
         const uint32_t bar = PAIR == 2 ? map_to_cta(smem_addr(&full[s]), 0) : 0u;
         const int a_row = w.tm * kTileM + static_cast<int>(rank) * kHalf;
-        constexpr int kBoxes = kAmn ? kHalf / kAtom : Cfg::kBK / kAtom;
 #pragma unroll
-        for (int j = 0; j < kBoxes; ++j) {
+        for (int j = 0; j < kBoxesA; ++j) {
+          if (j < j0 || j >= j1) continue;
           void* dst = sA + s * Cfg::kAHalfBytes + j * (kAmn ? Cfg::kBK * 128 : kAtomBytes);
           const int c0 = kAmn ? a_row + j * kAtom : kb * Cfg::kBK + j * kAtom;
           const int c1 = kAmn ? kb * Cfg::kBK : a_row;
@@ -454,9 +473,8 @@ __global__ void __launch_bounds__(kTileThreads, 1)
         const int b_row = w.tn * kTileN + static_cast<int>(rank) * kHalf;
         // K-major: [128 n x 64 k] boxes; MN-major: one [kBK k x 64 n] box per
         // 64-column chunk
-        constexpr int kBoxes = kBmn ? kHalf / kAtom : Cfg::kBK / kAtom;
 #pragma unroll
-        for (int j = 0; j < kBoxes; ++j) {
+        for (int j = 0; j < kBoxesB; ++j) {
           void* dst = sB + s * Cfg::kBHalfBytes + j * (kBmn ? Cfg::kBK * 128 : kAtomBytes);
           const int c0 = kBmn ? b_row + j * kAtom : kb * Cfg::kBK + j * kAtom;
           const int c1 = kBmn ? kb * Cfg::kBK : b_row;
@@ -475,27 +493,30 @@ __global__ void __launch_bounds__(kTileThreads, 1)
         // A diagonal tile of a symmetric kind multiplies a row block by
         // itself: only the A operand is loaded, and the MMA reads it twice.
         const bool diag = kSym && w.tm == w.tn;
+        // this producer's boxes of A: all of them (pid 0, off-diagonal),
+        // none (pid 1, off-diagonal), or its half of them (diagonal)
+        constexpr int kHalfA = kBoxesA / 2;
+        const int a0 = diag ? (pid == 0 ? 0 : kHalfA) : 0;
+        const int a1 = diag ? (pid == 0 ? kHalfA : kBoxesA) : (pid == 0 ? kBoxesA : 0);
+        const uint32_t bytes =
+            static_cast<uint32_t>(a1 - a0) * kBoxBytesA + (!diag && pid == 1 ? Cfg::kBHalfBytes : 0u);
         for (int kb = w.kb_begin; kb < w.kb_end; ++kb, ++it) {
-          if (it % Cfg::kProducers != pid) continue;
           const uint32_t s = it % S;
           const uint32_t ph = (it / S) & 1u;
           if (!mbar_wait_bounded(&empty[s], ph ^ 1u)) {
             ok = false;
             break;
           }
-          if (rank == 0)
-            mbar_arrive_expect_tx(&full[s], PAIR * (diag ? Cfg::kAHalfBytes : Cfg::kStageBytes));
-          load_a(s, w, kb);
-          if (!diag) load_b(s, w, kb);
+          if (rank == 0) mbar_arrive_expect_tx(&full[s], PAIR * bytes);
+          load_a(s, w, kb, a0, a1);
+          if (!diag && pid == 1) load_b(s, w, kb);
         }
       }
       if (!ok) atomicOr(&g_watchdog, MUON_POLAR_WATCHDOG_PRODUCER);
       if (rank == 0) {
-        // Drain: the pair's last loads (this producer's stages) land before
-        // the CTAs exit.
+        // Drain: the pair's last loads land before the CTAs exit.
         const uint32_t inflight = it < static_cast<uint32_t>(S) ? it : S;
         for (uint32_t i = it - inflight; i < it; ++i) {
-          if (i % Cfg::kProducers != pid) continue;
           if (!mbar_wait_bounded(&full[i % S], (i / S) & 1u)) {
             atomicOr(&g_watchdog, MUON_POLAR_WATCHDOG_DRAIN);
             break;
@@ -630,7 +651,10 @@ __global__ void __launch_bounds__(kTileThreads, 1)
         break;
       }
       tc_fence_after();
-      const bool mirror = kSym && !p.rows_mode && tc.tm != tc.tn;
+      bool mirror = kSym && !p.rows_mode && tc.tm != tc.tn;
+      if constexpr (KIND == kGramF32 || KIND == kPoly) {
+        if (p.packed) mirror = false;
+      }
       const int row0 = tc.tm * kTileM + static_cast<int>(rank) * kHalf;
       const int col0 = tc.tn * kTileN;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * kTileN;
@@ -782,10 +806,23 @@ __global__ void __launch_bounds__(kTileThreads, 1)
           if (SPLIT && reduce && c + 2 < Cfg::kChunks) load_parts(c + 2);
           const uint8_t* so = sOut + ro * Cfg::kOutChunkBytes;
           const uint8_t* sm = sMir + rm * Cfg::kMirChunkBytes;
+          bool packed = false;
+          if constexpr (KIND == kGramF32 || KIND == kPoly) packed = p.packed != 0;
+          if (packed) {
+            // the chunk's 128 x 64 block inside its 256 x 256 unit
+            const int col = col0 + c * kChunkCols;
+            const int unit = tc.b * p.packed_units +
+                             upper_index(row0 / kPairM, col / kPairN, p.packed_d);
 #pragma unroll
-          for (int h = 0; h < kChunkCols / Cfg::kBoxCols; ++h)
-            tma_store_3d(&tmap_out, so + h * (kHalf * 128),
-                         col0 + c * kChunkCols + h * Cfg::kBoxCols, row0, tc.b);
+            for (int h = 0; h < kChunkCols / Cfg::kBoxCols; ++h)
+              tma_store_3d(&tmap_out, so + h * (kHalf * 128), col % kPairN + h * Cfg::kBoxCols,
+                           row0 % kPairM, unit);
+          } else {
+#pragma unroll
+            for (int h = 0; h < kChunkCols / Cfg::kBoxCols; ++h)
+              tma_store_3d(&tmap_out, so + h * (kHalf * 128),
+                           col0 + c * kChunkCols + h * Cfg::kBoxCols, row0, tc.b);
+          }
           if (mirror) {
 #pragma unroll
             for (int h = 0; h < kHalf / Cfg::kBoxCols; ++h)

@@ -166,14 +166,21 @@ __device__ __forceinline__ uint32_t ld_acquire_cta_shared(uint32_t addr) {
   asm volatile("ld.acquire.cta.shared::cta.u32 %0, [%1];" : "=r"(v) : "r"(addr) : "memory");
   return v;
 }
-// Waits until *p >= target (written by other CTAs with release semantics).
-// Returns false once g_wait_limit_ns of wall-clock time have passed.
+// Whether count `v` has reached `target`, compared as sequence numbers
+// (their difference as a signed 32-bit value), so that the answer stays
+// right across a wrap of the counter.
+__device__ __forceinline__ bool count_reached(uint32_t v, uint32_t target) {
+  return static_cast<int32_t>(v - target) >= 0;
+}
+// Waits until *p has reached target (written by other CTAs with release
+// semantics).  Returns false once g_wait_limit_ns of wall-clock time have
+// passed.
 __device__ __forceinline__ bool wait_counter_bounded(const uint32_t* p, uint32_t target) {
-  if (ld_acquire_gpu(p) >= target) return true;
+  if (count_reached(ld_acquire_gpu(p), target)) return true;
   const uint64_t t0 = global_timer_ns();
   while (true) {
     __nanosleep(64);
-    if (ld_acquire_gpu(p) >= target) return true;
+    if (count_reached(ld_acquire_gpu(p), target)) return true;
     if (global_timer_ns() - t0 > g_wait_limit_ns) return false;
   }
 }

@@ -6,9 +6,10 @@ unaffected.
 
 The wait that is made to run out: in a two-step fused launch
 (muon_polar_steps_sm100, fused mode), every work item of matrix 1 in step 1
-waits until step 0's apply tiles of matrix 1 are all counted.  The test
-seeds that counter with 0xFFFFFFFF, so after step 0 it stands one below its
-target and never reaches it.  Each such wait happens before its item issues
+waits until step 0's apply tiles of matrix 1 are all counted.  Counts are
+compared as sequence numbers (a signed difference), and the test seeds that
+counter with 0xFFFFFFFF: it starts five below its target and, once step 0's
+four apply parts have added to it, stands one below for good.  Each such wait happens before its item issues
 any load (the producers and the epilogue's X tile both wait first), so when
 it gives up nothing is in flight; the kernel's waits are limited to 1 ms
 for the test (muon_polar_set_wait_limit_ns).  Nothing faults or hangs: every
