@@ -78,6 +78,10 @@ def parse_args():
                         "all-reduce each band while the next one computes (0: one all-reduce)")
     p.add_argument("--sm-reserve", type=int, default=16,
                    help="cfg5 with --overlap-bands: SMs the Gram bands leave to NCCL")
+    p.add_argument("--sharded", choices=["auto", "on", "off"], default="auto",
+                   help="also time the sharded workloads (configs 5 and 4) on the same GPUs "
+                        "and check the column-sharded result against one GPU, in the headline "
+                        "line under `sharded` (auto: with the default cfg1 workload)")
     p.add_argument("--workload", choices=["cfg1", "cfg3", "cfg4", "cfg5", "shape", "express"],
                    default="cfg1",
                    help="cfg1 (default, the headline): one step on [8,512,2048] per GPU; "
@@ -157,6 +161,48 @@ class ClockSampler:
 
 
 # --------------------------------------------------------------------- helpers
+def align_rows(m: int) -> int:
+    """Rows of the square Gram / polynomial buffers (a multiple of 256)."""
+    return -(-m // 256) * 256
+
+
+def rotation_sets(batch: int, m: int, n: int) -> int:
+    """Rotating input sets of the headline workload: enough that one cycle
+    touches more than three times the L2 (X, Y and the step's buffers)."""
+    k, g = min(m, n), max(m, n)
+    set_bytes = 3 * batch * k * g * 2 + 2 * batch * align_rows(k) ** 2 * 2
+    return int(min(8, max(2, -(-3 * L2_BYTES // set_bytes))))
+
+
+def workload_config(workload: str, world: int) -> dict:
+    """The `config` object of the JSON line, identical for both arms."""
+    shape_str = f"[{BATCH},{M},{N}]"
+    rot = rotation_sets(BATCH, M, N)
+    k, g = min(M, N), max(M, N)
+    touched = (3 * BATCH * k * g * 2 + 2 * BATCH * align_rows(k) ** 2 * 2) >> 20
+    return {
+        "workload": ("5-step polar_step loop on [8,512,2048] bf16 (BASELINE config 3) per GPU"
+                     if workload == "cfg3" else
+                     f"polar_express (5 steps, one call) on {shape_str} bf16 per GPU"
+                     if workload == "express" else
+                     f"polar_step {shape_str} bf16 single step per GPU" +
+                     (" (BASELINE config 1)" if workload == "cfg1" else "")),
+        "global_batch": BATCH * world, "m": M, "n": N,
+        "parallelism": f"batch-sharded x{world}, no data-path collective",
+        "l2": f"inputs larger than L2: {rot} rotating input sets ({rot} x {touched} MB touched "
+              f"per cycle > {L2_BYTES >> 20} MB L2)",
+    }
+
+
+def metric_name(workload: str) -> str:
+    shape_str = f"[{BATCH},{M},{N}]"
+    if workload == "cfg3":
+        return f"5-step Polar Express loop effective TFLOP/s at {shape_str} bf16"
+    if workload == "express":
+        return f"5-step polar_express call effective TFLOP/s at {shape_str} bf16"
+    return f"polar_step effective TFLOP/s at {shape_str} bf16"
+
+
 def measured_peaks():
     path = REPO / "MEASURED_PEAKS.json"
     if path.is_file():
@@ -213,6 +259,212 @@ def cpu_reference_rate(steps: int, warmup: int, budget_s: float, rows: int = 1):
     return rate, threads, sample
 
 
+# --------------------------------------------------------------------- sharded
+PARITY_SHAPE = (1024, 8192)
+
+
+def _max_over_ranks(ms: float, world: int, device) -> float:
+    import torch
+    import torch.distributed as dist
+
+    if world == 1:
+        return ms
+    t = torch.tensor([ms], device=device, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def _timed_updates(fn, updates: int, world: int, device, sync_all) -> float:
+    """ms per call of fn (one 5-step update) over `updates` calls, CUDA
+    events on the current stream, max over ranks."""
+    import torch
+
+    sync_all()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(updates):
+        fn()
+    e1.record()
+    e1.synchronize()
+    return _max_over_ranks(e0.elapsed_time(e1) / updates, world, device)
+
+
+def run_sharded(rank: int, world: int, device, sync_all) -> dict:
+    """The sharded workloads of BASELINE configs 5 and 4 on the job's GPUs,
+    each against the same workload on one GPU (rank 0's, timed in the same
+    process while the other ranks wait), plus a parity check of the
+    column-sharded result against the single-GPU polar_step chain.  Every
+    rank runs this (it issues collectives); the result is meaningful on
+    rank 0."""
+    import torch
+    import torch.distributed as dist
+
+    import muon_fusion_ascend950_b200 as pkg
+    from muon_fusion_ascend950_b200.distributed import (
+        ColumnShardedPolar, column_range, nominal_flops, partition_items)
+
+    gen = torch.Generator(device=device)
+    out = {}
+
+    def normalised_slab(m, n, seed):
+        """Columns of this rank of one normalised [m, n] matrix (global
+        Frobenius norm), generated on the device in slab order."""
+        cols = column_range(n, rank, world)
+        gen.manual_seed(seed * 1000 + rank)
+        x = torch.randn((m, len(cols)), generator=gen, device=device).to(torch.bfloat16)
+        sq = (x.float() ** 2).sum().reshape(1)
+        if world > 1:
+            dist.all_reduce(sq)
+        return (x / (sq.sqrt() * 1.01 + 1e-6)).to(torch.bfloat16)
+
+    def single_gpu_updates(x, updates):
+        def upd():
+            y = x
+            for a, b, c in COEFFICIENTS:
+                y = pkg.polar_step(y, a, b, c)
+        upd()
+        torch.cuda.synchronize(device)
+        return _timed_updates(upd, updates, 1, device, lambda: torch.cuda.synchronize(device))
+
+    # ---- config 5: one [8192, 65536] matrix, 5 steps, column-sharded
+    m5, n5 = 8192, 65536
+    flops5 = 5 * nominal_flops(m5, n5)
+    x_local = normalised_slab(m5, n5, 5)
+    driver = ColumnShardedPolar(m5, device, packed=True) if world > 1 else None
+    sampler = ClockSampler(int(device.index))
+    if driver is not None:
+        driver.run(x_local, COEFFICIENTS)  # warm-up
+        with sampler:
+            ms_n = _timed_updates(lambda: driver.run(x_local, COEFFICIENTS), 3, world, device,
+                                  sync_all)
+    sync_all()
+    ms_1 = None
+    if rank == 0:
+        gen.manual_seed(55)
+        x_full = torch.randn((1, m5, n5), generator=gen, device=device).to(torch.bfloat16)
+        x_full = x_full / (x_full.norm() * 1.01 + 1e-6)
+        ms_1 = single_gpu_updates(x_full, 2)
+        del x_full
+        torch.cuda.empty_cache()
+    sync_all()
+    cfg5 = {"workload": "5-step loop on one [8192,65536] bf16 matrix (BASELINE config 5)",
+            "ms_per_5_steps_1gpu": ms_1,
+            "tflops_1gpu": flops5 / (ms_1 * 1e-3) / 1e12 if ms_1 else None}
+    if driver is not None:
+        cfg5.update({
+            "parallelism": f"column-sharded x{world}: packed upper-triangle units, NCCL fp32 "
+                           "reduce-scatter + bf16 all-gathers of A and P per step",
+            "ms_per_5_steps": ms_n, "tflops": flops5 / (ms_n * 1e-3) / 1e12,
+            "efficiency": (ms_1 / (world * ms_n)) if ms_1 else None,
+            "collective_bytes_per_step": driver.collective_bytes(),
+            "clocks": sampler.summary(),
+        })
+        del driver
+    del x_local
+    torch.cuda.empty_cache()
+    out["cfg5"] = cfg5
+
+    # ---- config 4: 128 [4096,4096] + 96 [4096,11008], 5 steps, batch-sharded
+    kinds = [(4096, 4096)] * 128 + [(4096, 11008)] * 96
+    flops4 = 5 * sum(nominal_flops(*k) for k in kinds)
+
+    def cfg4_batches(items, seed):
+        gen.manual_seed(seed)
+        n_att = sum(1 for i in items if kinds[i] == (4096, 4096))
+        xs = []
+        for cnt, n in ((n_att, 4096), (len(items) - n_att, 11008)):
+            if cnt:
+                x = torch.randn((cnt, 4096, n), generator=gen, device=device).to(torch.bfloat16)
+                xs.append(x / (x.norm(dim=(-2, -1), keepdim=True) * 1.01 + 1e-6))
+        return xs
+
+    def cfg4_update(xs):
+        for x in xs:
+            y = x
+            for a, b, c in COEFFICIENTS:
+                y = pkg.polar_step(y, a, b, c)
+
+    ms4_1 = None
+    if rank == 0:
+        xs = cfg4_batches(list(range(len(kinds))), 44)
+        cfg4_update(xs)
+        torch.cuda.synchronize(device)
+        ms4_1 = _timed_updates(lambda: cfg4_update(xs), 1, 1, device,
+                               lambda: torch.cuda.synchronize(device))
+        del xs
+        torch.cuda.empty_cache()
+    sync_all()
+    cfg4 = {"workload": "Muon update of a 32-layer 7B model: 5-step loop on [128,4096,4096] + "
+                        "[96,4096,11008] bf16 (BASELINE config 4), the whole model",
+            "ms_per_update_1gpu": ms4_1,
+            "tflops_1gpu": flops4 / (ms4_1 * 1e-3) / 1e12 if ms4_1 else None}
+    if world > 1:
+        mine = partition_items([float(nominal_flops(*k)) for k in kinds], world)[rank]
+        xs = cfg4_batches(mine, 44 + rank)
+        cfg4_update(xs)
+        ms4_n = _timed_updates(lambda: cfg4_update(xs), 2, world, device, sync_all)
+        cfg4.update({"parallelism": f"batch-sharded x{world} (FLOP-balanced, no data-path "
+                                    "collective)",
+                     "ms_per_update": ms4_n, "tflops": flops4 / (ms4_n * 1e-3) / 1e12,
+                     "efficiency": (ms4_1 / (world * ms4_n)) if ms4_1 else None})
+        del xs
+        torch.cuda.empty_cache()
+    out["cfg4"] = cfg4
+
+    # ---- parity: a [1024, 8192] column-sharded 5-step result against the
+    # single-GPU polar_step chain and an fp32 evaluation of the reference
+    # formula (tests/test_polar_step.py:22-28), with the bound of the
+    # multi-GPU test: elementwise within rtol = atol = 6e-2 of the single-GPU
+    # chain, and a relative Frobenius error against fp32 at most 1.5x the
+    # single GPU's + 1e-3.
+    if world > 1:
+        mp_, np_ = PARITY_SHAPE
+        gen.manual_seed(77)  # the same matrix on every rank
+        x = torch.randn((mp_, np_), generator=gen, device=device).to(torch.bfloat16)
+        x = x / (x.norm() * 1.01 + 1e-6)
+        cols = column_range(np_, rank, world)
+        drv = ColumnShardedPolar(mp_, device, packed=True)
+        y_local = drv.run(x[:, cols.start:cols.stop].contiguous(), COEFFICIENTS).contiguous()
+        parts = [torch.empty_like(y_local) for _ in range(world)]
+        dist.all_gather(parts, y_local)
+        if rank == 0:
+            y = torch.cat(parts, dim=1).double()
+            single = x.unsqueeze(0)
+            for a, b, c in COEFFICIENTS:
+                single = pkg.polar_step(single, a, b, c)
+            single = single.squeeze(0).double()
+            tf32 = torch.backends.cuda.matmul.allow_tf32
+            torch.backends.cuda.matmul.allow_tf32 = False
+            ref = x.float()
+            for a, b, c in COEFFICIENTS:
+                g = ref @ ref.mT
+                ref = a * ref + (b * g + c * (g @ g)) @ ref
+            torch.backends.cuda.matmul.allow_tf32 = tf32
+            ref = ref.double()
+
+            def rel_fro(v):
+                return float((v - ref).norm() / ref.norm())
+
+            d = (y - single).abs()
+            within = bool((d <= 6e-2 + 6e-2 * single.abs()).all())
+            rs, r1 = rel_fro(y), rel_fro(single)
+            out["parity"] = {
+                "shape": list(PARITY_SHAPE), "steps": len(COEFFICIENTS), "ranks": world,
+                "path": "column-sharded, packed reduce-scatter / all-gathers",
+                "max_abs_vs_single_gpu": float(d.max()),
+                "max_abs_vs_fp32": float((y - ref).abs().max()),
+                "mean_abs_vs_fp32": float((y - ref).abs().mean()),
+                "rel_fro_vs_fp32": rs, "rel_fro_single_gpu_vs_fp32": r1,
+                "bound": "allclose(single, rtol=atol=6e-2) and rel_fro <= 1.5 x single + 1e-3",
+                "ok": within and rs <= 1.5 * r1 + 1e-3,
+            }
+        del drv, x, y_local, parts
+        torch.cuda.empty_cache()
+        sync_all()
+    return out
+
+
 # --------------------------------------------------------------------- arms
 def run_reference(args):
     rank, world, _ = dist_env()
@@ -222,13 +474,13 @@ def run_reference(args):
     ms = BATCH * nominal_flops_per_matrix(M, N) / (rate * 1e12) * 1e3
     line = {
         "impl": "reference",
-        "metric": "polar_step effective TFLOP/s at [8,512,2048] bf16",
+        "metric": metric_name("cfg1"),
         "value": rate, "unit": "TFLOP/s", "n_gpus": args.gpus, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": "polar_step [8,512,2048] bf16 single step (BASELINE config 1)",
-                   "global_batch": BATCH, "m": M, "n": N,
-                   "parallelism": "host CPU, rank 0 only"},
+        "config": workload_config("cfg1", args.gpus),
+        "timing": "host CPU (rank 0 only, every thread): the reference's PyTorch formula on a "
+                  "bounded sample of the workload, median of the timed steps",
         "cpu_baseline": {"value": rate, "unit": "TFLOP/s", "cores": threads, "kind": "port",
                          "sample": sample},
         "e2e": {"value": rate, "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
@@ -274,8 +526,7 @@ def run_ours(args):
     # the reference test does; enough rotating sets that one cycle touches
     # more than three times the L2 (8 sets at [8,512,2048])
     global ROTATION
-    set_bytes = 3 * BATCH * M * N * 2 + 2 * BATCH * api.padded_rows(M) ** 2 * 2
-    ROTATION = int(min(8, max(2, -(-3 * L2_BYTES // set_bytes))))
+    ROTATION = rotation_sets(BATCH, M, N)
     gen = torch.Generator(device=device)
     xs = []
     for i in range(ROTATION):
@@ -519,20 +770,19 @@ def run_ours(args):
     for g in graphs:
         g.reset()
     cycle.reset()
+    sharded = None
+    if args.sharded == "on" or (args.sharded == "auto" and args.workload == "cfg1"):
+        del xs, xs_k, gram, poly, y, scratch, host_in, host_out, dev_in
+        gc.collect()
+        torch.cuda.empty_cache()
+        sharded = run_sharded(rank, world, device, sync_all)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
     if rank != 0:
         return
-    cfg3 = args.workload == "cfg3"
-    shape_str = f"[{BATCH},{M},{N}]"
-    metric = f"polar_step effective TFLOP/s at {shape_str} bf16"
-    if cfg3:
-        metric = f"5-step Polar Express loop effective TFLOP/s at {shape_str} bf16"
-    elif args.workload == "express":
-        metric = f"5-step polar_express call effective TFLOP/s at {shape_str} bf16"
     line = {
-        "metric": metric,
+        "metric": metric_name(args.workload),
         "value": value,
         "unit": "TFLOP/s",
         "n_gpus": world,
@@ -546,22 +796,9 @@ def run_ours(args):
         "dtype": "bf16",
         "data": "synthetic",
         "pct_of_bf16_peak": 100.0 * value / (world * peak),
-        "config": {
-            "workload": ("5-step polar_step loop on [8,512,2048] bf16 (BASELINE config 3) per GPU"
-                         if cfg3 else
-                         f"polar_express (5 steps, one call) on {shape_str} bf16 per GPU"
-                         if args.workload == "express" else
-                         f"polar_step {shape_str} bf16 single step per GPU" +
-                         (" (BASELINE config 1)" if args.workload == "cfg1" else "")),
-            "global_batch": BATCH * world, "m": M, "n": N,
-            "parallelism": f"batch-sharded x{world}, no data-path collective",
-            "timing": (f"CUDA graphs of {ROTATION} consecutive public-API steps (one per "
-                       "input set; single-step graphs for the remainder of K), CUDA events, "
-                       "max over ranks"),
-            "l2": f"inputs larger than L2: {ROTATION} rotating input sets "
-                  f"({ROTATION} x {(3 * step_bytes + 2 * BATCH * mp * mp * 2) >> 20} MB touched "
-                  f"per cycle > {L2_BYTES >> 20} MB L2)",
-        },
+        "config": workload_config(args.workload, world),
+        "timing": (f"CUDA graphs of {ROTATION} consecutive public-API steps (one per input set; "
+                   "single-step graphs for the remainder of K), CUDA events, max over ranks"),
         "roofline": roofline,
         "cpu_baseline": cpu_baseline,
         "e2e": {"value": e2e_value, "unit": "TFLOP/s", "steps": e2e_steps,
@@ -575,7 +812,12 @@ def run_ours(args):
         "clocks": sampler.summary(),
         "gpu_launches": launches_per_step * args.steps,
     }
+    if sharded is not None:
+        line["sharded"] = sharded
     print(json.dumps(line), flush=True)
+    parity = (sharded or {}).get("parity")
+    if parity is not None and not parity["ok"]:
+        raise SystemExit("column-sharded parity check failed: " + json.dumps(parity))
 
 
 def run_large(args):

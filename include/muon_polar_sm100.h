@@ -164,6 +164,36 @@ int muon_polar_gram_f32_band_sm100(const void* x, void* gram_f32, int64_t batch,
                                    int sm_reserve, void* scratch, size_t scratch_bytes,
                                    void* stream);
 
+/* Packed upper triangle, for column-sharded multi-GPU callers (no
+ * counterpart in the reference, which runs on one device).  A symmetric
+ * Mp x Mp matrix is cut into 256 x 256 units; the d (d + 1) / 2 units (I, J)
+ * with I <= J (d = Mp / 256) are stored one after another, row by row of the
+ * unit grid, each as a dense row-major 256 x 256 block: [batch][units][256][256].
+ * The lower-left 128 x 128 quarter of a diagonal unit (I, I) is unspecified
+ * (it mirrors the upper-right one).  A collective on the packed form moves
+ * (d + 1) / (2 d) of the bytes of the full matrix.
+ *
+ * muon_polar_packed_units: units per matrix for `m` rows of X.
+ * muon_polar_gram_f32_packed_sm100: kernel (1), fp32, written packed (no
+ *   mirror), e.g. a rank's partial Gram before a reduce-scatter of the units.
+ *   Arguments as for muon_polar_gram_f32_sm100.
+ * muon_polar_poly_packed_sm100: kernel (2) on units [unit_begin, unit_begin +
+ *   unit_count) of each matrix, read from the full bf16 gram [batch][Mp][Mp],
+ *   written into their places in the packed bf16 buffer (other units are not
+ *   touched); the arithmetic of muon_polar_poly_sm100.
+ * muon_polar_unpack_sym_sm100: packed bf16 units -> the full symmetric
+ *   [batch][Mp][Mp] bf16 matrix (each unit and, off the diagonal, its
+ *   transpose). */
+int64_t muon_polar_packed_units(int64_t m);
+int muon_polar_gram_f32_packed_sm100(const void* x, void* packed_f32, int64_t batch, int64_t m,
+                                     int64_t n, int64_t ldx, void* scratch, size_t scratch_bytes,
+                                     void* stream);
+int muon_polar_poly_packed_sm100(const void* gram, void* packed_poly, int64_t batch, int64_t mp,
+                                 int64_t unit_begin, int64_t unit_count, float b, float c,
+                                 void* stream);
+int muon_polar_unpack_sym_sm100(const void* packed, void* full, int64_t batch, int64_t mp,
+                                void* stream);
+
 /* Kernel (2): poly[b] = bf16( b*f32(gram[b]) + c*(gram[b].gram[b])_f32 ),
  * both [batch][Mp][Mp] bf16, Mp a multiple of 128 (256 for the CTA-pair
  * kernels; muon_polar_padded_rows gives 256-multiples).  Products and the

@@ -83,6 +83,12 @@ SIGNATURES = {
     "muon_polar_decode_tile": (ctypes.c_int, [_I64, ctypes.c_int, _I64, _I64, _I64, _I64,
                                               ctypes.POINTER(_I64)]),
     "muon_polar_check_address_cache": (ctypes.c_int, []),
+    "muon_polar_packed_units": (_I64, [_I64]),
+    "muon_polar_gram_f32_packed_sm100": (ctypes.c_int, [_VP, _VP, _I64, _I64, _I64, _I64, _VP,
+                                                        ctypes.c_size_t, _VP]),
+    "muon_polar_poly_packed_sm100": (ctypes.c_int, [_VP, _VP, _I64, _I64, _I64, _I64,
+                                                    ctypes.c_float, ctypes.c_float, _VP]),
+    "muon_polar_unpack_sym_sm100": (ctypes.c_int, [_VP, _VP, _I64, _I64, _VP]),
 }
 
 WATCHDOG_PRODUCER = 0x1
@@ -278,6 +284,36 @@ class CAPI:
         self._check("muon_polar_gram_f32_band_sm100", self.lib.muon_polar_gram_f32_band_sm100(
             x.data_ptr(), gram_f32.data_ptr(), b, m, n, ld, int(row_begin), int(row_count),
             int(sm_reserve), sp, sb, self._stream(stream)))
+
+    # Packed upper-triangle units ([B, units, 256, 256]) for column-sharded
+    # callers: the rank's partial Gram is reduce-scattered by units.
+    def packed_units(self, m: int) -> int:
+        return int(self.lib.muon_polar_packed_units(int(m)))
+
+    def gram_f32_packed(self, x, packed_f32, n: Optional[int] = None, scratch=None,
+                        stream=None) -> None:
+        b, m, ld = x.shape
+        n = ld if n is None else n
+        sp, sb = _scratch(scratch)
+        self._check("muon_polar_gram_f32_packed_sm100",
+                    self.lib.muon_polar_gram_f32_packed_sm100(
+                        x.data_ptr(), packed_f32.data_ptr(), b, m, n, ld, sp, sb,
+                        self._stream(stream)))
+
+    def poly_packed(self, gram, packed_poly, b: float, c: float, unit_begin: int,
+                    unit_count: int, stream=None) -> None:
+        """Units [unit_begin, unit_begin + unit_count) of kernel (2)'s output
+        into their places in the packed buffer, from the full bf16 gram."""
+        bsz, mp, _ = gram.shape
+        self._check("muon_polar_poly_packed_sm100", self.lib.muon_polar_poly_packed_sm100(
+            gram.data_ptr(), packed_poly.data_ptr(), bsz, mp, int(unit_begin), int(unit_count),
+            float(b), float(c), self._stream(stream)))
+
+    def unpack_sym(self, packed, full, stream=None) -> None:
+        """Packed bf16 units -> the full symmetric [B, Mp, Mp] bf16 matrix."""
+        bsz, mp, _ = full.shape
+        self._check("muon_polar_unpack_sym_sm100", self.lib.muon_polar_unpack_sym_sm100(
+            packed.data_ptr(), full.data_ptr(), bsz, mp, self._stream(stream)))
 
     def poly(self, gram, poly, b: float, c: float, scratch=None, stream=None) -> None:
         bsz, mp, _ = gram.shape

@@ -1614,6 +1614,64 @@ __global__ void cast_f32_bf16_kernel(const float* __restrict__ src,
     dst[i] = static_cast<uint16_t>(float_to_bf16_bits(src[i]));
 }
 
+// Packed upper-triangle units -> full symmetric matrix, bf16.  One CTA per
+// 128 x 128 quarter (r, s) of unit (I, J) of matrix b: the quarter goes to
+// rows I*256 + r*128, columns J*256 + s*128 of `full`, and its transpose to
+// the mirrored place unless it lies on the diagonal.  The lower-left
+// quarter of a diagonal unit is not read: it is the mirror of the upper
+// right one (the Gram on single-CTA tiles never writes it).
+__global__ void __launch_bounds__(256) unpack_sym_kernel(const uint16_t* __restrict__ packed,
+                                                         uint16_t* __restrict__ full, int d2,
+                                                         int units, int64_t mp) {
+  __shared__ uint32_t tile[128][65];  // 128 rows x 128 bf16, one word of padding
+  grid_dependency_wait();
+  grid_launch_dependents();
+  const int u = static_cast<int>(blockIdx.x) >> 2;
+  const int r = (blockIdx.x >> 1) & 1, sq = blockIdx.x & 1;
+  const int b = blockIdx.y;
+  int I = 0, rem = u;
+  while (rem >= d2 - I) {
+    rem -= d2 - I;
+    ++I;
+  }
+  const int J = I + rem;
+  if (I == J && r == 1 && sq == 0) return;
+  const int64_t R0 = static_cast<int64_t>(I) * 256 + r * 128;
+  const int64_t C0 = static_cast<int64_t>(J) * 256 + sq * 128;
+  const uint16_t* src = packed + ((static_cast<int64_t>(b) * units + u) * 256 + r * 128) * 256 + sq * 128;
+  uint16_t* dst = full + static_cast<int64_t>(b) * mp * mp;
+  const bool mirror = !(I == J && r == sq);
+#pragma unroll 2
+  for (int i = 0; i < 8; ++i) {
+    const int e = i * 256 + threadIdx.x;  // 16-byte unit: row e / 16, column (e % 16) * 8
+    const int row = e >> 4, q = e & 15;
+    const uint4 v = *reinterpret_cast<const uint4*>(src + row * 256 + q * 8);
+    *reinterpret_cast<uint4*>(dst + (R0 + row) * mp + C0 + q * 8) = v;
+    if (mirror) {
+      tile[row][q * 4 + 0] = v.x;
+      tile[row][q * 4 + 1] = v.y;
+      tile[row][q * 4 + 2] = v.z;
+      tile[row][q * 4 + 3] = v.w;
+    }
+  }
+  if (!mirror) return;
+  __syncthreads();
+  const uint16_t* t16 = reinterpret_cast<const uint16_t*>(&tile[0][0]);
+#pragma unroll 2
+  for (int i = 0; i < 8; ++i) {
+    const int e = i * 256 + threadIdx.x;  // output row rr = column rr of the quarter
+    const int rr = e >> 4, q = e & 15;
+    uint32_t w[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const uint32_t lo = t16[(q * 8 + 2 * k) * 130 + rr];
+      const uint32_t hi = t16[(q * 8 + 2 * k + 1) * 130 + rr];
+      w[k] = lo | (hi << 16);
+    }
+    *reinterpret_cast<uint4*>(dst + (C0 + rr) * mp + R0 + q * 8) = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+}
+
 // ============================================================== host side
 
 namespace {
@@ -1954,6 +2012,22 @@ int encode_square(CUtensorMap* map, const void* base, int64_t batch, int64_t mp,
                          batch, mp, mp * mp, kAtom, box_rows);
 }
 
+// Upper-triangle units (256 x 256) of an mp x mp matrix.
+int64_t packed_units_of(int64_t mp) {
+  const int64_t d2 = mp / kPairM;
+  return d2 * (d2 + 1) / 2;
+}
+
+// Packed upper-triangle units, [batch][units][256][256] bf16 or fp32, boxes
+// of 128 rows x 128 bytes.
+int encode_packed(CUtensorMap* map, const void* base, int64_t batch, int64_t mp, bool f32) {
+  const int64_t units = packed_units_of(mp) * batch;
+  return f32 ? encode_3d(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, base, kPairN, kPairM, units,
+                         kPairN, kPairM * kPairN, 32, kHalf)
+             : encode_3d(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, kPairN, kPairM, units,
+                         kPairN, kPairM * kPairN, kAtom, kHalf);
+}
+
 // Upper-triangle tile grid of a symmetric kind: d x d tiles of kHalf * PAIR
 // rows per matrix, d (d + 1) / 2 of them computed.
 template <int PAIR>
@@ -1974,7 +2048,7 @@ template <int KIND, int PAIR>
 int gram_launch(DeviceState* st, const void* x, void* gram, int64_t batch, int64_t m,
                 int64_t n, int64_t ldx, void* scratch, size_t scratch_bytes,
                 bool fixed_scratch, cudaStream_t stream, int64_t band_begin = 0,
-                int64_t band_rows = 0, int sm_reserve = 0) {
+                int64_t band_rows = 0, int sm_reserve = 0, bool packed = false) {
   constexpr bool kT = KIND == kGramT;
   const int64_t mp = padded_rows(kT ? n : m);
   int units = 0;
@@ -1992,11 +2066,19 @@ int gram_launch(DeviceState* st, const void* x, void* gram, int64_t batch, int64
   if (rc != MUON_POLAR_OK) return rc;
   tm.b = tm.a;
   tm.aux = tm.a;
-  rc = encode_square(&tm.out, gram, batch, mp, KIND == kGramF32, kHalf);
-  if (rc != MUON_POLAR_OK) return rc;
-  rc = encode_square(&tm.mir, gram, batch, mp, KIND == kGramF32, kChunkCols);
-  if (rc != MUON_POLAR_OK) return rc;
   EpiParams p = {};
+  if (packed) {
+    rc = encode_packed(&tm.out, gram, batch, mp, KIND == kGramF32);
+    tm.mir = tm.out;
+    p.packed = 1;
+    p.packed_d = static_cast<int32_t>(mp / kPairM);
+    p.packed_units = static_cast<int32_t>(packed_units_of(mp));
+  } else {
+    rc = encode_square(&tm.out, gram, batch, mp, KIND == kGramF32, kHalf);
+    if (rc != MUON_POLAR_OK) return rc;
+    rc = encode_square(&tm.mir, gram, batch, mp, KIND == kGramF32, kChunkCols);
+  }
+  if (rc != MUON_POLAR_OK) return rc;
   sym_grid<PAIR>(p, batch, mp);
   if (band_rows > 0) {
     // the upper tiles of tile rows [t0, t0 + nt)
@@ -2027,7 +2109,7 @@ int gram_launch(DeviceState* st, const void* x, void* gram, int64_t batch, int64
 template <int KIND>
 int gram_impl(const void* x, void* gram, int64_t batch, int64_t m, int64_t n,
               int64_t ldx, void* scratch, size_t scratch_bytes,
-              cudaStream_t stream, bool fixed_scratch = false) {
+              cudaStream_t stream, bool fixed_scratch = false, bool packed = false) {
   int rc = check_x_args(x, batch, m, n, ldx);
   if (rc != MUON_POLAR_OK) return rc;
   if (gram == nullptr) return MUON_POLAR_ERR_INVALID_ARGUMENT;
@@ -2050,9 +2132,9 @@ int gram_impl(const void* x, void* gram, int64_t batch, int64_t m, int64_t n,
   if (fixed_scratch || use_pairs(dp * (dp + 1) / 2 * batch, pairs, cost_blocks<2>(depth),
                                  d * (d + 1) / 2 * batch, ctas, cost_blocks<1>(depth)))
     return gram_launch<KIND, 2>(st, x, gram, batch, m, n, ldx, scratch, scratch_bytes,
-                                fixed_scratch, stream);
+                                fixed_scratch, stream, 0, 0, 0, packed);
   return gram_launch<KIND, 1>(st, x, gram, batch, m, n, ldx, scratch, scratch_bytes,
-                              fixed_scratch, stream);
+                              fixed_scratch, stream, 0, 0, 0, packed);
 }
 
 // Kernel (1), fp32 output, on the upper tiles of the rows [row_begin,
@@ -2190,6 +2272,77 @@ int poly_rows_impl(const void* gram, void* poly, int64_t batch, int64_t mp, int6
                 row_count / kHalf * (mp / kHalf) * batch, ctas, cost_blocks<1>(mp)))
     return poly_rows_launch<2>(st, gram, poly, batch, mp, row_begin, row_count, b, c, stream);
   return poly_rows_launch<1>(st, gram, poly, batch, mp, row_begin, row_count, b, c, stream);
+}
+
+// Units [unit_begin, unit_begin + unit_count) of the upper triangle of P,
+// each written into its place in the packed buffer (CTA-pair tiles: one
+// tile per unit).
+int poly_packed_impl(const void* gram, void* packed, int64_t batch, int64_t mp,
+                     int64_t unit_begin, int64_t unit_count, float b, float c,
+                     cudaStream_t stream) {
+  if (gram == nullptr || packed == nullptr || batch <= 0 || mp <= 0 || (mp % kPairM) != 0 ||
+      batch > INT32_MAX || mp > (1 << 24))
+    return MUON_POLAR_ERR_INVALID_ARGUMENT;
+  const int64_t units = packed_units_of(mp);
+  if (unit_begin < 0 || unit_count <= 0 || unit_begin + unit_count > units ||
+      unit_count * batch > INT32_MAX)
+    return MUON_POLAR_ERR_INVALID_ARGUMENT;
+  if (!aligned16(gram) || !aligned16(packed)) return MUON_POLAR_ERR_ALIGNMENT;
+  DeviceState* st = nullptr;
+  int rc = current_device_state(&st);
+  if (rc != MUON_POLAR_OK) return rc;
+  int pairs = 0;
+  rc = tile_capacity<kPoly, 2>(st, &pairs);
+  if (rc != MUON_POLAR_OK) return rc;
+  TileMaps tm;
+  rc = encode_square(&tm.a, gram, batch, mp, false, kHalf);
+  if (rc != MUON_POLAR_OK) return rc;
+  tm.b = tm.a;
+  tm.aux = tm.a;
+  rc = encode_packed(&tm.out, packed, batch, mp, false);
+  if (rc != MUON_POLAR_OK) return rc;
+  tm.mir = tm.out;
+  EpiParams p = {};
+  sym_grid<2>(p, batch, mp);
+  p.tiles_per_batch = static_cast<int32_t>(unit_count);
+  p.total_tiles = static_cast<int32_t>(unit_count * batch);
+  p.tile_offset = static_cast<int32_t>(unit_begin);
+  p.packed = 1;
+  p.packed_d = static_cast<int32_t>(mp / kPairM);
+  p.packed_units = static_cast<int32_t>(units);
+  p.k_blocks = static_cast<int32_t>(k_blocks_of<kPoly, 2>(mp));
+  p.coef_b = b;
+  p.coef_c = c;
+  plan_no_splits(p);
+  return launch_tile<kPoly, 2>(st, tm, p, stream);
+}
+
+int unpack_sym_impl(const void* packed, void* full, int64_t batch, int64_t mp,
+                    cudaStream_t stream) {
+  if (packed == nullptr || full == nullptr || batch <= 0 || mp <= 0 || (mp % kPairM) != 0 ||
+      batch > 65535 || mp > (1 << 24))
+    return MUON_POLAR_ERR_INVALID_ARGUMENT;
+  if (!aligned16(packed) || !aligned16(full)) return MUON_POLAR_ERR_ALIGNMENT;
+  DeviceState* st = nullptr;
+  int rc = current_device_state(&st);
+  if (rc != MUON_POLAR_OK) return rc;
+  const int64_t units = packed_units_of(mp);
+  if (units * 4 > INT32_MAX) return MUON_POLAR_ERR_INVALID_ARGUMENT;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(units * 4), static_cast<unsigned>(batch), 1);
+  cfg.blockDim = dim3(256, 1, 1);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, unpack_sym_kernel, static_cast<const uint16_t*>(packed),
+                                     static_cast<uint16_t*>(full), static_cast<int>(mp / kPairM),
+                                     static_cast<int>(units), mp);
+  if (e != cudaSuccess) return static_cast<int>(e);
+  g_launch_count.fetch_add(1, std::memory_order_relaxed);
+  return MUON_POLAR_OK;
 }
 
 // Host-side fp32 -> bf16 round-to-nearest-even, the same rule as the
@@ -2842,6 +2995,27 @@ int muon_polar_gram_static_scratch_sm100(const void* x, void* gram, int64_t batc
                                          void* stream) {
   return gram_static_scratch_impl(x, gram, batch, m, n, ldx,
                                   static_cast<cudaStream_t>(stream));
+}
+
+int64_t muon_polar_packed_units(int64_t m) { return m <= 0 ? 0 : packed_units_of(padded_rows(m)); }
+
+int muon_polar_gram_f32_packed_sm100(const void* x, void* packed_f32, int64_t batch, int64_t m,
+                                     int64_t n, int64_t ldx, void* scratch, size_t scratch_bytes,
+                                     void* stream) {
+  return gram_impl<kGramF32>(x, packed_f32, batch, m, n, ldx, scratch, scratch_bytes,
+                             static_cast<cudaStream_t>(stream), false, /*packed=*/true);
+}
+
+int muon_polar_poly_packed_sm100(const void* gram, void* packed_poly, int64_t batch, int64_t mp,
+                                 int64_t unit_begin, int64_t unit_count, float b, float c,
+                                 void* stream) {
+  return poly_packed_impl(gram, packed_poly, batch, mp, unit_begin, unit_count, b, c,
+                          static_cast<cudaStream_t>(stream));
+}
+
+int muon_polar_unpack_sym_sm100(const void* packed, void* full, int64_t batch, int64_t mp,
+                                void* stream) {
+  return unpack_sym_impl(packed, full, batch, mp, static_cast<cudaStream_t>(stream));
 }
 
 int muon_polar_cast_f32_bf16_sm100(const void* src, void* dst, int64_t count,

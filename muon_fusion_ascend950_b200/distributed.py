@@ -8,23 +8,35 @@ workloads it is benchmarked on shard in two ways:
   them; there is no collective on the data path.  `partition_items` balances
   by nominal FLOPs (4 M^2 N + 2 M^3 per matrix).
 * **Column sharding** (one large matrix: config 5).  Rank r owns the column
-  slab X[:, r*N/G : (r+1)*N/G] for the whole iteration.  Per step:
-    1. partial Gram G_r = X_r X_r^T in fp32 (kernel 1, fp32 output),
-    2. one all-reduce (sum, fp32, Mp x Mp) over NCCL -- or, with
-       `overlap_bands`, kernel 1 runs band by band over the rows
-       (muon_polar_gram_f32_band_sm100, leaving `sm_reserve` SMs free) and
-       each band's rows are all-reduced on a second stream while the next
-       band computes,
-    3. A = bf16(sum) (cast kernel), P = b A + c A A (kernel 2), either
-       replicated on every rank or (shard_poly) as row slabs, rank r
-       computing rows [r Mp/G, (r+1) Mp/G) followed by an all-gather of the
-       bf16 slabs,
-    4. Y_r = a X_r + P X_r on the local slab (kernel 3).
-  The result equals the single-GPU step up to the fp32 summation order of
-  the Gram (A is rounded to bf16 once, after the sum, as on one GPU).
+  slab X[:, r*N/G : (r+1)*N/G] for the whole iteration.  Per step, by
+  default (`packed`), on the packed upper triangle of the symmetric
+  matrices (256 x 256 units, (d+1)/(2d) of the full matrix's bytes):
+    1. partial Gram G_r = X_r X_r^T in fp32, written as packed units
+       (kernel 1, muon_polar_gram_f32_packed_sm100),
+    2. one reduce-scatter (sum, fp32) of the units over NCCL: rank r
+       receives the summed units of its slab [r U/G, (r+1) U/G),
+    3. A = bf16(sum) of the slab (cast kernel: the one rounding of A, as on
+       one GPU), then an all-gather (bf16) of the packed A and an unpack to
+       the full symmetric matrix,
+    4. P = b A + c A A on the rank's units only (kernel 2,
+       muon_polar_poly_packed_sm100), an all-gather (bf16) of the packed P
+       and an unpack,
+    5. Y_r = a X_r + P X_r on the local slab (kernel 3).
+  Against an fp32 all-reduce of the full Mp x Mp Gram and a gather of P row
+  slabs, the collectives move about 3/8 of the bytes, and kernel 2 computes
+  each unit once instead of both triangles.  `packed=False` keeps that
+  earlier scheme: the all-reduce -- or, with `overlap_bands`, kernel 1 band
+  by band over the rows (muon_polar_gram_f32_band_sm100, leaving
+  `sm_reserve` SMs free), each band all-reduced on a second stream while the
+  next band computes -- then A = bf16(sum), and P replicated or (shard_poly)
+  as row slabs [r Mp/G, (r+1) Mp/G) followed by an all-gather.
+  Either way the result equals the single-GPU step up to the fp32 summation
+  order of the Gram (A is rounded to bf16 once, after the sum, as on one
+  GPU).
 
 Kernels are reached through a backend object with the methods of
-`capi.CAPI` (gram_f32, cast_f32_bf16, poly, apply).  The default backend is
+`capi.CAPI` (gram_f32, gram_f32_packed, cast_f32_bf16, unpack_sym,
+poly_packed, poly, apply, ...).  The default backend is
 the CUDA C ABI; there is no CPU fallback -- tests on CPU pass their own
 backend explicitly.
 """
@@ -101,7 +113,7 @@ class ColumnShardedPolar:
     SMs to the collective)."""
 
     def __init__(self, m: int, device, group=None, backend=None, shard_poly: bool = False,
-                 overlap_bands: int = 0, sm_reserve: int = 16):
+                 overlap_bands: int = 0, sm_reserve: int = 16, packed: bool = True):
         if backend is None:
             from .capi import capi
 
@@ -119,10 +131,29 @@ class ColumnShardedPolar:
             self.poly_slab = (rank * rows, rows)
         self.bands = gram_bands(self.mp, overlap_bands) if overlap_bands > 1 and world > 1 else []
         self.sm_reserve = sm_reserve
+        self.world, self.rank = world, rank
+        self.packed = bool(packed) and world > 1 and not self.bands
+        if self.packed:
+            units = backend.packed_units(m)
+            per = -(-units // world)
+            self.unit_slab = (rank * per, max(0, min(per, units - rank * per)))
+            unit = (256, 256)
+            # the last slab may end in padding units: zero in the partial Gram
+            # (never written), unused in A and P
+            self.packed_f32 = torch.zeros((per * world, *unit), dtype=torch.float32,
+                                          device=self.device)
+            self.slab_f32 = torch.empty((per, *unit), dtype=torch.float32, device=self.device)
+            self.slab_bf16 = torch.empty((per, *unit), dtype=torch.bfloat16, device=self.device)
+            self.packed_a = torch.empty((per * world, *unit), dtype=torch.bfloat16,
+                                        device=self.device)
+            self.packed_p = torch.zeros((per * world, *unit), dtype=torch.bfloat16,
+                                        device=self.device)
+            self.poly_slab = None
         self.comm = (torch.cuda.Stream(self.device)
                      if self.bands and self.device.type == "cuda" else None)
         shape = (1, self.mp, self.mp)
-        self.gram_f32 = torch.empty(shape, dtype=torch.float32, device=self.device)
+        self.gram_f32 = (torch.empty(shape, dtype=torch.float32, device=self.device)
+                         if not self.packed else None)
         self.gram = torch.empty(shape, dtype=torch.bfloat16, device=self.device)
         self.poly = torch.empty(shape, dtype=torch.bfloat16, device=self.device)
 
@@ -134,6 +165,10 @@ class ColumnShardedPolar:
             raise ValueError(f"x_local must be [{self.m}, n_local], got {tuple(x_local.shape)}")
         x3 = x_local.contiguous().unsqueeze(0)
         y3 = torch.empty_like(x3) if out is None else out.view(1, *out.shape[-2:])
+        if self.packed:
+            self._packed_gram_poly(x3, b, c)
+            self.backend.apply(self.poly, x3, y3, a)
+            return y3.squeeze(0)
         if self.bands:
             self._gram_reduce_bands(x3)
         else:
@@ -152,6 +187,37 @@ class ColumnShardedPolar:
                                         group=self.group)
         self.backend.apply(self.poly, x3, y3, a)
         return y3.squeeze(0)
+
+    def _packed_gram_poly(self, x3: torch.Tensor, b: float, c: float) -> None:
+        """A and P on the packed upper triangle (module docstring, steps
+        1-4).  Every rank issues the same three collectives in order."""
+        be = self.backend
+        # the kernels' layout is [batch][units][256][256]: batch 1 here
+        be.gram_f32_packed(x3, self.packed_f32.unsqueeze(0))
+        dist.reduce_scatter_tensor(self.slab_f32, self.packed_f32, op=dist.ReduceOp.SUM,
+                                   group=self.group)
+        be.cast_f32_bf16(self.slab_f32, self.slab_bf16)
+        dist.all_gather_into_tensor(self.packed_a, self.slab_bf16, group=self.group)
+        be.unpack_sym(self.packed_a.unsqueeze(0), self.gram)
+        begin, count = self.unit_slab
+        if count > 0:
+            be.poly_packed(self.gram, self.packed_p.unsqueeze(0), b, c, begin, count)
+        per = self.slab_f32.shape[0]
+        mine = self.packed_p[self.rank * per:(self.rank + 1) * per]
+        dist.all_gather_into_tensor(self.packed_p, mine, group=self.group)
+        be.unpack_sym(self.packed_p.unsqueeze(0), self.poly)
+
+    def collective_bytes(self) -> dict:
+        """Bytes each rank hands to the collectives per step (NCCL message
+        sizes, before any algorithm-dependent factor)."""
+        if not self.packed:
+            full = self.mp * self.mp
+            out = {"all_reduce_fp32": 4 * full}
+            if self.poly_slab is not None:
+                out["all_gather_bf16"] = 2 * full
+            return out
+        n = self.packed_f32.numel()
+        return {"reduce_scatter_fp32": 4 * n, "all_gather_bf16": 2 * 2 * n}
 
     def _gram_reduce_bands(self, x3: torch.Tensor) -> None:
         """Kernel 1 band by band; band i's rows are complete after its call

@@ -191,6 +191,52 @@ class CpuKernels:
         poly[:, rows].copy_(((b32 * a32[:, rows]) + (c32 * (a32[:, rows] @ a32.mT)))
                             .to(torch.bfloat16))
 
+    # Packed upper-triangle units ([B, units, 256, 256]), as the packed
+    # entry points of the C ABI lay them out.
+    @staticmethod
+    def packed_units(m: int) -> int:
+        d = align_up(m, 256) // 256
+        return d * (d + 1) // 2
+
+    @staticmethod
+    def unit_grid(mp: int) -> list:
+        d = mp // 256
+        return [(i, j) for i in range(d) for j in range(i, d)]
+
+    @classmethod
+    def gram_f32_packed(cls, x, out, n=None, scratch=None, stream=None):
+        m = x.shape[1]
+        mp = align_up(m, 256)
+        full = torch.zeros((x.shape[0], mp, mp), dtype=torch.float32)
+        xf = x.to(torch.float32)
+        full[:, :m, :m] = xf @ xf.mT
+        for u, (i, j) in enumerate(cls.unit_grid(mp)):
+            out[:, u] = full[:, 256 * i:256 * i + 256, 256 * j:256 * j + 256]
+
+    @classmethod
+    def poly_packed(cls, gram, out, b, c, unit_begin, unit_count, stream=None):
+        a32 = gram.to(torch.float32)
+        b32 = torch.tensor(b, dtype=torch.float32)
+        c32 = torch.tensor(c, dtype=torch.float32)
+        grid = cls.unit_grid(gram.shape[-1])
+        for u in range(unit_begin, unit_begin + unit_count):
+            i, j = grid[u]
+            rows, cols = slice(256 * i, 256 * i + 256), slice(256 * j, 256 * j + 256)
+            out[:, u] = ((b32 * a32[:, rows, cols]) + (c32 * (a32[:, rows] @ a32[:, cols].mT))
+                         ).to(torch.bfloat16)
+
+    @classmethod
+    def unpack_sym(cls, packed, full, stream=None):
+        for u, (i, j) in enumerate(cls.unit_grid(full.shape[-1])):
+            rows, cols = slice(256 * i, 256 * i + 256), slice(256 * j, 256 * j + 256)
+            blk = packed[:, u].clone()
+            if i == j:  # the lower-left quarter mirrors the upper-right one
+                blk[:, 128:, :128] = blk[:, :128, 128:].mT
+                full[:, rows, cols] = blk
+            else:
+                full[:, rows, cols] = blk
+                full[:, cols, rows] = blk.mT
+
     @staticmethod
     def apply(poly, x, y, a, n=None, stream=None):
         m = x.shape[1]

@@ -77,7 +77,8 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _column_worker(rank, world, port, m, n, steps, out_dir, shard_poly=False, overlap=0):
+def _column_worker(rank, world, port, m, n, steps, out_dir, shard_poly=False, overlap=0,
+                   packed=True):
     import datetime
 
     import torch.distributed as dist
@@ -93,9 +94,18 @@ def _column_worker(rank, world, port, m, n, steps, out_dir, shard_poly=False, ov
     cols = column_range(n, rank, world)
     x_local = x[:, cols.start:cols.stop].contiguous()
     driver = ColumnShardedPolar(m, "cpu", backend=CpuKernels(), shard_poly=shard_poly,
-                                overlap_bands=overlap)
+                                overlap_bands=overlap, packed=packed)
     assert len(driver.bands) == (min(overlap, driver.mp // 256) if overlap > 1 else 0)
-    if shard_poly:
+    assert driver.packed == (packed and overlap <= 1)
+    if driver.packed:
+        # units of the upper triangle, cut into equal slabs (the last padded)
+        d = driver.mp // 256
+        units = d * (d + 1) // 2
+        per = -(-units // world)
+        assert driver.unit_slab == (rank * per, max(0, min(per, units - rank * per)))
+        bytes_ = driver.collective_bytes()
+        assert bytes_["reduce_scatter_fp32"] == 4 * per * world * 256 * 256
+    elif shard_poly:
         # 2 ranks, Mp = 512: rank r computes polynomial rows [256 r, 256 r + 256)
         assert driver.poly_slab == (256 * rank, 256)
     y = driver.run(x_local, COEFFICIENTS[:steps])
@@ -104,25 +114,33 @@ def _column_worker(rank, world, port, m, n, steps, out_dir, shard_poly=False, ov
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("m,n,steps,shard_poly,overlap", [(96, 200, 1, False, 0),
-                                                        (130, 256, 2, False, 0),
-                                                        (300, 320, 2, True, 0),
-                                                        (600, 640, 2, False, 3)])
-def test_column_sharded_two_ranks_match_single(tmp_path, m, n, steps, shard_poly, overlap):
-    """Two gloo ranks, each owning a column slab, against the single-process
-    dataflow; `overlap` runs the Gram in row bands, each band all-reduced
-    on its own."""
+@pytest.mark.parametrize("m,n,steps,shard_poly,overlap,packed,world", [
+    (96, 200, 1, False, 0, True, 2),     # one unit: rank 1 has only padding
+    (130, 256, 2, False, 0, True, 2),
+    (520, 700, 2, False, 0, True, 2),    # 3 x 3 units, 6 of them packed
+    (1000, 1200, 1, False, 0, True, 3),  # 10 units on 3 ranks: 4 + 4 + 2
+    (300, 320, 2, True, 0, False, 2),    # all-reduce + polynomial row slabs
+    (600, 640, 1, False, 0, False, 2),   # all-reduce, polynomial replicated
+    (600, 640, 2, False, 3, False, 2)])  # all-reduce band by band
+def test_column_sharded_ranks_match_single(tmp_path, m, n, steps, shard_poly, overlap, packed,
+                                          world):
+    """gloo ranks, each owning a column slab, against the single-process
+    dataflow: by default on the packed upper triangle (reduce-scatter of
+    the fp32 units, all-gathers of packed A and P); `packed=False` with a
+    full all-reduce, `overlap` running the Gram in row bands, each band
+    all-reduced on its own."""
     ctx = mp.get_context("spawn")
     port = _free_port()
     procs = [ctx.Process(target=_column_worker,
-                         args=(r, 2, port, m, n, steps, str(tmp_path), shard_poly, overlap))
-             for r in range(2)]
+                         args=(r, world, port, m, n, steps, str(tmp_path), shard_poly, overlap,
+                               packed))
+             for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
-    y = torch.cat([torch.load(tmp_path / f"y{r}.pt") for r in range(2)], dim=1)
+    y = torch.cat([torch.load(tmp_path / f"y{r}.pt") for r in range(world)], dim=1)
     x = make_input((m, n), seed=7)
     ref = x.unsqueeze(0)
     for a, b, c in COEFFICIENTS[:steps]:

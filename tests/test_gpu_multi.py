@@ -28,7 +28,8 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, m, n, steps, out_dir, shard_poly=False, overlap=0):
+def _worker(rank, world, port, m, n, steps, out_dir, shard_poly=False, overlap=0,
+            packed=True):
     import datetime
 
     import torch
@@ -48,8 +49,10 @@ def _worker(rank, world, port, m, n, steps, out_dir, shard_poly=False, overlap=0
     x = make_input((m, n), seed=9)
     cols = column_range(n, rank, world)
     x_local = x[:, cols.start:cols.stop].contiguous().to(device)
-    driver = ColumnShardedPolar(m, device, shard_poly=shard_poly, overlap_bands=overlap)
-    assert (driver.poly_slab is not None) == shard_poly
+    driver = ColumnShardedPolar(m, device, shard_poly=shard_poly, overlap_bands=overlap,
+                                packed=packed)
+    assert driver.packed == (packed and overlap <= 1)
+    assert (driver.poly_slab is not None) == (shard_poly and not driver.packed)
     y = driver.run(x_local, COEFFICIENTS[:steps])
     torch.cuda.synchronize()
     torch.save(y.cpu(), os.path.join(out_dir, f"y{rank}.pt"))
@@ -58,18 +61,23 @@ def _worker(rank, world, port, m, n, steps, out_dir, shard_poly=False, overlap=0
 
 
 @pytest.mark.skipif(_gpus() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("m,n,steps,shard_poly,overlap", [(512, 4096, 1, False, 0),
-                                                        (1024, 8192, 5, False, 0),
-                                                        (1024, 8192, 5, True, 0),
-                                                        (1024, 8192, 5, True, 4)])
-def test_column_sharded_nccl_matches_single_gpu(tmp_path, m, n, steps, shard_poly, overlap):
+@pytest.mark.parametrize("m,n,steps,shard_poly,overlap,packed", [
+    (512, 4096, 1, False, 0, True),      # packed units: reduce-scatter + all-gathers
+    (1024, 8192, 5, False, 0, True),
+    (520, 3000, 5, False, 0, True),      # ragged: Mp = 768, slabs of 1504 / 1496 columns
+    (1024, 8192, 5, False, 0, False),    # full all-reduce, polynomial replicated
+    (1024, 8192, 5, True, 0, False),     # full all-reduce, polynomial row slabs
+    (1024, 8192, 5, True, 4, False)])    # all-reduce band by band
+def test_column_sharded_nccl_matches_single_gpu(tmp_path, m, n, steps, shard_poly, overlap,
+                                                packed):
     import muon_fusion_ascend950_b200 as pkg
     from oracle.polar_oracle import COEFFICIENTS, error_stats, make_input, reference_formula
 
     ctx = mp.get_context("spawn")
     port = _free_port()
     procs = [ctx.Process(target=_worker,
-                         args=(r, 2, port, m, n, steps, str(tmp_path), shard_poly, overlap))
+                         args=(r, 2, port, m, n, steps, str(tmp_path), shard_poly, overlap,
+                               packed))
              for r in range(2)]
     for p in procs:
         p.start()
