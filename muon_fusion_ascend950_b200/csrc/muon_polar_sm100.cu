@@ -484,6 +484,30 @@ __global__ void __launch_bounds__(kTileThreads, 1)
             tma_load_3d(dst, &tmap_b, &full[s], c0, c1, w.b);
         }
       };
+      if constexpr (KIND == kGramBf16 || KIND == kGramF32 || KIND == kGramT) {
+        // X is usually not written by the kernel this one waits for, and
+        // its first touch comes from DRAM: the CTA of each diagonal tile
+        // brings its row block of X (every row block has one) into L2 while
+        // the previous kernel finishes, so that each byte is fetched once.
+        // Measured on B200 at [8,512,2048] the Gram's first stage otherwise
+        // lands about 2 us after the wait; every CTA prefetching both of
+        // its operands requested X four times over and slowed the step.
+        if (pid == 0 && cluster < p.total_items) {
+          const WorkItem w = decode_item(p, cluster, kSym);
+          if (kSym && w.tm == w.tn) {
+            const int rows = w.tm * kTileM + static_cast<int>(rank) * kHalf;
+            for (int kb = w.kb_begin; kb < w.kb_end; ++kb) {
+#pragma unroll
+              for (int j = 0; j < kBoxesA; ++j) {
+                if constexpr (kAmn)
+                  tma_prefetch_l2_3d(&tmap_a, rows + j * kAtom, kb * Cfg::kBK, w.b);
+                else
+                  tma_prefetch_l2_3d(&tmap_a, kb * Cfg::kBK + j * kAtom, rows, w.b);
+              }
+            }
+          }
+        }
+      }
       grid_dependency_wait();
       grid_launch_dependents();
       uint32_t it = 0;

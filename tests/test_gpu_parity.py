@@ -74,7 +74,11 @@ def _assert_within_ulps(actual, expected64, ulps, what, abs_slack=0.0, max_frac=
     return frac
 
 
-MODES = ["single", "single_split", "pair", "pair_split"]
+# engine (single CTAs / CTA pairs) x split-K: none (no scratch), "split"
+# (uniform split forced wherever the device has room), "auto" (scratch
+# passed, plan by size as the operator runs it: the exchange split of the
+# off-diagonal tiles where it pays, e.g. the config-1 Gram on single CTAs)
+MODES = ["single", "single_split", "single_auto", "pair", "pair_split", "pair_auto"]
 _POLICY = {"single": 2, "pair": 1}
 
 
@@ -84,8 +88,8 @@ def mode_policy(api):
     returns whether the mode passes split-K scratch."""
     def set_mode(mode):
         api.set_kernel_policy(_POLICY[mode.split("_")[0]])
-        split = mode.endswith("_split")
-        api.set_split_mode(1 if split else 0)
+        split = mode.endswith("_split") or mode.endswith("_auto")
+        api.set_split_mode(1 if mode.endswith("_split") else 0)
         return split
     yield set_mode
     api.set_kernel_policy(0)
