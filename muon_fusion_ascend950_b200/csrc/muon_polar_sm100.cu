@@ -94,6 +94,15 @@ struct EpiParams {
   int32_t packed_d;      // units per side: mp / 256
   int32_t packed_units;  // units per matrix: packed_d (packed_d + 1) / 2
   int32_t tile_offset;
+  // Gram kinds with K-major X: X itself (rows of prefetch_row_bytes, matrices
+  // prefetch_batch_bytes apart, prefetch_rows rows of prefetch_lines 128-byte
+  // lines), for the L2 prefetch of the diagonal tiles' row blocks; null
+  // otherwise.
+  const uint8_t* prefetch_base;
+  int64_t prefetch_row_bytes;
+  int64_t prefetch_batch_bytes;
+  int32_t prefetch_rows;
+  int32_t prefetch_lines;
 };
 
 struct TileCoord {
@@ -484,56 +493,60 @@ __global__ void __launch_bounds__(kTileThreads, 1)
             tma_load_3d(dst, &tmap_b, &full[s], c0, c1, w.b);
         }
       };
-      if constexpr (KIND == kGramBf16 || KIND == kGramF32 || KIND == kGramT) {
-        // X is usually not written by the kernel this one waits for, and
-        // its first touch comes from DRAM: the CTA of each diagonal tile
-        // brings its row block of X (every row block has one) into L2 while
-        // the previous kernel finishes, so that each byte is fetched once.
-        // Measured on B200 at [8,512,2048] the Gram's first stage otherwise
-        // lands about 2 us after the wait; every CTA prefetching both of
-        // its operands requested X four times over and slowed the step.
-        if (pid == 0 && cluster < p.total_items) {
-          const WorkItem w = decode_item(p, cluster, kSym);
-          if (kSym && w.tm == w.tn) {
-            const int rows = w.tm * kTileM + static_cast<int>(rank) * kHalf;
-            for (int kb = w.kb_begin; kb < w.kb_end; ++kb) {
-#pragma unroll
-              for (int j = 0; j < kBoxesA; ++j) {
-                if constexpr (kAmn)
-                  tma_prefetch_l2_3d(&tmap_a, rows + j * kAtom, kb * Cfg::kBK, w.b);
-                else
-                  tma_prefetch_l2_3d(&tmap_a, kb * Cfg::kBK + j * kAtom, rows, w.b);
-              }
-            }
-          }
+      // This producer's share of an item: a diagonal tile of a symmetric
+      // kind multiplies a row block by itself, so only the A operand is
+      // loaded (the MMA reads it twice) and the producers split its boxes;
+      // otherwise producer 0 loads all of A, producer 1 all of B.
+      struct Share {
+        bool diag;
+        int a0, a1;
+        uint32_t bytes;
+      };
+      auto share_of = [&](const WorkItem& w) {
+        constexpr int kHalfA = kBoxesA / 2;
+        Share sh;
+        sh.diag = kSym && w.tm == w.tn;
+        sh.a0 = sh.diag ? (pid == 0 ? 0 : kHalfA) : 0;
+        sh.a1 = sh.diag ? (pid == 0 ? kHalfA : kBoxesA) : (pid == 0 ? kBoxesA : 0);
+        sh.bytes = static_cast<uint32_t>(sh.a1 - sh.a0) * kBoxBytesA +
+                   (!sh.diag && pid == 1 ? Cfg::kBHalfBytes : 0u);
+        return sh;
+      };
+      // The first stage's bookkeeping (decode, expected bytes) runs before
+      // the grid dependency wait, so that the loads follow the wait at once:
+      // measured on B200, code first executed after the wait stalls on
+      // instruction fetch (0.2-0.3 us per miss), about 0.8 us before the
+      // first load of each kernel; moving it ahead made the config-1 step
+      // 0.6 us faster.
+      uint32_t it = 0;
+      bool ok = true;
+      WorkItem w_first = {};
+      bool prepared = false;  // stage 0 is free and its bytes are expected
+      if (cluster < p.total_items) {
+        w_first = decode_item(p, cluster, kSym);
+        if (w_first.kb_begin < w_first.kb_end) {
+          if (rank == 0) mbar_arrive_expect_tx(&full[0], PAIR * share_of(w_first).bytes);
+          prepared = true;
         }
       }
       grid_dependency_wait();
       grid_launch_dependents();
-      uint32_t it = 0;
-      bool ok = true;
       for (int item = cluster; ok && item < p.total_items; item += nclusters) {
-        const WorkItem w = decode_item(p, item, kSym);
-        // A diagonal tile of a symmetric kind multiplies a row block by
-        // itself: only the A operand is loaded, and the MMA reads it twice.
-        const bool diag = kSym && w.tm == w.tn;
-        // this producer's boxes of A: all of them (pid 0, off-diagonal),
-        // none (pid 1, off-diagonal), or its half of them (diagonal)
-        constexpr int kHalfA = kBoxesA / 2;
-        const int a0 = diag ? (pid == 0 ? 0 : kHalfA) : 0;
-        const int a1 = diag ? (pid == 0 ? kHalfA : kBoxesA) : (pid == 0 ? kBoxesA : 0);
-        const uint32_t bytes =
-            static_cast<uint32_t>(a1 - a0) * kBoxBytesA + (!diag && pid == 1 ? Cfg::kBHalfBytes : 0u);
+        const WorkItem w = item == cluster ? w_first : decode_item(p, item, kSym);
+        const Share sh = share_of(w);
         for (int kb = w.kb_begin; kb < w.kb_end; ++kb, ++it) {
           const uint32_t s = it % S;
           const uint32_t ph = (it / S) & 1u;
-          if (!mbar_wait_bounded(&empty[s], ph ^ 1u)) {
-            ok = false;
-            break;
+          if (!prepared) {
+            if (!mbar_wait_bounded(&empty[s], ph ^ 1u)) {
+              ok = false;
+              break;
+            }
+            if (rank == 0) mbar_arrive_expect_tx(&full[s], PAIR * sh.bytes);
           }
-          if (rank == 0) mbar_arrive_expect_tx(&full[s], PAIR * bytes);
-          load_a(s, w, kb, a0, a1);
-          if (!diag && pid == 1) load_b(s, w, kb);
+          prepared = false;
+          load_a(s, w, kb, sh.a0, sh.a1);
+          if (!sh.diag && pid == 1) load_b(s, w, kb);
         }
       }
       if (!ok) atomicOr(&g_watchdog, MUON_POLAR_WATCHDOG_PRODUCER);
@@ -552,7 +565,9 @@ __global__ void __launch_bounds__(kTileThreads, 1)
       grid_launch_dependents();
     }
   } else if (warp == 1) {
-    grid_dependency_wait();
+    // The MMA warp reads no global memory (only shared memory that the
+    // producers fill after their dependency wait), so it does not wait for
+    // the previous grid.
     grid_launch_dependents();
     if (lane == 0 && rank == 0) {
       // ---------------- tcgen05 MMA issuer (leader CTA only)
@@ -651,6 +666,33 @@ __global__ void __launch_bounds__(kTileThreads, 1)
           mbar_arrive_cluster(acc ? tempty_leader1 : tempty_leader0);
       }
     };
+    if constexpr (KIND == kGramBf16 || KIND == kGramF32) {
+      // X is usually not written by the kernel this one waits for, and its
+      // first touch comes from DRAM: before the dependency wait the
+      // epilogue threads of each diagonal tile's CTA bring that tile's row
+      // block of X (every row block has one) into L2, so that each byte is
+      // fetched once.  Plain prefetch instructions leave the CTA's TMA unit
+      // to its operand loads; issuing the same prefetch as TMA boxes held
+      // a diagonal CTA's first loads back by up to 3 us when it started
+      // late (measured on B200 at [8,512,2048], where this form is 0.7 us
+      // faster per step).  Prefetching into L2, the point of coherence, is
+      // safe even while the previous kernel still writes X.
+      if (p.prefetch_base != nullptr && cluster < p.total_items) {
+        const WorkItem w = decode_item(p, cluster, kSym);
+        if (w.tm == w.tn) {
+          const int r0 = w.tm * kTileM + static_cast<int>(rank) * kHalf;
+          const int total = kHalf * p.prefetch_lines;
+          // line-major order: the first k-blocks of every row come first
+          for (int l = static_cast<int>(threadIdx.x) - kEpiLeader; l < total;
+               l += kPairEpiThreads) {
+            const int row = r0 + (l % kHalf);
+            if (row < p.prefetch_rows)
+              prefetch_l2(p.prefetch_base + w.b * p.prefetch_batch_bytes +
+                          row * p.prefetch_row_bytes + (l / kHalf) * 128);
+          }
+        }
+      }
+    }
     // Everything, X included, is loaded after the grid dependency wait:
     // measured on B200, loading the apply's X (operand stages and epilogue
     // tile) before it delayed the P loads queued behind it and made the
@@ -2104,6 +2146,13 @@ int gram_launch(DeviceState* st, const void* x, void* gram, int64_t batch, int64
   }
   if (rc != MUON_POLAR_OK) return rc;
   sym_grid<PAIR>(p, batch, mp);
+  if (!kT) {
+    p.prefetch_base = static_cast<const uint8_t*>(x);
+    p.prefetch_row_bytes = ldx * 2;
+    p.prefetch_batch_bytes = m * ldx * 2;
+    p.prefetch_rows = static_cast<int32_t>(m);
+    p.prefetch_lines = static_cast<int32_t>((n * 2 + 127) / 128);
+  }
   if (band_rows > 0) {
     // the upper tiles of tile rows [t0, t0 + nt)
     const int64_t th = kHalf * PAIR;

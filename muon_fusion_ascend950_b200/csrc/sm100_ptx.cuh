@@ -98,16 +98,12 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map,
       : "memory");
 }
 
-// Prefetch of one 3-D tile into L2 (no shared memory, no completion).  The
-// L2 is the point of coherence for every SM, so prefetching data that a
-// still-running kernel may write gives no stale reads: later loads see the
-// writes.
-__device__ __forceinline__ void tma_prefetch_l2_3d(const CUtensorMap* map, int32_t c0, int32_t c1,
-                                                   int32_t c2) {
-  asm volatile(
-      "cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];" ::"l"(map),
-      "r"(c0), "r"(c1), "r"(c2)
-      : "memory");
+// Prefetch of the 128-byte line holding `p` into L2 (no completion, no
+// register result).  The L2 is the point of coherence for every SM, so
+// prefetching data that a still-running kernel may write gives no stale
+// reads: later loads see the writes.
+__device__ __forceinline__ void prefetch_l2(const void* p) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(p) : "memory");
 }
 
 // 3-D tiled bulk tensor store shared -> global (bulk-group completion).
