@@ -466,19 +466,63 @@ def run_sharded(rank: int, world: int, device, sync_all) -> dict:
 
 
 # --------------------------------------------------------------------- arms
+def reference_large_rate(workload: str):
+    """The reference formula on the host CPU for configs 4 and 5, too large to
+    run whole: one matrix of each shape, extrapolated by count (config 4: the
+    5-step loop on one [4096,4096] and one [4096,11008] matrix, x128 and x96;
+    config 5: one step of the [8192,65536] matrix, x5).  Returns (TFLOP/s,
+    ms per update, threads, sample description)."""
+    import torch
+
+    from oracle.polar_oracle import make_input, nominal_flops, reference_formula
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    if workload == "cfg4":
+        parts = [((4096, 4096), 128, COEFFICIENTS), ((4096, 11008), 96, COEFFICIENTS)]
+        what = "the 5-step loop on one [4096,4096] and one [4096,11008] matrix, x128 and x96"
+    else:
+        parts = [((8192, 65536), 5, COEFFICIENTS[:1])]
+        what = "one step of the [8192,65536] matrix, x5"
+    flops = 0.0
+    ms = 0.0
+    for (m, n), count, rows in parts:
+        x = make_input((1, m, n), seed=0)
+        t0 = time.perf_counter()
+        reference_formula(x, rows)
+        ms += count * (time.perf_counter() - t0) * 1e3
+        flops += count * len(rows) * nominal_flops(m, n)
+        del x
+    return flops / (ms * 1e-3) / 1e12, ms, threads, (
+        f"{what} (bf16, one timed run each, no warm-up), extrapolated by count")
+
+
 def run_reference(args):
     rank, world, _ = dist_env()
     if rank != 0:
         return
-    rate, threads, sample = cpu_reference_rate(args.steps, args.warmup, budget_s=120.0)
-    ms = BATCH * nominal_flops_per_matrix(M, N) / (rate * 1e12) * 1e3
+    global BATCH, M, N
+    workload = args.workload
+    if workload in ("shape", "express"):
+        BATCH, M, N = (int(v) for v in args.shape.split(","))
+    if workload in ("cfg4", "cfg5"):
+        rate, ms, threads, sample = reference_large_rate(workload)
+        metric = f"{workload} effective TFLOP/s (nominal 4M^2N+2M^3 per matrix per step)"
+        config = {"workload": workload}
+    else:
+        rows = len(COEFFICIENTS) if workload in ("cfg3", "express") else 1
+        rate, threads, sample = cpu_reference_rate(args.steps, args.warmup, budget_s=120.0,
+                                                   rows=rows)
+        ms = rows * BATCH * nominal_flops_per_matrix(M, N) / (rate * 1e12) * 1e3
+        metric = metric_name(workload)
+        config = workload_config(workload, args.gpus)
     line = {
         "impl": "reference",
-        "metric": metric_name("cfg1"),
+        "metric": metric,
         "value": rate, "unit": "TFLOP/s", "n_gpus": args.gpus, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": workload_config("cfg1", args.gpus),
+        "config": config,
         "timing": "host CPU (rank 0 only, every thread): the reference's PyTorch formula on a "
                   "bounded sample of the workload, median of the timed steps",
         "cpu_baseline": {"value": rate, "unit": "TFLOP/s", "cores": threads, "kind": "port",

@@ -385,6 +385,13 @@ int muon_polar_device_pairs(int* pairs);
  * points, all devices).  Used by benchmarks to report launch counts. */
 uint64_t muon_polar_launch_count(void);
 
+/* Number of tensor maps the library has encoded with the driver in this
+ * process.  Maps are memoised on their arguments (address, sizes, strides,
+ * box), so repeated calls on the same buffers encode nothing; the binding
+ * keeps the reference's launch-state caches (binding.cpp:103-330) in this
+ * form. */
+uint64_t muon_polar_tensor_map_encodes(void);
+
 /* Sets the limit of every bounded wait inside this library's kernels on the
  * current device (default 2 s): a wait that has not ended after `limit_ns`
  * nanoseconds of wall-clock time gives up, sets its watchdog bit

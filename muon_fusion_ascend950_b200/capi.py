@@ -77,6 +77,7 @@ SIGNATURES = {
     "muon_polar_set_split_mode": (ctypes.c_int, [ctypes.c_int]),
     "muon_polar_device_pairs": (ctypes.c_int, [ctypes.POINTER(ctypes.c_int)]),
     "muon_polar_launch_count": (ctypes.c_uint64, []),
+    "muon_polar_tensor_map_encodes": (ctypes.c_uint64, []),
     "muon_polar_set_wait_limit_ns": (ctypes.c_int, [ctypes.c_uint64,
                                                     ctypes.POINTER(ctypes.c_uint64)]),
     "muon_polar_set_static_scratch_limit": (ctypes.c_size_t, [ctypes.c_size_t]),
@@ -194,6 +195,9 @@ class CAPI:
 
     def launch_count(self) -> int:
         return int(self.lib.muon_polar_launch_count())
+
+    def tensor_map_encodes(self) -> int:
+        return int(self.lib.muon_polar_tensor_map_encodes())
 
     def read_device_status(self, device: int, clear: bool = True) -> int:
         flags = ctypes.c_uint32(0)

@@ -1797,10 +1797,49 @@ int current_device_state(DeviceState** out) {
 
 // 3-D tiled map over a row-major [d2][d1][d0] tensor (d0 innermost), 128-byte
 // swizzle, out-of-bounds elements read as zero.
+// Encoded maps, memoised.  A map is a pure function of the arguments of
+// encode_3d (the address is part of the key, and device addresses are unique
+// across devices), so an entry stays valid even after its buffer is freed
+// and another takes the same address: it is what encoding again would give.
+// Direct-mapped on a hash of the key; a step launches three to five maps per
+// kernel, and a hit replaces the driver's encode by a compare and a copy.
+struct MapKey {
+  uint64_t v[7];
+  bool operator==(const MapKey& o) const {
+    for (int i = 0; i < 7; ++i)
+      if (v[i] != o.v[i]) return false;
+    return true;
+  }
+};
+struct MapCacheEntry {
+  MapKey key;
+  CUtensorMap map;
+  bool valid;
+};
+constexpr int kMapCacheSlots = 512;
+std::mutex g_map_mutex;
+MapCacheEntry g_map_cache[kMapCacheSlots];
+std::atomic<uint64_t> g_map_encodes{0};
+
 int encode_3d(CUtensorMap* map, CUtensorMapDataType dtype, size_t elem_bytes,
               const void* base, uint64_t d0, uint64_t d1, uint64_t d2,
               uint64_t stride1_elems, uint64_t stride2_elems, uint32_t box0,
               uint32_t box1) {
+  const MapKey key = {{reinterpret_cast<uintptr_t>(base), d0, d1, d2, stride1_elems,
+                       stride2_elems,
+                       (static_cast<uint64_t>(dtype) << 48) |
+                           (static_cast<uint64_t>(elem_bytes) << 40) |
+                           (static_cast<uint64_t>(box0) << 20) | box1}};
+  uint64_t h = 1469598103934665603ull;  // FNV-1a over the key words
+  for (uint64_t w : key.v) h = (h ^ w) * 1099511628211ull;
+  MapCacheEntry& slot = g_map_cache[(h ^ (h >> 29)) % kMapCacheSlots];
+  {
+    std::lock_guard<std::mutex> lock(g_map_mutex);
+    if (slot.valid && slot.key == key) {
+      *map = slot.map;
+      return MUON_POLAR_OK;
+    }
+  }
   EncodeTiledFn fn = encode_fn();
   if (fn == nullptr) return MUON_POLAR_ERR_DRIVER;
   const cuuint64_t dims[3] = {d0, d1, d2};
@@ -1813,7 +1852,13 @@ int encode_3d(CUtensorMap* map, CUtensorMapDataType dtype, size_t elem_bytes,
                   CU_TENSOR_MAP_SWIZZLE_128B,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS ? MUON_POLAR_OK : MUON_POLAR_ERR_TENSOR_MAP;
+  if (r != CUDA_SUCCESS) return MUON_POLAR_ERR_TENSOR_MAP;
+  g_map_encodes.fetch_add(1, std::memory_order_relaxed);
+  std::lock_guard<std::mutex> lock(g_map_mutex);
+  slot.key = key;
+  slot.map = *map;
+  slot.valid = true;
+  return MUON_POLAR_OK;
 }
 
 bool aligned16(const void* p) {
@@ -3164,6 +3209,10 @@ int muon_polar_device_pairs(int* pairs) {
 
 uint64_t muon_polar_launch_count(void) {
   return g_launch_count.load(std::memory_order_relaxed);
+}
+
+uint64_t muon_polar_tensor_map_encodes(void) {
+  return g_map_encodes.load(std::memory_order_relaxed);
 }
 
 int muon_polar_set_wait_limit_ns(uint64_t limit_ns, uint64_t* previous) {

@@ -399,6 +399,32 @@ def test_step_by_size_choice(api, cuda_device, shape, fused, step_mode):
     assert torch.equal(y0.view(torch.int16), y1.view(torch.int16))
 
 
+@pytest.mark.parametrize("shape", [(8, 512, 2048), (1, 129, 136), (16, 512, 2048)])
+def test_tensor_maps_are_memoised(api, cuda_device, shape):
+    """A step on the same buffers encodes no tensor map the second time
+    (the memo of the C ABI's launch state), and gives the same bits."""
+    bsz, m, n = shape
+    x = make_input(shape, seed=21).to(cuda_device)
+    ws = torch.empty(api.workspace_bytes(bsz, m), dtype=torch.uint8, device=cuda_device)
+    scratch = api.new_scratch(bsz, m, n)
+    y0 = torch.empty_like(x)
+    api.step(x, y0, ws, A1, B1, C1, scratch=scratch)
+    torch.cuda.synchronize()
+    before = api.tensor_map_encodes()
+    y1 = torch.empty_like(x)
+    api.step(x, y1, ws, A1, B1, C1, scratch=scratch)
+    api.step(x, y1, ws, A1, B1, C1, scratch=scratch)
+    torch.cuda.synchronize()
+    _check_watchdog(api)
+    # y1 is a new output buffer: at most its own maps are new (first call)
+    assert api.tensor_map_encodes() - before <= 3
+    again = api.tensor_map_encodes()
+    api.step(x, y1, ws, A1, B1, C1, scratch=scratch)
+    torch.cuda.synchronize()
+    assert api.tensor_map_encodes() == again
+    assert torch.equal(y0.view(torch.int16), y1.view(torch.int16))
+
+
 def test_torch_compile_matches_eager(op, cuda_device):
     """torch.compile (aot_eager backend, full graph) traces the operator with
     its FakeTensor kernel and runs it; the result equals eager bit for bit."""
