@@ -377,6 +377,17 @@ int muon_polar_set_step_mode(int mode);
  * summation order, and so the last bit, depends on the split. */
 int muon_polar_set_split_mode(int mode);
 
+/* Column halves of the single-CTA Gram and polynomial launches: when every
+ * item fits on the device at once and no split-K is planned, off-diagonal
+ * 128 x 128 tiles run as two 128 x 64 halves (twice the CTAs for the same
+ * work; each half stores its columns and their mirror).  Returns the
+ * previous mode:
+ *   0  by size (default): whenever the halves fit in one round;
+ *   1  the same (kept for symmetry with the other mode setters);
+ *   2  never.
+ * The results are bit-identical in every mode. */
+int muon_polar_set_halves_mode(int mode);
+
 /* Number of 2-CTA clusters (tcgen05 CTA pairs) of the Gram kernel the
  * current device runs at once; the persistent grids are this many pairs. */
 int muon_polar_device_pairs(int* pairs);

@@ -103,6 +103,12 @@ struct EpiParams {
   int64_t prefetch_batch_bytes;
   int32_t prefetch_rows;
   int32_t prefetch_lines;
+  // Column halves (PAIR = 1 symmetric kinds): item (i, j) of each matrix's
+  // tiles_m x tiles_m grid is the diagonal tile (i, i) for i == j, the left
+  // 64 columns of tile (i, j) for i < j and the right 64 columns of tile
+  // (j, i) for i > j, so every element of the upper triangle is computed
+  // once, by tiles_m^2 items of at most 128 x 128.
+  int32_t halves;
 };
 
 struct TileCoord {
@@ -143,17 +149,35 @@ __host__ __device__ __forceinline__ TileCoord decode_tile(int tile, bool sym,
   return t;
 }
 
-// One work item: its tile, its K range (k-blocks [kb_begin, kb_end)) and
-// its place among the tile's splits.
+// One work item: its tile, its K range (k-blocks [kb_begin, kb_end)), its
+// place among the tile's splits, and which column half of the tile it
+// computes (-1: the whole tile).
 struct WorkItem {
   int tile, b, tm, tn;
   int split, nsplit;
   int kb_begin, kb_end;
+  int half;
 };
 
 __host__ __device__ __forceinline__ WorkItem decode_item(const EpiParams& p, int item,
                                                          bool sym) {
   WorkItem w;
+  if (p.halves) {
+    const int d = p.tiles_m;
+    w.b = item / (d * d);
+    const int r = item - w.b * d * d;
+    const int i = r / d, j = r - (r / d) * d;
+    w.tm = i < j ? i : j;
+    w.tn = i < j ? j : i;
+    w.half = i == j ? -1 : (i < j ? 0 : 1);
+    w.tile = item;
+    w.split = 0;
+    w.nsplit = 1;
+    w.kb_begin = 0;
+    w.kb_end = p.k_blocks;
+    return w;
+  }
+  w.half = -1;
   const int tile = item / p.splits;
   const bool walk = sym && !p.rows_mode;
   const TileCoord tc = decode_tile(tile, walk, p.tiles_m, p.tiles_n, p.tiles_per_batch,
@@ -219,8 +243,12 @@ constexpr int64_t k_blocks_of(int64_t k) {
 
 // Shared-memory and tensor-memory plan of one CTA of polar_tile_kernel.
 // PAIR = 2: a 256 x 256 tile on a tcgen05 CTA pair (each CTA owns a 128 x 256
-// band); PAIR = 1: a 128 x 128 tile on one CTA.
-template <int KIND, int PAIR = 2>
+// band); PAIR = 1: a 128 x 128 tile on one CTA.  HALVES (PAIR = 1, symmetric
+// kinds, one work item per CTA): off-diagonal tiles are computed as two
+// 128 x 64 column halves, diagonal tiles whole (see decode_item); a half has
+// one epilogue chunk and a diagonal tile no mirror, so the polynomial's
+// epilogue needs two chunk regions (the mirror of a half shares the second).
+template <int KIND, int PAIR = 2, bool HALVES = false>
 struct PairCfg {
   static constexpr bool kSym = KIND != kApply && KIND != kApplyT;
   static constexpr bool kAux = KIND == kPoly || KIND == kApply || KIND == kApplyT;
@@ -239,13 +267,14 @@ struct PairCfg {
   static constexpr int kOutRegions = kAux ? kChunks : 1;
   // The polynomial double-buffers its mirror chunk (it still fits four
   // stages); the Gram single-buffers it.
-  static constexpr int kMirRegions = kSym ? (kAux ? 2 : 1) : 0;
+  static constexpr int kMirRegions = kSym ? ((kAux && !HALVES) ? 2 : 1) : 0;
   // Store groups that may still read shared memory when a chunk starts: the
   // region a chunk writes was last used by the chunk kMirRegions before it.
-  static constexpr int kPending = (kSym && kAux) ? 1 : 0;
+  static constexpr int kPending = (kSym && kAux && !HALVES) ? 1 : 0;
   static constexpr bool kWaitPerChunk = kSym;
   static constexpr uint32_t kEpiBytes =
-      kOutRegions * kOutChunkBytes + kMirRegions * kMirChunkBytes;
+      (HALVES && kAux) ? kOutRegions * kOutChunkBytes
+                       : kOutRegions * kOutChunkBytes + kMirRegions * kMirChunkBytes;
   static constexpr uint32_t kAHalfBytes = kHalf * kBK * 2;
   static constexpr uint32_t kBHalfBytes = kHalf * kBK * 2;
   static constexpr uint32_t kStageBytes = kAHalfBytes + kBHalfBytes;
@@ -371,7 +400,10 @@ constexpr int kProducerWarp2 = 10;
 // split-K paths out of the other launches cuts the kernel's registers (the
 // single-CTA Gram from 145 to 77, the pair apply from 158 to 101); measured
 // on B200 the config-1 step 38.9 -> 37.5 us.
-template <int KIND, int PAIR, bool SPLIT>
+// HALVES: the column-halves decomposition (PAIR = 1, symmetric kinds, one
+// item per CTA, no split-K; see EpiParams::halves).  tmap_b then has boxes
+// of 64 rows, the B operand of a half.
+template <int KIND, int PAIR, bool SPLIT, bool HALVES = false>
 __global__ void __launch_bounds__(kTileThreads, 1)
     polar_tile_kernel(const __grid_constant__ CUtensorMap tmap_a,
                       const __grid_constant__ CUtensorMap tmap_b,
@@ -379,7 +411,9 @@ __global__ void __launch_bounds__(kTileThreads, 1)
                       const __grid_constant__ CUtensorMap tmap_out,
                       const __grid_constant__ CUtensorMap tmap_mir,
                       const EpiParams p) {
-  using Cfg = PairCfg<KIND, PAIR>;
+  using Cfg = PairCfg<KIND, PAIR, HALVES>;
+  static_assert(!HALVES || (PAIR == 1 && Cfg::kSym && !SPLIT && KIND != kGramT),
+                "column halves: single-CTA symmetric kinds without split-K");
   constexpr int kTileM = Cfg::kTileM;
   constexpr int kTileN = Cfg::kTileN;
   constexpr int S = Cfg::kStages;
@@ -391,7 +425,9 @@ __global__ void __launch_bounds__(kTileThreads, 1)
   const uint32_t raw_addr = smem_addr(smem_raw);
   uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
   uint8_t* sOut = smem;
-  uint8_t* sMir = sOut + Cfg::kOutRegions * Cfg::kOutChunkBytes;
+  // (HALVES polynomial: a half's mirror shares the second chunk region,
+  // which only a diagonal tile uses as a chunk)
+  uint8_t* sMir = sOut + ((HALVES && Cfg::kAux) ? 1 : Cfg::kOutRegions) * Cfg::kOutChunkBytes;
   uint8_t* sA = smem + Cfg::kEpiBytes;
   uint8_t* sB = sA + S * Cfg::kAHalfBytes;
   uint64_t* full = reinterpret_cast<uint64_t*>(sB + S * Cfg::kBHalfBytes);
@@ -479,7 +515,8 @@ __global__ void __launch_bounds__(kTileThreads, 1)
       };
       auto load_b = [&](uint32_t s, const WorkItem& w, int kb) {
         const uint32_t bar = PAIR == 2 ? map_to_cta(smem_addr(&full[s]), 0) : 0u;
-        const int b_row = w.tn * kTileN + static_cast<int>(rank) * kHalf;
+        const int b_row = w.tn * kTileN + static_cast<int>(rank) * kHalf +
+                          (HALVES && w.half > 0 ? kChunkCols : 0);
         // K-major: [128 n x 64 k] boxes; MN-major: one [kBK k x 64 n] box per
         // 64-column chunk
 #pragma unroll
@@ -508,8 +545,11 @@ __global__ void __launch_bounds__(kTileThreads, 1)
         sh.diag = kSym && w.tm == w.tn;
         sh.a0 = sh.diag ? (pid == 0 ? 0 : kHalfA) : 0;
         sh.a1 = sh.diag ? (pid == 0 ? kHalfA : kBoxesA) : (pid == 0 ? kBoxesA : 0);
+        // (a column half's B operand is 64 rows: half the bytes)
         sh.bytes = static_cast<uint32_t>(sh.a1 - sh.a0) * kBoxBytesA +
-                   (!sh.diag && pid == 1 ? Cfg::kBHalfBytes : 0u);
+                   (!sh.diag && pid == 1
+                        ? (HALVES && w.half >= 0 ? Cfg::kBHalfBytes / 2 : Cfg::kBHalfBytes)
+                        : 0u);
         return sh;
       };
       // The first stage's bookkeeping (decode, expected bytes) runs before
@@ -571,13 +611,17 @@ __global__ void __launch_bounds__(kTileThreads, 1)
     grid_launch_dependents();
     if (lane == 0 && rank == 0) {
       // ---------------- tcgen05 MMA issuer (leader CTA only)
-      constexpr uint32_t idesc = idesc_bf16_f32(kTileN, kBmn ? 1u : 0u, kTileM, kAmn ? 1u : 0u);
+      constexpr uint32_t idesc_full =
+          idesc_bf16_f32(kTileN, kBmn ? 1u : 0u, kTileM, kAmn ? 1u : 0u);
+      constexpr uint32_t idesc_half =
+          idesc_bf16_f32(kChunkCols, kBmn ? 1u : 0u, kTileM, kAmn ? 1u : 0u);
       uint32_t it = 0;
       uint32_t t = 0;
       bool ok = true;
       for (int item = cluster; ok && item < p.total_items; item += nclusters, ++t) {
         const WorkItem w = decode_item(p, item, kSym);
         const bool diag = kSym && w.tm == w.tn;
+        const uint32_t idesc = (HALVES && w.half >= 0) ? idesc_half : idesc_full;
         const uint32_t acc = t & 1u;
         const uint32_t uph = (t >> 1) & 1u;
         if (!mbar_wait_bounded(&tempty[acc], uph ^ 1u)) {
@@ -652,9 +696,14 @@ __global__ void __launch_bounds__(kTileThreads, 1)
       const WorkItem w = decode_item(p, item, kSym);
       mbar_arrive_expect_tx(&aux_full[c], Cfg::kOutChunkBytes);
       tma_load_3d(sOut + c * Cfg::kOutChunkBytes, &tmap_aux, &aux_full[c],
-                  w.tn * kTileN + c * kChunkCols, w.tm * kTileM + static_cast<int>(rank) * kHalf,
-                  w.b);
+                  w.tn * kTileN + (HALVES && w.half > 0 ? kChunkCols : 0) + c * kChunkCols,
+                  w.tm * kTileM + static_cast<int>(rank) * kHalf, w.b);
       ++aux_issued[c];
+    };
+    // Chunks of an item's epilogue: one for a column half.
+    auto chunks_of = [&](int item) {
+      if constexpr (HALVES) return decode_item(p, item, kSym).half >= 0 ? 1 : Cfg::kChunks;
+      return Cfg::kChunks;
     };
     auto release_accumulator = [&](uint32_t acc) {
       tc_fence_before();
@@ -700,8 +749,10 @@ __global__ void __launch_bounds__(kTileThreads, 1)
     grid_dependency_wait();
     grid_launch_dependents();
     if constexpr (Cfg::kAux) {
-      if (leader && cluster < p.total_items)
-        for (int c = 0; c < Cfg::kChunks; ++c) load_aux_chunk(cluster, c);
+      if (leader && cluster < p.total_items) {
+        const int nch0 = chunks_of(cluster);
+        for (int c = 0; c < nch0; ++c) load_aux_chunk(cluster, c);
+      }
     }
     uint32_t t = 0;
     for (int item = cluster; item < p.total_items; item += nclusters, ++t) {
@@ -722,7 +773,8 @@ __global__ void __launch_bounds__(kTileThreads, 1)
         if (p.packed) mirror = false;
       }
       const int row0 = tc.tm * kTileM + static_cast<int>(rank) * kHalf;
-      const int col0 = tc.tn * kTileN;
+      const int col0 = tc.tn * kTileN + (HALVES && tc.half > 0 ? kChunkCols : 0);
+      const int nch = (HALVES && tc.half >= 0) ? 1 : Cfg::kChunks;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * kTileN;
       bool reduce = false;
       // Other splits' partial chunks c into buffer c % 2 of the (free)
@@ -805,6 +857,7 @@ __global__ void __launch_bounds__(kTileThreads, 1)
       tmem_ld_32x32b_x32(t_row + hc * 32, rbuf[0]);
 #pragma unroll
       for (int c = 0; c < Cfg::kChunks; ++c) {
+        if (HALVES && c >= nch) break;
         const int ro = c % Cfg::kOutRegions;
         const uint32_t out = out_base + ro * Cfg::kOutChunkBytes;
         constexpr int kMR = Cfg::kMirRegions > 0 ? Cfg::kMirRegions : 1;
@@ -815,7 +868,7 @@ __global__ void __launch_bounds__(kTileThreads, 1)
           named_barrier(1, kPairEpiThreads);
         }
         tmem_wait_ld(rbuf[c & 1]);
-        if (c + 1 < Cfg::kChunks)
+        if (c + 1 < nch)
           tmem_ld_32x32b_x32(t_row + (c + 1) * kChunkCols + hc * 32, rbuf[(c + 1) & 1]);
         else
           release_accumulator(acc);
@@ -896,7 +949,7 @@ __global__ void __launch_bounds__(kTileThreads, 1)
                            col0 + c * kChunkCols, tc.b);
           }
           bulk_commit_group();
-          if constexpr (Cfg::kAux) {
+          if constexpr (Cfg::kAux && !HALVES) {
             // region c - 1 has been read by its store: next item's chunk c - 1
             if (c >= 1 && next < p.total_items) {
               bulk_wait_group_read<1>();
@@ -905,7 +958,7 @@ __global__ void __launch_bounds__(kTileThreads, 1)
           }
         }
       }
-      if constexpr (Cfg::kAux) {
+      if constexpr (Cfg::kAux && !HALVES) {
         if (leader && next < p.total_items) {
           bulk_wait_group_read<0>();
           load_aux_chunk(next, Cfg::kChunks - 1);
@@ -1752,6 +1805,7 @@ struct DeviceState {
   int sms = 0;
   int cc_major = 0, cc_minor = 0;
   bool smem_attr_set[kNumInstances] = {};
+  bool smem_attr_set_halves[kNumInstances] = {};  // the HALVES kernels
   int capacity[kNumInstances] = {};  // tiles worked on at once (tile_capacity)
 };
 DeviceState g_devices[kMaxDevices];
@@ -1801,8 +1855,9 @@ int current_device_state(DeviceState** out) {
 // encode_3d (the address is part of the key, and device addresses are unique
 // across devices), so an entry stays valid even after its buffer is freed
 // and another takes the same address: it is what encoding again would give.
-// Direct-mapped on a hash of the key; a step launches three to five maps per
-// kernel, and a hit replaces the driver's encode by a compare and a copy.
+// 4-way set-associative on a mixed hash of the key, round-robin replacement
+// within a set; a step launches three to five maps per kernel, and a hit
+// replaces the driver's encode by a compare and a copy.
 struct MapKey {
   uint64_t v[7];
   bool operator==(const MapKey& o) const {
@@ -1816,10 +1871,18 @@ struct MapCacheEntry {
   CUtensorMap map;
   bool valid;
 };
-constexpr int kMapCacheSlots = 512;
+constexpr int kMapCacheSets = 128;
+constexpr int kMapCacheWays = 4;
 std::mutex g_map_mutex;
-MapCacheEntry g_map_cache[kMapCacheSlots];
+MapCacheEntry g_map_cache[kMapCacheSets][kMapCacheWays];
+uint8_t g_map_victim[kMapCacheSets];
 std::atomic<uint64_t> g_map_encodes{0};
+
+uint64_t mix64(uint64_t z) {  // splitmix64 finaliser
+  z = (z ^ (z >> 30)) * 0xbf58476d1ce4e5b9ull;
+  z = (z ^ (z >> 27)) * 0x94d049bb133111ebull;
+  return z ^ (z >> 31);
+}
 
 int encode_3d(CUtensorMap* map, CUtensorMapDataType dtype, size_t elem_bytes,
               const void* base, uint64_t d0, uint64_t d1, uint64_t d2,
@@ -1830,14 +1893,16 @@ int encode_3d(CUtensorMap* map, CUtensorMapDataType dtype, size_t elem_bytes,
                        (static_cast<uint64_t>(dtype) << 48) |
                            (static_cast<uint64_t>(elem_bytes) << 40) |
                            (static_cast<uint64_t>(box0) << 20) | box1}};
-  uint64_t h = 1469598103934665603ull;  // FNV-1a over the key words
-  for (uint64_t w : key.v) h = (h ^ w) * 1099511628211ull;
-  MapCacheEntry& slot = g_map_cache[(h ^ (h >> 29)) % kMapCacheSlots];
+  uint64_t h = 0;
+  for (uint64_t w : key.v) h = mix64(h ^ w);
+  const int set = static_cast<int>(h % kMapCacheSets);
   {
     std::lock_guard<std::mutex> lock(g_map_mutex);
-    if (slot.valid && slot.key == key) {
-      *map = slot.map;
-      return MUON_POLAR_OK;
+    for (MapCacheEntry& e : g_map_cache[set]) {
+      if (e.valid && e.key == key) {
+        *map = e.map;
+        return MUON_POLAR_OK;
+      }
     }
   }
   EncodeTiledFn fn = encode_fn();
@@ -1855,6 +1920,8 @@ int encode_3d(CUtensorMap* map, CUtensorMapDataType dtype, size_t elem_bytes,
   if (r != CUDA_SUCCESS) return MUON_POLAR_ERR_TENSOR_MAP;
   g_map_encodes.fetch_add(1, std::memory_order_relaxed);
   std::lock_guard<std::mutex> lock(g_map_mutex);
+  MapCacheEntry& slot = g_map_cache[set][g_map_victim[set]];
+  g_map_victim[set] = static_cast<uint8_t>((g_map_victim[set] + 1) % kMapCacheWays);
   slot.key = key;
   slot.map = *map;
   slot.valid = true;
@@ -1969,6 +2036,31 @@ void plan_no_splits(EpiParams& p) {
   p.counters = nullptr;
 }
 
+// Column halves (single-CTA symmetric launches): tiles_m^2 items per matrix
+// of at most 128 x 128 instead of tiles_m (tiles_m + 1) / 2 whole tiles, when
+// all of them fit on the device at once and no split-K is planned.  Measured
+// on B200, a single CTA's 128 x 128 tile is bound by shared-memory bandwidth
+// (the TMA writes and both MMA operand reads, about 125 cycles per
+// 128 x 128 x 16 MMA), and its time hardly depends on how many CTAs run (the
+// config-1 Gram: 11.6 us for 10 tiles, 12.6 us for 120): a half reads
+// 6 KiB and writes 6 KiB per 128 x 64 x 16 MMA, and twice as many CTAs share
+// the work.  Mode (muon_polar_set_halves_mode): 0 by size, 1 whenever the
+// items fit (tests), 2 never.
+std::atomic<int> g_halves_mode{0};
+
+void plan_halves(EpiParams& p, int64_t batch, int units) {
+  p.halves = 0;
+  const int mode = g_halves_mode.load(std::memory_order_relaxed);
+  if (mode == 2 || p.splits != 1 || p.rows_mode || p.packed || p.row_tile_begin != 0 ||
+      p.tile_offset != 0 || p.max_units > 0)
+    return;
+  const int64_t d = p.tiles_m;
+  const int64_t items = d * d * batch;
+  if (d < 2 || items > units) return;
+  p.halves = 1;
+  p.total_items = static_cast<int32_t>(items);
+}
+
 // Applies split-K to `p` if the scratch buffer allows it.
 template <int KIND, int PAIR>
 void plan_splits(EpiParams& p, void* scratch, size_t scratch_bytes, int units) {
@@ -2065,6 +2157,24 @@ int launch_tile(DeviceState* st, const TileMaps& maps, const EpiParams& p,
   int units = 0;
   int rc = tile_capacity<KIND, PAIR>(st, &units);
   if (rc != MUON_POLAR_OK) return rc;
+  constexpr bool kCanHalve = PAIR == 1 && PairCfg<KIND, PAIR>::kSym && KIND != kGramT;
+  if constexpr (kCanHalve) {
+    if (p.halves) {
+      // one work item per CTA (the kernel's column-halves layout needs it)
+      if (p.total_items > units || p.splits != 1) return MUON_POLAR_ERR_INVALID_ARGUMENT;
+      constexpr int inst = instance_of<KIND, PAIR>();
+      {
+        std::lock_guard<std::mutex> lock(g_attr_mutex);
+        if (!st->smem_attr_set_halves[inst]) {
+          cudaError_t e = cudaFuncSetAttribute(polar_tile_kernel<KIND, PAIR, false, true>,
+                                               cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               PairCfg<KIND, PAIR, true>::kSmemBytes);
+          if (e != cudaSuccess) return static_cast<int>(e);
+          st->smem_attr_set_halves[inst] = true;
+        }
+      }
+    }
+  }
   if (p.max_units > 0 && units > p.max_units) units = p.max_units;
   int ctas = PAIR * (p.total_items < units ? p.total_items : units);
   // Single-CTA tiles launch as clusters of two independent CTAs as well, so
@@ -2087,6 +2197,16 @@ int launch_tile(DeviceState* st, const TileMaps& maps, const EpiParams& p,
   cfg.attrs = attr;
   cfg.numAttrs = 2;
   cudaError_t e;
+  if constexpr (kCanHalve) {
+    if (p.halves) {
+      cfg.dynamicSmemBytes = PairCfg<KIND, PAIR, true>::kSmemBytes;
+      e = cudaLaunchKernelEx(&cfg, polar_tile_kernel<KIND, PAIR, false, true>, maps.a, maps.b,
+                             maps.aux, maps.out, maps.mir, p);
+      if (e != cudaSuccess) return static_cast<int>(e);
+      g_launch_count.fetch_add(1, std::memory_order_relaxed);
+      return MUON_POLAR_OK;
+    }
+  }
   if constexpr (PairCfg<KIND, PAIR>::kSym) {
     if (p.splits > 1)
       e = cudaLaunchKernelEx(&cfg, polar_tile_kernel<KIND, PAIR, true>, maps.a, maps.b, maps.aux,
@@ -2215,6 +2335,14 @@ int gram_launch(DeviceState* st, const void* x, void* gram, int64_t batch, int64
           scratch_bytes)
     return MUON_POLAR_ERR_STATIC_SCRATCH;
   plan_splits<KIND, PAIR>(p, scratch, scratch_bytes, units);
+  if constexpr (PAIR == 1 && !kT) {
+    if (!fixed_scratch) plan_halves(p, batch, units);
+    if (p.halves) {
+      rc = encode_3d(&tm.b, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, x, n, m, batch, ldx, m * ldx,
+                     kAtom, kChunkCols);
+      if (rc != MUON_POLAR_OK) return rc;
+    }
+  }
   if (fixed_scratch && p.splits > 1) {
     cudaError_t e = cudaMemsetAsync(scratch, 0, kCounterBytes, stream);
     if (e != cudaSuccess) return static_cast<int>(e);
@@ -2312,6 +2440,13 @@ int poly_launch(DeviceState* st, const void* gram, void* poly, int64_t batch, in
   p.coef_b = b;
   p.coef_c = c;
   plan_splits<kPoly, PAIR>(p, scratch, scratch_bytes, units);
+  if constexpr (PAIR == 1) {
+    plan_halves(p, batch, units);
+    if (p.halves) {
+      rc = encode_square(&tm.b, gram, batch, mp, false, kChunkCols);
+      if (rc != MUON_POLAR_OK) return rc;
+    }
+  }
   return launch_tile<kPoly, PAIR>(st, tm, p, stream);
 }
 
@@ -3192,6 +3327,11 @@ int muon_polar_set_kernel_policy(int policy) {
 int muon_polar_set_step_mode(int mode) {
   if (mode < 0 || mode > 2) return MUON_POLAR_ERR_INVALID_ARGUMENT;
   return g_step_mode.exchange(mode);
+}
+
+int muon_polar_set_halves_mode(int mode) {
+  if (mode < 0 || mode > 2) return MUON_POLAR_ERR_INVALID_ARGUMENT;
+  return g_halves_mode.exchange(mode);
 }
 
 int muon_polar_set_split_mode(int mode) {

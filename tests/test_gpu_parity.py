@@ -399,6 +399,42 @@ def test_step_by_size_choice(api, cuda_device, shape, fused, step_mode):
     assert torch.equal(y0.view(torch.int16), y1.view(torch.int16))
 
 
+@pytest.mark.parametrize("shape", [(8, 512, 2048), (4, 512, 2048), (1, 256, 1024),
+                                   (2, 150, 2064), (3, 640, 1000), (1, 1024, 512),
+                                   (9, 512, 2048)])
+def test_column_halves_match_whole_tiles(api, cuda_device, shape):
+    """The column-halves layout of the single-CTA Gram and polynomial (each
+    off-diagonal tile as two 128 x 64 halves, one item per CTA) gives the
+    bits of whole tiles: the Gram, the polynomial and a whole step, without
+    split-K.  (9, 512, 2048) has more items than CTAs, so the by-size rule
+    keeps whole tiles there and both modes agree trivially."""
+    bsz, m, n = shape
+    x = make_input(shape, seed=31).to(cuda_device)
+    mp = api.padded_rows(m)
+    prev_policy = api.set_kernel_policy(2)
+    outs = {}
+    try:
+        for mode in (2, 0):
+            api.set_halves_mode(mode)
+            g = torch.full((bsz, mp, mp), float("nan"), device=cuda_device, dtype=torch.bfloat16)
+            api.gram(x, g)
+            pm = torch.full_like(g, float("nan"))
+            api.poly(g, pm, B1, C1)
+            ws = torch.empty(api.workspace_bytes(bsz, m), dtype=torch.uint8, device=cuda_device)
+            y = torch.full_like(x, float("nan"))
+            api.step(x, y, ws, A1, B1, C1)
+            torch.cuda.synchronize()
+            _check_watchdog(api)
+            outs[mode] = (g, pm, y)
+    finally:
+        api.set_halves_mode(0)
+        api.set_kernel_policy(prev_policy)
+    for a, b in zip(outs[2], outs[0]):
+        assert torch.equal(a.view(torch.int16), b.view(torch.int16))
+    g = outs[0][0].float()
+    assert torch.equal(g, g.mT)  # both triangles written, exactly symmetric
+
+
 @pytest.mark.parametrize("shape", [(8, 512, 2048), (1, 129, 136), (16, 512, 2048)])
 def test_tensor_maps_are_memoised(api, cuda_device, shape):
     """A step on the same buffers encodes no tensor map the second time
