@@ -2663,10 +2663,20 @@ int apply_impl(const void* poly, const void* x, void* y, int64_t batch,
   if (rc != MUON_POLAR_OK) return rc;
   rc = tile_capacity<kApply, 1>(st, &ctas);
   if (rc != MUON_POLAR_OK) return rc;
-  if (use_pairs(padded_rows(m) / kPairM * ((n + kPairN - 1) / kPairN) * batch, pairs,
-                cost_blocks<2>(m),
-                (m + kHalf - 1) / kHalf * ((n + kHalf - 1) / kHalf) * batch, ctas,
-                cost_blocks<1>(m)))
+  // By size, a short apply (K = m <= 512) that the pairs finish in at most two
+  // rounds runs on single CTAs: its four rounds of 128 x 128 tiles end more
+  // evenly and store half the bytes per CTA in the last epilogue, which the
+  // pair engine's higher per-SM rate does not make up for.  Measured on B200
+  // (steps chained in CUDA graphs): [8,512,2048] 32.4 -> 31.9 us,
+  // [4,512,2048] 27.2 -> 26.0, [4,256,4096] 29.9 -> 28.2, [16,256,2048]
+  // 28.8 -> 28.0; with K = 1024 the pairs stay ahead ([2,1024,4096] 47.0
+  // against 49.2 us).
+  const int64_t tiles2 = padded_rows(m) / kPairM * ((n + kPairN - 1) / kPairN) * batch;
+  const bool short_apply =
+      g_policy.load(std::memory_order_relaxed) == 0 && m <= 512 && tiles2 <= 2 * pairs;
+  if (!short_apply && use_pairs(tiles2, pairs, cost_blocks<2>(m),
+                                (m + kHalf - 1) / kHalf * ((n + kHalf - 1) / kHalf) * batch,
+                                ctas, cost_blocks<1>(m)))
     return apply_launch<2>(st, poly, x, y, batch, m, n, ldx, ldy, a, stream);
   return apply_launch<1>(st, poly, x, y, batch, m, n, ldx, ldy, a, stream);
 }
