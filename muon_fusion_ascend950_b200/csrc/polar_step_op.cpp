@@ -129,9 +129,8 @@ at::Tensor RunPolarStep(const at::Tensor& x, double a, double b, double c, bool 
   int64_t ld = cols;
   if (!aligned) {
     ld = AlignUp(cols, 16);
-    at::Tensor padded = at::zeros({batch, rows, ld}, input.options());
-    padded.narrow(2, 0, cols).copy_(input);
-    input = padded;
+    // one kernel: a fresh (aligned) buffer with zero-filled pad columns
+    input = ld == cols ? input.clone() : at::constant_pad_nd(input, {0, ld - cols}, 0);
   }
   const auto stream = c10::cuda::getCurrentCUDAStream(x.device().index());
   void* raw_stream = static_cast<void*>(stream.stream());
@@ -229,9 +228,7 @@ at::Tensor PolarExpressCuda(const at::Tensor& x, at::ArrayRef<double> coefficien
                      (reinterpret_cast<uintptr_t>(input.data_ptr()) % 16) != 0)) {
     // read in place by the first step: the TMA row-stride rule needs a copy
     ldx = AlignUp(cols, 16);
-    at::Tensor padded = at::zeros({batch, rows, ldx}, input.options());
-    padded.narrow(2, 0, cols).copy_(input);
-    input = padded;
+    input = ldx == cols ? input.clone() : at::constant_pad_nd(input, {0, ldx - cols}, 0);
   } else if ((reinterpret_cast<uintptr_t>(input.data_ptr()) % 16) != 0) {
     input = input.clone();
   }
