@@ -159,26 +159,33 @@ struct WorkItem {
   int half;
 };
 
-__host__ __device__ __forceinline__ WorkItem decode_item(const EpiParams& p, int item,
-                                                         bool sym) {
+// Work item `item` of the column-halves layout (EpiParams::halves).
+__host__ __device__ __forceinline__ WorkItem decode_halves_item(const EpiParams& p, int item) {
   WorkItem w;
-  if (p.halves) {
-    const int d = p.tiles_m;
-    w.b = item / (d * d);
-    const int r = item - w.b * d * d;
-    const int i = r / d, j = r - (r / d) * d;
-    w.tm = i < j ? i : j;
-    w.tn = i < j ? j : i;
-    w.half = i == j ? -1 : (i < j ? 0 : 1);
-    w.tile = item;
-    w.split = 0;
-    w.nsplit = 1;
-    w.kb_begin = 0;
-    w.kb_end = p.k_blocks;
-    return w;
-  }
+  const int d = p.tiles_m;
+  w.b = item / (d * d);
+  const int r = item - w.b * d * d;
+  const int i = r / d, j = r - (r / d) * d;
+  w.tm = i < j ? i : j;
+  w.tn = i < j ? j : i;
+  w.half = i == j ? -1 : (i < j ? 0 : 1);
+  w.tile = item;
+  w.split = 0;
+  w.nsplit = 1;
+  w.kb_begin = 0;
+  w.kb_end = p.k_blocks;
+  return w;
+}
+
+// Work item `item` of the tile layouts: whole tiles (the upper triangle of
+// symmetric kinds), each cut into p.splits K ranges (SPLIT; otherwise one
+// item per tile).
+template <bool SPLIT>
+__host__ __device__ __forceinline__ WorkItem decode_tile_item(const EpiParams& p, int item,
+                                                              bool sym) {
+  WorkItem w;
   w.half = -1;
-  const int tile = item / p.splits;
+  const int tile = SPLIT ? item / p.splits : item;
   const bool walk = sym && !p.rows_mode;
   const TileCoord tc = decode_tile(tile, walk, p.tiles_m, p.tiles_n, p.tiles_per_batch,
                                    walk ? p.row_tile_begin : 0, walk ? p.tile_offset : 0);
@@ -186,10 +193,17 @@ __host__ __device__ __forceinline__ WorkItem decode_item(const EpiParams& p, int
   w.b = tc.b;
   w.tm = walk ? tc.tm : tc.tm + p.row_tile_begin;
   w.tn = tc.tn;
-  w.split = item - tile * p.splits;
-  w.nsplit = p.splits;
-  w.kb_begin = w.split * p.k_blocks / w.nsplit;
-  w.kb_end = (w.split + 1) * p.k_blocks / w.nsplit;
+  if constexpr (SPLIT) {
+    w.split = item - tile * p.splits;
+    w.nsplit = p.splits;
+    w.kb_begin = w.split * p.k_blocks / w.nsplit;
+    w.kb_end = (w.split + 1) * p.k_blocks / w.nsplit;
+  } else {
+    w.split = 0;
+    w.nsplit = 1;
+    w.kb_begin = 0;
+    w.kb_end = p.k_blocks;
+  }
   return w;
 }
 
@@ -420,6 +434,18 @@ __global__ void __launch_bounds__(kTileThreads, 1)
   constexpr bool kAmn = a_mn_major(KIND);
   constexpr bool kBmn = b_mn_major(KIND);
   constexpr bool kSym = Cfg::kSym;
+  // Each launch compiles in only the work-item decode of its layout, and the
+  // column-halves kernels no packed or rows-mode paths: code a kernel never
+  // runs still costs time (measured on B200, dropping the tile-walk decode
+  // and the packed paths from the halves kernels made the config-1 step
+  // 32.1 -> 31.0 us, [1,129,130] 13.3 -> 12.9 us; the split-K arithmetic
+  // from the decode of launches without it, 31.0 -> 30.8 us).
+  auto decode = [](const EpiParams& q, int item, bool sym) {
+    if constexpr (HALVES)
+      return decode_halves_item(q, item);
+    else
+      return decode_tile_item<SPLIT>(q, item, sym);
+  };
 
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_addr(smem_raw);
@@ -563,7 +589,7 @@ __global__ void __launch_bounds__(kTileThreads, 1)
       WorkItem w_first = {};
       bool prepared = false;  // stage 0 is free and its bytes are expected
       if (cluster < p.total_items) {
-        w_first = decode_item(p, cluster, kSym);
+        w_first = decode(p, cluster, kSym);
         if (w_first.kb_begin < w_first.kb_end) {
           if (rank == 0) mbar_arrive_expect_tx(&full[0], PAIR * share_of(w_first).bytes);
           prepared = true;
@@ -572,7 +598,7 @@ __global__ void __launch_bounds__(kTileThreads, 1)
       grid_dependency_wait();
       grid_launch_dependents();
       for (int item = cluster; ok && item < p.total_items; item += nclusters) {
-        const WorkItem w = item == cluster ? w_first : decode_item(p, item, kSym);
+        const WorkItem w = item == cluster ? w_first : decode(p, item, kSym);
         const Share sh = share_of(w);
         for (int kb = w.kb_begin; kb < w.kb_end; ++kb, ++it) {
           const uint32_t s = it % S;
@@ -619,7 +645,7 @@ __global__ void __launch_bounds__(kTileThreads, 1)
       uint32_t t = 0;
       bool ok = true;
       for (int item = cluster; ok && item < p.total_items; item += nclusters, ++t) {
-        const WorkItem w = decode_item(p, item, kSym);
+        const WorkItem w = decode(p, item, kSym);
         const bool diag = kSym && w.tm == w.tn;
         const uint32_t idesc = (HALVES && w.half >= 0) ? idesc_half : idesc_full;
         const uint32_t acc = t & 1u;
@@ -693,7 +719,7 @@ __global__ void __launch_bounds__(kTileThreads, 1)
     // store of this item's chunk c has read the region.
     uint32_t aux_issued[4] = {0u, 0u, 0u, 0u};
     auto load_aux_chunk = [&](int item, int c) {
-      const WorkItem w = decode_item(p, item, kSym);
+      const WorkItem w = decode(p, item, kSym);
       mbar_arrive_expect_tx(&aux_full[c], Cfg::kOutChunkBytes);
       tma_load_3d(sOut + c * Cfg::kOutChunkBytes, &tmap_aux, &aux_full[c],
                   w.tn * kTileN + (HALVES && w.half > 0 ? kChunkCols : 0) + c * kChunkCols,
@@ -702,7 +728,7 @@ __global__ void __launch_bounds__(kTileThreads, 1)
     };
     // Chunks of an item's epilogue: one for a column half.
     auto chunks_of = [&](int item) {
-      if constexpr (HALVES) return decode_item(p, item, kSym).half >= 0 ? 1 : Cfg::kChunks;
+      if constexpr (HALVES) return decode(p, item, kSym).half >= 0 ? 1 : Cfg::kChunks;
       return Cfg::kChunks;
     };
     auto release_accumulator = [&](uint32_t acc) {
@@ -727,7 +753,7 @@ __global__ void __launch_bounds__(kTileThreads, 1)
       // faster per step).  Prefetching into L2, the point of coherence, is
       // safe even while the previous kernel still writes X.
       if (p.prefetch_base != nullptr && cluster < p.total_items) {
-        const WorkItem w = decode_item(p, cluster, kSym);
+        const WorkItem w = decode(p, cluster, kSym);
         if (w.tm == w.tn) {
           const int r0 = w.tm * kTileM + static_cast<int>(rank) * kHalf;
           const int total = kHalf * p.prefetch_lines;
@@ -756,7 +782,7 @@ __global__ void __launch_bounds__(kTileThreads, 1)
     }
     uint32_t t = 0;
     for (int item = cluster; item < p.total_items; item += nclusters, ++t) {
-      const WorkItem tc = decode_item(p, item, kSym);
+      const WorkItem tc = decode(p, item, kSym);
       const uint32_t acc = t & 1u;
       const uint32_t uph = (t >> 1) & 1u;
       const int next = item + nclusters;
@@ -768,8 +794,8 @@ __global__ void __launch_bounds__(kTileThreads, 1)
         break;
       }
       tc_fence_after();
-      bool mirror = kSym && !p.rows_mode && tc.tm != tc.tn;
-      if constexpr (KIND == kGramF32 || KIND == kPoly) {
+      bool mirror = kSym && (HALVES || !p.rows_mode) && tc.tm != tc.tn;
+      if constexpr ((KIND == kGramF32 || KIND == kPoly) && !HALVES) {
         if (p.packed) mirror = false;
       }
       const int row0 = tc.tm * kTileM + static_cast<int>(rank) * kHalf;
@@ -926,7 +952,7 @@ __global__ void __launch_bounds__(kTileThreads, 1)
           const uint8_t* so = sOut + ro * Cfg::kOutChunkBytes;
           const uint8_t* sm = sMir + rm * Cfg::kMirChunkBytes;
           bool packed = false;
-          if constexpr (KIND == kGramF32 || KIND == kPoly) packed = p.packed != 0;
+          if constexpr ((KIND == kGramF32 || KIND == kPoly) && !HALVES) packed = p.packed != 0;
           if (packed) {
             // the chunk's 128 x 64 block inside its 256 x 256 unit
             const int col = col0 + c * kChunkCols;
