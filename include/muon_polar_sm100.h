@@ -388,6 +388,19 @@ int muon_polar_set_split_mode(int mode);
  * The results are bit-identical in every mode. */
 int muon_polar_set_halves_mode(int mode);
 
+/* K depth of the single-CTA bf16 Gram's pipeline stages (kernel 1 on small
+ * problems).  Returns the previous mode:
+ *   0  by size (default): three 64-column swizzle atoms per stage (K = 192,
+ *      two stages in flight) when that covers at most 4% more K than
+ *      two-atom stages (K = 128, three in flight) and the split-K planner,
+ *      counting K in the deeper stages, plans no split;
+ *   1  three atoms whenever that planner plans no split;
+ *   2  never.
+ * Unsplit, the results are bit-identical in every mode (the extra K reads
+ * zeros); where a deep unsplit launch replaces a split-K plan, the last bits
+ * differ as between split and unsplit results (the fp32 summation order). */
+int muon_polar_set_stage_mode(int mode);
+
 /* Number of 2-CTA clusters (tcgen05 CTA pairs) of the Gram kernel the
  * current device runs at once; the persistent grids are this many pairs. */
 int muon_polar_device_pairs(int* pairs);

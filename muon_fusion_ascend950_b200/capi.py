@@ -76,6 +76,7 @@ SIGNATURES = {
     "muon_polar_set_step_mode": (ctypes.c_int, [ctypes.c_int]),
     "muon_polar_set_split_mode": (ctypes.c_int, [ctypes.c_int]),
     "muon_polar_set_halves_mode": (ctypes.c_int, [ctypes.c_int]),
+    "muon_polar_set_stage_mode": (ctypes.c_int, [ctypes.c_int]),
     "muon_polar_device_pairs": (ctypes.c_int, [ctypes.POINTER(ctypes.c_int)]),
     "muon_polar_launch_count": (ctypes.c_uint64, []),
     "muon_polar_tensor_map_encodes": (ctypes.c_uint64, []),
@@ -195,6 +196,15 @@ class CAPI:
         prev = int(self.lib.muon_polar_set_halves_mode(int(mode)))
         if prev < 0:
             raise MuonPolarError("muon_polar_set_halves_mode", prev, self.status_string(prev))
+        return prev
+
+    def set_stage_mode(self, mode: int) -> int:
+        """0 = by size (K = 192 stages for the single-CTA bf16 Gram when
+        they cover at most 4% more K), 1 = whenever no split-K is planned,
+        2 = never; returns the previous mode."""
+        prev = int(self.lib.muon_polar_set_stage_mode(int(mode)))
+        if prev < 0:
+            raise MuonPolarError("muon_polar_set_stage_mode", prev, self.status_string(prev))
         return prev
 
     def device_pairs(self) -> int:

@@ -246,10 +246,13 @@ constexpr uint32_t kAtomBytes = kHalf * kAtom * 2;  // one [128 x 64] box, 16 Ki
 // measured on B200, 64 KiB stages make the pair Gram 7-12% faster at
 // 4096-8192 rows; the polynomial and the apply keep 32 KiB stages, which
 // leave room for four or five of them beside their larger epilogue buffers.
+// The single-CTA bf16 Gram also comes with three atoms per stage (kDeepBK:
+// 96 KiB stages, two in flight), chosen by size in gram_launch.
 template <int KIND, int PAIR>
 constexpr int stage_k() {
   return (PAIR == 1 || KIND == kGramBf16 || KIND == kGramT) ? 128 : 64;
 }
+constexpr int kDeepBK = 192;
 template <int KIND, int PAIR>
 constexpr int64_t k_blocks_of(int64_t k) {
   return (k + stage_k<KIND, PAIR>() - 1) / stage_k<KIND, PAIR>();
@@ -262,7 +265,7 @@ constexpr int64_t k_blocks_of(int64_t k) {
 // 128 x 64 column halves, diagonal tiles whole (see decode_item); a half has
 // one epilogue chunk and a diagonal tile no mirror, so the polynomial's
 // epilogue needs two chunk regions (the mirror of a half shares the second).
-template <int KIND, int PAIR = 2, bool HALVES = false>
+template <int KIND, int PAIR = 2, bool HALVES = false, int BK = 0>
 struct PairCfg {
   static constexpr bool kSym = KIND != kApply && KIND != kApplyT;
   static constexpr bool kAux = KIND == kPoly || KIND == kApply || KIND == kApplyT;
@@ -274,7 +277,7 @@ struct PairCfg {
   static constexpr int kChunks = kTileN / kChunkCols;
   static constexpr uint32_t kOutChunkBytes = kHalf * kChunkCols * kElem;
   static constexpr uint32_t kMirChunkBytes = kSym ? kChunkCols * kHalf * kElem : 0;
-  static constexpr int kBK = stage_k<KIND, PAIR>();
+  static constexpr int kBK = BK > 0 ? BK : stage_k<KIND, PAIR>();  // K per stage
   // Output regions: kAux kinds keep the whole 128 x kTileN input band (updated
   // in place, one region per chunk, never reused within a tile); the Gram
   // single-buffers its chunk region.
@@ -417,7 +420,9 @@ constexpr int kProducerWarp2 = 10;
 // HALVES: the column-halves decomposition (PAIR = 1, symmetric kinds, one
 // item per CTA, no split-K; see EpiParams::halves).  tmap_b then has boxes
 // of 64 rows, the B operand of a half.
-template <int KIND, int PAIR, bool SPLIT, bool HALVES = false>
+// BK: K per pipeline stage if not the kind's default (stage_k); kDeepBK for
+// the single-CTA bf16 Gram on long rows.
+template <int KIND, int PAIR, bool SPLIT, bool HALVES = false, int BK = 0>
 __global__ void __launch_bounds__(kTileThreads, 1)
     polar_tile_kernel(const __grid_constant__ CUtensorMap tmap_a,
                       const __grid_constant__ CUtensorMap tmap_b,
@@ -425,9 +430,11 @@ __global__ void __launch_bounds__(kTileThreads, 1)
                       const __grid_constant__ CUtensorMap tmap_out,
                       const __grid_constant__ CUtensorMap tmap_mir,
                       const EpiParams p) {
-  using Cfg = PairCfg<KIND, PAIR, HALVES>;
+  using Cfg = PairCfg<KIND, PAIR, HALVES, BK>;
   static_assert(!HALVES || (PAIR == 1 && Cfg::kSym && !SPLIT && KIND != kGramT),
                 "column halves: single-CTA symmetric kinds without split-K");
+  static_assert(BK == 0 || (PAIR == 1 && KIND == kGramBf16 && !SPLIT),
+                "deep stages: the single-CTA bf16 Gram without split-K");
   constexpr int kTileM = Cfg::kTileM;
   constexpr int kTileN = Cfg::kTileN;
   constexpr int S = Cfg::kStages;
@@ -1832,6 +1839,7 @@ struct DeviceState {
   int cc_major = 0, cc_minor = 0;
   bool smem_attr_set[kNumInstances] = {};
   bool smem_attr_set_halves[kNumInstances] = {};  // the HALVES kernels
+  bool smem_attr_set_deep[2] = {};  // the kDeepBK Gram kernels: whole tiles, halves
   int capacity[kNumInstances] = {};  // tiles worked on at once (tile_capacity)
 };
 DeviceState g_devices[kMaxDevices];
@@ -2087,6 +2095,23 @@ void plan_halves(EpiParams& p, int64_t batch, int units) {
   p.total_items = static_cast<int32_t>(items);
 }
 
+// Stage depth of the single-CTA bf16 Gram (muon_polar_set_stage_mode): 0 by
+// size, 1 whenever it runs without split-K (see gram_launch), 2 never.  By size, kDeepBK
+// stages when they cover at most 4% more K than two-atom stages: fewer,
+// larger stages for the K loop, with the last one's columns past n read as
+// zeros.  Measured on B200 (steps chained in CUDA graphs): [8,512,2048]
+// 30.74 -> 30.48 us, [2,150,2064] 21.8 -> 19.9 us; with 12.5% more K,
+// [4,512,1024] 19.3 -> 19.7 us and [1,1024,512] 19.7 -> 19.8 us.
+std::atomic<int> g_stage_mode{0};
+
+bool use_deep_stages(int64_t n) {
+  const int mode = g_stage_mode.load(std::memory_order_relaxed);
+  if (mode != 0) return mode == 1;
+  const int64_t k2 = (n + 127) / 128 * 128;
+  const int64_t k3 = (n + kDeepBK - 1) / kDeepBK * kDeepBK;
+  return k3 * 100 <= k2 * 104;
+}
+
 // Applies split-K to `p` if the scratch buffer allows it.
 template <int KIND, int PAIR>
 void plan_splits(EpiParams& p, void* scratch, size_t scratch_bytes, int units) {
@@ -2177,12 +2202,16 @@ int tile_capacity(DeviceState* st, int* capacity) {
   return MUON_POLAR_OK;
 }
 
+// `deep`: the single-CTA bf16 Gram with kDeepBK stages (p.k_blocks counted
+// in them; no split-K).
 template <int KIND, int PAIR>
 int launch_tile(DeviceState* st, const TileMaps& maps, const EpiParams& p,
-                cudaStream_t stream) {
+                cudaStream_t stream, bool deep = false) {
   int units = 0;
   int rc = tile_capacity<KIND, PAIR>(st, &units);
   if (rc != MUON_POLAR_OK) return rc;
+  constexpr bool kCanDeepen = PAIR == 1 && KIND == kGramBf16;
+  if (deep && (!kCanDeepen || p.splits != 1)) return MUON_POLAR_ERR_INVALID_ARGUMENT;
   constexpr bool kCanHalve = PAIR == 1 && PairCfg<KIND, PAIR>::kSym && KIND != kGramT;
   if constexpr (kCanHalve) {
     if (p.halves) {
@@ -2223,6 +2252,36 @@ int launch_tile(DeviceState* st, const TileMaps& maps, const EpiParams& p,
   cfg.attrs = attr;
   cfg.numAttrs = 2;
   cudaError_t e;
+  if constexpr (kCanDeepen) {
+    if (deep) {
+      const bool h = p.halves != 0;
+      {
+        std::lock_guard<std::mutex> lock(g_attr_mutex);
+        if (!st->smem_attr_set_deep[h]) {
+          e = h ? cudaFuncSetAttribute(polar_tile_kernel<KIND, PAIR, false, true, kDeepBK>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       PairCfg<KIND, PAIR, true, kDeepBK>::kSmemBytes)
+                : cudaFuncSetAttribute(polar_tile_kernel<KIND, PAIR, false, false, kDeepBK>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       PairCfg<KIND, PAIR, false, kDeepBK>::kSmemBytes);
+          if (e != cudaSuccess) return static_cast<int>(e);
+          st->smem_attr_set_deep[h] = true;
+        }
+      }
+      if (h) {
+        cfg.dynamicSmemBytes = PairCfg<KIND, PAIR, true, kDeepBK>::kSmemBytes;
+        e = cudaLaunchKernelEx(&cfg, polar_tile_kernel<KIND, PAIR, false, true, kDeepBK>,
+                               maps.a, maps.b, maps.aux, maps.out, maps.mir, p);
+      } else {
+        cfg.dynamicSmemBytes = PairCfg<KIND, PAIR, false, kDeepBK>::kSmemBytes;
+        e = cudaLaunchKernelEx(&cfg, polar_tile_kernel<KIND, PAIR, false, false, kDeepBK>,
+                               maps.a, maps.b, maps.aux, maps.out, maps.mir, p);
+      }
+      if (e != cudaSuccess) return static_cast<int>(e);
+      g_launch_count.fetch_add(1, std::memory_order_relaxed);
+      return MUON_POLAR_OK;
+    }
+  }
   if constexpr (kCanHalve) {
     if (p.halves) {
       cfg.dynamicSmemBytes = PairCfg<KIND, PAIR, true>::kSmemBytes;
@@ -2360,7 +2419,20 @@ int gram_launch(DeviceState* st, const void* x, void* gram, int64_t batch, int64
                                 choose_splits<KIND, PAIR>(p.total_tiles, p.k_blocks, units)) >
           scratch_bytes)
     return MUON_POLAR_ERR_STATIC_SCRATCH;
-  plan_splits<KIND, PAIR>(p, scratch, scratch_bytes, units);
+  // Deep stages (single-CTA bf16 Gram) are chosen before split-K: counted in
+  // kDeepBK blocks the K loop is shorter, and when the split planner then
+  // plans no split the launch runs unsplit on deep stages (measured on B200,
+  // [2,150,2064] 21.8 -> 19.9 us against four splits of K = 128 stages).
+  bool deep = false;
+  if constexpr (PAIR == 1 && KIND == kGramBf16) {
+    const int64_t kb3 = (n + kDeepBK - 1) / kDeepBK;
+    deep = !fixed_scratch && use_deep_stages(n) &&
+           (scratch == nullptr || choose_splits<KIND, PAIR>(p.total_tiles, kb3, units) == 1);
+  }
+  if (deep)
+    plan_no_splits(p);
+  else
+    plan_splits<KIND, PAIR>(p, scratch, scratch_bytes, units);
   if constexpr (PAIR == 1 && !kT) {
     if (!fixed_scratch) plan_halves(p, batch, units);
     if (p.halves) {
@@ -2373,7 +2445,8 @@ int gram_launch(DeviceState* st, const void* x, void* gram, int64_t batch, int64
     cudaError_t e = cudaMemsetAsync(scratch, 0, kCounterBytes, stream);
     if (e != cudaSuccess) return static_cast<int>(e);
   }
-  return launch_tile<KIND, PAIR>(st, tm, p, stream);
+  if (deep) p.k_blocks = static_cast<int32_t>((n + kDeepBK - 1) / kDeepBK);
+  return launch_tile<KIND, PAIR>(st, tm, p, stream, deep);
 }
 
 // `fixed_scratch` callers always run the CTA-pair engine (the size of their
@@ -3363,6 +3436,11 @@ int muon_polar_set_kernel_policy(int policy) {
 int muon_polar_set_step_mode(int mode) {
   if (mode < 0 || mode > 2) return MUON_POLAR_ERR_INVALID_ARGUMENT;
   return g_step_mode.exchange(mode);
+}
+
+int muon_polar_set_stage_mode(int mode) {
+  if (mode < 0 || mode > 2) return MUON_POLAR_ERR_INVALID_ARGUMENT;
+  return g_stage_mode.exchange(mode);
 }
 
 int muon_polar_set_halves_mode(int mode) {

@@ -501,3 +501,34 @@ def test_gram_f32_bands_assemble_the_gram(api, cuda_device, shape, bands, reserv
     finally:
         api.lib.muon_polar_set_split_mode(prev)
     assert torch.equal(banded, full)
+
+
+@pytest.mark.parametrize("shape", [(8, 512, 2048), (2, 150, 2064), (4, 512, 1024),
+                                   (1, 129, 136), (3, 640, 1000), (9, 512, 2048)])
+def test_deep_gram_stages_match(api, cuda_device, shape):
+    """The single-CTA bf16 Gram with three-atom stages (K = 192) gives the bits
+    of two-atom stages (K = 128): the k-steps run in the same order and the
+    last stage's columns past n add zeros.  Checked on the Gram and on a whole
+    step, with the column halves and with whole tiles ((9, 512, 2048)), and
+    on widths that are and are not multiples of 192."""
+    bsz, m, n = shape
+    x = make_input(shape, seed=37).to(cuda_device)
+    mp = api.padded_rows(m)
+    prev_policy = api.set_kernel_policy(2)
+    outs = {}
+    try:
+        for mode in (2, 1):
+            api.set_stage_mode(mode)
+            g = torch.full((bsz, mp, mp), float("nan"), device=cuda_device, dtype=torch.bfloat16)
+            api.gram(x, g)
+            ws = torch.empty(api.workspace_bytes(bsz, m), dtype=torch.uint8, device=cuda_device)
+            y = torch.full_like(x, float("nan"))
+            api.step(x, y, ws, A1, B1, C1)
+            torch.cuda.synchronize()
+            _check_watchdog(api)
+            outs[mode] = (g, y)
+    finally:
+        api.set_stage_mode(0)
+        api.set_kernel_policy(prev_policy)
+    for a, b in zip(outs[2], outs[1]):
+        assert torch.equal(a.view(torch.int16), b.view(torch.int16))
