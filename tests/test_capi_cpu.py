@@ -256,3 +256,26 @@ def test_wait_limit_setter_validation_without_device(api):
     for bad in (0, 999, 60_000_000_001):
         with pytest.raises(MuonPolarError):
             api.set_wait_limit_ns(bad)
+
+
+def test_mode_setters_round_trip_without_device(api):
+    """Every process-wide mode setter rejects out-of-range values with
+    MUON_POLAR_ERR_INVALID_ARGUMENT, leaves the mode unchanged then, and
+    returns the previous mode on a valid call (none needs a GPU)."""
+    lib = api.lib
+    setters = {  # name: highest valid mode
+        "muon_polar_set_kernel_policy": 2,
+        "muon_polar_set_split_mode": 2,
+        "muon_polar_set_step_mode": 2,
+        "muon_polar_set_halves_mode": 2,
+        "muon_polar_set_stage_mode": 2,
+    }
+    for name, hi in setters.items():
+        fn = getattr(lib, name)
+        start = fn(0)
+        assert 0 <= start <= hi, name
+        assert fn(hi + 1) == -1, name
+        assert fn(-1) == -1, name
+        for mode in range(hi + 1):
+            assert fn(mode) == (0 if mode == 0 else mode - 1), name
+        assert fn(start) == hi, name  # restore
