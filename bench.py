@@ -194,6 +194,30 @@ def workload_config(workload: str, world: int) -> dict:
     }
 
 
+def large_workload_config(workload: str, world: int, column_path: str = "packed",
+                          bands: int = 0, sm_reserve: int = 16, poly_slabs: bool = True) -> dict:
+    """The `config` object of configs 4 and 5, identical for both arms (the
+    reference arm describes the GPU arm's default column-sharded path)."""
+    if workload == "cfg4":
+        return {"workload": ("Muon update of a 32-layer 7B model: 5-step loop on [128,4096,4096] + "
+                             "[96,4096,11008] bf16 (BASELINE config 4)"),
+                "parallelism": f"batch-sharded x{world} (FLOP-balanced, no data-path collective)",
+                "l2": "inputs larger than L2"}
+    if world == 1:
+        parallelism = "single GPU"
+    elif column_path == "packed":
+        parallelism = (f"column-sharded x{world}: packed upper-triangle units, NCCL fp32 "
+                       "reduce-scatter + bf16 all-gathers of A and P per step")
+    else:
+        reduce = ("one NCCL fp32 all-reduce of the 8192x8192 partial Gram per step" if not bands
+                  else f"the partial Gram in {bands} row bands, each NCCL fp32 all-reduced while "
+                       f"the next computes ({sm_reserve} SMs left to NCCL)")
+        parallelism = (f"column-sharded x{world}, {reduce}, kernel 2 "
+                       + ("in row slabs + NCCL bf16 all-gather" if poly_slabs else "replicated"))
+    return {"workload": "5-step loop on one [8192,65536] bf16 matrix (BASELINE config 5)",
+            "parallelism": parallelism, "l2": "inputs larger than L2"}
+
+
 def metric_name(workload: str) -> str:
     shape_str = f"[{BATCH},{M},{N}]"
     if workload == "cfg3":
@@ -508,7 +532,7 @@ def run_reference(args):
     if workload in ("cfg4", "cfg5"):
         rate, ms, threads, sample = reference_large_rate(workload)
         metric = f"{workload} effective TFLOP/s (nominal 4M^2N+2M^3 per matrix per step)"
-        config = {"workload": workload}
+        config = large_workload_config(workload, args.gpus)
     else:
         rows = len(COEFFICIENTS) if workload in ("cfg3", "express") else 1
         rate, threads, sample = cpu_reference_rate(args.steps, args.warmup, budget_s=120.0,
@@ -911,9 +935,7 @@ def run_large(args):
                 for a, b, c in COEFFICIENTS:
                     y = pkg.polar_step(y, a, b, c)
 
-        workload = ("Muon update of a 32-layer 7B model: 5-step loop on [128,4096,4096] + "
-                    "[96,4096,11008] bf16 (BASELINE config 4)")
-        parallelism = f"batch-sharded x{world} (FLOP-balanced, no data-path collective)"
+        config = large_workload_config("cfg4", world)
     else:
         m, n = 8192, 65536
         cols = column_range(n, rank, world)
@@ -930,15 +952,10 @@ def run_large(args):
         def step():
             driver.run(x_local, COEFFICIENTS)
 
-        workload = "5-step loop on one [8192,65536] bf16 matrix (BASELINE config 5)"
-        reduce = ("one NCCL fp32 all-reduce of the 8192x8192 partial Gram per step"
-                  if not driver.bands else
-                  f"the partial Gram in {len(driver.bands)} row bands, each NCCL fp32 "
-                  f"all-reduced while the next computes ({args.sm_reserve} SMs left to NCCL)")
-        parallelism = (f"column-sharded x{world}, {reduce}, kernel 2 "
-                       + ("in row slabs + NCCL bf16 all-gather"
-                          if driver.poly_slab is not None else "replicated")
-                       if world > 1 else "single GPU")
+        config = large_workload_config(
+            "cfg5", world, column_path="packed" if driver.packed else "all-reduce",
+            bands=len(driver.bands), sm_reserve=args.sm_reserve,
+            poly_slabs=driver.poly_slab is not None)
 
     def sync_all():
         torch.cuda.synchronize(device)
@@ -982,9 +999,8 @@ def run_large(args):
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic",
         "pct_of_bf16_peak": 100.0 * value / (world * peak),
-        "config": {"workload": workload, "parallelism": parallelism,
-                   "timing": "eager public API / column-sharded driver, CUDA events, max over ranks",
-                   "l2": "inputs larger than L2"},
+        "config": config,
+        "timing": "eager public API / column-sharded driver, CUDA events, max over ranks",
         "roofline": {"bound": "tensor", "kernel": "whole step", "achieved": value / world,
                      "peak": peak, "unit": "TFLOP/s", "frac": value / world / peak,
                      "traffic": None, "peak_source": f"{peak_kind} bf16 dense (burst)"},
